@@ -1,0 +1,357 @@
+#!/usr/bin/env python
+"""MoE-layer prefill throughput (tokens/s) at a 16K-token chunk — BASELINE config 2.
+
+Workload: one Qwen3.5-35B-A3B-like MoE layer: hidden 2048, expert intermediate 512, 256
+experts top-8 (softmax), 64 experts resident on the GPU (the rest masked to -1 as for CPU
+experts), gate/up Q4_K and down Q6_K GGUF blocks, router logits N(0,1) plus a log-space
+Zipf(1.1) per-expert bias, bf16 activations N(0,1), weights N(0,0.02) quantized with the
+package's encoders. All data synthetic and seeded (no checkpoint is available here).
+
+A step = one kt_moe_prefill call over the chunk (routing permutation, tcgen05 gate/up
+GEMM with SwiGLU, tcgen05 down GEMM, combine), inputs resident in HBM. With --gpus N each
+rank processes its own 16K-token chunk against its own replica of the resident experts
+(token-parallel, no data-path collective: "scaling": "weak"); the time is the max over
+ranks of CUDA-event time.
+
+--impl reference times the reference's CPU implementation of the path as restated in
+oracle/ (the reference's own CPU expert library, kt-kernel + llama.cpp, ships only as
+patches on un-vendored sources and cannot be built here) on the host cores.
+"""
+import argparse
+import ctypes
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+sys.path.insert(0, str(ROOT / "kt-prefill-lend_b200"))
+
+METRIC = "MoE-layer prefill tok/s @16K chunk"
+CONFIG_NAME = "qwen3.5-35b-a3b-like MoE layer (BASELINE configs[1])"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-sample", type=int, default=256, help="tokens per CPU-baseline sample")
+    return ap.parse_args()
+
+
+def load_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d["hbm_gbs"], d["bf16_tflops"], d["bf16_tflops_sustained"], "measured"
+    return 6650.0, 1590.0, 1400.0, "fallback"
+
+
+def profile_traffic(name: str):
+    """per-launch DRAM bytes of a kernel from the committed ncu summary, or None"""
+    p = ROOT / "profiles" / name
+    if not p.exists():
+        return None
+    for line in p.read_text().splitlines():
+        if line.startswith("traffic_bytes_per_launch_full_size:"):
+            return float(line.split(":", 1)[1].strip())
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons for one GPU, sampled during the timed region"""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, uuid: str):
+        self.uuid = uuid
+        self.samples = []
+        self._stop = threading.Event()
+        self._t = None
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                r = subprocess.run(["nvidia-smi", "-i", self.uuid, f"--query-gpu={self.FIELDS}",
+                                    "--format=csv,noheader,nounits"], capture_output=True, text=True, timeout=5)
+                f = [x.strip() for x in r.stdout.strip().split(",")]
+                if len(f) == 7:
+                    self.samples.append((time.time(), float(f[0]), float(f[1]), f[3:]))
+            except Exception:
+                pass
+            self._stop.wait(0.1)
+
+    def start(self):
+        self._t = threading.Thread(target=self._run, daemon=True)
+        self._t.start()
+
+    def stop(self, t0, t1):
+        self._stop.set()
+        if self._t:
+            self._t.join(timeout=10)
+        win = [s for s in self.samples if t0 <= s[0] <= t1] or self.samples
+        if not win:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"], "samples": 0}
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for s in win for n, v in zip(names, s[3]) if v.lower().startswith("active")})
+        return {"sm_mhz": statistics.median(s[1] for s in win), "sm_max_mhz": max(s[2] for s in win),
+                "reasons": reasons, "samples": len(win)}
+
+
+def cpu_baseline(L, sample_tokens, threads):
+    """the restated reference arithmetic (q8_1 x GGUF integer dots, OpenMP) on a token sample"""
+    import numpy as np
+    import torch
+
+    from oracle import oracle as O
+
+    O.build()
+    os.environ["OMP_NUM_THREADS"] = str(threads)
+    n = min(sample_tokens, L.x.shape[0])
+    xb = L.x[:n].view(torch.int16).numpy().view(np.uint16)
+    ids = L.topk_ids[:n].numpy()
+    w = L.topk_weights[:n].numpy()
+    O.moe_ref_bf16(xb[:8], ids[:8], w[:8], L.type13, L.w13, L.type2, L.w2, L.inter)  # warm-up
+    times = []
+    for _ in range(2):
+        t = time.perf_counter()
+        O.moe_ref_bf16(xb, ids, w, L.type13, L.w13, L.type2, L.w2, L.inter)
+        times.append(time.perf_counter() - t)
+    return n / min(times), n
+
+
+def host_threads():
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+def run_reference(args, rank):
+    if rank != 0:
+        return
+    from kt_gguf_b200 import synth
+
+    threads = host_threads()
+    os.environ["OMP_NUM_THREADS"] = str(threads)
+    import numpy as np
+    import torch
+
+    from oracle import oracle as O
+
+    O.build()
+    L = synth.make_layer(args.seed, **synth.CONFIGS[2])
+    n = min(args.cpu_sample, L.x.shape[0])
+    xb = L.x.view(torch.int16).numpy().view(np.uint16)
+    ids = L.topk_ids.numpy()
+    w = L.topk_weights.numpy()
+    T = L.x.shape[0]
+
+    def step(i):
+        s = (i * n) % (T - n + 1)
+        O.moe_ref_bf16(xb[s:s + n], ids[s:s + n], w[s:s + n], L.type13, L.w13, L.type2, L.w2, L.inter)
+
+    for i in range(args.warmup):
+        step(i)
+    t0 = time.perf_counter()
+    for i in range(args.steps):
+        step(args.warmup + i)
+    dt = time.perf_counter() - t0
+    value = n * args.steps / dt
+    sample = f"{n} consecutive tokens of the 16K chunk per step (all their routes), extrapolated per token"
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "int8 x gguf (q8_1 activations), fp32 accumulate",
+        "data": "synthetic (seeded)",
+        "config": {"workload": CONFIG_NAME, "tokens": T, "hidden": 2048, "inter": 512, "experts": 256, "top_k": 8,
+                   "resident_experts": 64, "types": "Q4_K gate/up, Q6_K down", "device": "host CPU"},
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port", "sample": sample},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_b200(args, rank, world, local_rank):
+    import numpy as np
+    import torch
+
+    from kt_gguf_b200 import _native as Nt
+    from kt_gguf_b200 import kt_gguf_moe_multi as M
+    from kt_gguf_b200 import synth
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+    cfg = synth.CONFIGS[2]
+    L = synth.make_layer(args.seed + rank, **cfg)
+    T, K, N = L.x.shape[0], cfg["hidden"], cfg["inter"]
+    x = L.x.to(dev)
+    w13 = torch.from_numpy(L.w13).to(dev)
+    w2 = torch.from_numpy(L.w2).to(dev)
+    ids = L.topk_ids.to(dev)
+    wts = L.topk_weights.to(dev)
+    S, k = w13.shape[0], ids.shape[1]
+    lib = Nt.load()
+    ws = Nt.workspace(lib.kt_moe_prefill_workspace_size(T, k, K, N, S), dev)
+    out = torch.empty((T, K), dtype=torch.bfloat16, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(5)]
+    for e in ev:
+        e.record(stream)
+    handles = (ctypes.c_void_p * 4)(*[e.cuda_event for e in ev[1:]])
+    r_hot = int((L.topk_ids >= 0).sum())
+
+    def step(timed=None):
+        if timed is not None:
+            timed[0].record(stream)
+        Nt.check(lib.kt_moe_prefill_timed(Nt.ptr(x), T, K, N, Nt.ptr(ids), Nt.ptr(wts), k, Nt.ptr(w13), L.type13,
+                                          Nt.ptr(w2), L.type2, 0, S, Nt.ptr(out), Nt.ptr(ws), ws.numel(), stream.cuda_stream,
+                                          handles if timed is not None else None), "kt_moe_prefill")
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    assert Nt.workspace_status(ws) == Nt.KT_DEV_OK
+    # per-stage times (separate pass with stage events; each event pair is one step)
+    stage = [[] for _ in range(4)]
+    for _ in range(max(3, min(20, args.steps))):
+        step(ev)
+        torch.cuda.synchronize()
+        for i in range(4):
+            stage[i].append(ev[i].elapsed_time(ev[i + 1]))
+    stage_ms = [statistics.median(s) for s in stage]
+
+    uuid = torch.cuda.get_device_properties(dev).uuid
+    sampler = ClockSampler(f"GPU-{uuid}") if rank == 0 else None
+    if sampler:
+        sampler.start()
+        time.sleep(0.3)
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    t_begin, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    wall0 = time.time()
+    t_begin.record(stream)
+    for _ in range(args.steps):
+        step()
+    t_end.record(stream)
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    wall1 = time.time()
+    ms = t_begin.elapsed_time(t_end)
+    if dist:
+        m = torch.tensor([ms], device=dev)
+        dist.all_reduce(m, op=dist.ReduceOp.MAX)
+        ms = float(m.item())
+    clocks = sampler.stop(wall0, wall1) if sampler else None
+    assert Nt.workspace_status(ws) == Nt.KT_DEV_OK
+
+    # end to end through the public API: pinned host inputs in, host output back, every step
+    x_h = L.x.pin_memory()
+    ids_h = L.topk_ids.pin_memory()
+    w_h = L.topk_weights.pin_memory()
+    out_h = torch.empty((T, K), dtype=torch.bfloat16).pin_memory()
+
+    def e2e_step():
+        xd = x_h.to(dev, non_blocking=True)
+        idd = ids_h.to(dev, non_blocking=True)
+        wd = w_h.to(dev, non_blocking=True)
+        o = M.moe_prefill(xd, w13, w2, idd, wd, L.type13, L.type2, N, workspace=ws)
+        out_h.copy_(o, non_blocking=True)
+
+    for _ in range(3):
+        e2e_step()
+    torch.cuda.synchronize()
+    e_steps = max(5, args.steps // 4)
+    if dist:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(e_steps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e_ms = e0.elapsed_time(e1)
+    if dist:
+        m = torch.tensor([e_ms], device=dev)
+        dist.all_reduce(m, op=dist.ReduceOp.MAX)
+        e_ms = float(m.item())
+    h2d = x_h.numel() * 2 + ids_h.numel() * 4 + w_h.numel() * 4
+    d2h = out_h.numel() * 2
+
+    if rank == 0:
+        hbm, tf_burst, tf_sust, peak_kind = load_peaks()
+        flops_gate_up = 4.0 * K * N * r_hot
+        flops_down = 2.0 * K * N * r_hot
+        gate_up_tflops = flops_gate_up / (stage_ms[1] * 1e-3) / 1e12
+        traffic = profile_traffic("prefill_gate_up_config2.txt")
+        cpu = None
+        if world == 1 and not args.no_cpu_baseline:
+            threads = host_threads()
+            v, n = cpu_baseline(L, args.cpu_sample, threads)
+            cpu = {"value": v, "unit": "tokens/s", "cores": threads, "kind": "port",
+                   "sample": f"first {n} tokens of the chunk (all their routes), restated reference q8_1 x GGUF "
+                             f"integer-dot arithmetic, OpenMP"}
+        value = world * T * args.steps / (ms * 1e-3)
+        line = {
+            "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16 (GGUF Q4_K/Q6_K weights dequantized in-kernel, fp32 accumulate)",
+            "data": "synthetic (seeded)",
+            "config": {"workload": CONFIG_NAME, "tokens_per_gpu": T, "hidden": K, "inter": N, "experts": 256,
+                       "top_k": k, "resident_experts": S, "routed_to_resident": r_hot,
+                       "types": "Q4_K gate/up, Q6_K down", "parallelism": f"token-parallel x{world} (replicated slots)",
+                       "l2": "no flush: one step's working set (130 MB weights + 67 MB x + 0.66 GB H/Y) exceeds the 126 MB L2"},
+            "stage_ms": {"permute": stage_ms[0], "gate_up_gemm": stage_ms[1], "down_gemm": stage_ms[2],
+                         "combine": stage_ms[3]},
+            "roofline": {"bound": "tensor", "kernel": "kt_moe_gemm_kernel<Q4_K, gate/up>",
+                         "achieved": gate_up_tflops, "peak": tf_sust, "unit": "TFLOP/s",
+                         "frac": gate_up_tflops / tf_sust, "peak_kind": f"{peak_kind} bf16 sustained",
+                         "traffic": traffic,
+                         "down_gemm_tflops": flops_down / (stage_ms[2] * 1e-3) / 1e12,
+                         "layer_tflops": (flops_gate_up + flops_down) * args.steps / (ms * 1e-3) / 1e12},
+            "cpu_baseline": cpu,
+            "e2e": {"value": world * T * e_steps / (e_ms * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h},
+            "gpu_launches": 6 * args.steps,
+            "clocks": clocks,
+        }
+        print(json.dumps(line), flush=True)
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main():
+    args = parse()
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, rank)
+        return
+    run_b200(args, rank, world, local_rank)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,170 @@
+/*
+ * kt_gguf_b200.h — C ABI of the B200 (sm_100a) GGUF hot-expert MoE library
+ * (libkt_gguf_b200.so).
+ *
+ * Plain pointers and sizes only: every device pointer is a CUDA device address on the
+ * current device, `stream` is a cudaStream_t passed as void*, and nothing here allocates
+ * device memory: outputs and scratch ("workspace") come from the caller, sized by the
+ * *_workspace_size queries. All calls are asynchronous on `stream` and never synchronize
+ * the host, so they can be captured into CUDA graphs.
+ *
+ * Return value: KT_OK, or a KT_ERR_* code for arguments rejected on the host (nothing is
+ * launched then). Kernels that wait on on-chip barriers bound every wait; if one runs out
+ * they write KT_DEV_TIMEOUT into the workspace's status word, which kt_workspace_status()
+ * reads after the stream has finished.
+ *
+ * Types: ggml type ids KT_GGML_Q8_0 (8), KT_GGML_Q4_K (12), KT_GGML_Q6_K (14),
+ * KT_GGML_IQ3_S (21). Activation dtypes: KT_DTYPE_F32 (0), KT_DTYPE_F16 (1), KT_DTYPE_BF16 (2).
+ *
+ * Weight layout (as the reference's KTGGUFHotExpertsMethod, hot/kt_gguf_hot.py:17-20):
+ *   w13  uint8 [n_slots, 2*inter, row_bytes(hidden)]   rows [gate; up]
+ *   w2   uint8 [n_slots, hidden,  row_bytes(inter)]
+ * or, with w_is_table = 1, w points at an int64 device table of n_slots per-slot addresses
+ * (the reference's KT_PTR_TABLE build, kt_gguf_moe_multi.cu:184-189). Slot addresses in a
+ * table must be 16-byte aligned.
+ * Slot ids: route p uses slot ids[p]; ids outside [0, n_slots) (the reference uses -1 for
+ * experts on the CPU) produce zero rows / contribute nothing.
+ */
+#ifndef KT_GGUF_B200_H
+#define KT_GGUF_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define KT_OK 0
+#define KT_ERR_ARG 1       /* invalid argument (null pointer, bad shape, unsupported size) */
+#define KT_ERR_TYPE 2      /* ggml type without a kernel here */
+#define KT_ERR_WORKSPACE 3 /* workspace smaller than the *_workspace_size query */
+#define KT_ERR_CUDA 4      /* a CUDA call or launch failed */
+#define KT_ERR_DEVICE 5    /* the GPU is not an sm_100 part */
+
+#define KT_DEV_OK 0
+#define KT_DEV_TIMEOUT 1
+
+#define KT_GGML_Q8_0 8
+#define KT_GGML_Q4_K 12
+#define KT_GGML_Q6_K 14
+#define KT_GGML_IQ3_S 21
+
+#define KT_DTYPE_F32 0
+#define KT_DTYPE_F16 1
+#define KT_DTYPE_BF16 2
+
+/* Library version (major * 10000 + minor * 100 + patch). */
+int kt_version(void);
+/* Static description of a status code. */
+const char* kt_status_string(int status);
+/* 1 if the current device is an sm_100 GPU this library was built for, else 0. */
+int kt_device_supported(void);
+
+/* Bytes of one row of `cols` values in GGUF blocks of `ggml_type`.
+ * Replaces BLOCK_INFO / _row_bytes (hot/kt_gguf_hot.py:62-93). */
+int kt_gguf_row_bytes(int ggml_type, int64_t cols, int64_t* row_bytes);
+
+/* Reads the device status word of a workspace used by a previous call (synchronizes the
+ * stream first). *status = KT_DEV_OK or KT_DEV_TIMEOUT. */
+int kt_workspace_status(const void* workspace, void* stream, int* status);
+
+/* q8_1 activation quantizer: x [rows, cols] (dtype) -> qx [rows, qrow] bytes, with
+ * qrow = ceil(cols / 512) * 512 / 32 * 36. Replaces quantize_row_q8_1_cuda
+ * (hot/kt_gguf_moe_multi/kt_gguf_moe_multi.cu:600-650); bit-identical blocks. */
+int kt_quantize_q8_1(const void* x, int x_dtype, int64_t rows, int64_t cols, void* qx, void* stream);
+
+/* Decode GEMV workspace for kt_moe_a8_vec_multi / _routes / kt_dense_a8_vec. */
+size_t kt_moe_a8_vec_workspace_size(int64_t tokens, int64_t cols, int64_t routes, int n_slots);
+
+/* Y[p, r] = row r of slot topk_ids[p] . q8_1(X[p / top_k]) for p < tokens*top_k, in X's dtype;
+ * zero rows for ids outside [0, n_slots). x [tokens, cols], y [tokens*top_k, rows].
+ * Replaces the torch op kt_moe_a8_vec_multi (hot/kt_gguf_moe_multi/kt_gguf_moe_multi.cu:653-935,
+ * bound at hot/kt_gguf_moe_multi.py:81-82): same sums, every route of a slot sharing one read
+ * of its weights, at any token count. */
+int kt_moe_a8_vec_multi(const void* x, int x_dtype, int64_t tokens, int64_t cols, const void* w, int w_is_table,
+                        int n_slots, const int32_t* topk_ids, int64_t top_k, int ggml_type, int64_t rows, void* y,
+                        void* workspace, size_t workspace_bytes, void* stream);
+
+/* The per-route contract of the reference's KT_PER_ROUTE build (hot/kt_gguf_moe_multi.py:85-87).
+ * Sums are identical to kt_moe_a8_vec_multi per route. */
+int kt_moe_a8_vec_routes(const void* x, int x_dtype, int64_t tokens, int64_t cols, const void* w, int w_is_table,
+                         int n_slots, const int32_t* topk_ids, int64_t top_k, int ggml_type, int64_t rows, void* y,
+                         void* workspace, size_t workspace_bytes, void* stream);
+
+/* Workspace for kt_dense_a8_vec. */
+size_t kt_dense_a8_vec_workspace_size(int64_t tokens, int64_t cols);
+
+/* y [tokens, rows] = x [tokens, cols] . W^T for a dense GGUF weight w [rows, row_bytes]
+ * (hot/kt_gguf_moe_multi.py:103-112). */
+int kt_dense_a8_vec(const void* x, int x_dtype, int64_t tokens, int64_t cols, const void* w, int ggml_type,
+                    int64_t rows, void* y, void* workspace, size_t workspace_bytes, void* stream);
+
+/* GGUF rows [rows, row_bytes] -> out [rows, cols] in out_dtype. The fp32 values are
+ * bit-identical to ggml's dequantize_row_* (and gguf-py); f16/bf16 are those rounded to
+ * nearest even. Replaces dequant_experts (flash-next-gguf patch, kt_gguf_dequant.py). */
+int kt_gguf_dequantize(const void* w, int ggml_type, int64_t rows, int64_t cols, void* out, int out_dtype,
+                       void* stream);
+
+/* h [rows, n] = silu(h13[:, :n]) * h13[:, n:] in fp32, stored in dtype (sgl-kernel
+ * silu_and_mul, called at hot/kt_gguf_hot.py:260). */
+int kt_silu_and_mul(const void* h13, int dtype, int64_t rows, int64_t n, void* h, void* stream);
+
+/* res [tokens, cols] = sum over k of dtype(out[t, k] * dtype(w[t, k])), accumulated in fp32
+ * in k order and rounded once (the reference's _combine, hot/kt_gguf_hot.py:43-71). */
+int kt_moe_combine(const void* out, int dtype, const float* w, int64_t tokens, int64_t top_k, int64_t cols, void* res,
+                   void* stream);
+
+/* HotCache.route (hot/kt_hot_cache.py:62-75, 121-143): slot_out[i] = log2slot[ids[i]],
+ * cpu_out[i] = log2cpu[ids[i]], counts[ids[i]] += 1 (counts may be NULL). */
+int kt_hot_route(const int32_t* ids, int64_t n, const int32_t* log2slot, const int32_t* log2cpu, float* counts,
+                 int32_t* slot_out, int32_t* cpu_out, void* stream);
+
+/* Router top-k over logits [tokens, n_experts] fp32: softmax, then the k largest
+ * probabilities (ties to the lower id), optionally renormalised to sum 1. */
+int kt_topk_softmax(const float* logits, int64_t tokens, int n_experts, int k, int renormalize, float* weights,
+                    int32_t* ids, void* stream);
+
+/* DeepSeek-V3 grouped routing: sigmoid scores, selection by score + bias (bias may be
+ * NULL), group score = sum of the group's two best, keep topk_group groups, k experts;
+ * weights = unbiased scores, optionally renormalised, times scale. */
+int kt_topk_grouped(const float* logits, const float* bias, int64_t tokens, int n_experts, int n_group, int topk_group,
+                    int k, int renormalize, float scale, float* weights, int32_t* ids, void* stream);
+
+/* Prefill MoE layer workspace (permutation, H and Y staging, status word). */
+size_t kt_moe_prefill_workspace_size(int64_t tokens, int64_t top_k, int64_t hidden, int64_t inter, int n_slots);
+
+/* Byte offsets inside a kt_moe_prefill workspace, for inspection after a call:
+ * offsets[0] status word (int), [1] per-slot route counts (int32 [n_slots]),
+ * [2] tile list (int32 [n_tiles][3]: slot, first sorted row, rows), [3] n_tiles (int32),
+ * [4] token of each sorted row (int32 [tokens*top_k]), [5] sorted row of each route
+ * (int32 [tokens*top_k], -1 if not resident), [6] H (bf16 [tokens*top_k, inter]),
+ * [7] per-route outputs Y (bf16 [tokens*top_k, hidden]). Rows past the resident routes are
+ * unused. Returns KT_OK. */
+int kt_moe_prefill_workspace_layout(int64_t tokens, int64_t top_k, int64_t hidden, int64_t inter, int n_slots,
+                                    size_t offsets[8]);
+
+/* One MoE layer on the GPU-resident slots, for prefill chunks:
+ *   out[t] = sum_k w[t,k] * W2[s] (silu(W13g[s] x_t) * W13u[s] x_t),  s = topk_ids[t, k]
+ * with bf16 activations x/out [tokens, hidden], fp32 topk_weights, slot ids as above.
+ * The expert GEMMs run on tcgen05 with the GGUF weights dequantized in shared memory to
+ * bf16 (fp32 accumulation); H and the per-route outputs are rounded to bf16 and combined
+ * with the reference combine's rounding (hot/kt_gguf_hot.py:43-71). Replaces the hot
+ * method's apply (hot/kt_gguf_hot.py:240-304) at prefill sizes and the streamer's
+ * dequant + cutlass_fused_moe group body. hidden % 256 == 0, inter % 256 == 0. */
+int kt_moe_prefill(const void* x, int64_t tokens, int64_t hidden, int64_t inter, const int32_t* topk_ids,
+                   const float* topk_weights, int64_t top_k, const void* w13, int type13, const void* w2, int type2,
+                   int w_is_table, int n_slots, void* out, void* workspace, size_t workspace_bytes, void* stream);
+
+/* kt_moe_prefill that also records four caller-created CUDA events (cudaEvent_t as void*)
+ * on `stream` after its stages: [0] routing permutation, [1] gate/up GEMM, [2] down GEMM,
+ * [3] combine. For per-stage timing; stage_events may be NULL. */
+int kt_moe_prefill_timed(const void* x, int64_t tokens, int64_t hidden, int64_t inter, const int32_t* topk_ids,
+                         const float* topk_weights, int64_t top_k, const void* w13, int type13, const void* w2, int type2,
+                         int w_is_table, int n_slots, void* out, void* workspace, size_t workspace_bytes, void* stream,
+                         void* const* stage_events);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* KT_GGUF_B200_H */

@@ -1,0 +1,311 @@
+// capi.cu — the exported C ABI (include/kt_gguf_b200.h): argument checks, workspace
+// carving, and the launch sequences of the decode GEMV and the prefill layer.
+#include <string.h>
+
+#include "../../include/kt_gguf_b200.h"
+#include "kt_common.cuh"
+#include "kt_kernels.h"
+
+#define KT_EXPORT extern "C" __attribute__((visibility("default")))
+
+namespace {
+
+inline cudaStream_t S(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+
+inline bool type_ok(int t) { return t == KT_Q8_0 || t == KT_Q4_K || t == KT_Q6_K || t == KT_IQ3_S; }
+inline bool dtype_ok(int d) { return d == KT_DT_F32 || d == KT_DT_F16 || d == KT_DT_BF16; }
+
+inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+// bump allocator over a caller workspace
+struct Carve {
+  uint8_t* base;
+  size_t off = 0;
+  explicit Carve(void* b) : base((uint8_t*)b) {}
+  template <typename T>
+  T* take(size_t count, size_t align = 256) {
+    off = align_up(off, align);
+    T* p = reinterpret_cast<T*>(reinterpret_cast<uintptr_t>(base) + off);  // base 0: offsets
+    off += sizeof(T) * count;
+    return p;
+  }
+};
+
+int num_sms() {
+  int dev = 0, n = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  return n > 0 ? n : 148;
+}
+
+int launch_rc(int rc) {
+  if (rc) return rc == -1 ? KT_ERR_ARG : KT_ERR_CUDA;
+  return cudaGetLastError() == cudaSuccess ? KT_OK : KT_ERR_CUDA;
+}
+
+// decode GEMV workspace layout
+struct VecWs {
+  int* status;
+  uint8_t* qx;
+  int32_t* groups;
+  int32_t* order;
+  size_t bytes;
+};
+
+VecWs vec_ws(void* ws, int64_t tokens, int64_t cols, int64_t routes, int n_slots) {
+  Carve c(ws);
+  VecWs v;
+  v.status = c.take<int>(4);
+  v.qx = c.take<uint8_t>((size_t)tokens * kt_q8_1_row_bytes(cols));
+  v.groups = c.take<int32_t>(1 + 3 * (size_t)(n_slots + 1));
+  v.order = c.take<int32_t>((size_t)routes);
+  v.bytes = align_up(c.off, 256);
+  return v;
+}
+
+int moe_vec(const void* x, int x_dtype, int64_t tokens, int64_t cols, const void* w, int table, int n_slots,
+            const int32_t* ids, int64_t top_k, int type, int64_t rows, void* y, void* ws, size_t ws_bytes, void* stream) {
+  if (!type_ok(type)) return KT_ERR_TYPE;
+  if (!dtype_ok(x_dtype) || tokens < 0 || cols <= 0 || rows <= 0 || top_k <= 0 || n_slots <= 0) return KT_ERR_ARG;
+  if (cols % kt_block_info(type).qk || rows > (1 << 30)) return KT_ERR_ARG;
+  if (tokens == 0) return KT_OK;
+  if (!x || !w || !ids || !y || !ws) return KT_ERR_ARG;
+  const int64_t routes = tokens * top_k;
+  VecWs v = vec_ws(ws, tokens, cols, routes, n_slots);
+  if (ws_bytes < v.bytes) return KT_ERR_WORKSPACE;
+  cudaStream_t s = S(stream);
+  if (cudaMemsetAsync(v.status, 0, sizeof(int), s) != cudaSuccess) return KT_ERR_CUDA;
+  int rc = kt_launch_quantize_q8_1(x, x_dtype, tokens, cols, v.qx, s);
+  if (rc) return launch_rc(rc);
+  rc = kt_launch_group_routes(ids, routes, n_slots, v.groups, v.order, s);
+  if (rc) return launch_rc(rc);
+  const int max_groups = (int)(routes < (int64_t)n_slots + 1 ? routes : (int64_t)n_slots + 1);
+  rc = kt_launch_moe_vec(type, w, table, v.qx, kt_q8_1_row_bytes(cols), v.groups, v.order, max_groups, (int)top_k,
+                         (int)rows, (int)cols, x_dtype, y, s);
+  return launch_rc(rc);
+}
+
+// prefill workspace layout
+struct PreWs {
+  int* status;
+  int32_t* counts;
+  int32_t* cursor;
+  int32_t* tiles;
+  int32_t* n_tiles;
+  int32_t* sorted_token;
+  int32_t* route_pos;
+  uint16_t* h;
+  uint16_t* y;
+  size_t bytes;
+};
+
+PreWs pre_ws(void* ws, int64_t tokens, int64_t top_k, int64_t hidden, int64_t inter, int n_slots) {
+  Carve c(ws);
+  PreWs p;
+  const int64_t R = tokens * top_k;
+  const int tn = kt_gemm_tile_tokens();
+  p.status = c.take<int>(4);
+  p.counts = c.take<int32_t>(n_slots);
+  p.cursor = c.take<int32_t>(n_slots);
+  p.tiles = c.take<int32_t>(3 * (size_t)(R / tn + n_slots + 1));
+  p.n_tiles = c.take<int32_t>(4);
+  p.sorted_token = c.take<int32_t>(R);
+  p.route_pos = c.take<int32_t>(R);
+  p.h = c.take<uint16_t>((size_t)R * inter, 1024);
+  p.y = c.take<uint16_t>((size_t)R * hidden, 1024);
+  p.bytes = align_up(c.off, 256);
+  return p;
+}
+
+}  // namespace
+
+KT_EXPORT int kt_version(void) { return 100; }
+
+KT_EXPORT const char* kt_status_string(int status) {
+  switch (status) {
+    case KT_OK: return "ok";
+    case KT_ERR_ARG: return "invalid argument";
+    case KT_ERR_TYPE: return "unsupported ggml type";
+    case KT_ERR_WORKSPACE: return "workspace too small";
+    case KT_ERR_CUDA: return "CUDA error";
+    case KT_ERR_DEVICE: return "device is not sm_100";
+  }
+  return "unknown status";
+}
+
+KT_EXPORT int kt_device_supported(void) {
+  int dev = 0, major = 0, minor = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+  cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+  cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev);
+  return major == 10 && minor == 0;
+}
+
+KT_EXPORT int kt_gguf_row_bytes(int ggml_type, int64_t cols, int64_t* row_bytes) {
+  if (!type_ok(ggml_type)) return KT_ERR_TYPE;
+  const KtBlockInfo bi = kt_block_info(ggml_type);
+  if (!row_bytes || cols < 0 || cols % bi.qk) return KT_ERR_ARG;
+  *row_bytes = cols / bi.qk * bi.bytes;
+  return KT_OK;
+}
+
+KT_EXPORT int kt_workspace_status(const void* workspace, void* stream, int* status) {
+  if (!workspace || !status) return KT_ERR_ARG;
+  if (cudaStreamSynchronize(S(stream)) != cudaSuccess) return KT_ERR_CUDA;
+  int v = 0;
+  if (cudaMemcpy(&v, workspace, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess) return KT_ERR_CUDA;
+  *status = v;
+  return KT_OK;
+}
+
+KT_EXPORT int kt_quantize_q8_1(const void* x, int x_dtype, int64_t rows, int64_t cols, void* qx, void* stream) {
+  if (!dtype_ok(x_dtype) || rows < 0 || cols <= 0) return KT_ERR_ARG;
+  if (rows == 0) return KT_OK;
+  if (!x || !qx) return KT_ERR_ARG;
+  return launch_rc(kt_launch_quantize_q8_1(x, x_dtype, rows, cols, qx, S(stream)));
+}
+
+KT_EXPORT size_t kt_moe_a8_vec_workspace_size(int64_t tokens, int64_t cols, int64_t routes, int n_slots) {
+  return vec_ws(nullptr, tokens, cols, routes, n_slots).bytes;
+}
+
+KT_EXPORT int kt_moe_a8_vec_multi(const void* x, int x_dtype, int64_t tokens, int64_t cols, const void* w,
+                                  int w_is_table, int n_slots, const int32_t* topk_ids, int64_t top_k, int ggml_type,
+                                  int64_t rows, void* y, void* workspace, size_t workspace_bytes, void* stream) {
+  return moe_vec(x, x_dtype, tokens, cols, w, w_is_table, n_slots, topk_ids, top_k, ggml_type, rows, y, workspace,
+                 workspace_bytes, stream);
+}
+
+KT_EXPORT int kt_moe_a8_vec_routes(const void* x, int x_dtype, int64_t tokens, int64_t cols, const void* w,
+                                   int w_is_table, int n_slots, const int32_t* topk_ids, int64_t top_k, int ggml_type,
+                                   int64_t rows, void* y, void* workspace, size_t workspace_bytes, void* stream) {
+  return moe_vec(x, x_dtype, tokens, cols, w, w_is_table, n_slots, topk_ids, top_k, ggml_type, rows, y, workspace,
+                 workspace_bytes, stream);
+}
+
+KT_EXPORT size_t kt_dense_a8_vec_workspace_size(int64_t tokens, int64_t cols) {
+  return align_up(kt_moe_a8_vec_workspace_size(tokens, cols, tokens, 1), 256) + align_up(sizeof(int32_t) * (size_t)tokens, 256);
+}
+
+KT_EXPORT int kt_dense_a8_vec(const void* x, int x_dtype, int64_t tokens, int64_t cols, const void* w, int ggml_type,
+                              int64_t rows, void* y, void* workspace, size_t workspace_bytes, void* stream) {
+  // a dense weight is a one-slot MoE whose routes all use slot 0; the route ids live in
+  // the workspace tail (zeroed here)
+  const size_t need = kt_moe_a8_vec_workspace_size(tokens, cols, tokens, 1);
+  const size_t ids_off = align_up(need, 256);
+  if (workspace_bytes < ids_off + sizeof(int32_t) * (size_t)tokens) return KT_ERR_WORKSPACE;
+  if (tokens <= 0) return tokens == 0 ? KT_OK : KT_ERR_ARG;
+  int32_t* ids = reinterpret_cast<int32_t*>((uint8_t*)workspace + ids_off);
+  if (cudaMemsetAsync(ids, 0, sizeof(int32_t) * tokens, S(stream)) != cudaSuccess) return KT_ERR_CUDA;
+  return moe_vec(x, x_dtype, tokens, cols, w, 0, 1, ids, 1, ggml_type, rows, y, workspace, need, stream);
+}
+
+KT_EXPORT int kt_gguf_dequantize(const void* w, int ggml_type, int64_t rows, int64_t cols, void* out, int out_dtype,
+                                 void* stream) {
+  if (!type_ok(ggml_type)) return KT_ERR_TYPE;
+  if (!dtype_ok(out_dtype) || rows < 0 || cols < 0 || cols % kt_block_info(ggml_type).qk) return KT_ERR_ARG;
+  if (rows == 0 || cols == 0) return KT_OK;
+  if (!w || !out) return KT_ERR_ARG;
+  return launch_rc(kt_launch_dequant(ggml_type, w, rows, cols, out, out_dtype, S(stream)));
+}
+
+KT_EXPORT int kt_silu_and_mul(const void* h13, int dtype, int64_t rows, int64_t n, void* h, void* stream) {
+  if (!dtype_ok(dtype) || rows < 0 || n < 0) return KT_ERR_ARG;
+  if (rows == 0 || n == 0) return KT_OK;
+  if (!h13 || !h) return KT_ERR_ARG;
+  return launch_rc(kt_launch_silu_and_mul(h13, dtype, rows, n, h, S(stream)));
+}
+
+KT_EXPORT int kt_moe_combine(const void* out, int dtype, const float* w, int64_t tokens, int64_t top_k, int64_t cols,
+                             void* res, void* stream) {
+  if (!dtype_ok(dtype) || tokens < 0 || top_k <= 0 || cols < 0) return KT_ERR_ARG;
+  if (tokens == 0 || cols == 0) return KT_OK;
+  if (!out || !w || !res) return KT_ERR_ARG;
+  return launch_rc(kt_launch_combine(out, dtype, w, tokens, top_k, cols, res, S(stream)));
+}
+
+KT_EXPORT int kt_hot_route(const int32_t* ids, int64_t n, const int32_t* log2slot, const int32_t* log2cpu, float* counts,
+                           int32_t* slot_out, int32_t* cpu_out, void* stream) {
+  if (n < 0) return KT_ERR_ARG;
+  if (n == 0) return KT_OK;
+  if (!ids || !log2slot || !log2cpu || !slot_out || !cpu_out) return KT_ERR_ARG;
+  return launch_rc(kt_launch_route(ids, n, log2slot, log2cpu, counts, slot_out, cpu_out, S(stream)));
+}
+
+KT_EXPORT int kt_topk_softmax(const float* logits, int64_t tokens, int n_experts, int k, int renormalize, float* weights,
+                              int32_t* ids, void* stream) {
+  if (tokens < 0 || n_experts <= 0 || k <= 0) return KT_ERR_ARG;
+  if (tokens == 0) return KT_OK;
+  if (!logits || !weights || !ids) return KT_ERR_ARG;
+  return launch_rc(kt_launch_topk_softmax(logits, tokens, n_experts, k, renormalize, weights, ids, S(stream)));
+}
+
+KT_EXPORT int kt_topk_grouped(const float* logits, const float* bias, int64_t tokens, int n_experts, int n_group,
+                              int topk_group, int k, int renormalize, float scale, float* weights, int32_t* ids,
+                              void* stream) {
+  if (tokens < 0 || n_experts <= 0 || k <= 0) return KT_ERR_ARG;
+  if (tokens == 0) return KT_OK;
+  if (!logits || !weights || !ids) return KT_ERR_ARG;
+  return launch_rc(kt_launch_topk_grouped(logits, bias, tokens, n_experts, n_group, topk_group, k, renormalize, scale,
+                                          weights, ids, S(stream)));
+}
+
+KT_EXPORT size_t kt_moe_prefill_workspace_size(int64_t tokens, int64_t top_k, int64_t hidden, int64_t inter,
+                                               int n_slots) {
+  return pre_ws(nullptr, tokens, top_k, hidden, inter, n_slots).bytes;
+}
+
+KT_EXPORT int kt_moe_prefill_workspace_layout(int64_t tokens, int64_t top_k, int64_t hidden, int64_t inter,
+                                              int n_slots, size_t offsets[8]) {
+  if (!offsets) return KT_ERR_ARG;
+  PreWs p = pre_ws(nullptr, tokens, top_k, hidden, inter, n_slots);
+  const void* ptrs[8] = {p.status, p.counts, p.tiles, p.n_tiles, p.sorted_token, p.route_pos, p.h, p.y};
+  for (int i = 0; i < 8; ++i) offsets[i] = (size_t)(uintptr_t)ptrs[i];
+  return KT_OK;
+}
+
+KT_EXPORT int kt_moe_prefill_timed(const void* x, int64_t tokens, int64_t hidden, int64_t inter,
+                                   const int32_t* topk_ids, const float* topk_weights, int64_t top_k, const void* w13,
+                                   int type13, const void* w2, int type2, int w_is_table, int n_slots, void* out,
+                                   void* workspace, size_t workspace_bytes, void* stream, void* const* stage_events) {
+  if (!type_ok(type13) || !type_ok(type2)) return KT_ERR_TYPE;
+  if (tokens < 0 || top_k <= 0 || n_slots <= 0 || hidden <= 0 || inter <= 0) return KT_ERR_ARG;
+  if (hidden % 256 || inter % 256 || hidden > (1 << 20) || inter > (1 << 20)) return KT_ERR_ARG;
+  if (tokens * top_k > (int64_t)1 << 30) return KT_ERR_ARG;
+  if (tokens == 0) return KT_OK;
+  if (!x || !topk_ids || !topk_weights || !w13 || !w2 || !out || !workspace) return KT_ERR_ARG;
+  if (((uintptr_t)x | (uintptr_t)out) & 15) return KT_ERR_ARG;
+  PreWs p = pre_ws(workspace, tokens, top_k, hidden, inter, n_slots);
+  if (workspace_bytes < p.bytes) return KT_ERR_WORKSPACE;
+  cudaStream_t s = S(stream);
+  auto mark = [&](int i) {
+    if (stage_events && stage_events[i]) cudaEventRecord(reinterpret_cast<cudaEvent_t>(stage_events[i]), s);
+  };
+  const int64_t R = tokens * top_k;
+  if (cudaMemsetAsync(p.status, 0, sizeof(int), s) != cudaSuccess) return KT_ERR_CUDA;
+  int rc = kt_launch_permute(topk_ids, R, (int)top_k, n_slots, kt_gemm_tile_tokens(), p.counts, p.cursor, p.tiles,
+                             p.n_tiles, p.sorted_token, p.route_pos, s);
+  if (rc) return launch_rc(rc);
+  mark(0);
+  const int grid = num_sms();
+  rc = kt_launch_gemm_gate_up(type13, x, tokens, (int)hidden, (int)inter, w13, w_is_table, p.tiles, p.n_tiles,
+                              p.sorted_token, p.h, p.status, grid, s);
+  if (rc) return launch_rc(rc);
+  mark(1);
+  rc = kt_launch_gemm_down(type2, p.h, R, (int)hidden, (int)inter, w2, w_is_table, p.tiles, p.n_tiles, p.y, p.status,
+                           grid, s);
+  if (rc) return launch_rc(rc);
+  mark(2);
+  rc = kt_launch_combine_sorted(p.y, p.route_pos, topk_weights, tokens, top_k, hidden, (uint16_t*)out, s);
+  if (rc) return launch_rc(rc);
+  mark(3);
+  return launch_rc(0);
+}
+
+KT_EXPORT int kt_moe_prefill(const void* x, int64_t tokens, int64_t hidden, int64_t inter, const int32_t* topk_ids,
+                             const float* topk_weights, int64_t top_k, const void* w13, int type13, const void* w2,
+                             int type2, int w_is_table, int n_slots, void* out, void* workspace, size_t workspace_bytes,
+                             void* stream) {
+  return kt_moe_prefill_timed(x, tokens, hidden, inter, topk_ids, topk_weights, top_k, w13, type13, w2, type2,
+                              w_is_table, n_slots, out, workspace, workspace_bytes, stream, nullptr);
+}

@@ -1,0 +1,218 @@
+// gguf_dot.cuh — per-chunk integer dot products of one GGUF weight block against q8_1
+// activations, and the scalar/vector dequantizers of the four hot-path types.
+//
+// A "chunk" is the unit one lane handles in the decode GEMV: the same split of a block
+// that the reference's vec_dot_*_q8_1 functions use (Q8_0: 8 values, Q4_K: 16 values from
+// two sub-blocks, Q6_K: 8 values, IQ3_S: one 32-value sub-block). The integer part of
+// every chunk (dp4a sums, scale unpacking, grid lookups, sign handling) is exact; the
+// fp32 combination is written in the same expression order as the reference
+// (hot/kt_gguf_moe_multi/vecdotq.cuh:969-982, 1326-1367, 1625-1646, 1875-1900).
+#pragma once
+#include "kt_common.cuh"
+
+template <int TYPE>
+struct KtChunk;
+
+// chunks per block and value/byte geometry of the GEMV split
+template <>
+struct KtChunk<KT_Q8_0> {
+  static constexpr int QK = 32, BYTES = 34, CPB = 4, VDR = 2;
+};
+template <>
+struct KtChunk<KT_Q4_K> {
+  static constexpr int QK = 256, BYTES = 144, CPB = 16, VDR = 2;
+};
+template <>
+struct KtChunk<KT_Q6_K> {
+  static constexpr int QK = 256, BYTES = 210, CPB = 32, VDR = 1;
+};
+template <>
+struct KtChunk<KT_IQ3_S> {
+  static constexpr int QK = 256, BYTES = 110, CPB = 8, VDR = 1;
+};
+
+__device__ __forceinline__ float kt_q8_1_d(const uint8_t* b8) { return __low2float(*reinterpret_cast<const half2*>(b8)); }
+
+// ---- Q8_0: d_w * d_a * sum(q_w * q_a) over 8 values (iqs in {0,2,4,6})
+__device__ __forceinline__ float kt_vd_q8_0(const uint8_t* bx, const uint8_t* by, int iqs) {
+  int sumi = 0;
+#pragma unroll
+  for (int i = 0; i < 2; ++i) sumi = __dp4a(kt_ld_b2(bx + 2 + 4 * (iqs + i)), kt_ld_b4(by + 4 + 4 * (iqs + i)), sumi);
+  const float d80 = kt_h2f(*reinterpret_cast<const uint16_t*>(bx));
+  const float d81 = kt_q8_1_d(by);
+  return d80 * d81 * sumi;
+}
+
+// ---- Q4_K: 16 values from sub-blocks (bq8_offset, bq8_offset + 1); iqs in {0,2,...,30}
+__device__ __forceinline__ float kt_vd_q4_k(const uint8_t* bx, const uint8_t* by0, int iqs) {
+  const int bq8_offset = 2 * ((iqs / 2) / 4);
+  const uint8_t* q4 = bx + 16 + 16 * bq8_offset + 4 * ((iqs / 2) % 4);
+  const int v0 = kt_ld_b4(q4), v1 = kt_ld_b4(q4 + 16);
+  const uint16_t* s16 = reinterpret_cast<const uint16_t*>(bx + 4);
+  uint16_t aux0, aux1;
+  const int j = bq8_offset / 2;
+  if (j < 2) {
+    aux0 = s16[j + 0] & 0x3f3f;
+    aux1 = s16[j + 2] & 0x3f3f;
+  } else {
+    aux0 = ((s16[j + 2] >> 0) & 0x0f0f) | ((s16[j - 2] & 0xc0c0) >> 2);
+    aux1 = ((s16[j + 2] >> 4) & 0x0f0f) | ((s16[j - 0] & 0xc0c0) >> 2);
+  }
+  float sumf_d = 0.0f, sumf_m = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const uint8_t* b8 = by0 + KT_Q8_1_BYTES * (bq8_offset + i);
+    const float d8 = kt_q8_1_d(b8);
+    const int u0 = kt_ld_b4(b8 + 4 + 4 * ((iqs / 2) % 4));
+    const int u1 = kt_ld_b4(b8 + 4 + 4 * ((iqs / 2) % 4) + 16);
+    const int v0i = (v0 >> (4 * i)) & 0x0F0F0F0F;
+    const int v1i = (v1 >> (4 * i)) & 0x0F0F0F0F;
+    const int dot1 = __dp4a(v1i, u1, __dp4a(v0i, u0, 0));
+    const int dot2 = __dp4a(0x01010101, u1, __dp4a(0x01010101, u0, 0));
+    const int sc = (i ? (aux0 >> 8) : aux0) & 0xff;
+    const int m = (i ? (aux1 >> 8) : aux1) & 0xff;
+    sumf_d += d8 * (dot1 * sc);
+    sumf_m += d8 * (dot2 * m);
+  }
+  const float2 dm = __half22float2(*reinterpret_cast<const half2*>(bx));
+  return dm.x * sumf_d - dm.y * sumf_m;
+}
+
+// ---- Q6_K: 8 values; iqs in 0..31
+__device__ __forceinline__ float kt_vd_q6_k(const uint8_t* bx, const uint8_t* by0, int iqs) {
+  const int bq8_offset = 4 * (iqs / 16) + (iqs % 16) / 8;
+  const int scale_offset = 8 * (iqs / 16) + (iqs % 16) / 4;
+  const int vh_shift = 2 * ((iqs % 16) / 8);
+  const int vl = kt_ld_b2(bx + 4 * iqs);
+  const int vh = kt_ld_b2(bx + 128 + 4 * (8 * (iqs / 16) + iqs % 8)) >> vh_shift;
+  const int8_t* scales = reinterpret_cast<const int8_t*>(bx + 192 + scale_offset);
+  float sumf = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const uint8_t* b8 = by0 + KT_Q8_1_BYTES * (bq8_offset + 2 * i);
+    const int u = kt_ld_b4(b8 + 4 + 4 * (iqs % 8));
+    const float d8 = kt_q8_1_d(b8);
+    const int sc = scales[4 * i];
+    const int vil = (vl >> (4 * i)) & 0x0F0F0F0F;
+    const int vih = ((vh >> (4 * i)) << 4) & 0x30303030;
+    const int vi = __vsubss4((vil | vih), 0x20202020);
+    sumf += d8 * (__dp4a(vi, u, 0) * sc);
+  }
+  return kt_h2f(*reinterpret_cast<const uint16_t*>(bx + 208)) * sumf;
+}
+
+// ---- IQ3_S: one 32-value sub-block (ib32 = iqs in 0..7); grid from shared memory
+__device__ __forceinline__ float kt_vd_iq3_s(const uint8_t* bx, const uint8_t* by0, int ib32, const uint32_t* grid) {
+  const uint8_t* qs = bx + 2 + 8 * ib32;
+  const int qh = bx[66 + ib32];
+  const uint8_t* signs = bx + 74 + 4 * ib32;
+  const uint8_t* b8 = by0 + KT_Q8_1_BYTES * ib32;
+  const uint8_t* q8 = b8 + 4;
+  int sumi = 0;
+#pragma unroll
+  for (int l = 0; l < 4; ++l) {
+    const uint32_t g1 = grid[qs[2 * l + 0] | ((qh << (8 - 2 * l)) & 256)];
+    const uint32_t g2 = grid[qs[2 * l + 1] | ((qh << (7 - 2 * l)) & 256)];
+    const uint32_t s0 = __vcmpeq4(((signs[l] & 0xf) * 0x01010101u) & 0x08040201u, 0x08040201u);
+    const uint32_t s1 = __vcmpeq4(((signs[l] >> 4) * 0x01010101u) & 0x08040201u, 0x08040201u);
+    const int gl = (int)__vsub4(g1 ^ s0, s0);
+    const int gh = (int)__vsub4(g2 ^ s1, s1);
+    sumi = __dp4a(gl, kt_ld_b4(q8 + 0), sumi);
+    sumi = __dp4a(gh, kt_ld_b4(q8 + 4), sumi);
+    q8 += 8;
+  }
+  const float d =
+      kt_h2f(*reinterpret_cast<const uint16_t*>(bx)) * (1 + 2 * ((bx[106 + ib32 / 2] >> 4 * (ib32 % 2)) & 0xf)) * kt_q8_1_d(b8);
+  return d * sumi;
+}
+
+template <int TYPE>
+__device__ __forceinline__ float kt_vec_dot(const uint8_t* bx, const uint8_t* by, int iqs, const uint32_t* grid) {
+  if constexpr (TYPE == KT_Q8_0) return kt_vd_q8_0(bx, by, iqs);
+  if constexpr (TYPE == KT_Q4_K) return kt_vd_q4_k(bx, by, iqs);
+  if constexpr (TYPE == KT_Q6_K) return kt_vd_q6_k(bx, by, iqs);
+  if constexpr (TYPE == KT_IQ3_S) return kt_vd_iq3_s(bx, by, iqs, grid);
+  return 0.0f;
+}
+
+// ------------------------------------------------------------------ dequantization
+// Each function writes the fp32 values of 32 consecutive elements [32*sub, 32*sub + 32)
+// of one block, with ggml's operation order (products that are exact in fp32 first, one
+// rounding at the end), so the values are bit-identical to ggml / gguf-py.
+
+__device__ __forceinline__ void kt_dq32_q8_0(const uint8_t* b, float* y) {
+  const float d = kt_h2f(b[0] | (b[1] << 8));
+#pragma unroll
+  for (int j = 0; j < 32; ++j) y[j] = (float)(int8_t)b[2 + j] * d;
+}
+
+__device__ __forceinline__ void kt_q4k_scale_min(int j, const uint8_t* q, int& sc, int& m) {
+  if (j < 4) {
+    sc = q[j] & 63;
+    m = q[j + 4] & 63;
+  } else {
+    sc = (q[j + 4] & 0xF) | ((q[j - 4] >> 6) << 4);
+    m = (q[j + 4] >> 4) | ((q[j] >> 6) << 4);
+  }
+}
+
+__device__ __forceinline__ void kt_dq32_q4_k(const uint8_t* b, int sub, float* y) {
+  const float d = kt_h2f(b[0] | (b[1] << 8)), dmin = kt_h2f(b[2] | (b[3] << 8));
+  int sc, m;
+  kt_q4k_scale_min(sub, b + 4, sc, m);
+  const float d1 = __fmul_rn(d, (float)sc), m1 = __fmul_rn(dmin, (float)m);
+  const uint8_t* q = b + 16 + 32 * (sub / 2);
+  const int sh = 4 * (sub & 1);
+#pragma unroll
+  for (int l = 0; l < 32; ++l) y[l] = __fsub_rn(__fmul_rn(d1, (float)((q[l] >> sh) & 0xF)), m1);
+}
+
+__device__ __forceinline__ void kt_dq32_q6_k(const uint8_t* b, int sub, float* y) {
+  // sub 0..7: half n = sub / 4, quarter (sub % 4) selects ql low/high nibble and qh bits
+  const int n = sub / 4, qq = sub % 4;
+  const uint8_t* ql = b + 64 * n + 32 * (qq & 1);
+  const uint8_t* qh = b + 128 + 32 * n;
+  const int8_t* sc = reinterpret_cast<const int8_t*>(b + 192) + 8 * n;
+  const float d = kt_h2f(b[208] | (b[209] << 8));
+  const int lsh = 4 * (qq >> 1), hsh = 2 * qq;
+#pragma unroll
+  for (int l = 0; l < 32; ++l) {
+    const int q = (int)(((ql[l] >> lsh) & 0xF) | (((qh[l] >> hsh) & 3) << 4)) - 32;
+    y[l] = __fmul_rn(__fmul_rn(d, (float)sc[l / 16 + 2 * qq]), (float)q);
+  }
+}
+
+__device__ __forceinline__ void kt_dq32_iq3_s(const uint8_t* b, int sub, float* y, const uint32_t* grid) {
+  const float d = kt_h2f(b[0] | (b[1] << 8));
+  const int s = (b[106 + sub / 2] >> (4 * (sub % 2))) & 0xf;
+  const float db = __fmul_rn(d, (float)(1 + 2 * s));
+  const uint8_t* qs = b + 2 + 8 * sub;
+  const int qh = b[66 + sub];
+  const uint8_t* signs = b + 74 + 4 * sub;
+#pragma unroll
+  for (int l = 0; l < 4; ++l) {
+    const uint32_t g1 = grid[qs[2 * l + 0] | ((qh << (8 - 2 * l)) & 256)];
+    const uint32_t g2 = grid[qs[2 * l + 1] | ((qh << (7 - 2 * l)) & 256)];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float v1 = __fmul_rn(db, (float)((g1 >> (8 * j)) & 0xff));
+      const float v2 = __fmul_rn(db, (float)((g2 >> (8 * j)) & 0xff));
+      y[8 * l + j] = (signs[l] >> j) & 1 ? -v1 : v1;
+      y[8 * l + 4 + j] = (signs[l] >> (j + 4)) & 1 ? -v2 : v2;
+    }
+  }
+}
+
+// 32 consecutive values starting at element 32*sub32 of a row made of blocks of TYPE
+template <int TYPE>
+__device__ __forceinline__ void kt_dq32(const uint8_t* row, int sub32, float* y, const uint32_t* grid) {
+  if constexpr (TYPE == KT_Q8_0) {
+    kt_dq32_q8_0(row + sub32 * 34, y);
+  } else {
+    constexpr int BS = KtChunk<TYPE>::BYTES;
+    const uint8_t* b = row + (sub32 / 8) * BS;
+    if constexpr (TYPE == KT_Q4_K) kt_dq32_q4_k(b, sub32 % 8, y);
+    if constexpr (TYPE == KT_Q6_K) kt_dq32_q6_k(b, sub32 % 8, y);
+    if constexpr (TYPE == KT_IQ3_S) kt_dq32_iq3_s(b, sub32 % 8, y, grid);
+  }
+}

@@ -1,0 +1,53 @@
+// kt_kernels.h — internal launcher declarations shared by the .cu files of the library.
+// The public C ABI is include/kt_gguf_b200.h; nothing here is exported.
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+struct KtGemmArgs {
+  const uint8_t* w;             // slot base (plain layout) or int64 table of per-slot addresses
+  int table;
+  int64_t row_bytes;            // bytes of one GGUF weight row
+  int K;                        // reduction length of this phase
+  int N;                        // expert intermediate size
+  int K_out;                    // rows of W2 (hidden size); phase 1: unused
+  const int32_t* tiles;         // [n_tiles][3]: slot, first sorted position, tokens (<= 256)
+  const int32_t* n_tiles;       // device scalar
+  int n_wtiles;                 // weight tiles per token tile
+  const int32_t* sorted_token;  // token of each sorted position (phase 1)
+  uint16_t* out;                // bf16 output rows (H or Y), row = sorted position
+  int64_t out_ld;
+  int* status;                  // device status word
+};
+
+int kt_launch_quantize_q8_1(const void* x, int dtype, int64_t rows, int64_t cols, void* qx, cudaStream_t s);
+int kt_launch_group_routes(const int32_t* ids, int64_t routes, int n_slots, int32_t* groups, int32_t* order,
+                           cudaStream_t s);
+int kt_launch_moe_vec(int type, const void* w, int table, const void* qx, int64_t qrow, const int32_t* groups,
+                      const int32_t* order, int max_groups, int top_k, int rows, int cols, int dtype, void* y,
+                      cudaStream_t s);
+
+int kt_launch_dequant(int type, const void* w, int64_t rows, int64_t cols, void* out, int out_dtype, cudaStream_t s);
+int kt_launch_silu_and_mul(const void* h13, int dtype, int64_t rows, int64_t n, void* h, cudaStream_t s);
+int kt_launch_combine(const void* out, int dtype, const float* w, int64_t T, int64_t top_k, int64_t K, void* res,
+                      cudaStream_t s);
+int kt_launch_combine_sorted(const uint16_t* y, const int32_t* route_pos, const float* w, int64_t T, int64_t top_k,
+                             int64_t K, uint16_t* res, cudaStream_t s);
+int kt_launch_route(const int32_t* ids, int64_t n, const int32_t* slot_tab, const int32_t* cpu_tab, float* counts,
+                    int32_t* slot_out, int32_t* cpu_out, cudaStream_t s);
+int kt_launch_topk_softmax(const float* logits, int64_t T, int E, int k, int renorm, float* weights, int32_t* ids,
+                           cudaStream_t s);
+int kt_launch_topk_grouped(const float* logits, const float* bias, int64_t T, int E, int n_group, int topk_group, int k,
+                           int renorm, float scale, float* weights, int32_t* ids, cudaStream_t s);
+
+// prefill permutation: routes sorted by slot, token tiles of kt_gemm_tile_tokens() rows
+int kt_launch_permute(const int32_t* ids, int64_t routes, int top_k, int n_slots, int tile_tokens, int32_t* counts,
+                      int32_t* cursor, int32_t* tiles, int32_t* n_tiles, int32_t* sorted_token, int32_t* route_pos,
+                      cudaStream_t s);
+
+int kt_launch_gemm_gate_up(int type, const void* x, int64_t T, int K, int N, const void* w13, int table,
+                           const int32_t* tiles, const int32_t* n_tiles, const int32_t* sorted_token, void* h,
+                           int* status, int grid, cudaStream_t s);
+int kt_launch_gemm_down(int type, const void* h, int64_t R, int K, int N, const void* w2, int table, const int32_t* tiles,
+                        const int32_t* n_tiles, void* y, int* status, int grid, cudaStream_t s);
+int kt_gemm_tile_tokens();

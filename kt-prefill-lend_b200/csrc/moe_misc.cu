@@ -1,0 +1,438 @@
+// moe_misc.cu — the small kernels around the expert GEMMs:
+//   dequant      GGUF rows -> fp32/f16/bf16 (bit-identical fp32 values to ggml / gguf-py)
+//   silu_and_mul h = silu(g) * u on [rows, 2n] (the sgl-kernel op the reference calls,
+//                hot/kt_gguf_hot.py:260)
+//   combine      res[t] = bf16(sum_k fp32(bf16(out[t,k] * bf16(w[t,k])))) — the rounding
+//                and order of the reference's fused combine (hot/kt_gguf_hot.py:43-71)
+//   route        HotCache.route: slot / CPU ids by table lookup and route counts
+//                (hot/kt_hot_cache.py:62-75, 121-143)
+//   topk         router top-k: softmax, and DeepSeek-V3 grouped sigmoid routing
+//   permute      counting sort of routes by slot into 256-token tiles for the prefill GEMM
+#include "gguf_dot.cuh"
+#include "kt_kernels.h"
+
+// ------------------------------------------------------------------ dequant
+
+template <int TYPE, int DT>
+__global__ void kt_dequant_kernel(const uint8_t* __restrict__ w, int64_t rows, int64_t cols, int64_t row_bytes,
+                                  void* __restrict__ out) {
+  __shared__ uint32_t grid_s[512];
+  if constexpr (TYPE == KT_IQ3_S) {
+    for (int i = threadIdx.x; i < 512; i += blockDim.x) grid_s[i] = kt_iq3s_grid_dev[i];
+    __syncthreads();
+  }
+  const int64_t subs = cols / 32;
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= rows * subs) return;
+  const int64_t r = i / subs, sub = i % subs;
+  float y[32];
+  kt_dq32<TYPE>(w + r * row_bytes, (int)sub, y, grid_s);
+#pragma unroll
+  for (int j = 0; j < 32; ++j) kt_store_act<DT>(out, r * cols + sub * 32 + j, y[j]);
+}
+
+template <int TYPE>
+static int dequant_t(const void* w, int64_t rows, int64_t cols, void* out, int dt, cudaStream_t s) {
+  const KtBlockInfo bi = kt_block_info(TYPE);
+  const int64_t rb = cols / bi.qk * bi.bytes;
+  const int64_t n = rows * (cols / 32);
+  const unsigned blocks = (unsigned)((n + 255) / 256);
+  if (n == 0) return 0;
+  switch (dt) {
+    case KT_DT_F32: kt_dequant_kernel<TYPE, KT_DT_F32><<<blocks, 256, 0, s>>>((const uint8_t*)w, rows, cols, rb, out); break;
+    case KT_DT_F16: kt_dequant_kernel<TYPE, KT_DT_F16><<<blocks, 256, 0, s>>>((const uint8_t*)w, rows, cols, rb, out); break;
+    case KT_DT_BF16: kt_dequant_kernel<TYPE, KT_DT_BF16><<<blocks, 256, 0, s>>>((const uint8_t*)w, rows, cols, rb, out); break;
+    default: return -1;
+  }
+  return 0;
+}
+
+int kt_launch_dequant(int type, const void* w, int64_t rows, int64_t cols, void* out, int out_dtype, cudaStream_t s) {
+  const KtBlockInfo bi = kt_block_info(type);
+  if (!bi.qk || cols % bi.qk) return -1;
+  switch (type) {
+    case KT_Q8_0: return dequant_t<KT_Q8_0>(w, rows, cols, out, out_dtype, s);
+    case KT_Q4_K: return dequant_t<KT_Q4_K>(w, rows, cols, out, out_dtype, s);
+    case KT_Q6_K: return dequant_t<KT_Q6_K>(w, rows, cols, out, out_dtype, s);
+    case KT_IQ3_S: return dequant_t<KT_IQ3_S>(w, rows, cols, out, out_dtype, s);
+  }
+  return -1;
+}
+
+// ------------------------------------------------------------------ silu_and_mul
+
+template <int DT>
+__global__ void kt_silu_and_mul_kernel(const void* __restrict__ h13, int64_t rows, int64_t n, void* __restrict__ h) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= rows * n) return;
+  const int64_t r = i / n, j = i % n;
+  const float g = kt_load_act<DT>(h13, r * 2 * n + j);
+  const float u = kt_load_act<DT>(h13, r * 2 * n + n + j);
+  kt_store_act<DT>(h, i, g / (1.0f + expf(-g)) * u);
+}
+
+int kt_launch_silu_and_mul(const void* h13, int dtype, int64_t rows, int64_t n, void* h, cudaStream_t s) {
+  const int64_t tot = rows * n;
+  if (tot == 0) return 0;
+  const unsigned blocks = (unsigned)((tot + 255) / 256);
+  switch (dtype) {
+    case KT_DT_F32: kt_silu_and_mul_kernel<KT_DT_F32><<<blocks, 256, 0, s>>>(h13, rows, n, h); break;
+    case KT_DT_F16: kt_silu_and_mul_kernel<KT_DT_F16><<<blocks, 256, 0, s>>>(h13, rows, n, h); break;
+    case KT_DT_BF16: kt_silu_and_mul_kernel<KT_DT_BF16><<<blocks, 256, 0, s>>>(h13, rows, n, h); break;
+    default: return -1;
+  }
+  return 0;
+}
+
+// ------------------------------------------------------------------ combine
+
+template <int DT>
+__device__ __forceinline__ float kt_round_dt(float v) {
+  if constexpr (DT == KT_DT_F32) return v;
+  if constexpr (DT == KT_DT_F16) return __half2float(__float2half_rn(v));
+  return __bfloat162float(__float2bfloat16_rn(v));
+}
+
+// out [T, top_k, K] in DT; the route weight is cast to DT first (out.mul_(w.to(out.dtype)))
+template <int DT>
+__global__ void kt_combine_kernel(const void* __restrict__ out, const float* __restrict__ w, int64_t T, int top_k,
+                                  int64_t K, void* __restrict__ res) {
+  const int64_t t = blockIdx.x;
+  for (int64_t c = threadIdx.x; c < K; c += blockDim.x) {
+    float acc = 0.0f;
+    for (int k = 0; k < top_k; ++k) {
+      const float o = kt_load_act<DT>(out, (t * top_k + k) * K + c);
+      const float wk = kt_round_dt<DT>(w[t * top_k + k]);
+      acc += kt_round_dt<DT>(o * wk);
+    }
+    kt_store_act<DT>(res, t * K + c, acc);
+  }
+}
+
+int kt_launch_combine(const void* out, int dtype, const float* w, int64_t T, int64_t top_k, int64_t K, void* res,
+                      cudaStream_t s) {
+  if (T == 0 || K == 0) return 0;
+  if (T > 0x7fffffff) return -1;
+  const unsigned grid = (unsigned)T;
+  switch (dtype) {
+    case KT_DT_F32: kt_combine_kernel<KT_DT_F32><<<grid, 256, 0, s>>>(out, w, T, (int)top_k, K, res); break;
+    case KT_DT_F16: kt_combine_kernel<KT_DT_F16><<<grid, 256, 0, s>>>(out, w, T, (int)top_k, K, res); break;
+    case KT_DT_BF16: kt_combine_kernel<KT_DT_BF16><<<grid, 256, 0, s>>>(out, w, T, (int)top_k, K, res); break;
+    default: return -1;
+  }
+  return 0;
+}
+
+// Same arithmetic over the prefill layout: route (t, k) lives at sorted row route_pos[t*top_k+k]
+// of y [R, K] bf16, or is absent (-1: not on this device, contributes a zero row).
+// Each thread produces 8 consecutive columns with 16-byte loads.
+__global__ void kt_combine_sorted_kernel(const uint16_t* __restrict__ y, const int32_t* __restrict__ route_pos,
+                                         const float* __restrict__ w, int64_t T, int top_k, int64_t K,
+                                         uint16_t* __restrict__ res) {
+  const int64_t t = blockIdx.x;
+  for (int64_t c = (int64_t)threadIdx.x * 8; c < K; c += (int64_t)blockDim.x * 8) {
+    float acc[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[j] = 0.0f;
+    for (int k = 0; k < top_k; ++k) {
+      const int32_t pos = route_pos[t * top_k + k];
+      if (pos < 0) continue;  // bf16(0 * w) adds an exact zero
+      const float wk = kt_bf2f(kt_f2bf(w[t * top_k + k]));
+      const uint4 v = *reinterpret_cast<const uint4*>(y + (int64_t)pos * K + c);
+      const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        acc[2 * j] += kt_bf2f(kt_f2bf(kt_bf2f((uint16_t)(u[j] & 0xffff)) * wk));
+        acc[2 * j + 1] += kt_bf2f(kt_f2bf(kt_bf2f((uint16_t)(u[j] >> 16)) * wk));
+      }
+    }
+    uint4 o;
+    o.x = kt_pack_bf2(acc[0], acc[1]);
+    o.y = kt_pack_bf2(acc[2], acc[3]);
+    o.z = kt_pack_bf2(acc[4], acc[5]);
+    o.w = kt_pack_bf2(acc[6], acc[7]);
+    *reinterpret_cast<uint4*>(res + t * K + c) = o;
+  }
+}
+
+int kt_launch_combine_sorted(const uint16_t* y, const int32_t* route_pos, const float* w, int64_t T, int64_t top_k,
+                             int64_t K, uint16_t* res, cudaStream_t s) {
+  if (T == 0) return 0;
+  if (K % 8 || T > 0x7fffffff) return -1;
+  const int64_t vec = K / 8;
+  const int threads = (int)(vec < 256 ? (vec + 31) / 32 * 32 : 256);
+  kt_combine_sorted_kernel<<<(unsigned)T, threads, 0, s>>>(y, route_pos, w, T, (int)top_k, K, res);
+  return 0;
+}
+
+// ------------------------------------------------------------------ route (HotCache.route)
+
+__global__ void kt_route_kernel(const int32_t* __restrict__ ids, int64_t n, const int32_t* __restrict__ slot_tab,
+                                const int32_t* __restrict__ cpu_tab, float* __restrict__ counts,
+                                int32_t* __restrict__ slot_out, int32_t* __restrict__ cpu_out) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const int32_t e = ids[i];
+  slot_out[i] = slot_tab[e];
+  cpu_out[i] = cpu_tab[e];
+  if (counts) atomicAdd(&counts[e], 1.0f);
+}
+
+int kt_launch_route(const int32_t* ids, int64_t n, const int32_t* slot_tab, const int32_t* cpu_tab, float* counts,
+                    int32_t* slot_out, int32_t* cpu_out, cudaStream_t s) {
+  if (n == 0) return 0;
+  kt_route_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(ids, n, slot_tab, cpu_tab, counts, slot_out, cpu_out);
+  return 0;
+}
+
+// ------------------------------------------------------------------ router top-k
+// One warp per token. Selection takes the largest score; ties go to the lower expert id.
+
+__device__ __forceinline__ void warp_argmax(float& v, int& i) {
+#pragma unroll
+  for (int m = 16; m > 0; m >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, v, m);
+    const int oi = __shfl_xor_sync(0xffffffffu, i, m);
+    if (ov > v || (ov == v && oi < i)) {
+      v = ov;
+      i = oi;
+    }
+  }
+}
+
+constexpr int kMaxExpertsPerLane = 32;  // E <= 1024
+
+__global__ void kt_topk_softmax_kernel(const float* __restrict__ logits, int64_t T, int E, int k, int renorm,
+                                       float* __restrict__ weights, int32_t* __restrict__ ids) {
+  const int64_t t = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  if (t >= T) return;
+  float v[kMaxExpertsPerLane];
+  float mx = -INFINITY;
+#pragma unroll
+  for (int j = 0; j < kMaxExpertsPerLane; ++j) {
+    const int e = lane + 32 * j;
+    v[j] = e < E ? logits[t * E + e] : -INFINITY;
+    mx = fmaxf(mx, v[j]);
+  }
+#pragma unroll
+  for (int m = 16; m > 0; m >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, m));
+  float sum = 0.0f;
+#pragma unroll
+  for (int j = 0; j < kMaxExpertsPerLane; ++j) {
+    v[j] = (lane + 32 * j) < E ? expf(v[j] - mx) : -1.0f;
+    sum += v[j] > 0.0f ? v[j] : 0.0f;
+  }
+#pragma unroll
+  for (int m = 16; m > 0; m >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, m);
+  float picked = 0.0f, mine_w = 0.0f;
+  int mine_i = -1;
+  for (int r = 0; r < k; ++r) {
+    float bv = -1.0f;
+    int bi = 0x7fffffff;
+#pragma unroll
+    for (int j = 0; j < kMaxExpertsPerLane; ++j)
+      if (v[j] > bv) {
+        bv = v[j];
+        bi = lane + 32 * j;
+      }
+    warp_argmax(bv, bi);
+    const float p = bv / sum;
+    picked += p;
+    if (lane == r) {
+      mine_w = p;
+      mine_i = bi;
+    }
+#pragma unroll
+    for (int j = 0; j < kMaxExpertsPerLane; ++j)
+      if (lane + 32 * j == bi) v[j] = -2.0f;
+  }
+  if (lane < k) {
+    weights[t * k + lane] = renorm ? mine_w / picked : mine_w;
+    ids[t * k + lane] = mine_i;
+  }
+}
+
+int kt_launch_topk_softmax(const float* logits, int64_t T, int E, int k, int renorm, float* weights, int32_t* ids,
+                           cudaStream_t s) {
+  if (E > 32 * kMaxExpertsPerLane || k > 32 || k > E) return -1;
+  if (T == 0) return 0;
+  kt_topk_softmax_kernel<<<(unsigned)((T + 7) / 8), 256, 0, s>>>(logits, T, E, k, renorm, weights, ids);
+  return 0;
+}
+
+// DeepSeek-V3 routing: s = sigmoid(logit); selection score s + bias; group score = sum of the
+// two best selection scores in the group; keep topk_group groups; top-k experts among them by
+// selection score; weight = s (unbiased), renormalised over the k and multiplied by scale.
+__global__ void kt_topk_grouped_kernel(const float* __restrict__ logits, const float* __restrict__ bias, int64_t T, int E,
+                                       int n_group, int topk_group, int k, int renorm, float scale,
+                                       float* __restrict__ weights, int32_t* __restrict__ ids) {
+  const int64_t t = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  if (t >= T) return;
+  const int gsize = E / n_group;
+  float sc[kMaxExpertsPerLane], sel[kMaxExpertsPerLane];
+#pragma unroll
+  for (int j = 0; j < kMaxExpertsPerLane; ++j) {
+    const int e = lane + 32 * j;
+    if (e < E) {
+      sc[j] = 1.0f / (1.0f + expf(-logits[t * E + e]));
+      sel[j] = sc[j] + (bias ? bias[e] : 0.0f);
+    } else {
+      sc[j] = 0.0f;
+      sel[j] = -INFINITY;
+    }
+  }
+  // group scores: top-2 selection scores of each group, summed (lane g computes group g)
+  __shared__ float gs_all[8][64];
+  float* gs = gs_all[threadIdx.x / 32];
+  for (int g = 0; g < n_group; ++g) {
+    float b1 = -INFINITY, b2 = -INFINITY;
+#pragma unroll
+    for (int j = 0; j < kMaxExpertsPerLane; ++j) {
+      const int e = lane + 32 * j;
+      if (e < E && e / gsize == g) {
+        const float x = sel[j];
+        if (x > b1) {
+          b2 = b1;
+          b1 = x;
+        } else if (x > b2) {
+          b2 = x;
+        }
+      }
+    }
+#pragma unroll
+    for (int m = 16; m > 0; m >>= 1) {
+      const float o1 = __shfl_xor_sync(0xffffffffu, b1, m), o2 = __shfl_xor_sync(0xffffffffu, b2, m);
+      const float n1 = fmaxf(b1, o1);
+      const float n2 = fmaxf(fminf(b1, o1), fmaxf(b2, o2));
+      b1 = n1;
+      b2 = n2;
+    }
+    if (lane == 0) gs[g] = b1 + b2;
+  }
+  __syncwarp();
+  // keep the topk_group best groups
+  uint64_t keep = 0;
+  for (int r = 0; r < topk_group; ++r) {
+    float bv = -INFINITY;
+    int bg = 0;
+    for (int g = 0; g < n_group; ++g)
+      if (!((keep >> g) & 1) && gs[g] > bv) {
+        bv = gs[g];
+        bg = g;
+      }
+    keep |= 1ull << bg;
+  }
+#pragma unroll
+  for (int j = 0; j < kMaxExpertsPerLane; ++j) {
+    const int e = lane + 32 * j;
+    if (e < E && !((keep >> (e / gsize)) & 1)) sel[j] = -INFINITY;
+  }
+  float picked = 0.0f, mine_w = 0.0f;
+  int mine_i = -1;
+  for (int r = 0; r < k; ++r) {
+    float bv = -INFINITY;
+    int bi = 0x7fffffff;
+    float bs = 0.0f;
+#pragma unroll
+    for (int j = 0; j < kMaxExpertsPerLane; ++j)
+      if (sel[j] > bv) {
+        bv = sel[j];
+        bi = lane + 32 * j;
+        bs = sc[j];
+      }
+#pragma unroll
+    for (int m = 16; m > 0; m >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, bv, m);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, m);
+      const float os = __shfl_xor_sync(0xffffffffu, bs, m);
+      if (ov > bv || (ov == bv && oi < bi)) {
+        bv = ov;
+        bi = oi;
+        bs = os;
+      }
+    }
+    picked += bs;
+    if (lane == r) {
+      mine_w = bs;
+      mine_i = bi;
+    }
+#pragma unroll
+    for (int j = 0; j < kMaxExpertsPerLane; ++j)
+      if (lane + 32 * j == bi) sel[j] = -INFINITY;
+  }
+  if (lane < k) {
+    weights[t * k + lane] = (renorm ? mine_w / picked : mine_w) * scale;
+    ids[t * k + lane] = mine_i;
+  }
+}
+
+int kt_launch_topk_grouped(const float* logits, const float* bias, int64_t T, int E, int n_group, int topk_group, int k,
+                           int renorm, float scale, float* weights, int32_t* ids, cudaStream_t s) {
+  if (E > 32 * kMaxExpertsPerLane || k > 32 || n_group > 64 || n_group <= 0 || E % n_group || topk_group > n_group ||
+      k > (E / n_group) * topk_group)
+    return -1;
+  if (T == 0) return 0;
+  kt_topk_grouped_kernel<<<(unsigned)((T + 7) / 8), 256, 0, s>>>(logits, bias, T, E, n_group, topk_group, k, renorm,
+                                                                scale, weights, ids);
+  return 0;
+}
+
+// ------------------------------------------------------------------ permute for the prefill GEMM
+// counts[n_slots] (zeroed by the count kernel's caller), then one CTA scans them into the
+// tile list, then every route gets its sorted position.
+
+__global__ void kt_perm_count_kernel(const int32_t* __restrict__ ids, int64_t routes, int n_slots,
+                                     int32_t* __restrict__ counts) {
+  const int64_t p = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (p >= routes) return;
+  const int32_t e = ids[p];
+  if (e >= 0 && e < n_slots) atomicAdd(&counts[e], 1);
+}
+
+__global__ void kt_perm_scan_kernel(const int32_t* __restrict__ counts, int n_slots, int tile_tokens,
+                                    int32_t* __restrict__ cursor, int32_t* __restrict__ tiles,
+                                    int32_t* __restrict__ n_tiles) {
+  // single thread: n_slots is at most a few thousand
+  if (threadIdx.x != 0) return;
+  int32_t off = 0, nt = 0;
+  for (int e = 0; e < n_slots; ++e) {
+    const int32_t c = counts[e];
+    cursor[e] = off;
+    for (int32_t r = 0; r < c; r += tile_tokens) {
+      tiles[3 * nt + 0] = e;
+      tiles[3 * nt + 1] = off + r;
+      tiles[3 * nt + 2] = min(tile_tokens, c - r);
+      ++nt;
+    }
+    off += c;
+  }
+  *n_tiles = nt;
+}
+
+__global__ void kt_perm_scatter_kernel(const int32_t* __restrict__ ids, int64_t routes, int top_k, int n_slots,
+                                       int32_t* __restrict__ cursor, int32_t* __restrict__ sorted_token,
+                                       int32_t* __restrict__ route_pos) {
+  const int64_t p = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (p >= routes) return;
+  const int32_t e = ids[p];
+  if (e >= 0 && e < n_slots) {
+    const int32_t pos = atomicAdd(&cursor[e], 1);
+    sorted_token[pos] = (int32_t)(p / top_k);
+    route_pos[p] = pos;
+  } else {
+    route_pos[p] = -1;
+  }
+}
+
+int kt_launch_permute(const int32_t* ids, int64_t routes, int top_k, int n_slots, int tile_tokens, int32_t* counts,
+                      int32_t* cursor, int32_t* tiles, int32_t* n_tiles, int32_t* sorted_token, int32_t* route_pos,
+                      cudaStream_t s) {
+  if (cudaMemsetAsync(counts, 0, sizeof(int32_t) * n_slots, s) != cudaSuccess) return -3;
+  const unsigned blocks = (unsigned)((routes + 255) / 256);
+  if (routes > 0) kt_perm_count_kernel<<<blocks, 256, 0, s>>>(ids, routes, n_slots, counts);
+  kt_perm_scan_kernel<<<1, 32, 0, s>>>(counts, n_slots, tile_tokens, cursor, tiles, n_tiles);
+  if (routes > 0) kt_perm_scatter_kernel<<<blocks, 256, 0, s>>>(ids, routes, top_k, n_slots, cursor, sorted_token, route_pos);
+  return 0;
+}

@@ -1,0 +1,289 @@
+// moe_vec.cu — decode path: q8_1 activation quantizer, route grouping, and the
+// multi-token GGUF MoE GEMV (window and per-route semantics of kt_moe_a8_vec_multi).
+//
+// Reference behaviour (hot/kt_gguf_moe_multi/kt_gguf_moe_multi.cu):
+//   quantize_q8_1 (:600-650): per 32 values d = amax/127, q = roundf(x/d), s = sum(x);
+//     rows padded with zeros to a multiple of 512 values.
+//   moe_vec_q (:132-217) + moe_vec_q_rows (:74-130): Y[p, r] = sum over the row's chunks of
+//     vec_dot(W[ids[p]] row r, q8_1(X[p / top_k])); lane t of a warp takes chunks t, t+32, ...
+//     in order and an xor butterfly (16,8,4,2,1) reduces the lanes; ids < 0 give zero rows.
+//
+// B200 design: routes are first grouped by expert slot (one tiny kernel), so every CTA
+// owns one expert and a tile of rows and reads that tile of raw GGUF bytes from HBM once,
+// with 16-byte vector loads into shared memory, for all the expert's routes in the call
+// (the reference's window build does this for up to 4 routes, its per-route build not
+// at all). Each warp then walks rows with the reference's lane-to-chunk assignment and
+// butterfly, so every route's sum has the reference's order.
+#include "gguf_dot.cuh"
+#include "kt_kernels.h"
+
+// ------------------------------------------------------------------ q8_1 quantizer
+
+template <int DT>
+__global__ void __launch_bounds__(256) kt_quantize_q8_1_kernel(const void* __restrict__ x, uint8_t* __restrict__ qx,
+                                                               int64_t rows, int64_t cols, int64_t kpad) {
+  const int64_t ix = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;  // column in the padded row
+  const int64_t row = blockIdx.y + (int64_t)blockIdx.z * 65535;
+  if (row >= rows || ix >= kpad) return;
+  const float xi = ix < cols ? kt_load_act<DT>(x, row * cols + ix) : 0.0f;
+  float amax = fabsf(xi), sum = xi;
+#pragma unroll
+  for (int mask = 16; mask > 0; mask >>= 1) {
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, mask, 32));
+    sum += __shfl_xor_sync(0xffffffffu, sum, mask, 32);
+  }
+  const float d = amax / 127;
+  const int8_t q = amax == 0.0f ? 0 : (int8_t)roundf(xi / d);
+  uint8_t* blk = qx + row * (kpad / 32 * KT_Q8_1_BYTES) + (ix / 32) * KT_Q8_1_BYTES;
+  blk[4 + (ix % 32)] = (uint8_t)q;
+  if (ix % 32 == 0) {
+    half2 ds = __halves2half2(__float2half(d), __float2half(sum));
+    *reinterpret_cast<half2*>(blk) = ds;
+  }
+}
+
+int kt_launch_quantize_q8_1(const void* x, int dtype, int64_t rows, int64_t cols, void* qx, cudaStream_t s) {
+  if (rows <= 0) return 0;
+  const int64_t kpad = (cols + 511) / 512 * 512;
+  const int64_t zr = (rows + 65534) / 65535;
+  dim3 grid((unsigned)((kpad + 255) / 256), (unsigned)(rows < 65535 ? rows : 65535), (unsigned)zr);
+  switch (dtype) {
+    case KT_DT_F32: kt_quantize_q8_1_kernel<KT_DT_F32><<<grid, 256, 0, s>>>(x, (uint8_t*)qx, rows, cols, kpad); break;
+    case KT_DT_F16: kt_quantize_q8_1_kernel<KT_DT_F16><<<grid, 256, 0, s>>>(x, (uint8_t*)qx, rows, cols, kpad); break;
+    case KT_DT_BF16: kt_quantize_q8_1_kernel<KT_DT_BF16><<<grid, 256, 0, s>>>(x, (uint8_t*)qx, rows, cols, kpad); break;
+    default: return -1;
+  }
+  return 0;
+}
+
+// ------------------------------------------------------------------ route grouping
+// One CTA: counting sort of the routes by expert slot. Routes with an id outside
+// [0, n_slots) form the "zero" group (slot -1). Outputs, in the workspace:
+//   groups[0]            number of groups G
+//   groups[1 + 3g + 0]   slot of group g (-1 for the zero group)
+//   groups[1 + 3g + 1]   first position of the group in `order`
+//   groups[1 + 3g + 2]   routes in the group
+//   order[R]             route indices grouped by slot
+// Order inside a group is not fixed (atomics); every route's result is independent of it.
+
+__global__ void __launch_bounds__(1024) kt_group_routes_kernel(const int32_t* __restrict__ ids, int64_t routes,
+                                                               int n_slots, int32_t* __restrict__ groups,
+                                                               int32_t* __restrict__ order) {
+  extern __shared__ int32_t cnt[];  // n_slots + 1 counters, then n_slots + 1 cursors
+  int32_t* cur = cnt + (n_slots + 1);
+  for (int i = threadIdx.x; i < n_slots + 1; i += blockDim.x) cnt[i] = 0;
+  __syncthreads();
+  for (int64_t p = threadIdx.x; p < routes; p += blockDim.x) {
+    const int32_t e = ids[p];
+    atomicAdd(&cnt[(e >= 0 && e < n_slots) ? e + 1 : 0], 1);
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int32_t off = 0, g = 0;
+    for (int i = 0; i < n_slots + 1; ++i) {
+      const int32_t c = cnt[i];
+      cur[i] = off;
+      if (c) {
+        groups[1 + 3 * g + 0] = i - 1;
+        groups[1 + 3 * g + 1] = off;
+        groups[1 + 3 * g + 2] = c;
+        ++g;
+      }
+      off += c;
+    }
+    groups[0] = g;
+  }
+  __syncthreads();
+  for (int64_t p = threadIdx.x; p < routes; p += blockDim.x) {
+    const int32_t e = ids[p];
+    const int k = (e >= 0 && e < n_slots) ? e + 1 : 0;
+    order[atomicAdd(&cur[k], 1)] = (int32_t)p;
+  }
+}
+
+int kt_launch_group_routes(const int32_t* ids, int64_t routes, int n_slots, int32_t* groups, int32_t* order,
+                           cudaStream_t s) {
+  const size_t smem = sizeof(int32_t) * 2 * (size_t)(n_slots + 1);
+  if (smem > 200 * 1024) return -1;
+  if (smem > 48 * 1024) cudaFuncSetAttribute(kt_group_routes_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  kt_group_routes_kernel<<<1, 1024, smem, s>>>(ids, routes, n_slots, groups, order);
+  return 0;
+}
+
+// ------------------------------------------------------------------ GEMV
+
+struct KtVecArgs {
+  const uint8_t* w;            // slot base (plain layout) or int64 table of slot addresses
+  int table;                   // 1: w is the table
+  const uint8_t* qx;           // q8_1 activations [tokens, qrow] bytes
+  int64_t qrow;                // bytes per q8_1 row
+  const int32_t* groups;       // from kt_group_routes
+  const int32_t* order;
+  int top_k;
+  int rows, cols;
+  int64_t row_bytes;
+  int rows_per_cta;
+  int members_per_pass;
+  void* y;                     // [routes, rows]
+};
+
+// LPR lanes per row: 32, or 16 when a row has at most 16 chunks (two rows per warp).
+template <int TYPE, int DT, int LPR>
+__global__ void __launch_bounds__(256) kt_moe_vec_kernel(const KtVecArgs a) {
+  extern __shared__ __align__(16) uint8_t smem[];
+  __shared__ uint32_t grid_s[512];
+  using C = KtChunk<TYPE>;
+  const int g = blockIdx.y;
+  const int ngroups = a.groups[0];
+  if (g >= ngroups) return;
+  const int slot = a.groups[1 + 3 * g + 0];
+  const int start = a.groups[1 + 3 * g + 1];
+  const int count = a.groups[1 + 3 * g + 2];
+  const int r0 = blockIdx.x * a.rows_per_cta;
+  if (r0 >= a.rows) return;
+  const int nr = min(a.rows_per_cta, a.rows - r0);
+  const int tid = threadIdx.x;
+
+  if (slot < 0) {  // routes not on this device: zero rows
+    for (int64_t i = tid; i < (int64_t)count * nr; i += blockDim.x) {
+      const int p = a.order[start + i / nr];
+      kt_store_act<DT>(a.y, (int64_t)p * a.rows + r0 + i % nr, 0.0f);
+    }
+    return;
+  }
+  if constexpr (TYPE == KT_IQ3_S) {
+    for (int i = tid; i < 512; i += blockDim.x) grid_s[i] = kt_iq3s_grid_dev[i];
+  }
+  // raw rows [r0, r0 + nr) of the slot into shared memory
+  const uint8_t* wbase = a.table ? reinterpret_cast<const uint8_t*>(reinterpret_cast<const int64_t*>(a.w)[slot])
+                                 : a.w + (int64_t)slot * a.rows * a.row_bytes;
+  const uint8_t* src = wbase + (int64_t)r0 * a.row_bytes;
+  const int64_t tile_bytes = (int64_t)nr * a.row_bytes;
+  uint8_t* wt = smem;
+  if ((((uintptr_t)src) & 15) == 0 && (tile_bytes & 15) == 0) {
+    const uint4* s4 = reinterpret_cast<const uint4*>(src);
+    uint4* d4 = reinterpret_cast<uint4*>(wt);
+    for (int64_t i = tid; i < tile_bytes / 16; i += blockDim.x) d4[i] = __ldg(s4 + i);
+  } else {  // GGUF blocks are always 2-byte aligned
+    const uint16_t* s2 = reinterpret_cast<const uint16_t*>(src);
+    uint16_t* d2 = reinterpret_cast<uint16_t*>(wt);
+    for (int64_t i = tid; i < tile_bytes / 2; i += blockDim.x) d2[i] = __ldg(s2 + i);
+  }
+  const int64_t wt_bytes = (tile_bytes + 15) & ~(int64_t)15;
+  uint8_t* act = smem + wt_bytes;
+  const int nblocks = a.cols / C::QK;
+  const int nchunks = nblocks * C::CPB;
+  const int warp = tid / 32, lane = tid % 32;
+  constexpr int RPW = 32 / LPR;  // rows per warp pass
+  const int sub = lane / LPR, sl = lane % LPR;
+
+  for (int m0 = 0; m0 < count; m0 += a.members_per_pass) {
+    const int nm = min(a.members_per_pass, count - m0);
+    __syncthreads();  // previous pass done with `act`; first pass: weights visible
+    for (int m = 0; m < nm; ++m) {
+      const int p = a.order[start + m0 + m];
+      const uint4* s4 = reinterpret_cast<const uint4*>(a.qx + (int64_t)(p / a.top_k) * a.qrow);
+      uint4* d4 = reinterpret_cast<uint4*>(act + (int64_t)m * a.qrow);
+      for (int64_t i = tid; i < a.qrow / 16; i += blockDim.x) d4[i] = __ldg(s4 + i);
+    }
+    __syncthreads();
+    for (int rr = warp * RPW; rr < nr; rr += (blockDim.x / 32) * RPW) {
+      const int r = rr + sub;
+      const bool live = r < nr;
+      const uint8_t* wrow = wt + (int64_t)(live ? r : 0) * a.row_bytes;
+      for (int mb = 0; mb < nm; mb += 8) {
+        float acc[8];
+#pragma unroll
+        for (int m = 0; m < 8; ++m) acc[m] = 0.0f;
+        if (live) {
+          for (int c = sl; c < nchunks; c += LPR) {
+            const int i = c / C::CPB, iqs = C::VDR * (c % C::CPB);
+            const uint8_t* bx = wrow + (int64_t)i * C::BYTES;
+            const int64_t yoff = (int64_t)i * (C::QK / 32) * KT_Q8_1_BYTES;
+#pragma unroll
+            for (int m = 0; m < 8; ++m)
+              if (mb + m < nm) acc[m] += kt_vec_dot<TYPE>(bx, act + (int64_t)(mb + m) * a.qrow + yoff, iqs, grid_s);
+          }
+        }
+#pragma unroll
+        for (int m = 0; m < 8; ++m) {
+          float t = acc[m];
+#pragma unroll
+          for (int mask = LPR / 2; mask > 0; mask >>= 1) t += __shfl_xor_sync(0xffffffffu, t, mask);
+          if (live && sl == 0 && mb + m < nm) {
+            const int p = a.order[start + m0 + mb + m];
+            kt_store_act<DT>(a.y, (int64_t)p * a.rows + r0 + r, t);
+          }
+        }
+      }
+    }
+  }
+}
+
+template <int TYPE, int DT>
+static int launch_vec_t(const KtVecArgs& a, int max_groups, int lpr, size_t smem, cudaStream_t s) {
+  dim3 grid((a.rows + a.rows_per_cta - 1) / a.rows_per_cta, max_groups);
+  if (lpr == 16) {
+    auto k = kt_moe_vec_kernel<TYPE, DT, 16>;
+    cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    k<<<grid, 256, smem, s>>>(a);
+  } else {
+    auto k = kt_moe_vec_kernel<TYPE, DT, 32>;
+    cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    k<<<grid, 256, smem, s>>>(a);
+  }
+  return 0;
+}
+
+template <int TYPE>
+static int launch_vec_dt(const KtVecArgs& a, int dtype, int max_groups, int lpr, size_t smem, cudaStream_t s) {
+  switch (dtype) {
+    case KT_DT_F32: return launch_vec_t<TYPE, KT_DT_F32>(a, max_groups, lpr, smem, s);
+    case KT_DT_F16: return launch_vec_t<TYPE, KT_DT_F16>(a, max_groups, lpr, smem, s);
+    case KT_DT_BF16: return launch_vec_t<TYPE, KT_DT_BF16>(a, max_groups, lpr, smem, s);
+  }
+  return -1;
+}
+
+// Rows per CTA: a power of two giving a tile of at most ~24 KB of raw rows, at least 8.
+static int pick_rows_per_cta(int64_t row_bytes, int rows) {
+  int rpc = 8;
+  while (rpc < 64 && (int64_t)(rpc * 2) * row_bytes <= 24 * 1024) rpc *= 2;
+  return rpc;
+}
+
+int kt_launch_moe_vec(int type, const void* w, int table, const void* qx, int64_t qrow, const int32_t* groups,
+                      const int32_t* order, int max_groups, int top_k, int rows, int cols, int dtype, void* y,
+                      cudaStream_t s) {
+  const KtBlockInfo bi = kt_block_info(type);
+  if (!bi.qk || cols % bi.qk) return -1;
+  KtVecArgs a;
+  a.w = (const uint8_t*)w;
+  a.table = table;
+  a.qx = (const uint8_t*)qx;
+  a.qrow = qrow;
+  a.groups = groups;
+  a.order = order;
+  a.top_k = top_k;
+  a.rows = rows;
+  a.cols = cols;
+  a.row_bytes = (int64_t)cols / bi.qk * bi.bytes;
+  a.rows_per_cta = pick_rows_per_cta(a.row_bytes, rows);
+  const int64_t wt_bytes = ((int64_t)a.rows_per_cta * a.row_bytes + 15) & ~(int64_t)15;
+  int mpp = 8;
+  while (mpp > 1 && wt_bytes + mpp * qrow > 200 * 1024) mpp /= 2;
+  a.members_per_pass = mpp;
+  a.y = y;
+  const size_t smem = (size_t)(wt_bytes + mpp * qrow);
+  if (smem > 220 * 1024) return -2;
+  int chunks_per_block = type == KT_Q8_0 ? 4 : type == KT_Q4_K ? 16 : type == KT_Q6_K ? 32 : 8;
+  const int nchunks = cols / bi.qk * chunks_per_block;
+  const int lpr = nchunks <= 16 ? 16 : 32;
+  switch (type) {
+    case KT_Q8_0: return launch_vec_dt<KT_Q8_0>(a, dtype, max_groups, lpr, smem, s);
+    case KT_Q4_K: return launch_vec_dt<KT_Q4_K>(a, dtype, max_groups, lpr, smem, s);
+    case KT_Q6_K: return launch_vec_dt<KT_Q6_K>(a, dtype, max_groups, lpr, smem, s);
+    case KT_IQ3_S: return launch_vec_dt<KT_IQ3_S>(a, dtype, max_groups, lpr, smem, s);
+  }
+  return -1;
+}

@@ -1,0 +1,170 @@
+"""Multi-token GGUF MoE GEMV for the KT hot experts — B200 (sm_100a) implementation.
+
+Drop-in for the reference module sglang.srt.layers.moe.kt_gguf_moe_multi
+(hot/kt_gguf_moe_multi.py): same public names, signatures and return shapes.
+
+`moe_a8_vec_multi(X, W, ids, top_k, type, rows, tokens)`: Y [tokens*top_k, rows] in X's
+dtype; route p is row block `ids[p]` of W against q8_1(X[p // top_k]); ids < 0 (experts on
+the CPU) give zero rows. The routes of one slot share one read of its weights at any token
+count (the reference shares it within windows of up to KT_GGUF_MOE_MAXM tokens).
+
+`moe_a8_vec_routes(...)`: the reference's per-route build. Here both names run the same
+kernel and give identical sums per route.
+
+With table=True, W is an int64 device table of per-slot weight addresses (the reference's
+KT_PTR_TABLE build for KV-lent slots, hot/kt_gguf_moe_multi.py:20-24); addresses must be
+16-byte aligned.
+
+`dense_a8_vec(X, W, type)`: a dense GGUF linear [rows, row_bytes] as a one-slot MoE.
+
+`moe_prefill(...)`: the whole expert layer for prefill chunks on tcgen05 (no counterpart
+name in the reference module; it replaces the streamer's dequant + CUTLASS group body for
+resident slots).
+
+Everything reaches CUDA through libkt_gguf_b200.so (include/kt_gguf_b200.h). There is no
+CPU path: CPU tensors and non-sm_100 devices raise.
+"""
+import os
+
+import torch
+
+from . import _native as N
+
+MAX_TOKENS = int(os.environ.get("KT_GGUF_MOE_MAXM", "4"))
+MMV_Y = int(os.environ.get("KT_GGUF_MOE_MMV_Y", "2"))  # kept for compatibility; the B200 kernel sizes its own CTAs
+RPW = int(os.environ.get("KT_GGUF_MOE_RPW", "4"))
+DENSE = os.environ.get("KT_GGUF_DENSE_MULTI", "1") == "1"
+DENSE_MMV_Y = int(os.environ.get("KT_GGUF_DENSE_MMV_Y", "4"))
+DENSE_RPW = int(os.environ.get("KT_GGUF_DENSE_RPW", "1"))
+DENSE_MIN_ROWS = 513
+ROUTES = os.environ.get("KT_GGUF_MOE_ROUTES", "1") == "1"
+# ggml types this build has kernels for (Q8_0, Q4_K, Q6_K, IQ3_S)
+DENSE_TYPES = set(N.SUPPORTED_TYPES)
+SUPPORTED_TYPES = set(N.SUPPORTED_TYPES)
+
+
+def _load(mmv_y=None, rpw=None, per_route=False, table=False):
+    """The native library (the reference JIT-builds one extension per configuration; here
+    one prebuilt library serves every configuration)."""
+    return N.load()
+
+
+def enabled() -> bool:
+    return os.environ.get("KT_GGUF_MOE_MULTI", "1") == "1"
+
+
+def _check_common(X, W, ids, qtype, table):
+    N.require_device(X)
+    if qtype not in SUPPORTED_TYPES:
+        raise ValueError(f"ggml type {qtype} has no B200 kernel (supported: {sorted(SUPPORTED_TYPES)})")
+    if X.dim() != 2:
+        raise ValueError(f"X must be [tokens, cols], got {tuple(X.shape)}")
+    if ids.dtype != torch.int32:
+        raise TypeError(f"topk ids must be int32 (got {ids.dtype})")
+    if table:
+        if W.dtype != torch.int64 or W.dim() != 1:
+            raise TypeError("with table=True, W must be a 1-D int64 table of slot addresses")
+    elif W.dtype != torch.uint8 or W.dim() != 3 or not W.is_contiguous():
+        raise TypeError("W must be a contiguous uint8 [slots, rows, row_bytes] tensor")
+    for t in (W, ids):
+        if t.device != X.device:
+            raise ValueError("X, W and ids must be on the same device")
+
+
+def _vec(entry, X, W, ids, top_k, qtype, rows, tokens, table):
+    _check_common(X, W, ids, qtype, table)
+    X = X.contiguous()
+    ids = ids.contiguous()
+    cols = X.shape[1]
+    if tokens > X.shape[0] or ids.numel() < tokens * top_k:
+        raise ValueError("tokens / top_k exceed X or ids")
+    if not table and W.shape[1] != rows:
+        raise ValueError(f"W has {W.shape[1]} rows per slot, expected {rows}")
+    if not table and W.shape[2] != N.row_bytes(qtype, cols):
+        raise ValueError(f"W row bytes {W.shape[2]} do not match type {qtype} at {cols} columns")
+    n_slots = W.numel() if table else W.shape[0]
+    Y = torch.empty((tokens * top_k, rows), dtype=X.dtype, device=X.device)
+    if tokens == 0:
+        return Y
+    lib = N.load()
+    ws_bytes = lib.kt_moe_a8_vec_workspace_size(tokens, cols, tokens * top_k, n_slots)
+    ws = N.workspace(ws_bytes, X.device)
+    fn = getattr(lib, entry)
+    N.check(fn(N.ptr(X), N.dtype_code(X), tokens, cols, N.ptr(W), int(table), n_slots, N.ptr(ids), top_k, qtype, rows,
+               N.ptr(Y), N.ptr(ws), ws.numel(), N.stream_of(X)), entry)
+    return Y
+
+
+def moe_a8_vec_multi(X, W, ids, top_k, qtype, rows, tokens, table=False):
+    return _vec("kt_moe_a8_vec_multi", X, W, ids, top_k, qtype, rows, tokens, table)
+
+
+def moe_a8_vec_routes(X, W, ids, top_k, qtype, rows, tokens, table=False):
+    """ggml_moe_a8_vec's contract at any token count: route p's rows from expert ids[p], zeros for ids < 0."""
+    return _vec("kt_moe_a8_vec_routes", X, W, ids, top_k, qtype, rows, tokens, table)
+
+
+def reads_table(tokens: int) -> bool:
+    """Whether the hot method's kernel for a window of this many tokens reads the slot
+    weights through the pointer table. Every B200 kernel does (GEMV and prefill GEMM)."""
+    return enabled()
+
+
+def dense_ok(x, qweight, qtype) -> bool:
+    return (DENSE and 2 <= x.shape[0] <= MAX_TOKENS and qtype in DENSE_TYPES and qweight.dim() == 2
+            and qweight.shape[0] >= DENSE_MIN_ROWS and qweight.dtype == torch.uint8 and qweight.is_contiguous())
+
+
+def dense_a8_vec(x, qweight, qtype):
+    """y = x @ W^T for a GGUF weight [rows, row_bytes], each row read once for all tokens."""
+    N.require_device(x)
+    if qtype not in SUPPORTED_TYPES:
+        raise ValueError(f"ggml type {qtype} has no B200 kernel")
+    x = x.contiguous()
+    T, cols = x.shape
+    rows = qweight.shape[0]
+    if qweight.dtype != torch.uint8 or qweight.dim() != 2 or qweight.shape[1] != N.row_bytes(qtype, cols):
+        raise TypeError("qweight must be a uint8 [rows, row_bytes] GGUF matrix matching x")
+    y = torch.empty((T, rows), dtype=x.dtype, device=x.device)
+    if T == 0:
+        return y
+    lib = N.load()
+    ws = N.workspace(lib.kt_dense_a8_vec_workspace_size(T, cols), x.device)
+    N.check(lib.kt_dense_a8_vec(N.ptr(x), N.dtype_code(x), T, cols, N.ptr(qweight.contiguous()), qtype, rows, N.ptr(y),
+                                N.ptr(ws), ws.numel(), N.stream_of(x)), "kt_dense_a8_vec")
+    return y
+
+
+def moe_prefill(x, w13, w2, topk_ids, topk_weights, type13, type2, inter, table=False, out=None, workspace=None):
+    """out [T, K] bf16 = sum_k w[t,k] * down(silu(gate x) * up x) over resident slots, on tcgen05.
+
+    x [T, K] bf16; w13 [S, 2*inter, row_bytes] / w2 [S, K, row_bytes] uint8 (or int64 slot
+    address tables with table=True); topk_ids [T, k] int32 slot ids (-1: not resident);
+    topk_weights [T, k] float32. `workspace` (uint8, optional) is reused when large enough.
+    """
+    N.require_device(x)
+    if x.dtype != torch.bfloat16:
+        raise TypeError("the prefill path takes bf16 activations")
+    if type13 not in SUPPORTED_TYPES or type2 not in SUPPORTED_TYPES:
+        raise ValueError("unsupported ggml type")
+    if topk_ids.dtype != torch.int32 or topk_weights.dtype != torch.float32:
+        raise TypeError("topk ids must be int32 and weights float32")
+    x = x.contiguous()
+    T, K = x.shape
+    top_k = topk_ids.shape[1]
+    n_slots = w13.numel() if table else w13.shape[0]
+    if not table:
+        if w13.shape[1] != 2 * inter or w13.shape[2] != N.row_bytes(type13, K):
+            raise ValueError("w13 shape does not match [S, 2*inter, row_bytes(K)]")
+        if w2.shape[1] != K or w2.shape[2] != N.row_bytes(type2, inter):
+            raise ValueError("w2 shape does not match [S, K, row_bytes(inter)]")
+    if out is None:
+        out = torch.empty((T, K), dtype=torch.bfloat16, device=x.device)
+    lib = N.load()
+    need = lib.kt_moe_prefill_workspace_size(T, top_k, K, inter, n_slots)
+    if workspace is None or workspace.numel() < need:
+        workspace = N.workspace(need, x.device)
+    N.check(lib.kt_moe_prefill(N.ptr(x), T, K, inter, N.ptr(topk_ids.contiguous()), N.ptr(topk_weights.contiguous()), top_k,
+                               N.ptr(w13), type13, N.ptr(w2), type2, int(table), n_slots, N.ptr(out), N.ptr(workspace),
+                               workspace.numel(), N.stream_of(x)), "kt_moe_prefill")
+    return out

@@ -1,0 +1,48 @@
+"""Generates tests/golden/gguf_dequant.npz: known-answer vectors for the GGUF dequantizers.
+
+The reference ships no fixtures for this path, so the known answers come from gguf-py
+0.19.0 (`gguf.quants.dequantize`, numpy restatements of ggml's dequantize_row_*), an
+implementation independent of this repository. For each hot-path type the file holds
+  <type>_blocks  uint8  : 48 rows of 512 values (2 super-blocks / 16 Q8_0 blocks per row):
+                           rows 0-23 encoded from N(0, 0.02) weights by gguf_encode.c,
+                           rows 24-47 random bytes with finite scales (every code pattern)
+  <type>_values  float32: gguf-py's dequantization of those rows
+plus the IQ3_S codebook as uint32 words.
+
+Run from the repository root: python tests/golden/make_golden.py
+"""
+import sys
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parents[2]
+sys.path.insert(0, str(ROOT / "kt-prefill-lend_b200"))
+
+from gguf import GGMLQuantizationType as Q  # noqa: E402
+from gguf.quants import IQ3_S, dequantize  # noqa: E402
+
+from kt_gguf_b200 import synth  # noqa: E402
+
+TYPES = {8: Q.Q8_0, 12: Q.Q4_K, 14: Q.Q6_K, 21: Q.IQ3_S}
+
+
+def main():
+    rng = np.random.default_rng(20261201)
+    out = {}
+    for t, qt in TYPES.items():
+        enc = synth.quantize(rng.standard_normal((24, 512), dtype=np.float32) * 0.02, t)
+        rnd = synth.random_blocks(rng, t, 24, 512)
+        blocks = np.concatenate([enc, rnd])
+        out[f"{t}_blocks"] = blocks
+        out[f"{t}_values"] = dequantize(blocks, qt).reshape(48, 512).astype(np.float32)
+    IQ3_S.init_grid()
+    g = IQ3_S.grid.reshape(512, 4).astype(np.uint32)
+    out["iq3s_grid"] = g[:, 0] | (g[:, 1] << 8) | (g[:, 2] << 16) | (g[:, 3] << 24)
+    path = Path(__file__).with_name("gguf_dequant.npz")
+    np.savez_compressed(path, **out)
+    print(path, {k: v.shape for k, v in out.items()})
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,87 @@
+"""GGUF formats and the CPU oracle's dequantizers against the golden vectors (no GPU)."""
+import re
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+from oracle import oracle as O
+
+GOLDEN = np.load(Path(__file__).with_name("golden") / "gguf_dequant.npz")
+TYPES = (8, 12, 14, 21)
+REF_COMMON = Path("/root/reference/hot/kt_gguf_moe_multi/ggml-common.h")
+
+
+def test_block_sizes_known_answers():
+    # hot/kt_gguf_hot.py:76-80 BLOCK_INFO for the hot-path types
+    assert O.BLOCK == {8: (32, 34), 12: (256, 144), 14: (256, 210), 21: (256, 110)}
+    from kt_gguf_b200 import synth
+
+    assert synth.BLOCK == O.BLOCK
+    assert O.row_bytes(12, 2048) == 8 * 144 and O.row_bytes(14, 512) == 420 and O.row_bytes(21, 512) == 220
+
+
+@pytest.mark.parametrize("qtype", TYPES)
+def test_oracle_dequant_matches_golden_bit_exact(qtype):
+    blocks = GOLDEN[f"{qtype}_blocks"]
+    want = GOLDEN[f"{qtype}_values"]
+    got = O.dequant(qtype, blocks, 512)
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+
+
+def test_iq3s_grid_matches_golden_and_header():
+    import importlib.util
+
+    from kt_gguf_b200 import synth  # noqa: F401  (package importable)
+
+    header = Path(__file__).resolve().parents[1] / "kt-prefill-lend_b200" / "csrc" / "iq3s_grid.h"
+    words = [int(x, 16) for x in re.findall(r"0x([0-9a-f]{8})u", header.read_text())]
+    assert np.array_equal(np.array(words, dtype=np.uint32), GOLDEN["iq3s_grid"])
+    assert importlib.util.find_spec("gguf") is not None
+
+
+@pytest.mark.skipif(not REF_COMMON.exists(), reason="reference tree not mounted")
+def test_iq3s_grid_matches_reference_table():
+    # the reference's own codebook (ggml-common.h:598-665), read as text
+    src = REF_COMMON.read_text()
+    body = re.search(r"iq3s_grid\[512\]\s*=\s*\{(.*?)\};", src, re.S).group(1)
+    ref = np.array([int(x, 16) for x in re.findall(r"0x[0-9a-fA-F]+", body)], dtype=np.uint32)
+    assert np.array_equal(ref, GOLDEN["iq3s_grid"])
+
+
+@pytest.mark.parametrize("qtype,tol", [(8, 0.01), (12, 0.12), (14, 0.03), (21, 0.25)])
+def test_encoder_round_trip(qtype, tol):
+    from kt_gguf_b200 import synth
+
+    rng = np.random.default_rng(qtype)
+    x = rng.standard_normal((16, 1024), dtype=np.float32) * 0.02
+    back = O.dequant(qtype, synth.quantize(x, qtype), 1024)
+    assert O.rel_l2(back, x) < tol
+
+
+def test_q8_1_known_answers():
+    # d = amax/127, q = roundf(x/d), s = sum of the unquantized values, zero padding to 512
+    x = np.zeros((1, 40), dtype=np.float32)
+    x[0, :32] = np.arange(32) - 16.0  # amax 16
+    x[0, 32:40] = 0.5
+    q = O.quantize_q8_1(x)
+    assert q.shape == (1, 16 * 36)
+    d = q[0, 0:2].view(np.float16)[0]
+    s = q[0, 2:4].view(np.float16)[0]
+    assert d == np.float16(16 / 127) and s == np.float16(-16.0)
+    codes = q[0, 4:36].view(np.int8)
+    assert np.array_equal(codes, np.round((np.arange(32) - 16) * 127 / 16).astype(np.int8))
+    blk1 = q[0, 36:72]
+    assert blk1[0:2].view(np.float16)[0] == np.float16(0.5 / 127)
+    assert np.all(blk1[4:12].view(np.int8) == 127) and np.all(blk1[12:36] == 0)
+    assert np.all(q[0, 72:] == 0)  # all-zero padded blocks: d = 0, s = 0, q = 0
+
+
+def test_bf16_helpers_round_to_nearest_even():
+    x = np.array([1.0, 1.00390625, 1.01171875, -3.0e38, 1e-40, np.inf], dtype=np.float32)
+    b = O.f32_to_bf16(x)
+    back = O.bf16_to_f32(b)
+    import torch
+
+    want = torch.from_numpy(x).to(torch.bfloat16).to(torch.float32).numpy()
+    assert np.array_equal(back.view(np.uint32), want.view(np.uint32))

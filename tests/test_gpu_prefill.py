@@ -1,0 +1,149 @@
+"""GPU parity of the prefill layer (tcgen05 grouped GEMM with in-kernel GGUF dequant)
+through the C ABI: the routing permutation exactly, H and Y against torch fp32 math on the
+bit-exact dequantized weights, and the layer output against the fp32 dequant-then-matmul
+oracle within the north-star tolerance (rel-L2 <= 5e-3, bf16 activations)."""
+import ctypes
+
+import numpy as np
+import pytest
+import torch
+
+from kt_gguf_b200 import _native as Nt
+from kt_gguf_b200 import kernels as Kn
+from kt_gguf_b200 import kt_gguf_moe_multi as M
+from kt_gguf_b200 import synth
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+TOL_FP32_ORACLE = 5e-3   # north-star bound vs the fp32 dequant-then-matmul oracle
+TOL_STAGE = 4e-3         # H / Y vs fp32 math on the same bf16 operands (bf16 output rounding)
+
+
+def run_prefill(L: synth.MoELayer, dev):
+    x = L.x.to(dev)
+    w13 = torch.from_numpy(L.w13).to(dev)
+    w2 = torch.from_numpy(L.w2).to(dev)
+    ids = L.topk_ids.to(dev)
+    w = L.topk_weights.to(dev)
+    lib = Nt.load()
+    T, K = L.x.shape
+    k = ids.shape[1]
+    S = w13.shape[0]
+    ws = Nt.workspace(lib.kt_moe_prefill_workspace_size(T, k, K, L.inter, S), dev)
+    out = M.moe_prefill(x, w13, w2, ids, w, L.type13, L.type2, L.inter, workspace=ws)
+    torch.cuda.synchronize()
+    assert Nt.workspace_status(ws) == Nt.KT_DEV_OK
+    offs = (ctypes.c_size_t * 8)()
+    lib.kt_moe_prefill_workspace_layout(T, k, K, L.inter, S, offs)
+    R = T * k
+    view = lambda i, dt, n: ws[offs[i]:offs[i] + n * torch.tensor([], dtype=dt).element_size()].view(dt)
+    st = dict(
+        counts=view(1, torch.int32, S).cpu(),
+        sorted_token=view(4, torch.int32, R).cpu(),
+        route_pos=view(5, torch.int32, R).cpu(),
+        h=view(6, torch.bfloat16, R * L.inter).view(R, L.inter),
+        y=view(7, torch.bfloat16, R * K).view(R, K),
+    )
+    return out, st, (x, w13, w2)
+
+
+def check_layer(L: synth.MoELayer, dev):
+    out, st, (x, w13, w2) = run_prefill(L, dev)
+    T, K = L.x.shape
+    N = L.inter
+    ids = L.topk_ids.reshape(-1)
+    k = L.topk_ids.shape[1]
+    S = L.w13.shape[0]
+    # permutation: exact
+    resident = (ids >= 0) & (ids < S)
+    assert torch.equal(st["counts"], torch.bincount(ids[resident].long(), minlength=S).int())
+    pos = st["route_pos"]
+    assert torch.all(pos[~resident] == -1)
+    rp = pos[resident].long()
+    assert torch.equal(torch.sort(rp).values, torch.arange(int(resident.sum())))
+    tok = torch.arange(T * k) // k
+    assert torch.equal(st["sorted_token"][rp], tok[resident].int())
+    # H and Y against fp32 math on bf16 operands
+    W13 = Kn.gguf_dequantize(w13, L.type13, K, torch.bfloat16).float()
+    W2 = Kn.gguf_dequantize(w2, L.type2, N, torch.bfloat16).float()
+    xs = x.float()[tok[resident].to(dev)]
+    slot = ids[resident].long().to(dev)
+    h_want = torch.empty((len(slot), N), device=dev)
+    y_want = torch.empty((len(slot), K), device=dev)
+    h_got = st["h"][rp.to(dev)].float()
+    for s in range(S):
+        m = slot == s
+        if not bool(m.any()):
+            continue
+        g = xs[m] @ W13[s, :N].T
+        u = xs[m] @ W13[s, N:].T
+        h_want[m] = torch.nn.functional.silu(g) * u
+        y_want[m] = h_got[m].to(torch.bfloat16).float() @ W2[s].T
+    assert O.rel_l2(h_got.cpu().numpy(), h_want.cpu().numpy()) < TOL_STAGE
+    y_got = st["y"][rp.to(dev)].float()
+    assert O.rel_l2(y_got.cpu().numpy(), y_want.cpu().numpy()) < TOL_STAGE
+    # layer output against the fp32 oracle and the reference arithmetic
+    xb = L.x.view(torch.int16).numpy().view(np.uint16)
+    f = O.moe_fp32(xb, L.topk_ids.numpy(), L.topk_weights.numpy(), L.type13, L.w13, L.type2, L.w2, N)
+    got = out.float().cpu().numpy()
+    err_fp32 = O.rel_l2(got, f)
+    assert err_fp32 < TOL_FP32_ORACLE, err_fp32
+    return err_fp32
+
+
+@pytest.mark.parametrize("type13,type2", [(12, 14), (21, 21), (8, 8), (12, 12), (14, 14)])
+def test_prefill_layer_types(cuda_device, type13, type2):
+    L = synth.make_layer(seed=type13 * 10 + type2, tokens=300, hidden=512, inter=256, n_experts=8, top_k=4,
+                         type13=type13, type2=type2, n_hot=6)
+    check_layer(L, cuda_device)
+
+
+def test_prefill_layer_config2_shapes_small(cuda_device):
+    # config 2 geometry (hidden 2048, inter 512, Q4_K/Q6_K, 256 experts top-8, 64 hot,
+    # Zipf(1.1)) at 1,024 tokens so the CPU oracle finishes in seconds
+    L = synth.make_layer(seed=0, tokens=1024, hidden=2048, inter=512, n_experts=256, top_k=8, type13=12, type2=14,
+                         n_hot=64, zipf=1.1)
+    err = check_layer(L, cuda_device)
+    ref = O.moe_ref_bf16(L.x.view(torch.int16).numpy().view(np.uint16), L.topk_ids.numpy(), L.topk_weights.numpy(),
+                         12, L.w13, 14, L.w2, 512)
+    out, _, _ = run_prefill(L, cuda_device)
+    gap_ref = O.rel_l2(out.float().cpu().numpy(), O.bf16_to_f32(ref))
+    assert gap_ref < 3e-2 and err < TOL_FP32_ORACLE
+
+
+def test_prefill_tile_edges(cuda_device):
+    # slot 0 gets exactly 256 routes (one full tile), slot 1 257 (a 1-row tile), slot 2 one route
+    T, k = 300, 2
+    L = synth.make_layer(seed=5, tokens=T, hidden=512, inter=256, n_experts=4, top_k=k, type13=12, type2=14, n_hot=4)
+    ids = torch.full((T, k), -1, dtype=torch.int32)
+    ids[:256, 0] = 0
+    ids[:257, 1] = 1
+    ids[299, 0] = 2
+    L.topk_ids = ids
+    check_layer(L, cuda_device)
+
+
+def test_prefill_nothing_resident(cuda_device):
+    L = synth.make_layer(seed=6, tokens=64, hidden=512, inter=256, n_experts=4, top_k=2, type13=12, type2=14, n_hot=4)
+    L.topk_ids = torch.full_like(L.topk_ids, -1)
+    out, st, _ = run_prefill(L, cuda_device)
+    assert torch.all(out == 0)
+
+
+def test_prefill_pointer_table(cuda_device):
+    L = synth.make_layer(seed=8, tokens=200, hidden=512, inter=256, n_experts=6, top_k=3, type13=21, type2=21, n_hot=6)
+    dev = cuda_device
+    out, _, (x, w13, w2) = run_prefill(L, dev)
+    c13 = [w13[s].clone() for s in range(6)]
+    c2 = [w2[s].clone() for s in range(6)]
+    t13 = torch.tensor([c.data_ptr() for c in c13], dtype=torch.int64, device=dev)
+    t2 = torch.tensor([c.data_ptr() for c in c2], dtype=torch.int64, device=dev)
+    out_t = M.moe_prefill(x, t13, t2, L.topk_ids.to(dev), L.topk_weights.to(dev), 21, 21, L.inter, table=True)
+    assert torch.equal(out, out_t)
+
+
+def test_prefill_deterministic(cuda_device):
+    L = synth.make_layer(seed=9, tokens=512, hidden=512, inter=256, n_experts=8, top_k=4, type13=12, type2=14, n_hot=8)
+    a, _, _ = run_prefill(L, cuda_device)
+    b, _, _ = run_prefill(L, cuda_device)
+    assert torch.equal(a, b)

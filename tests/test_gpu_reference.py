@@ -1,0 +1,78 @@
+"""Pins the oracle and the B200 GEMV to the reference kernel itself: the reference's
+kt_gguf_moe_multi.cu, compiled for sm_100a from the reference tree by oracle/build_ref.py
+(window and per-route builds), run on the same seeded inputs.
+
+Skipped when the reference modules were not built (no reference tree where build() ran).
+"""
+import numpy as np
+import pytest
+import torch
+
+from kt_gguf_b200 import kt_gguf_moe_multi as M
+from kt_gguf_b200 import synth
+from oracle import build_ref
+from oracle import oracle as O
+
+pytestmark = [pytest.mark.gpu,
+              pytest.mark.skipif(not (build_ref.available("kt_ref_window") and build_ref.available("kt_ref_routes")),
+                                 reason="reference kernel not built (oracle/build_ref.py)")]
+
+CASES = [(8, 2048, 768), (8, 768, 2048), (12, 2048, 1024), (14, 512, 2048), (21, 2048, 1024), (21, 512, 2048)]
+
+
+def bits(t):
+    return t.view(torch.int16).cpu().numpy().view(np.uint16)
+
+
+@pytest.fixture(scope="module")
+def ref_mods():
+    return build_ref.load_module("kt_ref_window"), build_ref.load_module("kt_ref_routes")
+
+
+@pytest.mark.parametrize("qtype,cols,rows", CASES)
+@pytest.mark.parametrize("tokens,top_k", [(1, 8), (3, 10), (4, 4)])
+def test_window_kernel_vs_reference(cuda_device, ref_mods, qtype, cols, rows, tokens, top_k):
+    win, routes = ref_mods
+    slots = 12
+    rng = np.random.default_rng(qtype * 7 + tokens)
+    W = np.stack([synth.quantize(rng.standard_normal((rows, cols), dtype=np.float32) * 0.02, qtype)
+                  for _ in range(slots)])
+    x = torch.randn((tokens, cols), generator=torch.Generator().manual_seed(tokens + cols)).to(torch.bfloat16)
+    # distinct ids within a token (router top-k), some routes on the CPU (-1)
+    ids = np.stack([rng.permutation(slots)[:top_k] for _ in range(tokens)]).astype(np.int32)
+    ids[rng.random(ids.shape) < 0.2] = -1
+    ids_t = torch.from_numpy(ids.reshape(-1)).to(cuda_device)
+    Wd = torch.from_numpy(W).to(cuda_device)
+    xd = x.to(cuda_device)
+    y_ref = win.kt_moe_a8_vec_multi(xd, Wd, ids_t, top_k, qtype, rows, tokens)
+    y_ref_routes = routes.kt_moe_a8_vec_multi(xd, Wd, ids_t, top_k, qtype, rows, tokens)
+    y = M.moe_a8_vec_multi(xd, Wd, ids_t, top_k, qtype, rows, tokens)
+    torch.cuda.synchronize()
+    # the reference's own claim: window and per-route builds give identical sums
+    assert torch.equal(y_ref, y_ref_routes)
+    # oracle pinned to the reference kernel
+    want = O.moe_vec(qtype, W, O.quantize_q8_1(x.float().numpy()), ids.reshape(-1), top_k, rows, cols)
+    ob = O.f32_to_bf16(want)
+    rb = bits(y_ref)
+    assert (ob != rb).mean() < 2e-3
+    assert O.rel_l2(O.bf16_to_f32(rb), want) < 1e-3
+    # the B200 kernel against the reference kernel
+    gb = bits(y)
+    mismatch = (gb != rb).mean()
+    assert mismatch < 2e-3, mismatch
+    assert O.rel_l2(O.bf16_to_f32(gb), O.bf16_to_f32(rb)) < 1e-3
+
+
+@pytest.mark.parametrize("qtype,cols,rows", [(12, 2048, 1024), (21, 512, 2048)])
+def test_per_route_build_at_prefill_size(cuda_device, ref_mods, qtype, cols, rows):
+    _, routes = ref_mods
+    rng = np.random.default_rng(3)
+    slots, tokens, top_k = 8, 96, 8
+    W = np.stack([synth.quantize(rng.standard_normal((rows, cols), dtype=np.float32) * 0.02, qtype)
+                  for _ in range(slots)])
+    x = torch.randn((tokens, cols), generator=torch.Generator().manual_seed(2)).to(torch.bfloat16)
+    ids = torch.from_numpy(np.stack([rng.permutation(slots)[:top_k] for _ in range(tokens)]).astype(np.int32))
+    xd, Wd, idd = x.to(cuda_device), torch.from_numpy(W).to(cuda_device), ids.reshape(-1).to(cuda_device)
+    y_ref = routes.kt_moe_a8_vec_multi(xd, Wd, idd, top_k, qtype, rows, tokens)
+    y = M.moe_a8_vec_routes(xd, Wd, idd, top_k, qtype, rows, tokens)
+    assert (bits(y) != bits(y_ref)).mean() < 2e-3
