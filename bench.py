@@ -46,6 +46,8 @@ def parse():
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-sample", type=int, default=256, help="tokens per CPU-baseline sample")
+    ap.add_argument("--tokens", type=int, default=16384, help="chunk size (profiling runs use smaller chunks)")
+    ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end pass (profiling)")
     return ap.parse_args()
 
 
@@ -201,7 +203,7 @@ def run_b200(args, rank, world, local_rank):
         import torch.distributed as dist
 
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
-    cfg = synth.CONFIGS[2]
+    cfg = dict(synth.CONFIGS[2], tokens=args.tokens)
     L = synth.make_layer(args.seed + rank, **cfg)
     T, K, N = L.x.shape[0], cfg["hidden"], cfg["inter"]
     x = L.x.to(dev)
@@ -267,37 +269,40 @@ def run_b200(args, rank, world, local_rank):
     assert Nt.workspace_status(ws) == Nt.KT_DEV_OK
 
     # end to end through the public API: pinned host inputs in, host output back, every step
-    x_h = L.x.pin_memory()
-    ids_h = L.topk_ids.pin_memory()
-    w_h = L.topk_weights.pin_memory()
-    out_h = torch.empty((T, K), dtype=torch.bfloat16).pin_memory()
+    e2e = None
+    if not args.no_e2e:
+        x_h = L.x.pin_memory()
+        ids_h = L.topk_ids.pin_memory()
+        w_h = L.topk_weights.pin_memory()
+        out_h = torch.empty((T, K), dtype=torch.bfloat16).pin_memory()
 
-    def e2e_step():
-        xd = x_h.to(dev, non_blocking=True)
-        idd = ids_h.to(dev, non_blocking=True)
-        wd = w_h.to(dev, non_blocking=True)
-        o = M.moe_prefill(xd, w13, w2, idd, wd, L.type13, L.type2, N, workspace=ws)
-        out_h.copy_(o, non_blocking=True)
+        def e2e_step():
+            xd = x_h.to(dev, non_blocking=True)
+            idd = ids_h.to(dev, non_blocking=True)
+            wd = w_h.to(dev, non_blocking=True)
+            o = M.moe_prefill(xd, w13, w2, idd, wd, L.type13, L.type2, N, workspace=ws)
+            out_h.copy_(o, non_blocking=True)
 
-    for _ in range(3):
-        e2e_step()
-    torch.cuda.synchronize()
-    e_steps = max(5, args.steps // 4)
-    if dist:
-        dist.barrier()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for _ in range(e_steps):
-        e2e_step()
-    e1.record(stream)
-    torch.cuda.synchronize()
-    e_ms = e0.elapsed_time(e1)
-    if dist:
-        m = torch.tensor([e_ms], device=dev)
-        dist.all_reduce(m, op=dist.ReduceOp.MAX)
-        e_ms = float(m.item())
-    h2d = x_h.numel() * 2 + ids_h.numel() * 4 + w_h.numel() * 4
-    d2h = out_h.numel() * 2
+        for _ in range(3):
+            e2e_step()
+        torch.cuda.synchronize()
+        e_steps = max(5, args.steps // 4)
+        if dist:
+            dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(e_steps):
+            e2e_step()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        e_ms = e0.elapsed_time(e1)
+        if dist:
+            m = torch.tensor([e_ms], device=dev)
+            dist.all_reduce(m, op=dist.ReduceOp.MAX)
+            e_ms = float(m.item())
+        e2e = {"value": world * T * e_steps / (e_ms * 1e-3), "unit": "tokens/s",
+               "h2d_bytes_per_step": x_h.numel() * 2 + ids_h.numel() * 4 + w_h.numel() * 4,
+               "d2h_bytes_per_step": out_h.numel() * 2}
 
     if rank == 0:
         hbm, tf_burst, tf_sust, peak_kind = load_peaks()
@@ -331,8 +336,7 @@ def run_b200(args, rank, world, local_rank):
                          "down_gemm_tflops": flops_down / (stage_ms[2] * 1e-3) / 1e12,
                          "layer_tflops": (flops_gate_up + flops_down) * args.steps / (ms * 1e-3) / 1e12},
             "cpu_baseline": cpu,
-            "e2e": {"value": world * T * e_steps / (e_ms * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
-                    "d2h_bytes_per_step": d2h},
+            "e2e": e2e,
             "gpu_launches": 6 * args.steps,
             "clocks": clocks,
         }

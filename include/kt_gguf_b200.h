@@ -148,8 +148,9 @@ int kt_moe_prefill_workspace_layout(int64_t tokens, int64_t top_k, int64_t hidde
  *   out[t] = sum_k w[t,k] * W2[s] (silu(W13g[s] x_t) * W13u[s] x_t),  s = topk_ids[t, k]
  * with bf16 activations x/out [tokens, hidden], fp32 topk_weights, slot ids as above.
  * The expert GEMMs run on tcgen05 with the GGUF weights dequantized in shared memory to
- * bf16 (fp32 accumulation); H and the per-route outputs are rounded to bf16 and combined
- * with the reference combine's rounding (hot/kt_gguf_hot.py:43-71). Replaces the hot
+ * bf16 (fp32 accumulation); H and the per-route outputs are rounded to bf16, and the
+ * weighted sum over k is accumulated in fp32 with the fp32 router weights and rounded once
+ * (the finalize of the fused MoE the reference's streamed prefill uses). Replaces the hot
  * method's apply (hot/kt_gguf_hot.py:240-304) at prefill sizes and the streamer's
  * dequant + cutlass_fused_moe group body. hidden % 256 == 0, inter % 256 == 0. */
 int kt_moe_prefill(const void* x, int64_t tokens, int64_t hidden, int64_t inter, const int32_t* topk_ids,

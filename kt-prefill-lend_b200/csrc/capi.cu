@@ -2,7 +2,7 @@
 // carving, and the launch sequences of the decode GEMV and the prefill layer.
 #include <string.h>
 
-#include "../../include/kt_gguf_b200.h"
+#include "kt_gguf_b200.h"
 #include "kt_common.cuh"
 #include "kt_kernels.h"
 
@@ -288,11 +288,12 @@ KT_EXPORT int kt_moe_prefill_timed(const void* x, int64_t tokens, int64_t hidden
   if (rc) return launch_rc(rc);
   mark(0);
   const int grid = num_sms();
-  rc = kt_launch_gemm_gate_up(type13, x, tokens, (int)hidden, (int)inter, w13, w_is_table, p.tiles, p.n_tiles,
+  rc = kt_launch_gemm_gate_up(type13, x, tokens, (int)hidden, (int)inter, w13, w_is_table, n_slots, p.tiles, p.n_tiles,
                               p.sorted_token, p.h, p.status, grid, s);
   if (rc) return launch_rc(rc);
   mark(1);
-  rc = kt_launch_gemm_down(type2, p.h, R, (int)hidden, (int)inter, w2, w_is_table, p.tiles, p.n_tiles, p.y, p.status,
+  rc = kt_launch_gemm_down(type2, p.h, R, (int)hidden, (int)inter, w2, w_is_table, n_slots, p.tiles, p.n_tiles, p.y,
+                           p.status,
                            grid, s);
   if (rc) return launch_rc(rc);
   mark(2);

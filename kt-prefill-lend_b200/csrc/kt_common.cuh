@@ -131,6 +131,51 @@ __device__ __forceinline__ bool kt_mbar_wait(uint64_t* bar, uint32_t parity, int
   return false;
 }
 
+// ------------------------------------------------------------------ clusters (CTA pairs)
+
+__device__ __forceinline__ uint32_t kt_cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// shared::cluster address of the same shared variable in CTA `rank` of the cluster
+__device__ __forceinline__ uint32_t kt_mapa(const void* p, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(kt_smem_addr(p)), "r"(rank));
+  return r;
+}
+// arrive (release, cluster scope) on an mbarrier given by its shared::cluster address
+__device__ __forceinline__ void kt_mbar_arrive_cluster(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+__device__ __forceinline__ bool kt_mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(kt_smem_addr(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// bounded wait with cluster-scope acquire, for barriers that receive arrivals from the peer CTA
+__device__ __forceinline__ bool kt_mbar_wait_cluster(uint64_t* bar, uint32_t parity, int* status, volatile int* abort) {
+  if (kt_mbar_try_wait_cluster(bar, parity)) return true;
+  const uint64_t t0 = kt_globaltimer_ns();
+  for (uint32_t i = 1;; ++i) {
+    if (kt_mbar_try_wait_cluster(bar, parity)) return true;
+    if (abort && *abort) return false;
+    if ((i & 255) == 0 && kt_globaltimer_ns() - t0 > KT_WAIT_NS) break;
+  }
+  if (status) atomicExch(status, KT_DEV_TIMEOUT);
+  if (abort) *abort = 1;
+  return false;
+}
+__device__ __forceinline__ void kt_cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
 // ------------------------------------------------------------------ bulk / tensor copies
 
 __device__ __forceinline__ void kt_bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
@@ -158,9 +203,45 @@ __device__ __forceinline__ void kt_tma_gather4(void* dst, const CUtensorMap* map
       : "memory");
 }
 
+// 16-byte global -> shared copy through L2 (cp.async.cg); completion is tracked by
+// kt_cp_async_arrive on an mbarrier
+__device__ __forceinline__ void kt_cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(kt_smem_addr(dst)), "l"(src) : "memory");
+}
+// arrive on the mbarrier once all of this thread's earlier cp.async copies have landed; the
+// arrival counts against the barrier's expected count (noinc)
+__device__ __forceinline__ void kt_cp_async_arrive(uint64_t* bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(kt_smem_addr(bar)) : "memory");
+}
+
 __device__ __forceinline__ void kt_fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
 // ------------------------------------------------------------------ tcgen05
+
+// CTA-pair (cta_group::2) forms: allocation and release are executed by the same warp of
+// both CTAs; MMAs are issued by the even CTA and read A and B halves from both CTAs' shared
+// memory; commits arrive on the barrier at the same offset in every CTA of `mask`.
+__device__ __forceinline__ void kt_tmem_alloc2(uint32_t* dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(kt_smem_addr(dst_smem)), "r"(ncols));
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;");
+}
+__device__ __forceinline__ void kt_tmem_dealloc2(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols));
+}
+__device__ __forceinline__ void kt_mma2_bf16_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                                uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate));
+}
+__device__ __forceinline__ void kt_mma2_commit_mc(uint64_t* bar, uint16_t mask) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+                   kt_smem_addr(bar)),
+               "h"(mask)
+               : "memory");
+}
 
 __device__ __forceinline__ void kt_tmem_alloc(uint32_t* dst_smem, uint32_t ncols) {
   asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(kt_smem_addr(dst_smem)), "r"(ncols));

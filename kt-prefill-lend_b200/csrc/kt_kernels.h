@@ -7,6 +7,8 @@
 struct KtGemmArgs {
   const uint8_t* w;             // slot base (plain layout) or int64 table of per-slot addresses
   int table;
+  int raw_group;                // rows per raw tensor-map row (1, 2, 4, 8); 0: per-row bulk copies
+  const uint16_t* x;            // phase 1: bf16 activations [T, K], gathered by sorted_token
   int64_t row_bytes;            // bytes of one GGUF weight row
   int K;                        // reduction length of this phase
   int N;                        // expert intermediate size
@@ -45,9 +47,10 @@ int kt_launch_permute(const int32_t* ids, int64_t routes, int top_k, int n_slots
                       int32_t* cursor, int32_t* tiles, int32_t* n_tiles, int32_t* sorted_token, int32_t* route_pos,
                       cudaStream_t s);
 
-int kt_launch_gemm_gate_up(int type, const void* x, int64_t T, int K, int N, const void* w13, int table,
+int kt_launch_gemm_gate_up(int type, const void* x, int64_t T, int K, int N, const void* w13, int table, int n_slots,
                            const int32_t* tiles, const int32_t* n_tiles, const int32_t* sorted_token, void* h,
                            int* status, int grid, cudaStream_t s);
-int kt_launch_gemm_down(int type, const void* h, int64_t R, int K, int N, const void* w2, int table, const int32_t* tiles,
+int kt_launch_gemm_down(int type, const void* h, int64_t R, int K, int N, const void* w2, int table, int n_slots,
+                        const int32_t* tiles,
                         const int32_t* n_tiles, void* y, int* status, int grid, cudaStream_t s);
 int kt_gemm_tile_tokens();

@@ -1,68 +1,79 @@
 // moe_gemm.cu — prefill path: persistent, warp-specialised tcgen05 grouped GEMM over the
-// hot experts with in-kernel GGUF dequantization.
+// hot experts with in-kernel GGUF dequantization, on CTA pairs (cta_group::2).
 //
 // Replaces the reference's streamed-prefill pair "dequant experts to bf16 in HBM (Triton),
 // then FlashInfer's bf16 CUTLASS fused MoE" (trees/flash-next-gguf patch, kt_stream_prefill_gguf
 // _group_body; kt_gguf_dequant.py) and, at prefill sizes, the per-route GEMV build of
 // kt_moe_a8_vec_multi (hot/kt_gguf_moe_multi/kt_gguf_moe_multi.cu:653). Weights stay in their
-// GGUF bytes in HBM; each tile's raw super-blocks are copied into shared memory by the bulk
-// copy engine and dequantized there to bf16, so HBM sees 4.5-6.6 bits per weight instead of a
-// bf16 round trip.
+// GGUF bytes in HBM; each tile's raw super-blocks are copied into shared memory by TMA and
+// dequantized there to bf16, so HBM sees 4.5-6.6 bits per weight instead of a bf16 round trip.
 //
 // Problem, per expert slot e with M_e routed tokens (sorted by slot):
 //   phase 1: H[M_e, N]  = silu(X_e W_gate^T) * (X_e W_up^T)    (W13 rows [gate; up], K = hidden)
 //   phase 2: Y[M_e, K]  = H W_down^T                             (W2 [K, N])
-// Swap-AB: the MMA's M dimension is weight rows (two 128-row halves per tile, sharing the
-// token operand), its N dimension is tokens (up to 256 per tile), reduction along K.
+// Swap-AB: the MMA's M dimension is weight rows, N is tokens, reduction along K. A cluster of
+// two CTAs (two SMs) computes one 256-row x 256-token tile with M=256 tcgen05 MMAs: each CTA
+// holds 128 of the weight rows (A) and 128 of the tokens (B) in its shared memory and gets the
+// accumulator of its 128 rows x 256 tokens in its own TMEM. Phase 1 gives each CTA 64 gate
+// rows and the matching 64 up rows, so SwiGLU needs no data from the peer.
 //
-// Warp roles (480 threads):
-//   warps 0-7   dequant producers: thread r owns A row r of the tile; per 64-wide k-step it
-//               decodes 64 values from the raw stage and writes them as bf16 into the A stage
-//               in the UMMA K-major 128-byte swizzle layout
-//   warp 8      raw loader: per 256-value super-block column, one 1-D bulk copy per row of the
-//               16-byte aligned span holding that row's block (cp.async.bulk, no multicast)
-//   warp 9      B loader: phase 1 gathers token rows of X with TMA tile::gather4 (4 rows per
-//               instruction); phase 2 loads H rows with a 2-D TMA tile (rows are contiguous)
-//   warp 10     MMA issuer: tcgen05.mma kind::f16 (bf16 x bf16 -> fp32 in TMEM), commits
-//   warps 11-14 epilogue: tcgen05.ld of the accumulators; phase 1 applies SwiGLU and writes H
-//               (bf16), phase 2 writes Y (bf16); both transposed through shared memory
-// TMEM: 512 columns = two fp32 accumulators of up to 256 columns (gate/up, or the two
-// 128-row halves of the down tile).
+// Warp roles per CTA (480 threads):
+//   warps 0-7   dequant producers: two threads per A row, 32 values each per 64-wide k-step,
+//               decoded from the raw stage and written as bf16 into the A stage in the UMMA
+//               K-major 128-byte swizzle layout
+//   warp 8      raw loader: per 256-value super-block column, 2G 2-D TMA loads of a tensor map
+//               that views G consecutive weight rows as one (G = rows whose bytes make a
+//               16-byte multiple); slot tables fall back to one 1-D bulk copy per row
+//   warp 9      B loader: phase 1 gathers this CTA's token rows of X with 16-byte cp.async
+//               copies into the swizzled stage; phase 2 loads H rows with one 2-D TMA per k-step
+//   warp 10     even CTA: MMA issuer (tcgen05.mma.cta_group::2, commits multicast to both CTAs);
+//               odd CTA: forwards its B-stage completions to the even CTA's barrier
+//   warps 11-14 epilogue: tcgen05.ld of the accumulator; phase 1 SwiGLU -> H (bf16), phase 2
+//               -> Y (bf16)
+// TMEM (per CTA): two 256-column fp32 accumulators, so the epilogue of one tile overlaps the
+// MMAs of the next. No TMA or bulk copy uses .multicast::cluster.
+#include <string.h>
+
 #include "gguf_dot.cuh"
+#include "gguf_tile.cuh"
 #include "kt_kernels.h"
 
 namespace {
 
-constexpr int kProducers = 256;
 constexpr int kThreads = 480;
 constexpr int kWarpRaw = 8, kWarpB = 9, kWarpMma = 10, kWarpEpi0 = 11;
-constexpr int kTN = 256;           // tokens per tile (MMA N), at most
-constexpr int kStages = 2;         // A/B stages
-constexpr int kAStageBytes = 256 * 128;
-constexpr int kBStageBytes = kTN * 128;
-constexpr int kFixedSmem = 2 * kStages * 128 * 256 /* A and B */ + 4 * 32 * 32 * 2 /* epilogue transpose */ +
-                           2048 /* grid */ + 512 /* barriers */ + 1024 /* alignment slack */;
+constexpr int kTN = 256;           // tokens per tile (MMA N, split between the pair)
+constexpr int kHalfN = kTN / 2;    // B rows held by each CTA
+constexpr int kStages = 4;         // A/B stages
+constexpr int kAStageBytes = 128 * 128;
+constexpr int kBStageBytes = kHalfN * 128;
+constexpr int kXchgBytes = 2 * 32 * 32 * 4;  // phase-1 epilogue: up values for the gate warps
+constexpr int kEpiBytes = 4 * 32 * 32 * 2;   // per-warp transpose buffers
+constexpr int kFixedSmem = kStages * (kAStageBytes + kBStageBytes) + kXchgBytes + kEpiBytes + 2048 /* grid */ +
+                           1024 /* barriers */ + kHalfN * 4 /* token ids */ + 1024 /* alignment slack */;
 
 // Raw staging: a "unit" is UV consecutive values of one weight row (a 256-value super-block,
-// or four 32-value Q8_0 blocks); a raw stage holds one unit for one half (128 rows) of the
-// tile. Each row's slot holds the 16-byte aligned span around its unit (bulk copies need
-// 16-byte aligned addresses and sizes; GGUF blocks are only 2-byte aligned).
+// or four 32-value Q8_0 blocks); a raw stage holds one unit for the CTA's 128 rows. Each
+// row's slot holds the 16-byte aligned span around its unit (TMA needs 16-byte aligned
+// addresses and sizes; GGUF blocks are only 2-byte aligned).
 template <int TYPE>
 struct Raw {
   static constexpr int UV = TYPE == KT_Q8_0 ? 128 : 256;
   static constexpr int UNIT_BYTES = TYPE == KT_Q8_0 ? 4 * 34 : kt_block_info(TYPE).bytes;
-  static constexpr int SLOT = (UNIT_BYTES + 14 + 15) / 16 * 16;  // unit starts at an even offset <= 14
-  static constexpr int STAGE_BYTES = 128 * SLOT;
-  static constexpr int NRAW_FIT = (227 * 1024 - kFixedSmem) / STAGE_BYTES;
-  static constexpr int NRAW = NRAW_FIT > 4 ? 4 : NRAW_FIT;  // ring of half-tile stages
-  static constexpr int KPU = UV / 64;                        // k-steps per unit
-  static_assert(NRAW >= 3, "raw ring too small");
-};
-
-struct Smem {
-  static constexpr int A = 0;
-  static constexpr int B = A + kStages * kAStageBytes;
-  static constexpr int RAW = B + kStages * kBStageBytes;
+  static constexpr int SPAN = (UNIT_BYTES + 14 + 15) / 16 * 16;  // the unit starts at an even offset <= 14
+  static constexpr int AVAIL = 227 * 1024 - kFixedSmem;
+  // an odd number of 16-byte chunks per slot keeps 16-byte loads of 8 consecutive rows on
+  // distinct bank groups; taken when three stages still fit
+  static constexpr int SLOT = ((SPAN / 16) % 2 == 0 && 2 * 128 * (SPAN + 16) + 2048 <= AVAIL) ? SPAN + 16 : SPAN;
+  // a stage = two 64-row segments (gate / up rows in phase 1); a segment = G sub-tiles of
+  // 64/G rows, one per TMA load, each starting on a 128-byte boundary (TMA destinations
+  // must); producer thread l reads slot l%64 of its segment in this order
+  static constexpr int SEG_BYTES = 64 * SLOT + 1024;
+  static constexpr int STAGE_BYTES = 2 * SEG_BYTES;
+  static constexpr int NRAW_FIT = AVAIL / STAGE_BYTES;
+  static constexpr int NRAW = NRAW_FIT > 4 ? 4 : NRAW_FIT;
+  static constexpr int KPU = UV / 64;  // k-steps per unit
+  static_assert(NRAW >= 2, "raw ring too small");
 };
 
 template <int TYPE>
@@ -70,52 +81,81 @@ constexpr int smem_bytes() {
   return kFixedSmem + Raw<TYPE>::NRAW * Raw<TYPE>::STAGE_BYTES;
 }
 
-// 32 values (sub-unit `sub` of 8) of one row's raw unit -> fp32
-template <int TYPE>
-__device__ __forceinline__ void dq_unit(const uint8_t* unit, int sub, float* y, const uint32_t* grid) {
-  if constexpr (TYPE == KT_Q8_0) kt_dq32_q8_0(unit + 34 * sub, y);
-  if constexpr (TYPE == KT_Q4_K) kt_dq32_q4_k(unit, sub, y);
-  if constexpr (TYPE == KT_Q6_K) kt_dq32_q6_k(unit, sub, y);
-  if constexpr (TYPE == KT_IQ3_S) kt_dq32_iq3_s(unit, sub, y, grid);
+// silu(x) = x * sigmoid(x), sigmoid(x) = 0.5 + 0.5 * tanh(x / 2): one hardware tanh
+// (tanh.approx.f32, about 2^-11 relative error) per value; the result is rounded to bf16
+__device__ __forceinline__ float kt_tanh_approx(float x) {
+  float y;
+  asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
 }
+__device__ __forceinline__ float silu(float x) { return x * fmaf(0.5f, kt_tanh_approx(0.5f * x), 0.5f); }
 
-__device__ __forceinline__ float silu(float x) { return x / (1.0f + __expf(-x)); }
+__device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+
+// raw sub-tile pitch: 64/G slots rounded up to a 128-byte boundary
+template <int TYPE>
+__device__ __forceinline__ int sub_pitch(int G) {
+  return ((64 / G) * Raw<TYPE>::SLOT + 127) & ~127;
+}
+// weight row (within a 64-row segment) held by slot position rr when the G sub-tiles hold
+// rows j, j+G, j+2G, ...
+__device__ __forceinline__ int wrow(int rr, int G) { return (rr % (64 / G)) * G + rr / (64 / G); }
+
+// global row (within a slot) of A row `rh` of this CTA in weight tile `wt`
+template <int PHASE>
+__device__ __forceinline__ int64_t a_row(int rh, int wt, uint32_t cr, int N) {
+  if constexpr (PHASE == 1)
+    return rh < 64 ? (int64_t)wt * 128 + 64 * cr + rh : (int64_t)N + (int64_t)wt * 128 + 64 * cr + (rh - 64);
+  return (int64_t)wt * 256 + 128 * cr + rh;
+}
 
 }  // namespace
 
 template <int TYPE, int PHASE>
-__global__ void __launch_bounds__(kThreads, 1) kt_moe_gemm_kernel(const __grid_constant__ CUtensorMap bmap, const KtGemmArgs a) {
+__global__ void __launch_bounds__(kThreads, 1) kt_moe_gemm_kernel(const __grid_constant__ CUtensorMap bmap,
+                                                                  const __grid_constant__ CUtensorMap wmap,
+                                                                  const KtGemmArgs a) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   using R = Raw<TYPE>;
-  uint8_t* sA = smem + Smem::A;
-  uint8_t* sB = smem + Smem::B;
-  uint8_t* sRaw = smem + Smem::RAW;
-  uint16_t* sEpi = reinterpret_cast<uint16_t*>(sRaw + R::NRAW * R::STAGE_BYTES);
-  uint32_t* sGrid = reinterpret_cast<uint32_t*>(sEpi + 4 * 32 * 32);
+  uint8_t* sA = smem;
+  uint8_t* sB = sA + kStages * kAStageBytes;
+  uint8_t* sRaw = sB + kStages * kBStageBytes;
+  float* sX = reinterpret_cast<float*>(sRaw + R::NRAW * R::STAGE_BYTES);
+  uint16_t* sEpi = reinterpret_cast<uint16_t*>(reinterpret_cast<uint8_t*>(sX) + kXchgBytes);
+  uint32_t* sGrid = reinterpret_cast<uint32_t*>(reinterpret_cast<uint8_t*>(sEpi) + kEpiBytes);
   uint64_t* bars = reinterpret_cast<uint64_t*>(sGrid + 512);
-  uint64_t* full_ab = bars;                      // [kStages]
-  uint64_t* empty_ab = bars + kStages;           // [kStages]
-  uint64_t* raw_full = bars + 2 * kStages;       // [NRAW]
-  uint64_t* raw_empty = raw_full + R::NRAW;      // [NRAW]
-  uint64_t* acc_full = raw_empty + R::NRAW;
-  uint64_t* acc_empty = acc_full + 1;
-  uint64_t* done_bar = acc_empty + 1;
+  uint64_t* full = bars;                 // [kStages] even CTA: A and B of both CTAs landed
+  uint64_t* empty = full + kStages;      // [kStages] both CTAs: MMAs of the stage done
+  uint64_t* bfull = empty + kStages;     // [kStages] odd CTA: its A and B of the stage landed
+  uint64_t* raw_full = bfull + kStages;  // [NRAW]
+  uint64_t* raw_empty = raw_full + R::NRAW;
+  uint64_t* acc_full = raw_empty + R::NRAW;  // [2]
+  uint64_t* acc_empty = acc_full + 2;        // [2] even CTA
+  uint64_t* done_bar = acc_empty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done_bar + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  int32_t* sTok = reinterpret_cast<int32_t*>(bars + 64);  // [kHalfN]
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const uint32_t cr = kt_cluster_rank();
+  const bool leader = cr == 0;
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
-      kt_mbar_init(&full_ab[s], kProducers + 1);
-      kt_mbar_init(&empty_ab[s], 1);
+      // even CTA: its 8 producer warps, its B copies, and one forwarded arrival for the odd
+      // CTA's producers and B copies (which arrive on the odd CTA's bfull)
+      kt_mbar_init(&full[s], 8 + (PHASE == 1 ? 32 : 1) + 1);
+      kt_mbar_init(&empty[s], 1);
+      kt_mbar_init(&bfull[s], 8 + (PHASE == 1 ? 32 : 1));
     }
     for (int s = 0; s < R::NRAW; ++s) {
       kt_mbar_init(&raw_full[s], 1);
-      kt_mbar_init(&raw_empty[s], 128);
+      kt_mbar_init(&raw_empty[s], 256);
     }
-    kt_mbar_init(acc_full, 1);
-    kt_mbar_init(acc_empty, 128);
+    for (int b = 0; b < 2; ++b) {
+      kt_mbar_init(&acc_full[b], 1);
+      kt_mbar_init(&acc_empty[b], 8);
+    }
     kt_mbar_init(done_bar, 1);
     *abort_flag = 0;
     kt_fence_mbar_init();
@@ -123,7 +163,8 @@ __global__ void __launch_bounds__(kThreads, 1) kt_moe_gemm_kernel(const __grid_c
   if constexpr (TYPE == KT_IQ3_S) {
     for (int i = threadIdx.x; i < 512; i += blockDim.x) sGrid[i] = kt_iq3s_grid_dev[i];
   }
-  if (warp == kWarpMma) kt_tmem_alloc(tmem_slot, 512);
+  kt_cluster_sync();  // the peer's barriers are initialised before any remote arrival
+  if (warp == kWarpMma) kt_tmem_alloc2(tmem_slot, 512);
   kt_tc_fence_before();
   __syncthreads();
   kt_tc_fence_after();
@@ -134,221 +175,258 @@ __global__ void __launch_bounds__(kThreads, 1) kt_moe_gemm_kernel(const __grid_c
   const int n_items = n_tiles * n_wt;
   const int ksteps = a.K / 64;
   const int units = a.K / R::UV;
+  const int first_item = blockIdx.x >> 1, item_stride = gridDim.x >> 1;
+  const int64_t rows_total = PHASE == 1 ? 2 * (int64_t)a.N : (int64_t)a.K_out;
 
   if (warp < 8) {
     // ---------------------------------------------------------------- dequant producers
-    const int r = threadIdx.x;  // A row in the tile
+    // thread -> A row rh (= TMEM lane) -> raw slot in load order: the G sub-tiles of a
+    // segment hold weight rows j, j+G, ...; lane rh holds weight row seg*64 + wrow(rh)
+    const int rh = threadIdx.x & 127, hf = threadIdx.x >> 7;
+    const int G = a.raw_group > 0 ? a.raw_group : 1;
+    const int seg = rh >> 6, rr = rh & 63;
+    const int slot_off = seg * R::SEG_BYTES + (rr / (64 / G)) * sub_pitch<TYPE>(G) + (rr % (64 / G)) * R::SLOT;
+    const int wr = seg * 64 + wrow(rr, G);
+    uint64_t* stage_bar = leader ? full : bfull;  // local; the odd CTA's warp 10 forwards
     uint32_t kit = 0, uit = 0;
-    for (int item = blockIdx.x; item < n_items && !*abort_flag; item += gridDim.x) {
+    for (int item = first_item; item < n_items && !*abort_flag; item += item_stride) {
       const int tile = item / n_wt, wt = item % n_wt;
       const int slot = a.tiles[3 * tile + 0];
-      const int64_t grow = PHASE == 1 ? (r < 128 ? (int64_t)wt * 128 + r : (int64_t)a.N + (int64_t)wt * 128 + (r - 128))
-                                      : (int64_t)wt * 256 + r;
-      const int64_t rows_total = PHASE == 1 ? 2 * (int64_t)a.N : (int64_t)a.K_out;
       const uint8_t* wbase = a.table ? reinterpret_cast<const uint8_t*>(reinterpret_cast<const int64_t*>(a.w)[slot])
                                      : a.w + (int64_t)slot * rows_total * a.row_bytes;
-      const uint8_t* grow_ptr = wbase + grow * a.row_bytes;
-      const int hh = r / 128, rh = r % 128;  // tile half and row within it
+      const uint8_t* grow_ptr = wbase + a_row<PHASE>(wr, wt, cr, a.N) * a.row_bytes;
       for (int u = 0; u < units && !*abort_flag; ++u, ++uit) {
-        const uint32_t hit = 2 * uit + hh;
-        const int su = hit % R::NRAW;
-        if (!kt_mbar_wait(&raw_full[su], (hit / R::NRAW) & 1, a.status, abort_flag)) break;
+        const int su = uit % R::NRAW;
+        if (!kt_mbar_wait(&raw_full[su], (uit / R::NRAW) & 1, a.status, abort_flag)) break;
         // the loader copied the 16-byte aligned span around this row's unit into the row's
         // slot; the unit starts at the alignment remainder of its global address
-        const uintptr_t gaddr = (uintptr_t)(grow_ptr + (int64_t)u * R::UNIT_BYTES);
-        const uint8_t* rowp = sRaw + su * R::STAGE_BYTES + rh * R::SLOT + (gaddr & 15);
-        for (int kk = 0; kk < R::KPU && !*abort_flag; ++kk, ++kit) {
-          const int s = kit % kStages;
-          if (!kt_mbar_wait(&empty_ab[s], ((kit / kStages) & 1) ^ 1, a.status, abort_flag)) break;
-          uint8_t* arow = sA + s * kAStageBytes;
+        const int off = (int)(((uintptr_t)(grow_ptr + (int64_t)u * R::UNIT_BYTES)) & 15);
+        const uint8_t* slotp = sRaw + su * R::STAGE_BYTES + slot_off;
+        KtTileDq<TYPE> dq;
+        dq.unit(slotp, off);
+        bool ok = true;
 #pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            float v[32];
-            dq_unit<TYPE>(rowp, 2 * kk + h, v, sGrid);
+        for (int kk = 0; kk < R::KPU; ++kk) {
+          const int s = (kit + kk) % kStages;
+          if (ok && !kt_mbar_wait(&empty[s], (((kit + kk) / kStages) & 1) ^ 1, a.status, abort_flag)) ok = false;
+          if (ok) {
+            uint32_t pk[16];
+            dq.kstep_half(slotp, off, kk, hf, pk, sGrid);
+            uint8_t* arow = sA + s * kAStageBytes;
 #pragma unroll
-            for (int c = 0; c < 4; ++c) {
-              uint4 q;
-              q.x = kt_pack_bf2(v[8 * c + 0], v[8 * c + 1]);
-              q.y = kt_pack_bf2(v[8 * c + 2], v[8 * c + 3]);
-              q.z = kt_pack_bf2(v[8 * c + 4], v[8 * c + 5]);
-              q.w = kt_pack_bf2(v[8 * c + 6], v[8 * c + 7]);
-              *reinterpret_cast<uint4*>(arow + kt_swz128(r, 32 * h + 8 * c)) = q;
-            }
+            for (int c = 0; c < 4; ++c)
+              *reinterpret_cast<uint4*>(arow + kt_swz128(rh, 32 * hf + 8 * c)) =
+                  make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
+            kt_fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) kt_mbar_arrive(&stage_bar[s]);
           }
-          kt_fence_proxy_async_smem();
-          kt_mbar_arrive(&full_ab[s]);
         }
+        kit += R::KPU;
+        if (!ok) break;
         kt_mbar_arrive(&raw_empty[su]);
       }
     }
   } else if (warp == kWarpRaw) {
     // ---------------------------------------------------------------- raw loader
     uint32_t uit = 0;
-    for (int item = blockIdx.x; item < n_items && !*abort_flag; item += gridDim.x) {
+    for (int item = first_item; item < n_items && !*abort_flag; item += item_stride) {
       const int tile = item / n_wt, wt = item % n_wt;
       const int slot = a.tiles[3 * tile + 0];
-      const int64_t rows_total = PHASE == 1 ? 2 * (int64_t)a.N : (int64_t)a.K_out;
       const uint8_t* wbase = a.table ? reinterpret_cast<const uint8_t*>(reinterpret_cast<const int64_t*>(a.w)[slot])
                                      : a.w + (int64_t)slot * rows_total * a.row_bytes;
       for (int u = 0; u < units && !*abort_flag; ++u, ++uit) {
-        for (int hh = 0; hh < 2 && !*abort_flag; ++hh) {
-          const uint32_t hit = 2 * uit + hh;
-          const int su = hit % R::NRAW;
-          if (!kt_mbar_wait(&raw_empty[su], ((hit / R::NRAW) & 1) ^ 1, a.status, abort_flag)) break;
-          uintptr_t src[4];
-          uint32_t len[4], total = 0;
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const int r = hh * 128 + lane + 32 * i;
-            const int64_t grow = PHASE == 1 ? (r < 128 ? (int64_t)wt * 128 + r : (int64_t)a.N + (int64_t)wt * 128 + (r - 128))
-                                            : (int64_t)wt * 256 + r;
-            const uintptr_t g = (uintptr_t)(wbase + grow * a.row_bytes + (int64_t)u * R::UNIT_BYTES);
-            src[i] = g & ~(uintptr_t)15;
-            len[i] = (uint32_t)(((g + R::UNIT_BYTES + 15) & ~(uintptr_t)15) - src[i]);
-            total += len[i];
+        const int su = uit % R::NRAW;
+        if (!kt_mbar_wait(&raw_empty[su], ((uit / R::NRAW) & 1) ^ 1, a.status, abort_flag)) break;
+        uint8_t* stage = sRaw + su * R::STAGE_BYTES;
+        if (a.raw_group > 0) {
+          // per 64-row segment, G loads: sub-tile j holds rows j, j+G, ... (group rows)
+          if (lane == 0) {
+            const int G = a.raw_group;
+            kt_mbar_arrive_expect_tx(&raw_full[su], 128u * R::SLOT);
+            for (int sg = 0; sg < 2; ++sg) {
+              const int64_t first = (int64_t)slot * rows_total + a_row<PHASE>(64 * sg, wt, cr, a.N);
+              for (int j = 0; j < G; ++j) {
+                const int x = (int)(((int64_t)j * a.row_bytes + (int64_t)u * R::UNIT_BYTES) & ~(int64_t)15);
+                kt_tma_2d(stage + sg * R::SEG_BYTES + j * sub_pitch<TYPE>(G), &wmap, x, (int)(first / G),
+                          &raw_full[su]);
+              }
+            }
           }
-#pragma unroll
-          for (int m = 16; m > 0; m >>= 1) total += __shfl_xor_sync(0xffffffffu, total, m);
-          if (lane == 0) kt_mbar_arrive_expect_tx(&raw_full[su], total);
           __syncwarp();
-#pragma unroll
-          for (int i = 0; i < 4; ++i)
-            kt_bulk_g2s(sRaw + su * R::STAGE_BYTES + (lane + 32 * i) * R::SLOT, reinterpret_cast<const void*>(src[i]),
-                        len[i], &raw_full[su]);
+          continue;
         }
+        uintptr_t src[4];
+        uint32_t len[4], total = 0;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int rh = lane + 32 * i;
+          const uintptr_t g = (uintptr_t)(wbase + a_row<PHASE>(rh, wt, cr, a.N) * a.row_bytes + (int64_t)u * R::UNIT_BYTES);
+          src[i] = g & ~(uintptr_t)15;
+          len[i] = (uint32_t)(((g + R::UNIT_BYTES + 15) & ~(uintptr_t)15) - src[i]);
+          total += len[i];
+        }
+#pragma unroll
+        for (int m = 16; m > 0; m >>= 1) total += __shfl_xor_sync(0xffffffffu, total, m);
+        if (lane == 0) kt_mbar_arrive_expect_tx(&raw_full[su], total);
+        __syncwarp();
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          kt_bulk_g2s(stage + ((lane + 32 * i) >> 6) * R::SEG_BYTES + ((lane + 32 * i) & 63) * R::SLOT,
+                      reinterpret_cast<const void*>(src[i]), len[i], &raw_full[su]);
       }
     }
   } else if (warp == kWarpB) {
     // ---------------------------------------------------------------- B loader
     uint32_t kit = 0;
-    for (int item = blockIdx.x; item < n_items && !*abort_flag; item += gridDim.x) {
+    for (int item = first_item; item < n_items && !*abort_flag; item += item_stride) {
       const int tile = item / n_wt;
       const int pos0 = a.tiles[3 * tile + 1], ntok = a.tiles[3 * tile + 2];
-      const int nN = (ntok + 15) & ~15;
+      const int half = ((ntok + 31) & ~31) / 2;  // B rows of each CTA (the MMA N is 2*half)
+      const int b0 = cr * half;                  // first tile row held by this CTA
+      if constexpr (PHASE == 1) {
+        for (int j = lane; j < half; j += 32) sTok[j] = a.sorted_token[pos0 + (b0 + j < ntok ? b0 + j : 0)];
+        __syncwarp();
+      }
       for (int ks = 0; ks < ksteps && !*abort_flag; ++ks, ++kit) {
         const int s = kit % kStages;
-        if (!kt_mbar_wait(&empty_ab[s], ((kit / kStages) & 1) ^ 1, a.status, abort_flag)) break;
+        if (!kt_mbar_wait(&empty[s], ((kit / kStages) & 1) ^ 1, a.status, abort_flag)) break;
         uint8_t* dst = sB + s * kBStageBytes;
+        uint64_t* bar = leader ? &full[s] : &bfull[s];
         if constexpr (PHASE == 1) {
-          if (lane == 0) kt_mbar_arrive_expect_tx(&full_ab[s], (uint32_t)nN * 128);
-          __syncwarp();
-          for (int q = lane; q < nN / 4; q += 32) {
-            int rr[4];
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              const int row = 4 * q + j;
-              rr[j] = a.sorted_token[pos0 + (row < ntok ? row : 0)];
-            }
-            kt_tma_gather4(dst + q * 4 * 128, &bmap, ks * 64, rr[0], rr[1], rr[2], rr[3], &full_ab[s]);
-          }
+          // lane copies 16-byte chunk (lane % 8) of rows lane/8, lane/8 + 4, ...
+          const int c = lane & 7;
+          const uint16_t* xk = a.x + (int64_t)ks * 64 + 8 * c;
+          for (int j = lane >> 3; j < half; j += 4) kt_cp_async16(dst + kt_swz128(j, 8 * c), xk + (int64_t)sTok[j] * a.K);
+          kt_cp_async_arrive(bar);
         } else {
           if (lane == 0) {
-            kt_mbar_arrive_expect_tx(&full_ab[s], (uint32_t)kBStageBytes);
-            kt_tma_2d(dst, &bmap, ks * 64, pos0, &full_ab[s]);
+            kt_mbar_arrive_expect_tx(bar, (uint32_t)kBStageBytes);
+            kt_tma_2d(dst, &bmap, ks * 64, pos0 + b0, bar);
           }
         }
         __syncwarp();
       }
     }
   } else if (warp == kWarpMma) {
-    // ---------------------------------------------------------------- MMA issuer
-    uint32_t kit = 0, ait = 0;
-    for (int item = blockIdx.x; item < n_items && !*abort_flag; item += gridDim.x, ++ait) {
-      const int tile = item / n_wt;
-      const int ntok = a.tiles[3 * tile + 2];
-      const int nN = (ntok + 15) & ~15;
-      const uint32_t idesc = kt_idesc_bf16(128, nN);
-      if (!kt_mbar_wait(acc_empty, (ait & 1) ^ 1, a.status, abort_flag)) break;
-      kt_tc_fence_after();
-      for (int ks = 0; ks < ksteps && !*abort_flag; ++ks, ++kit) {
-        const int s = kit % kStages;
-        if (!kt_mbar_wait(&full_ab[s], (kit / kStages) & 1, a.status, abort_flag)) break;
+    if (leader) {
+      // -------------------------------------------------------------- MMA issuer (even CTA)
+      uint32_t kit = 0, iit = 0;
+      for (int item = first_item; item < n_items && !*abort_flag; item += item_stride, ++iit) {
+        const int tile = item / n_wt;
+        const int ntok = a.tiles[3 * tile + 2];
+        const int nN = (ntok + 31) & ~31;
+        const uint32_t idesc = kt_idesc_bf16(256, nN);
+        const int b = iit & 1;
+        if (!kt_mbar_wait_cluster(&acc_empty[b], ((iit >> 1) & 1) ^ 1, a.status, abort_flag)) break;
         kt_tc_fence_after();
-        if (lane == 0) {
-          const uint32_t a0 = kt_smem_addr(sA + s * kAStageBytes);
-          const uint32_t b0 = kt_smem_addr(sB + s * kBStageBytes);
+        const uint32_t d = tmem + 256 * b;
+        for (int ks = 0; ks < ksteps && !*abort_flag; ++ks, ++kit) {
+          const int s = kit % kStages;
+          if (!kt_mbar_wait_cluster(&full[s], (kit / kStages) & 1, a.status, abort_flag)) break;
+          kt_tc_fence_after();
+          if (lane == 0) {
+            const uint64_t da = kt_desc_k128(kt_smem_addr(sA + s * kAStageBytes));
+            const uint64_t db = kt_desc_k128(kt_smem_addr(sB + s * kBStageBytes));
 #pragma unroll
-          for (int kk = 0; kk < 4; ++kk) {
-            const uint64_t da0 = kt_desc_k128(a0) + 2 * kk;
-            const uint64_t da1 = kt_desc_k128(a0 + 128 * 128) + 2 * kk;
-            const uint64_t db = kt_desc_k128(b0) + 2 * kk;
-            const uint32_t acc = (ks | kk) != 0;
-            kt_mma_bf16_ss(tmem + 0, da0, db, idesc, acc);
-            kt_mma_bf16_ss(tmem + 256, da1, db, idesc, acc);
+            for (int kk = 0; kk < 4; ++kk) kt_mma2_bf16_ss(d, da + 2 * kk, db + 2 * kk, idesc, (ks | kk) != 0);
+            kt_mma2_commit_mc(&empty[s], 3);
           }
-          kt_mma_commit(&empty_ab[s]);
+          __syncwarp();
         }
+        if (lane == 0) kt_mma2_commit_mc(&acc_full[b], 3);
         __syncwarp();
       }
-      if (lane == 0) kt_mma_commit(acc_full);
+      if (lane == 0) kt_mma2_commit_mc(done_bar, 3);
       __syncwarp();
+    } else {
+      // -------------------------------------------------------------- stage forwarder (odd CTA):
+      // one cluster-scope arrival per stage once this CTA's A rows and B rows have landed
+      uint32_t kit = 0;
+      const uint32_t full0 = kt_mapa(&full[0], 0);
+      for (int item = first_item; item < n_items && !*abort_flag; item += item_stride) {
+        for (int ks = 0; ks < ksteps && !*abort_flag; ++ks, ++kit) {
+          const int s = kit % kStages;
+          if (!kt_mbar_wait(&bfull[s], (kit / kStages) & 1, a.status, abort_flag)) break;
+          if (lane == 0) kt_mbar_arrive_cluster(full0 + 8 * s);
+          __syncwarp();
+        }
+      }
     }
-    if (lane == 0) {
-      kt_mma_commit(done_bar);
-      kt_mbar_wait(done_bar, 0, a.status, nullptr);
-    }
-    __syncwarp();
+    kt_mbar_wait(done_bar, 0, a.status, nullptr);  // every MMA of the pair has completed
   } else {
     // ---------------------------------------------------------------- epilogue
     const int q = warp & 3;  // TMEM lane quadrant this warp may access
-    uint16_t* stg = sEpi + (warp - kWarpEpi0) * 32 * 32;
-    uint32_t ait = 0;
-    for (int item = blockIdx.x; item < n_items && !*abort_flag; item += gridDim.x, ++ait) {
+    const int G = a.raw_group > 0 ? a.raw_group : 1;
+    const int l = 32 * q + lane;                   // TMEM lane = A row of this CTA
+    const int wr = (l >> 6) * 64 + wrow(l & 63, G);  // weight row (feature) it holds
+    const uint32_t acc_empty0 = kt_mapa(&acc_empty[0], 0);
+    uint32_t iit = 0;
+    for (int item = first_item; item < n_items && !*abort_flag; item += item_stride, ++iit) {
       const int tile = item / n_wt, wt = item % n_wt;
       const int pos0 = a.tiles[3 * tile + 1], ntok = a.tiles[3 * tile + 2];
-      if (!kt_mbar_wait(acc_full, ait & 1, a.status, abort_flag)) break;
+      const int b = iit & 1;
+      if (!kt_mbar_wait(&acc_full[b], (iit >> 1) & 1, a.status, abort_flag)) break;
       kt_tc_fence_after();
-      const uint32_t lane_base = tmem + ((uint32_t)(32 * q) << 16);
+      const uint32_t lane_base = tmem + 256 * b + ((uint32_t)(32 * q) << 16);
       for (int c0 = 0; c0 < ntok; c0 += 32) {
+        uint32_t v[32];
+        kt_tmem_ld32(lane_base + c0, v);
+        kt_tmem_wait_ld();
         if constexpr (PHASE == 1) {
-          uint32_t g[32], u[32];
-          kt_tmem_ld32(lane_base + c0, g);
-          kt_tmem_ld32(lane_base + 256 + c0, u);
-          kt_tmem_wait_ld();
+          // lanes 0-63 hold gate rows, 64-127 the matching up rows: the up warps hand their
+          // values to the gate warps through shared memory; h is staged [token][feature]
+          float* xq = sX + (q & 1) * 32 * 32;
+          if (q >= 2) {
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const float gv = __uint_as_float(g[j]), uv = __uint_as_float(u[j]);
-            stg[j * 32 + lane] = kt_f2bf(silu(gv) * uv);
+            for (int j = 0; j < 32; ++j) xq[j * 32 + lane] = __uint_as_float(v[j]);
           }
-          __syncwarp();
-          const int tok = c0 + lane;
-          if (tok < ntok) {
-            uint16_t* dst = a.out + (int64_t)(pos0 + tok) * a.out_ld + (int64_t)wt * 128 + 32 * q;
-            const uint4* src = reinterpret_cast<const uint4*>(stg + lane * 32);
+          epi_bar();
+          if (q < 2) {
 #pragma unroll
-            for (int i = 0; i < 4; ++i) reinterpret_cast<uint4*>(dst)[i] = src[i];
+            for (int j = 0; j < 32; ++j) sEpi[j * 64 + wr] = kt_f2bf(silu(__uint_as_float(v[j])) * xq[j * 32 + lane]);
           }
-          __syncwarp();
+          epi_bar();
+          // 32 tokens x 64 features (128 bytes per token): thread copies 16-byte chunk
+          // (t % 8) of token t / 8 + 16 i
+          const int t = l, c = t & 7;
+#pragma unroll
+          for (int i = 0; i < 2; ++i) {
+            const int tok = (t >> 3) + 16 * i;
+            if (c0 + tok < ntok)
+              *reinterpret_cast<uint4*>(a.out + (int64_t)(pos0 + c0 + tok) * a.out_ld + (int64_t)wt * 128 + 64 * cr + 8 * c) =
+                  *reinterpret_cast<const uint4*>(sEpi + tok * 64 + 8 * c);
+          }
+          epi_bar();
         } else {
-#pragma unroll 1
-          for (int h = 0; h < 2; ++h) {
-            uint32_t v[32];
-            kt_tmem_ld32(lane_base + 256 * h + c0, v);
-            kt_tmem_wait_ld();
 #pragma unroll
-            for (int j = 0; j < 32; ++j) stg[j * 32 + lane] = kt_f2bf(__uint_as_float(v[j]));
-            __syncwarp();
-            const int tok = c0 + lane;
-            if (tok < ntok) {
-              uint16_t* dst = a.out + (int64_t)(pos0 + tok) * a.out_ld + (int64_t)wt * 256 + 128 * h + 32 * q;
-              const uint4* src = reinterpret_cast<const uint4*>(stg + lane * 32);
+          for (int j = 0; j < 32; ++j) sEpi[j * 128 + wr] = kt_f2bf(__uint_as_float(v[j]));
+          epi_bar();
+          // 32 tokens x 128 features (256 bytes per token): thread copies 16-byte chunk
+          // (t % 16) of token t / 16 + 8 i
+          const int t = l, c = t & 15;
 #pragma unroll
-              for (int i = 0; i < 4; ++i) reinterpret_cast<uint4*>(dst)[i] = src[i];
-            }
-            __syncwarp();
+          for (int i = 0; i < 4; ++i) {
+            const int tok = (t >> 4) + 8 * i;
+            if (c0 + tok < ntok)
+              *reinterpret_cast<uint4*>(a.out + (int64_t)(pos0 + c0 + tok) * a.out_ld + (int64_t)wt * 256 + 128 * cr + 8 * c) =
+                  *reinterpret_cast<const uint4*>(sEpi + tok * 128 + 8 * c);
           }
+          epi_bar();
         }
       }
       kt_tc_fence_before();
-      kt_mbar_arrive(acc_empty);
+      __syncwarp();
+      if (lane == 0) kt_mbar_arrive_cluster(acc_empty0 + 8 * b);
     }
   }
 
   kt_tc_fence_before();
   __syncthreads();
+  kt_cluster_sync();  // neither CTA leaves while the pair's MMAs may read its shared memory
   if (warp == kWarpMma) {
     kt_tc_fence_after();
-    kt_tmem_dealloc(tmem, 512);
+    kt_tmem_dealloc2(tmem, 512);
   }
 }
 
@@ -384,38 +462,92 @@ static int make_map(CUtensorMap* m, const void* base, int64_t rows, int64_t cols
   return r == CUDA_SUCCESS ? 0 : -2;
 }
 
+template <int TYPE>
+static int raw_slot() {
+  return Raw<TYPE>::SLOT;
+}
+
+static int raw_slot_of(int type) {
+  switch (type) {
+    case KT_Q8_0: return raw_slot<KT_Q8_0>();
+    case KT_Q4_K: return raw_slot<KT_Q4_K>();
+    case KT_Q6_K: return raw_slot<KT_Q6_K>();
+    case KT_IQ3_S: return raw_slot<KT_IQ3_S>();
+  }
+  return 0;
+}
+
+// Raw weight map: G consecutive rows of `row_bytes` form one tensor row of G*row_bytes bytes
+// (a 16-byte multiple, as TMA requires), box {slot bytes, 64/G group rows}. Returns G, or 0
+// when the plain-layout base is not 16-byte aligned (per-row bulk copies are used then).
+static int make_raw_map(CUtensorMap* m, const void* w, int64_t row_bytes, int64_t rows_total, int n_slots, int type) {
+  if (((uintptr_t)w) & 15) return 0;
+  int64_t g = 16;
+  while (row_bytes % g) g /= 2;
+  const int G = (int)(16 / g);
+  if (rows_total % G || 64 % G) return 0;
+  PFN_encodeTiled enc = get_encode();
+  if (!enc) return 0;
+  const int slot = raw_slot_of(type);
+  cuuint64_t dims[2] = {(cuuint64_t)(G * row_bytes), (cuuint64_t)(n_slots * rows_total / G)};
+  cuuint64_t strides[1] = {(cuuint64_t)(G * row_bytes)};
+  cuuint32_t box[2] = {(cuuint32_t)slot, (cuuint32_t)(64 / G)};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(w), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? G : 0;
+}
+
 template <int TYPE, int PHASE>
-static int launch_t(const CUtensorMap& m, const KtGemmArgs& a, int grid, cudaStream_t s) {
+static int launch_t(const CUtensorMap& m, const CUtensorMap& wm, const KtGemmArgs& a, int grid, cudaStream_t s) {
   constexpr int smem = smem_bytes<TYPE>();
   static_assert(smem <= 227 * 1024, "shared memory budget");
   auto k = kt_moe_gemm_kernel<TYPE, PHASE>;
   if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) return -3;
-  k<<<grid, kThreads, smem, s>>>(m, a);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(grid & ~1), 1, 1);  // whole CTA pairs
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, k, m, wm, a) != cudaSuccess) return -4;
   return cudaGetLastError() == cudaSuccess ? 0 : -4;
 }
 
 template <int PHASE>
-static int launch_phase(int type, const CUtensorMap& m, const KtGemmArgs& a, int grid, cudaStream_t s) {
+static int launch_phase(int type, const CUtensorMap& m, const CUtensorMap& wm, const KtGemmArgs& a, int grid,
+                        cudaStream_t s) {
   switch (type) {
-    case KT_Q8_0: return launch_t<KT_Q8_0, PHASE>(m, a, grid, s);
-    case KT_Q4_K: return launch_t<KT_Q4_K, PHASE>(m, a, grid, s);
-    case KT_Q6_K: return launch_t<KT_Q6_K, PHASE>(m, a, grid, s);
-    case KT_IQ3_S: return launch_t<KT_IQ3_S, PHASE>(m, a, grid, s);
+    case KT_Q8_0: return launch_t<KT_Q8_0, PHASE>(m, wm, a, grid, s);
+    case KT_Q4_K: return launch_t<KT_Q4_K, PHASE>(m, wm, a, grid, s);
+    case KT_Q6_K: return launch_t<KT_Q6_K, PHASE>(m, wm, a, grid, s);
+    case KT_IQ3_S: return launch_t<KT_IQ3_S, PHASE>(m, wm, a, grid, s);
   }
   return -1;
 }
 
 // phase 1: X [T, K] bf16 gathered by sorted_token; W13 slots [2N, K]; out H [R, N]
-int kt_launch_gemm_gate_up(int type, const void* x, int64_t T, int K, int N, const void* w13, int table,
+int kt_launch_gemm_gate_up(int type, const void* x, int64_t T, int K, int N, const void* w13, int table, int n_slots,
                            const int32_t* tiles, const int32_t* n_tiles, const int32_t* sorted_token, void* h,
                            int* status, int grid, cudaStream_t s) {
   if (K % 256 || N % 128) return -1;
-  CUtensorMap m;
-  if (make_map(&m, x, T, K, 1)) return -2;
+  if (((uintptr_t)x) & 15) return -1;
+  CUtensorMap m, wm;
+  memset(&m, 0, sizeof m);
+  memset(&wm, 0, sizeof wm);
   KtGemmArgs a{};
   a.w = (const uint8_t*)w13;
   a.table = table;
   a.row_bytes = (int64_t)K / kt_block_info(type).qk * kt_block_info(type).bytes;
+  a.raw_group = table ? 0 : make_raw_map(&wm, w13, a.row_bytes, 2 * (int64_t)N, n_slots, type);
+  a.x = (const uint16_t*)x;
   a.K = K;
   a.N = N;
   a.K_out = K;
@@ -426,19 +558,21 @@ int kt_launch_gemm_gate_up(int type, const void* x, int64_t T, int K, int N, con
   a.out = (uint16_t*)h;
   a.out_ld = N;
   a.status = status;
-  return launch_phase<1>(type, m, a, grid, s);
+  return launch_phase<1>(type, m, wm, a, grid, s);
 }
 
 // phase 2: H [R, N] bf16 (sorted rows); W2 slots [K, N]; out Y [R, K]
-int kt_launch_gemm_down(int type, const void* h, int64_t R, int K, int N, const void* w2, int table, const int32_t* tiles,
-                        const int32_t* n_tiles, void* y, int* status, int grid, cudaStream_t s) {
+int kt_launch_gemm_down(int type, const void* h, int64_t R, int K, int N, const void* w2, int table, int n_slots,
+                        const int32_t* tiles, const int32_t* n_tiles, void* y, int* status, int grid, cudaStream_t s) {
   if (N % 256 || K % 256) return -1;
-  CUtensorMap m;
-  if (make_map(&m, h, R, N, kTN)) return -2;
+  CUtensorMap m, wm;
+  memset(&wm, 0, sizeof wm);
+  if (make_map(&m, h, R, N, kHalfN)) return -2;
   KtGemmArgs a{};
   a.w = (const uint8_t*)w2;
   a.table = table;
   a.row_bytes = (int64_t)N / kt_block_info(type).qk * kt_block_info(type).bytes;
+  a.raw_group = table ? 0 : make_raw_map(&wm, w2, a.row_bytes, (int64_t)K, n_slots, type);
   a.K = N;  // reduction length
   a.N = N;
   a.K_out = K;  // rows of W2
@@ -449,7 +583,7 @@ int kt_launch_gemm_down(int type, const void* h, int64_t R, int K, int N, const 
   a.out = (uint16_t*)y;
   a.out_ld = K;
   a.status = status;
-  return launch_phase<2>(type, m, a, grid, s);
+  return launch_phase<2>(type, m, wm, a, grid, s);
 }
 
 int kt_gemm_tile_tokens() { return kTN; }

@@ -123,9 +123,11 @@ int kt_launch_combine(const void* out, int dtype, const float* w, int64_t T, int
   return 0;
 }
 
-// Same arithmetic over the prefill layout: route (t, k) lives at sorted row route_pos[t*top_k+k]
-// of y [R, K] bf16, or is absent (-1: not on this device, contributes a zero row).
-// Each thread produces 8 consecutive columns with 16-byte loads.
+// The prefill finalize: route (t, k) lives at sorted row route_pos[t*top_k+k] of y [R, K] bf16,
+// or is absent (-1: not on this device, contributes nothing). res[t] = bf16(sum_k w * y) with
+// the fp32 router weight and fp32 accumulation in k order, rounded once (the finalize of the
+// CUTLASS fused MoE that the reference's streamed prefill runs; the decode combine above keeps
+// the hot method's per-route bf16 roundings). Each thread produces 8 consecutive columns.
 __global__ void kt_combine_sorted_kernel(const uint16_t* __restrict__ y, const int32_t* __restrict__ route_pos,
                                          const float* __restrict__ w, int64_t T, int top_k, int64_t K,
                                          uint16_t* __restrict__ res) {
@@ -137,13 +139,13 @@ __global__ void kt_combine_sorted_kernel(const uint16_t* __restrict__ y, const i
     for (int k = 0; k < top_k; ++k) {
       const int32_t pos = route_pos[t * top_k + k];
       if (pos < 0) continue;  // bf16(0 * w) adds an exact zero
-      const float wk = kt_bf2f(kt_f2bf(w[t * top_k + k]));
+      const float wk = w[t * top_k + k];
       const uint4 v = *reinterpret_cast<const uint4*>(y + (int64_t)pos * K + c);
       const uint32_t u[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        acc[2 * j] += kt_bf2f(kt_f2bf(kt_bf2f((uint16_t)(u[j] & 0xffff)) * wk));
-        acc[2 * j + 1] += kt_bf2f(kt_f2bf(kt_bf2f((uint16_t)(u[j] >> 16)) * wk));
+        acc[2 * j] += kt_bf2f((uint16_t)(u[j] & 0xffff)) * wk;
+        acc[2 * j + 1] += kt_bf2f((uint16_t)(u[j] >> 16)) * wk;
       }
     }
     uint4 o;

@@ -55,10 +55,12 @@ def test_window_kernel_vs_reference(cuda_device, ref_mods, qtype, cols, rows, to
     ob = O.f32_to_bf16(want)
     rb = bits(y_ref)
     assert (ob != rb).mean() < 2e-3
-    assert O.rel_l2(O.bf16_to_f32(rb), want) < 1e-3
+    assert O.rel_l2(O.bf16_to_f32(rb), O.bf16_to_f32(ob)) < 2e-4
     # the B200 kernel against the reference kernel
     gb = bits(y)
     mismatch = (gb != rb).mean()
+    print(f"\nREFPIN type={qtype} cols={cols} rows={rows} tokens={tokens} top_k={top_k}: "
+          f"oracle!=ref {(ob != rb).mean():.2e}  b200!=ref {mismatch:.2e}  b200!=oracle {(gb != ob).mean():.2e}")
     assert mismatch < 2e-3, mismatch
     assert O.rel_l2(O.bf16_to_f32(gb), O.bf16_to_f32(rb)) < 1e-3
 
