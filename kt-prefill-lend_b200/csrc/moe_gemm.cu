@@ -17,15 +17,16 @@
 // accumulator of its 128 rows x 256 tokens in its own TMEM. Phase 1 gives each CTA 64 gate
 // rows and the matching 64 up rows, so SwiGLU needs no data from the peer.
 //
-// Warp roles per CTA (480 threads):
+// Warp roles per CTA (512 threads):
 //   warps 0-7   dequant producers: two threads per A row, 32 values each per 64-wide k-step,
 //               decoded from the raw stage and written as bf16 into the A stage in the UMMA
 //               K-major 128-byte swizzle layout
 //   warp 8      raw loader: per 256-value super-block column, 2G 2-D TMA loads of a tensor map
 //               that views G consecutive weight rows as one (G = rows whose bytes make a
 //               16-byte multiple); slot tables fall back to one 1-D bulk copy per row
-//   warp 9      B loader: phase 1 gathers this CTA's token rows of X with 16-byte cp.async
-//               copies into the swizzled stage; phase 2 loads H rows with one 2-D TMA per k-step
+//   warps 9, 15 B loaders: phase 1 gathers this CTA's token rows of X with 16-byte cp.async
+//               copies into the swizzled stage (two warps: one warp's copies alone cannot keep
+//               up); phase 2 loads H rows with one 2-D TMA per k-step (warp 9)
 //   warp 10     even CTA: MMA issuer (tcgen05.mma.cta_group::2, commits multicast to both CTAs);
 //               odd CTA: forwards its B-stage completions to the even CTA's barrier
 //   warps 11-14 epilogue: tcgen05.ld of the accumulator; phase 1 SwiGLU -> H (bf16), phase 2
@@ -40,8 +41,9 @@
 
 namespace {
 
-constexpr int kThreads = 480;
-constexpr int kWarpRaw = 8, kWarpB = 9, kWarpMma = 10, kWarpEpi0 = 11;
+constexpr int kThreads = 512;
+constexpr int kWarpRaw = 8, kWarpB = 9, kWarpMma = 10, kWarpEpi0 = 11, kWarpB2 = 15;
+constexpr int kGatherWarps = 2;  // phase 1: warps 9 and 15 gather token rows
 constexpr int kTN = 256;           // tokens per tile (MMA N, split between the pair)
 constexpr int kHalfN = kTN / 2;    // B rows held by each CTA
 constexpr int kStages = 4;         // A/B stages
@@ -50,7 +52,7 @@ constexpr int kBStageBytes = kHalfN * 128;
 constexpr int kXchgBytes = 2 * 32 * 32 * 4;  // phase-1 epilogue: up values for the gate warps
 constexpr int kEpiBytes = 4 * 32 * 32 * 2;   // per-warp transpose buffers
 constexpr int kFixedSmem = kStages * (kAStageBytes + kBStageBytes) + kXchgBytes + kEpiBytes + 2048 /* grid */ +
-                           1024 /* barriers */ + kHalfN * 4 /* token ids */ + 1024 /* alignment slack */;
+                           1024 /* barriers */ + 1024 /* alignment slack */;
 
 // Raw staging: a "unit" is UV consecutive values of one weight row (a 256-value super-block,
 // or four 32-value Q8_0 blocks); a raw stage holds one unit for the CTA's 128 rows. Each
@@ -135,7 +137,6 @@ __global__ void __launch_bounds__(kThreads, 1) kt_moe_gemm_kernel(const __grid_c
   uint64_t* done_bar = acc_empty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done_bar + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  int32_t* sTok = reinterpret_cast<int32_t*>(bars + 64);  // [kHalfN]
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const uint32_t cr = kt_cluster_rank();
@@ -144,9 +145,9 @@ __global__ void __launch_bounds__(kThreads, 1) kt_moe_gemm_kernel(const __grid_c
     for (int s = 0; s < kStages; ++s) {
       // even CTA: its 8 producer warps, its B copies, and one forwarded arrival for the odd
       // CTA's producers and B copies (which arrive on the odd CTA's bfull)
-      kt_mbar_init(&full[s], 8 + (PHASE == 1 ? 32 : 1) + 1);
+      kt_mbar_init(&full[s], 8 + (PHASE == 1 ? 32 * kGatherWarps : 1) + 1);
       kt_mbar_init(&empty[s], 1);
-      kt_mbar_init(&bfull[s], 8 + (PHASE == 1 ? 32 : 1));
+      kt_mbar_init(&bfull[s], 8 + (PHASE == 1 ? 32 * kGatherWarps : 1));
     }
     for (int s = 0; s < R::NRAW; ++s) {
       kt_mbar_init(&raw_full[s], 1);
@@ -276,17 +277,25 @@ __global__ void __launch_bounds__(kThreads, 1) kt_moe_gemm_kernel(const __grid_c
                       reinterpret_cast<const void*>(src[i]), len[i], &raw_full[su]);
       }
     }
-  } else if (warp == kWarpB) {
-    // ---------------------------------------------------------------- B loader
+  } else if (warp == kWarpB || warp == kWarpB2) {
+    // ---------------------------------------------------------------- B loaders
+    const int gw = warp == kWarpB ? 0 : 1;
+    constexpr int NR = kHalfN / (4 * kGatherWarps);  // rows per lane per k-step (phase 1)
     uint32_t kit = 0;
     for (int item = first_item; item < n_items && !*abort_flag; item += item_stride) {
       const int tile = item / n_wt;
       const int pos0 = a.tiles[3 * tile + 1], ntok = a.tiles[3 * tile + 2];
       const int half = ((ntok + 31) & ~31) / 2;  // B rows of each CTA (the MMA N is 2*half)
       const int b0 = cr * half;                  // first tile row held by this CTA
+      // phase 1: lane copies 16-byte chunk (lane % 8) of rows lane/8 + 4*(gw + 2i); the
+      // token ids of those rows are kept in registers for the whole tile
+      int tokr[NR];
       if constexpr (PHASE == 1) {
-        for (int j = lane; j < half; j += 32) sTok[j] = a.sorted_token[pos0 + (b0 + j < ntok ? b0 + j : 0)];
-        __syncwarp();
+#pragma unroll
+        for (int i = 0; i < NR; ++i) {
+          const int j = (lane >> 3) + 4 * (gw + kGatherWarps * i);
+          tokr[i] = j < half ? a.sorted_token[pos0 + (b0 + j < ntok ? b0 + j : 0)] : 0;
+        }
       }
       for (int ks = 0; ks < ksteps && !*abort_flag; ++ks, ++kit) {
         const int s = kit % kStages;
@@ -294,12 +303,15 @@ __global__ void __launch_bounds__(kThreads, 1) kt_moe_gemm_kernel(const __grid_c
         uint8_t* dst = sB + s * kBStageBytes;
         uint64_t* bar = leader ? &full[s] : &bfull[s];
         if constexpr (PHASE == 1) {
-          // lane copies 16-byte chunk (lane % 8) of rows lane/8, lane/8 + 4, ...
           const int c = lane & 7;
           const uint16_t* xk = a.x + (int64_t)ks * 64 + 8 * c;
-          for (int j = lane >> 3; j < half; j += 4) kt_cp_async16(dst + kt_swz128(j, 8 * c), xk + (int64_t)sTok[j] * a.K);
+#pragma unroll
+          for (int i = 0; i < NR; ++i) {
+            const int j = (lane >> 3) + 4 * (gw + kGatherWarps * i);
+            if (j < half) kt_cp_async16(dst + kt_swz128(j, 8 * c), xk + (int64_t)tokr[i] * a.K);
+          }
           kt_cp_async_arrive(bar);
-        } else {
+        } else if (gw == 0) {
           if (lane == 0) {
             kt_mbar_arrive_expect_tx(bar, (uint32_t)kBStageBytes);
             kt_tma_2d(dst, &bmap, ks * 64, pos0 + b0, bar);
@@ -354,7 +366,7 @@ __global__ void __launch_bounds__(kThreads, 1) kt_moe_gemm_kernel(const __grid_c
       }
     }
     kt_mbar_wait(done_bar, 0, a.status, nullptr);  // every MMA of the pair has completed
-  } else {
+  } else if (warp >= kWarpEpi0 && warp < kWarpEpi0 + 4) {
     // ---------------------------------------------------------------- epilogue
     const int q = warp & 3;  // TMEM lane quadrant this warp may access
     const int G = a.raw_group > 0 ? a.raw_group : 1;
