@@ -92,6 +92,23 @@ int kt_moe_a8_vec_routes(const void* x, int x_dtype, int64_t tokens, int64_t col
                          int n_slots, const int32_t* topk_ids, int64_t top_k, int ggml_type, int64_t rows, void* y,
                          void* workspace, size_t workspace_bytes, void* stream);
 
+/* Size of the library's own scratch area used by kt_moe_a8_vec_multi_static (2 MiB). */
+#define KT_STATIC_SCRATCH_BYTES (2u << 20)
+
+/* kt_moe_a8_vec_multi without a caller workspace, for callers that cannot allocate device
+ * memory per call (graph capture under a frozen pool, host frameworks that own all device
+ * memory, C callers without an allocator). No counterpart in the reference: its op always
+ * allocated through torch.
+ * Scratch comes from a fixed KT_STATIC_SCRATCH_BYTES array inside the library, held on every
+ * GPU that loads it until the process exits; calls whose scratch need
+ * (kt_moe_a8_vec_workspace_size) exceeds it return KT_ERR_WORKSPACE. The first call on a
+ * device looks up the array's address, so make it before any stream capture. All calls on a
+ * device share the array: calls that can overlap on the GPU (other streams, concurrent
+ * graphs) race and must be serialised by the caller. Nothing is allocated or freed. */
+int kt_moe_a8_vec_multi_static(const void* x, int x_dtype, int64_t tokens, int64_t cols, const void* w, int w_is_table,
+                               int n_slots, const int32_t* topk_ids, int64_t top_k, int ggml_type, int64_t rows,
+                               void* y, void* stream);
+
 /* Workspace for kt_dense_a8_vec. */
 size_t kt_dense_a8_vec_workspace_size(int64_t tokens, int64_t cols);
 

@@ -2,6 +2,8 @@
 // carving, and the launch sequences of the decode GEMV and the prefill layer.
 #include <string.h>
 
+#include <mutex>
+
 #include "kt_gguf_b200.h"
 #include "kt_common.cuh"
 #include "kt_kernels.h"
@@ -309,4 +311,47 @@ KT_EXPORT int kt_moe_prefill(const void* x, int64_t tokens, int64_t hidden, int6
                              void* stream) {
   return kt_moe_prefill_timed(x, tokens, hidden, inter, topk_ids, topk_weights, top_k, w13, type13, w2, type2,
                               w_is_table, n_slots, out, workspace, workspace_bytes, stream, nullptr);
+}
+
+// ------------------------------------------------------------------ allocation-free decode GEMV
+// Some callers cannot hand this library device memory on every call: code that runs while a
+// CUDA graph is being captured under a frozen memory pool, plugins whose host framework owns
+// all of the GPU's memory, or plain C callers with no device allocator at all. For them the
+// decode GEMV can use a fixed scratch area that lives in the library itself: a file-scope
+// __device__ array of KT_STATIC_SCRATCH_BYTES, which every GPU that loads the library holds
+// until the process exits. All calls on a device share it (see the header for the rules).
+
+static __device__ __align__(256) uint8_t kt_static_scratch[KT_STATIC_SCRATCH_BYTES];
+
+namespace {
+std::mutex g_static_scratch_mu;
+void* g_static_scratch_ptr[256] = {};  // device address of kt_static_scratch, per device ordinal
+}  // namespace
+
+KT_EXPORT int kt_moe_a8_vec_multi_static(const void* x, int x_dtype, int64_t tokens, int64_t cols, const void* w,
+                                         int w_is_table, int n_slots, const int32_t* topk_ids, int64_t top_k,
+                                         int ggml_type, int64_t rows, void* y, void* stream) {
+  if (tokens < 0 || cols <= 0 || top_k <= 0 || n_slots <= 0) return KT_ERR_ARG;
+  if (tokens == 0) return KT_OK;
+  // the scratch this call needs must fit the fixed area
+  if (kt_moe_a8_vec_workspace_size(tokens, cols, tokens * top_k, n_slots) > (size_t)KT_STATIC_SCRATCH_BYTES)
+    return KT_ERR_WORKSPACE;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 256) return KT_ERR_CUDA;
+  void* scratch = nullptr;
+  {
+    // first call on this device: look up the array's device address with the device current
+    // (the host-side name is only a stand-in, not a device address)
+    std::lock_guard<std::mutex> lock(g_static_scratch_mu);
+    if (!g_static_scratch_ptr[dev]) {
+      void* p = nullptr;
+      if (cudaGetSymbolAddress(&p, kt_static_scratch) != cudaSuccess || !p) return KT_ERR_CUDA;
+      g_static_scratch_ptr[dev] = p;
+    }
+    scratch = g_static_scratch_ptr[dev];
+  }
+  // moe_vec clears the status word at the start of every call; every other scratch byte it
+  // reads is written earlier in the same call
+  return moe_vec(x, x_dtype, tokens, cols, w, w_is_table, n_slots, topk_ids, top_k, ggml_type, rows, y, scratch,
+                 (size_t)KT_STATIC_SCRATCH_BYTES, stream);
 }
