@@ -1,0 +1,115 @@
+"""The reference-facing hot-expert method and hot cache on the GPU.
+
+KTGGUFHotExpertsMethod is built as the KT wrapper builds it (hot/kt_gguf_hot.py:163-304):
+create_weights, process_weights_after_loading from a GGUF reader (a fake in `_readers`
+serving synthetic experts), then apply() on a dispatch output. Prefill-sized chunks run
+the tcgen05 layer (checked against the fp32 dequant-then-matmul oracle, rel-L2 <= 5e-3);
+decode windows run the q8_1 GEMV path (checked against the restated reference layer).
+HotCache.route is checked against table gathers and an exact count histogram."""
+from types import SimpleNamespace
+
+import numpy as np
+import pytest
+import torch
+
+from kt_gguf_b200 import kt_gguf_hot as H
+from kt_gguf_b200 import kt_hot_cache as C
+from kt_gguf_b200 import synth
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+TOL_FP32_ORACLE = 5e-3  # north-star bound, bf16 activations
+TOL_REF_LAYER = 2e-3    # GEMV path vs the restated reference layer (same q8_1 / bf16 arithmetic)
+
+
+class FakeGGUF:
+    """Serves one synthetic layer's experts the way _GGUFExperts serves a GGUF file."""
+
+    def __init__(self, L: synth.MoELayer):
+        self.L = L
+        self.E, self.inter, self.K = L.w13.shape[0], L.inter, L.hidden
+
+    def types(self, layer_idx):
+        return (self.L.type13, self.L.type13, self.L.type2)
+
+    def slice(self, layer_idx, proj, N, rank, experts):
+        e = experts.numpy()
+        if proj == "gate":
+            v = self.L.w13[e, :N]
+        elif proj == "up":
+            v = self.L.w13[e, N:]
+        else:
+            v = self.L.w2[e]
+        return torch.from_numpy(np.ascontiguousarray(v))
+
+
+def build_method(L: synth.MoELayer, key: str):
+    H._readers[key] = FakeGGUF(L)
+    kt = SimpleNamespace(num_gpu_experts=L.w13.shape[0], weight_path=key, layer_idx=0)
+    layer = torch.nn.Module()
+    layer.moe_tp_rank, layer.moe_tp_size = 0, 1
+    m = H.KTGGUFHotExpertsMethod(kt, layer)
+    m.create_weights(layer, L.w13.shape[0], L.hidden, L.inter, torch.bfloat16)
+    m.process_weights_after_loading(layer)
+    m.create_moe_runner(layer, None)
+    return m, layer
+
+
+def apply(m, layer, L, dev):
+    d = SimpleNamespace(hidden_states=L.x.to(dev), topk_output=(L.topk_weights.to(dev), L.topk_ids.to(dev), None))
+    out = m.apply(layer, d).hidden_states
+    torch.cuda.synchronize()
+    return out
+
+
+def test_hot_method_loads_slots_from_reader(cuda_device):
+    L = synth.make_layer(11, 8, 2048, 512, 32, 8, 12, 14, n_hot=8)
+    m, layer = build_method(L, "fake://load")
+    assert torch.equal(layer.w13_qweight.cpu(), torch.from_numpy(L.w13))
+    assert torch.equal(layer.w2_qweight.cpu(), torch.from_numpy(L.w2))
+    assert (m.type13, m.type2) == (12, 14)
+
+
+@pytest.mark.parametrize("type13,type2", [(12, 14), (8, 8), (21, 21)])
+def test_hot_method_prefill_chunk(cuda_device, type13, type2):
+    L = synth.make_layer(5, 384, 2048, 512, 48, 8, type13, type2, n_hot=24, zipf=1.1)
+    m, layer = build_method(L, f"fake://prefill{type13}")
+    assert m._use_prefill(L.x, 384)
+    out = apply(m, layer, L, cuda_device)
+    want = O.moe_fp32(L.x.view(torch.int16).numpy().view(np.uint16), L.topk_ids.numpy(), L.topk_weights.numpy(),
+                      type13, L.w13, type2, L.w2, L.inter)
+    err = O.rel_l2(out.float().cpu().numpy(), want)
+    assert err <= TOL_FP32_ORACLE, err
+
+
+@pytest.mark.parametrize("tokens", [1, 4, 16])
+def test_hot_method_decode_window(cuda_device, tokens):
+    L = synth.make_layer(7, tokens, 2048, 512, 32, 8, 12, 14, n_hot=16)
+    m, layer = build_method(L, f"fake://decode{tokens}")
+    assert not m._use_prefill(L.x, tokens)
+    out = apply(m, layer, L, cuda_device)
+    x16 = L.x.view(torch.int16).numpy().view(np.uint16)
+    ref = O.bf16_to_f32(O.moe_ref_bf16(x16, L.topk_ids.numpy(), L.topk_weights.numpy(), 12, L.w13, 14, L.w2, L.inter))
+    err = O.rel_l2(out.float().cpu().numpy(), ref)
+    assert err <= TOL_REF_LAYER, err
+
+
+def test_hot_cache_route_on_gpu(cuda_device):
+    E, NS = 64, 16
+    c = C.HotCache(1, E, NS, cuda_device, 0)
+    c.layers[0] = (None, None)
+    perm = np.random.default_rng(2).permutation(E)[:NS]
+    for s, e in enumerate(perm.tolist()):
+        c._set(0, s, e)
+    c.push_tables()
+    assert c.check_tables() == ""
+    g = torch.Generator().manual_seed(4)
+    for T in (1, 4, 700):  # decode window and a long extend (one kernel at every size)
+        ids = torch.stack([torch.randperm(E, generator=g)[:8] for _ in range(T)]).to(torch.int32)
+        before = c.counts.clone()
+        slot, cpu = c.route(0, ids.to(cuda_device))
+        torch.cuda.synchronize()
+        assert torch.equal(slot.cpu(), c.log2slot_cpu[0][ids.long()])
+        assert torch.equal(cpu.cpu(), c.log2cpu_cpu[0][ids.long()])
+        hist = torch.bincount(ids.reshape(-1).long(), minlength=E).float()
+        assert torch.equal((c.counts - before)[0].cpu(), hist)
