@@ -144,22 +144,27 @@ __device__ __forceinline__ uint32_t kt_mapa(const void* p, uint32_t rank) {
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(kt_smem_addr(p)), "r"(rank));
   return r;
 }
-// arrive (release, cluster scope) on an mbarrier given by its shared::cluster address
+// arrive on an mbarrier of either CTA of the pair, given by its shared::cluster address.
+// Default semantics (release at CTA scope), as CUTLASS's cluster barrier uses for peer
+// arrivals: what an arrival publishes is shared memory of the arriving CTA that the arriving
+// thread has already observed complete (it acquired the local barrier guarding it). A
+// release at cluster scope makes every such arrival wait for a cluster-wide fence; on the
+// pair's stage-forwarding path that fence cost more than an MMA k-step.
 __device__ __forceinline__ void kt_mbar_arrive_cluster(uint32_t cluster_addr) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
 }
 __device__ __forceinline__ bool kt_mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(ok)
       : "r"(kt_smem_addr(bar)), "r"(parity)
       : "memory");
   return ok != 0;
 }
-// bounded wait with cluster-scope acquire, for barriers that receive arrivals from the peer CTA
+// bounded wait on a barrier that also receives arrivals from the peer CTA
 __device__ __forceinline__ bool kt_mbar_wait_cluster(uint64_t* bar, uint32_t parity, int* status, volatile int* abort) {
   if (kt_mbar_try_wait_cluster(bar, parity)) return true;
   const uint64_t t0 = kt_globaltimer_ns();

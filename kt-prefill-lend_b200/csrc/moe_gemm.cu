@@ -17,20 +17,23 @@
 // accumulator of its 128 rows x 256 tokens in its own TMEM. Phase 1 gives each CTA 64 gate
 // rows and the matching 64 up rows, so SwiGLU needs no data from the peer.
 //
-// Warp roles per CTA (512 threads):
-//   warps 0-7   dequant producers: two threads per A row, 32 values each per 64-wide k-step,
-//               decoded from the raw stage and written as bf16 into the A stage in the UMMA
-//               K-major 128-byte swizzle layout
-//   warp 8      raw loader: per 256-value super-block column, 2G 2-D TMA loads of a tensor map
-//               that views G consecutive weight rows as one (G = rows whose bytes make a
-//               16-byte multiple); slot tables fall back to one 1-D bulk copy per row
-//   warps 9, 15 B loaders: phase 1 gathers this CTA's token rows of X with 16-byte cp.async
-//               copies into the swizzled stage (two warps: one warp's copies alone cannot keep
-//               up); phase 2 loads H rows with one 2-D TMA per k-step (warp 9)
-//   warp 10     even CTA: MMA issuer (tcgen05.mma.cta_group::2, commits multicast to both CTAs);
-//               odd CTA: forwards its B-stage completions to the even CTA's barrier
-//   warps 11-14 epilogue: tcgen05.ld of the accumulator; phase 1 SwiGLU -> H (bf16), phase 2
-//               -> Y (bf16)
+// Warp roles per CTA (P = 8 producer warps in phase 1, 16 in phase 2):
+//   warps 0..P-1  dequant producers: two (phase 1) or four (phase 2) threads per A row, each
+//                 decoding 16 values per k-step quarter from the raw stage and writing them as
+//                 bf16 into the A stage in the UMMA K-major 128-byte swizzle layout
+//   warp P        raw loader: per 256-value super-block column, 2G 2-D TMA loads of a tensor
+//                 map that views G consecutive weight rows as one (G = rows whose bytes make a
+//                 16-byte multiple); slot tables fall back to one 1-D bulk copy per row
+//   warp P+1      B loader: phase 1 gathers this CTA's token rows of X with 16-byte cp.async
+//                 copies into the swizzled stage, together with warp P+7 (one warp's copies
+//                 alone cannot keep up); phase 2 loads H rows with one 2-D TMA per k-step
+//   warp P+2      even CTA: MMA issuer (tcgen05.mma.cta_group::2, commits multicast to both
+//                 CTAs); odd CTA: forwards its stage completions to the even CTA's barrier
+//   warps P+3..P+6 epilogue: tcgen05.ld of the accumulator; phase 1 SwiGLU -> H (bf16),
+//                 phase 2 -> Y (bf16)
+// The pair's two CTAs meet on the even CTA's stage barriers: the odd CTA's producers and B
+// copies complete a local barrier, and one warp forwards each completed stage with a single
+// remote arrival.
 // TMEM (per CTA): two 256-column fp32 accumulators, so the epilogue of one tile overlaps the
 // MMAs of the next. No TMA or bulk copy uses .multicast::cluster.
 #include <string.h>
@@ -41,9 +44,20 @@
 
 namespace {
 
-constexpr int kThreads = 512;
-constexpr int kWarpRaw = 8, kWarpB = 9, kWarpMma = 10, kWarpEpi0 = 11, kWarpB2 = 15;
-constexpr int kGatherWarps = 2;  // phase 1: warps 9 and 15 gather token rows
+constexpr int kGatherWarps = 2;  // phase 1: two warps gather token rows
+
+// Warp roles per phase. Phase 1 runs 8 producer warps (two threads per A row) beside its two
+// gather warps: more producers take issue slots from the gathers, which bound phase 1.
+// Phase 2 loads B with one TMA per k-step and runs 16 producer warps (four threads per A
+// row), which shortens each producer's per-k-step latency, the bound of phase 2.
+template <int PHASE>
+struct Roles {
+  static constexpr int kProd = PHASE == 1 ? 8 : 16;           // producer warps
+  static constexpr int kRaw = kProd, kB = kProd + 1, kMma = kProd + 2, kEpi0 = kProd + 3;
+  static constexpr int kB2 = PHASE == 1 ? kProd + 7 : -1;     // second gather warp
+  static constexpr int kThreads = 32 * (PHASE == 1 ? kProd + 8 : kProd + 7);
+  static constexpr int kQuarters = 4 * 128 / (32 * kProd);  // k-step quarters per producer thread
+};
 constexpr int kTN = 256;           // tokens per tile (MMA N, split between the pair)
 constexpr int kHalfN = kTN / 2;    // B rows held by each CTA
 constexpr int kStages = 4;         // A/B stages
@@ -114,10 +128,13 @@ __device__ __forceinline__ int64_t a_row(int rh, int wt, uint32_t cr, int N) {
 }  // namespace
 
 template <int TYPE, int PHASE>
-__global__ void __launch_bounds__(kThreads, 1) kt_moe_gemm_kernel(const __grid_constant__ CUtensorMap bmap,
+__global__ void __launch_bounds__(Roles<PHASE>::kThreads, 1) kt_moe_gemm_kernel(const __grid_constant__ CUtensorMap bmap,
                                                                   const __grid_constant__ CUtensorMap wmap,
                                                                   const KtGemmArgs a) {
   extern __shared__ uint8_t smem_raw[];
+  using RL = Roles<PHASE>;
+  constexpr int kProdWarps = RL::kProd, kWarpRaw = RL::kRaw, kWarpB = RL::kB, kWarpMma = RL::kMma,
+                kWarpEpi0 = RL::kEpi0, kWarpB2 = RL::kB2;
   uint8_t* smem = reinterpret_cast<uint8_t*>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   using R = Raw<TYPE>;
   uint8_t* sA = smem;
@@ -143,15 +160,15 @@ __global__ void __launch_bounds__(kThreads, 1) kt_moe_gemm_kernel(const __grid_c
   const bool leader = cr == 0;
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
-      // even CTA: its 8 producer warps, its B copies, and one forwarded arrival for the odd
-      // CTA's producers and B copies (which arrive on the odd CTA's bfull)
-      kt_mbar_init(&full[s], 8 + (PHASE == 1 ? 32 * kGatherWarps : 1) + 1);
+      // even CTA: its producer warps, its B copies, and one forwarded arrival for the odd CTA's
+      // producers and B copies (which arrive on the odd CTA's bfull)
+      kt_mbar_init(&full[s], kProdWarps + (PHASE == 1 ? 32 * kGatherWarps : 1) + 1);
       kt_mbar_init(&empty[s], 1);
-      kt_mbar_init(&bfull[s], 8 + (PHASE == 1 ? 32 * kGatherWarps : 1));
+      kt_mbar_init(&bfull[s], kProdWarps + (PHASE == 1 ? 32 * kGatherWarps : 1));
     }
     for (int s = 0; s < R::NRAW; ++s) {
       kt_mbar_init(&raw_full[s], 1);
-      kt_mbar_init(&raw_empty[s], 256);
+      kt_mbar_init(&raw_empty[s], kProdWarps);
     }
     for (int b = 0; b < 2; ++b) {
       kt_mbar_init(&acc_full[b], 1);
@@ -179,11 +196,11 @@ __global__ void __launch_bounds__(kThreads, 1) kt_moe_gemm_kernel(const __grid_c
   const int first_item = blockIdx.x >> 1, item_stride = gridDim.x >> 1;
   const int64_t rows_total = PHASE == 1 ? 2 * (int64_t)a.N : (int64_t)a.K_out;
 
-  if (warp < 8) {
+  if (warp < kProdWarps) {
     // ---------------------------------------------------------------- dequant producers
     // thread -> A row rh (= TMEM lane) -> raw slot in load order: the G sub-tiles of a
     // segment hold weight rows j, j+G, ...; lane rh holds weight row seg*64 + wrow(rh)
-    const int rh = threadIdx.x & 127, hf = threadIdx.x >> 7;
+    const int rh = threadIdx.x & 127, qt0 = (threadIdx.x >> 7) * RL::kQuarters;
     const int G = a.raw_group > 0 ? a.raw_group : 1;
     const int seg = rh >> 6, rr = rh & 63;
     const int slot_off = seg * R::SEG_BYTES + (rr / (64 / G)) * sub_pitch<TYPE>(G) + (rr % (64 / G)) * R::SLOT;
@@ -211,13 +228,16 @@ __global__ void __launch_bounds__(kThreads, 1) kt_moe_gemm_kernel(const __grid_c
           const int s = (kit + kk) % kStages;
           if (ok && !kt_mbar_wait(&empty[s], (((kit + kk) / kStages) & 1) ^ 1, a.status, abort_flag)) ok = false;
           if (ok) {
-            uint32_t pk[16];
-            dq.kstep_half(slotp, off, kk, hf, pk, sGrid);
             uint8_t* arow = sA + s * kAStageBytes;
 #pragma unroll
-            for (int c = 0; c < 4; ++c)
-              *reinterpret_cast<uint4*>(arow + kt_swz128(rh, 32 * hf + 8 * c)) =
-                  make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
+            for (int j = 0; j < RL::kQuarters; ++j) {
+              uint32_t pk[8];
+              dq.kstep_quarter(slotp, off, kk, qt0 + j, pk, sGrid);
+#pragma unroll
+              for (int c = 0; c < 2; ++c)
+                *reinterpret_cast<uint4*>(arow + kt_swz128(rh, 16 * (qt0 + j) + 8 * c)) =
+                    make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
+            }
             kt_fence_proxy_async_smem();
             __syncwarp();
             if (lane == 0) kt_mbar_arrive(&stage_bar[s]);
@@ -225,7 +245,8 @@ __global__ void __launch_bounds__(kThreads, 1) kt_moe_gemm_kernel(const __grid_c
         }
         kit += R::KPU;
         if (!ok) break;
-        kt_mbar_arrive(&raw_empty[su]);
+        __syncwarp();
+        if (lane == 0) kt_mbar_arrive(&raw_empty[su]);
       }
     }
   } else if (warp == kWarpRaw) {
@@ -277,7 +298,7 @@ __global__ void __launch_bounds__(kThreads, 1) kt_moe_gemm_kernel(const __grid_c
                       reinterpret_cast<const void*>(src[i]), len[i], &raw_full[su]);
       }
     }
-  } else if (warp == kWarpB || warp == kWarpB2) {
+  } else if (warp == kWarpB || (PHASE == 1 && warp == kWarpB2)) {
     // ---------------------------------------------------------------- B loaders
     const int gw = warp == kWarpB ? 0 : 1;
     constexpr int NR = kHalfN / (4 * kGatherWarps);  // rows per lane per k-step (phase 1)
@@ -313,6 +334,8 @@ __global__ void __launch_bounds__(kThreads, 1) kt_moe_gemm_kernel(const __grid_c
           kt_cp_async_arrive(bar);
         } else if (gw == 0) {
           if (lane == 0) {
+            // 128 rows from the first row of this CTA's half; rows past the tile belong to the
+            // next tile or lie past the end (zero fill) and only reach unused accumulator columns
             kt_mbar_arrive_expect_tx(bar, (uint32_t)kBStageBytes);
             kt_tma_2d(dst, &bmap, ks * 64, pos0 + b0, bar);
           }
@@ -519,7 +542,7 @@ static int launch_t(const CUtensorMap& m, const CUtensorMap& wm, const KtGemmArg
   if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) return -3;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)(grid & ~1), 1, 1);  // whole CTA pairs
-  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.blockDim = dim3(Roles<PHASE>::kThreads, 1, 1);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = s;
   cudaLaunchAttribute attr[1];
