@@ -153,8 +153,10 @@ size_t kt_moe_prefill_workspace_size(int64_t tokens, int64_t top_k, int64_t hidd
 
 /* Byte offsets inside a kt_moe_prefill workspace, for inspection after a call:
  * offsets[0] status word (int), [1] per-slot route counts (int32 [n_slots]),
- * [2] tile list (int32 [n_tiles][3]: slot, first sorted row, rows), [3] n_tiles (int32),
- * [4] token of each sorted row (int32 [tokens*top_k]), [5] sorted row of each route
+ * [2] tile list (int32 [n_tiles][3]: slot, first sorted row, rows), [3] n_tiles and the
+ * number of resident routes (int32 [2]),
+ * [4] token of each sorted row (int32 [tokens*top_k]; sorted rows of one slot are in no
+ * particular order), [5] sorted row of each route
  * (int32 [tokens*top_k], -1 if not resident), [6] H (bf16 [tokens*top_k, inter]),
  * [7] per-route outputs Y (bf16 [tokens*top_k, hidden]). Rows past the resident routes are
  * unused. Returns KT_OK. */
@@ -169,7 +171,8 @@ int kt_moe_prefill_workspace_layout(int64_t tokens, int64_t top_k, int64_t hidde
  * weighted sum over k is accumulated in fp32 with the fp32 router weights and rounded once
  * (the finalize of the fused MoE the reference's streamed prefill uses). Replaces the hot
  * method's apply (hot/kt_gguf_hot.py:240-304) at prefill sizes and the streamer's
- * dequant + cutlass_fused_moe group body. hidden % 256 == 0, inter % 256 == 0. */
+ * dequant + cutlass_fused_moe group body. hidden % 256 == 0, inter % 256 == 0,
+ * 1 <= top_k <= 32, 1 <= n_slots <= 8192. */
 int kt_moe_prefill(const void* x, int64_t tokens, int64_t hidden, int64_t inter, const int32_t* topk_ids,
                    const float* topk_weights, int64_t top_k, const void* w13, int type13, const void* w2, int type2,
                    int w_is_table, int n_slots, void* out, void* workspace, size_t workspace_bytes, void* stream);

@@ -91,7 +91,7 @@ int moe_vec(const void* x, int x_dtype, int64_t tokens, int64_t cols, const void
 struct PreWs {
   int* status;
   int32_t* counts;
-  int32_t* cursor;
+  int32_t* hist;  // per permute block and slot: route count, then first sorted position
   int32_t* tiles;
   int32_t* n_tiles;
   int32_t* sorted_token;
@@ -108,7 +108,7 @@ PreWs pre_ws(void* ws, int64_t tokens, int64_t top_k, int64_t hidden, int64_t in
   const int tn = kt_gemm_tile_tokens();
   p.status = c.take<int>(4);
   p.counts = c.take<int32_t>(n_slots);
-  p.cursor = c.take<int32_t>(n_slots);
+  p.hist = c.take<int32_t>((size_t)kt_permute_hist_ints(R, n_slots));
   p.tiles = c.take<int32_t>(3 * (size_t)(R / tn + n_slots + 1));
   p.n_tiles = c.take<int32_t>(4);
   p.sorted_token = c.take<int32_t>(R);
@@ -271,7 +271,8 @@ KT_EXPORT int kt_moe_prefill_timed(const void* x, int64_t tokens, int64_t hidden
                                    int type13, const void* w2, int type2, int w_is_table, int n_slots, void* out,
                                    void* workspace, size_t workspace_bytes, void* stream, void* const* stage_events) {
   if (!type_ok(type13) || !type_ok(type2)) return KT_ERR_TYPE;
-  if (tokens < 0 || top_k <= 0 || n_slots <= 0 || hidden <= 0 || inter <= 0) return KT_ERR_ARG;
+  if (tokens < 0 || top_k <= 0 || top_k > 32 || n_slots <= 0 || n_slots > kPermMaxSlots || hidden <= 0 || inter <= 0)
+    return KT_ERR_ARG;
   if (hidden % 256 || inter % 256 || hidden > (1 << 20) || inter > (1 << 20)) return KT_ERR_ARG;
   if (tokens * top_k > (int64_t)1 << 30) return KT_ERR_ARG;
   if (tokens == 0) return KT_OK;
@@ -285,7 +286,7 @@ KT_EXPORT int kt_moe_prefill_timed(const void* x, int64_t tokens, int64_t hidden
   };
   const int64_t R = tokens * top_k;
   if (cudaMemsetAsync(p.status, 0, sizeof(int), s) != cudaSuccess) return KT_ERR_CUDA;
-  int rc = kt_launch_permute(topk_ids, R, (int)top_k, n_slots, kt_gemm_tile_tokens(), p.counts, p.cursor, p.tiles,
+  int rc = kt_launch_permute(topk_ids, R, (int)top_k, n_slots, kt_gemm_tile_tokens(), p.counts, p.hist, p.tiles,
                              p.n_tiles, p.sorted_token, p.route_pos, s);
   if (rc) return launch_rc(rc);
   mark(0);

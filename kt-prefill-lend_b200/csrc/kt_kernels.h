@@ -42,9 +42,12 @@ int kt_launch_topk_softmax(const float* logits, int64_t T, int E, int k, int ren
 int kt_launch_topk_grouped(const float* logits, const float* bias, int64_t T, int E, int n_group, int topk_group, int k,
                            int renorm, float scale, float* weights, int32_t* ids, cudaStream_t s);
 
-// prefill permutation: routes sorted by slot, token tiles of kt_gemm_tile_tokens() rows
+// prefill permutation: routes sorted by slot, token tiles of kt_gemm_tile_tokens() rows;
+// hist holds kt_permute_hist_ints() ints; n_tiles[0] = tiles, n_tiles[1] = resident routes
+constexpr int kPermMaxSlots = 8192;
+int64_t kt_permute_hist_ints(int64_t routes, int n_slots);
 int kt_launch_permute(const int32_t* ids, int64_t routes, int top_k, int n_slots, int tile_tokens, int32_t* counts,
-                      int32_t* cursor, int32_t* tiles, int32_t* n_tiles, int32_t* sorted_token, int32_t* route_pos,
+                      int32_t* hist, int32_t* tiles, int32_t* n_tiles, int32_t* sorted_token, int32_t* route_pos,
                       cudaStream_t s);
 
 int kt_launch_gemm_gate_up(int type, const void* x, int64_t T, int K, int N, const void* w13, int table, int n_slots,

@@ -44,7 +44,10 @@
 
 namespace {
 
-constexpr int kGatherWarps = 2;  // phase 1: two warps gather token rows
+#ifndef KT_GATHER_WARPS
+#define KT_GATHER_WARPS 2
+#endif
+constexpr int kGatherWarps = KT_GATHER_WARPS;  // phase 1: warps gathering token rows
 
 // Warp roles per phase. Phase 1 runs 8 producer warps (two threads per A row) beside its two
 // gather warps: more producers take issue slots from the gathers, which bound phase 1.
@@ -54,9 +57,10 @@ template <int PHASE>
 struct Roles {
   static constexpr int kProd = PHASE == 1 ? 8 : 16;           // producer warps
   static constexpr int kRaw = kProd, kB = kProd + 1, kMma = kProd + 2, kEpi0 = kProd + 3;
-  static constexpr int kB2 = PHASE == 1 ? kProd + 7 : -1;     // second gather warp
-  static constexpr int kThreads = 32 * (PHASE == 1 ? kProd + 8 : kProd + 7);
-  static constexpr int kQuarters = 4 * 128 / (32 * kProd);  // k-step quarters per producer thread
+  static constexpr int kB2 = PHASE == 1 ? kProd + 7 : -1;     // further gather warps: kB2, kB2 + 1, ...
+  static constexpr int kThreads = 32 * (PHASE == 1 ? kProd + 6 + kGatherWarps : kProd + 7);
+  static constexpr int kQuarters = 4 * 128 / (32 * kProd);  // k-step quarters per producer thread (2 or 1)
+  static_assert(kQuarters == 1 || kQuarters == 2, "two or four producer threads per A row");
 };
 constexpr int kTN = 256;           // tokens per tile (MMA N, split between the pair)
 constexpr int kHalfN = kTN / 2;    // B rows held by each CTA
@@ -229,6 +233,7 @@ __global__ void __launch_bounds__(Roles<PHASE>::kThreads, 1) kt_moe_gemm_kernel(
           if (ok && !kt_mbar_wait(&empty[s], (((kit + kk) / kStages) & 1) ^ 1, a.status, abort_flag)) ok = false;
           if (ok) {
             uint8_t* arow = sA + s * kAStageBytes;
+            // quarters beat one wider half per thread here: more independent loads in flight
 #pragma unroll
             for (int j = 0; j < RL::kQuarters; ++j) {
               uint32_t pk[8];
@@ -298,9 +303,9 @@ __global__ void __launch_bounds__(Roles<PHASE>::kThreads, 1) kt_moe_gemm_kernel(
                       reinterpret_cast<const void*>(src[i]), len[i], &raw_full[su]);
       }
     }
-  } else if (warp == kWarpB || (PHASE == 1 && warp == kWarpB2)) {
+  } else if (warp == kWarpB || (PHASE == 1 && warp >= kWarpB2)) {
     // ---------------------------------------------------------------- B loaders
-    const int gw = warp == kWarpB ? 0 : 1;
+    const int gw = warp == kWarpB ? 0 : 1 + (warp - kWarpB2);
     constexpr int NR = kHalfN / (4 * kGatherWarps);  // rows per lane per k-step (phase 1)
     uint32_t kit = 0;
     for (int item = first_item; item < n_items && !*abort_flag; item += item_stride) {

@@ -128,24 +128,35 @@ int kt_launch_combine(const void* out, int dtype, const float* w, int64_t T, int
 // the fp32 router weight and fp32 accumulation in k order, rounded once (the finalize of the
 // CUTLASS fused MoE that the reference's streamed prefill runs; the decode combine above keeps
 // the hot method's per-route bf16 roundings). Each thread produces 8 consecutive columns.
+template <int KMAX>
 __global__ void kt_combine_sorted_kernel(const uint16_t* __restrict__ y, const int32_t* __restrict__ route_pos,
                                          const float* __restrict__ w, int64_t T, int top_k, int64_t K,
                                          uint16_t* __restrict__ res) {
   const int64_t t = blockIdx.x;
+  // the token's routes: positions and weights (KMAX >= top_k), then all row loads in flight
+  int32_t pos[KMAX];
+  float wk[KMAX];
+#pragma unroll
+  for (int k = 0; k < KMAX; ++k) {
+    pos[k] = k < top_k ? route_pos[t * top_k + k] : -1;
+    wk[k] = k < top_k ? w[t * top_k + k] : 0.0f;
+  }
   for (int64_t c = (int64_t)threadIdx.x * 8; c < K; c += (int64_t)blockDim.x * 8) {
+    uint4 v[KMAX];
+#pragma unroll
+    for (int k = 0; k < KMAX; ++k)
+      v[k] = pos[k] >= 0 ? __ldcs(reinterpret_cast<const uint4*>(y + (int64_t)pos[k] * K + c)) : make_uint4(0, 0, 0, 0);
     float acc[8];
 #pragma unroll
     for (int j = 0; j < 8; ++j) acc[j] = 0.0f;
-    for (int k = 0; k < top_k; ++k) {
-      const int32_t pos = route_pos[t * top_k + k];
-      if (pos < 0) continue;  // bf16(0 * w) adds an exact zero
-      const float wk = w[t * top_k + k];
-      const uint4 v = *reinterpret_cast<const uint4*>(y + (int64_t)pos * K + c);
-      const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int k = 0; k < KMAX; ++k) {
+      if (pos[k] < 0) continue;  // bf16(0 * w) adds an exact zero
+      const uint32_t u[4] = {v[k].x, v[k].y, v[k].z, v[k].w};
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        acc[2 * j] += kt_bf2f((uint16_t)(u[j] & 0xffff)) * wk;
-        acc[2 * j + 1] += kt_bf2f((uint16_t)(u[j] >> 16)) * wk;
+        acc[2 * j] += kt_bf2f((uint16_t)(u[j] & 0xffff)) * wk[k];
+        acc[2 * j + 1] += kt_bf2f((uint16_t)(u[j] >> 16)) * wk[k];
       }
     }
     uint4 o;
@@ -160,10 +171,18 @@ __global__ void kt_combine_sorted_kernel(const uint16_t* __restrict__ y, const i
 int kt_launch_combine_sorted(const uint16_t* y, const int32_t* route_pos, const float* w, int64_t T, int64_t top_k,
                              int64_t K, uint16_t* res, cudaStream_t s) {
   if (T == 0) return 0;
-  if (K % 8 || T > 0x7fffffff) return -1;
+  if (K % 8 || T > 0x7fffffff || top_k > 32) return -1;
   const int64_t vec = K / 8;
   const int threads = (int)(vec < 256 ? (vec + 31) / 32 * 32 : 256);
-  kt_combine_sorted_kernel<<<(unsigned)T, threads, 0, s>>>(y, route_pos, w, T, (int)top_k, K, res);
+  const int k = (int)top_k;
+  if (k <= 4)
+    kt_combine_sorted_kernel<4><<<(unsigned)T, threads, 0, s>>>(y, route_pos, w, T, k, K, res);
+  else if (k <= 8)
+    kt_combine_sorted_kernel<8><<<(unsigned)T, threads, 0, s>>>(y, route_pos, w, T, k, K, res);
+  else if (k <= 16)
+    kt_combine_sorted_kernel<16><<<(unsigned)T, threads, 0, s>>>(y, route_pos, w, T, k, K, res);
+  else
+    kt_combine_sorted_kernel<32><<<(unsigned)T, threads, 0, s>>>(y, route_pos, w, T, k, K, res);
   return 0;
 }
 
@@ -382,45 +401,134 @@ int kt_launch_topk_grouped(const float* logits, const float* bias, int64_t T, in
 }
 
 // ------------------------------------------------------------------ permute for the prefill GEMM
-// counts[n_slots] (zeroed by the count kernel's caller), then one CTA scans them into the
-// tile list, then every route gets its sorted position.
+// Three kernels, no global atomics:
+//   hist     one block per kPermBlock routes: shared-memory histogram over slots with
+//            warp-aggregated atomics; each route keeps its rank among the block's routes of
+//            its slot (in route_pos, temporarily); the block's histogram goes to hist[b][*]
+//   scan     one block: per slot, exclusive prefix over blocks (hist becomes each block's
+//            first position per slot) plus the slot's base (exclusive prefix over slots);
+//            counts[] and the token tiles (<= tile_tokens rows each, in slot order)
+//   scatter  position = hist[b][slot] + rank: sorted_token[pos], route_pos[route]
+constexpr int kPermBlock = 1024;
 
-__global__ void kt_perm_count_kernel(const int32_t* __restrict__ ids, int64_t routes, int n_slots,
-                                     int32_t* __restrict__ counts) {
-  const int64_t p = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (p >= routes) return;
-  const int32_t e = ids[p];
-  if (e >= 0 && e < n_slots) atomicAdd(&counts[e], 1);
+__global__ void __launch_bounds__(kPermBlock) kt_perm_hist_kernel(const int32_t* __restrict__ ids, int64_t routes,
+                                                                  int n_slots, int32_t* __restrict__ hist,
+                                                                  int32_t* __restrict__ rank) {
+  extern __shared__ int32_t sh[];
+  for (int e = threadIdx.x; e < n_slots; e += blockDim.x) sh[e] = 0;
+  __syncthreads();
+  const int64_t p = (int64_t)blockIdx.x * kPermBlock + threadIdx.x;
+  const int32_t e = p < routes ? ids[p] : -1;
+  const bool valid = e >= 0 && e < n_slots;
+  const int lane = threadIdx.x & 31;
+  const uint32_t peers = __match_any_sync(0xffffffffu, valid ? e : -1);
+  const int leader = __ffs(peers) - 1;
+  int base = 0;
+  if (valid && lane == leader) base = atomicAdd(&sh[e], __popc(peers));
+  base = __shfl_sync(0xffffffffu, base, leader);
+  if (p < routes) rank[p] = valid ? base + __popc(peers & ((1u << lane) - 1)) : -1;
+  __syncthreads();
+  for (int e2 = threadIdx.x; e2 < n_slots; e2 += blockDim.x) hist[(int64_t)blockIdx.x * n_slots + e2] = sh[e2];
 }
 
-__global__ void kt_perm_scan_kernel(const int32_t* __restrict__ counts, int n_slots, int tile_tokens,
-                                    int32_t* __restrict__ cursor, int32_t* __restrict__ tiles,
-                                    int32_t* __restrict__ n_tiles) {
-  // single thread: n_slots is at most a few thousand
-  if (threadIdx.x != 0) return;
-  int32_t off = 0, nt = 0;
-  for (int e = 0; e < n_slots; ++e) {
-    const int32_t c = counts[e];
-    cursor[e] = off;
-    for (int32_t r = 0; r < c; r += tile_tokens) {
-      tiles[3 * nt + 0] = e;
-      tiles[3 * nt + 1] = off + r;
-      tiles[3 * nt + 2] = min(tile_tokens, c - r);
-      ++nt;
+// exclusive scan of v over the block (1024 threads); returns the total in *total
+__device__ __forceinline__ int32_t kt_block_exclusive_scan(int32_t v, int32_t* warp_sums, int32_t* total) {
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  int32_t x = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int32_t y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
+  }
+  if (lane == 31) warp_sums[wid] = x;
+  __syncthreads();
+  if (wid == 0) {
+    int32_t w = lane < (int)(blockDim.x >> 5) ? warp_sums[lane] : 0;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int32_t y = __shfl_up_sync(0xffffffffu, w, o);
+      if (lane >= o) w += y;
     }
+    warp_sums[lane] = w;  // inclusive
+  }
+  __syncthreads();
+  const int32_t excl = x - v + (wid > 0 ? warp_sums[wid - 1] : 0);
+  *total = warp_sums[(blockDim.x >> 5) - 1];
+  __syncthreads();
+  return excl;
+}
+
+// warp w handles slots w, w + 32, ...; lanes walk the blocks (independent loads in flight)
+__global__ void __launch_bounds__(kPermBlock) kt_perm_scan_kernel(int32_t* __restrict__ hist, int n_blocks, int n_slots,
+                                                                  int tile_tokens, int32_t* __restrict__ counts,
+                                                                  int32_t* __restrict__ tiles,
+                                                                  int32_t* __restrict__ n_tiles) {
+  __shared__ int32_t warp_sums[32];
+  __shared__ int32_t sbase[kPermMaxSlots];
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  // 1. per-slot totals
+  for (int e = wid; e < n_slots; e += nw) {
+    int32_t v = 0;
+    for (int b = lane; b < n_blocks; b += 32) v += hist[(int64_t)b * n_slots + e];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    if (lane == 0) counts[e] = v;
+  }
+  __syncthreads();
+  // 2. slot bases and tile offsets: exclusive scans over the slots (thread t owns [e0, e1))
+  const int per = (n_slots + blockDim.x - 1) / blockDim.x;
+  const int e0 = min(n_slots, (int)threadIdx.x * per), e1 = min(n_slots, e0 + per);
+  int32_t my_routes = 0, my_tiles = 0;
+  for (int e = e0; e < e1; ++e) {
+    my_routes += counts[e];
+    my_tiles += (counts[e] + tile_tokens - 1) / tile_tokens;
+  }
+  int32_t total_routes, total_tiles;
+  int32_t off = kt_block_exclusive_scan(my_routes, warp_sums, &total_routes);
+  int32_t t = kt_block_exclusive_scan(my_tiles, warp_sums, &total_tiles);
+  for (int e = e0; e < e1; ++e) {
+    const int32_t c = counts[e];
+    for (int32_t r = 0; r < c; r += tile_tokens, ++t) {
+      tiles[3 * t + 0] = e;
+      tiles[3 * t + 1] = off + r;
+      tiles[3 * t + 2] = min(tile_tokens, c - r);
+    }
+    sbase[e] = off;
     off += c;
   }
-  *n_tiles = nt;
+  __syncthreads();
+  // 3. hist[b][e] <- base(e) + routes of slot e in the blocks before b
+  for (int e = wid; e < n_slots; e += nw) {
+    int32_t carry = sbase[e];
+    for (int b0 = 0; b0 < n_blocks; b0 += 32) {
+      const int b = b0 + lane;
+      const int32_t v = b < n_blocks ? hist[(int64_t)b * n_slots + e] : 0;
+      int32_t x = v;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int32_t y = __shfl_up_sync(0xffffffffu, x, o);
+        if (lane >= o) x += y;
+      }
+      if (b < n_blocks) hist[(int64_t)b * n_slots + e] = carry + x - v;
+      carry += __shfl_sync(0xffffffffu, x, 31);
+    }
+  }
+  if (threadIdx.x == 0) {
+    n_tiles[0] = total_tiles;
+    n_tiles[1] = total_routes;
+  }
 }
 
-__global__ void kt_perm_scatter_kernel(const int32_t* __restrict__ ids, int64_t routes, int top_k, int n_slots,
-                                       int32_t* __restrict__ cursor, int32_t* __restrict__ sorted_token,
-                                       int32_t* __restrict__ route_pos) {
-  const int64_t p = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+__global__ void __launch_bounds__(kPermBlock) kt_perm_scatter_kernel(const int32_t* __restrict__ ids, int64_t routes,
+                                                                     int top_k, int n_slots,
+                                                                     const int32_t* __restrict__ hist,
+                                                                     int32_t* __restrict__ sorted_token,
+                                                                     int32_t* __restrict__ route_pos) {
+  const int64_t p = (int64_t)blockIdx.x * kPermBlock + threadIdx.x;
   if (p >= routes) return;
   const int32_t e = ids[p];
   if (e >= 0 && e < n_slots) {
-    const int32_t pos = atomicAdd(&cursor[e], 1);
+    const int32_t pos = hist[(int64_t)blockIdx.x * n_slots + e] + route_pos[p];
     sorted_token[pos] = (int32_t)(p / top_k);
     route_pos[p] = pos;
   } else {
@@ -428,13 +536,17 @@ __global__ void kt_perm_scatter_kernel(const int32_t* __restrict__ ids, int64_t 
   }
 }
 
+int64_t kt_permute_hist_ints(int64_t routes, int n_slots) { return ((routes + kPermBlock - 1) / kPermBlock) * n_slots; }
+
 int kt_launch_permute(const int32_t* ids, int64_t routes, int top_k, int n_slots, int tile_tokens, int32_t* counts,
-                      int32_t* cursor, int32_t* tiles, int32_t* n_tiles, int32_t* sorted_token, int32_t* route_pos,
+                      int32_t* hist, int32_t* tiles, int32_t* n_tiles, int32_t* sorted_token, int32_t* route_pos,
                       cudaStream_t s) {
-  if (cudaMemsetAsync(counts, 0, sizeof(int32_t) * n_slots, s) != cudaSuccess) return -3;
-  const unsigned blocks = (unsigned)((routes + 255) / 256);
-  if (routes > 0) kt_perm_count_kernel<<<blocks, 256, 0, s>>>(ids, routes, n_slots, counts);
-  kt_perm_scan_kernel<<<1, 32, 0, s>>>(counts, n_slots, tile_tokens, cursor, tiles, n_tiles);
-  if (routes > 0) kt_perm_scatter_kernel<<<blocks, 256, 0, s>>>(ids, routes, top_k, n_slots, cursor, sorted_token, route_pos);
+  if (n_slots <= 0 || n_slots > kPermMaxSlots) return -1;
+  const int nb = (int)((routes + kPermBlock - 1) / kPermBlock);
+  if (nb > 0)
+    kt_perm_hist_kernel<<<nb, kPermBlock, n_slots * sizeof(int32_t), s>>>(ids, routes, n_slots, hist, route_pos);
+  kt_perm_scan_kernel<<<1, kPermBlock, 0, s>>>(hist, nb, n_slots, tile_tokens, counts, tiles, n_tiles);
+  if (nb > 0)
+    kt_perm_scatter_kernel<<<nb, kPermBlock, 0, s>>>(ids, routes, top_k, n_slots, hist, sorted_token, route_pos);
   return 0;
 }

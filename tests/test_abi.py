@@ -64,6 +64,9 @@ def test_argument_errors_before_any_launch():
                               None) == N.KT_ERR_TYPE
     assert lib.kt_moe_prefill(P(16), 16, 2048, 512, P(16), P(16), 8, P(16), 12, P(16), 14, 0, 64, P(16), P(16), 64,
                               None) == N.KT_ERR_WORKSPACE
+    # the permute keeps a shared-memory histogram over slots: at most 8192 slots
+    assert lib.kt_moe_prefill(P(16), 16, 2048, 512, P(16), P(16), 8, P(16), 12, P(16), 14, 0, 8193, P(16), P(16),
+                              1 << 40, None) == N.KT_ERR_ARG
     assert lib.kt_topk_softmax(None, 0, 256, 8, 0, None, None, None) == N.KT_OK
 
 
