@@ -13,6 +13,11 @@ rank processes its own 16K-token chunk against its own replica of the resident e
 (token-parallel, no data-path collective: "scaling": "weak"); the time is the max over
 ranks of CUDA-event time.
 
+--config 1 / 3 print the other BASELINE configurations (one JSON line per point): config 1
+(Q8_0, 256 tokens, with the CPU baseline on the whole chunk and the rel-L2 against the fp32
+oracle) and config 3 (IQ3_S, 512 experts top-10: the decode GEMV at M = 1, 4, 16, 64 against
+the HBM roofline with L2 flushed before every call, and the prefill GEMMs at M = 2048, 16384).
+
 --impl reference times the reference's CPU implementation of the path as restated in
 oracle/ (the reference's own CPU expert library, kt-kernel + llama.cpp, ships only as
 patches on un-vendored sources and cannot be built here) on the host cores.
@@ -48,6 +53,13 @@ def parse():
     ap.add_argument("--cpu-sample", type=int, default=256, help="tokens per CPU-baseline sample")
     ap.add_argument("--tokens", type=int, default=16384, help="chunk size (profiling runs use smaller chunks)")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end pass (profiling)")
+    ap.add_argument("--config", type=int, default=2, choices=[1, 2, 3],
+                    help="2: the headline line (default); 1 and 3: the other BASELINE configs, one JSON line per point")
+    ap.add_argument("--m-list", default="1,4,16,64,2048,16384",
+                    help="sweep token counts (config 3, or config 2 with --sweep): below 128 the decode GEMV, "
+                         "from 128 the prefill GEMMs")
+    ap.add_argument("--sweep", action="store_true", help="config 2: run the decode/prefill sweep instead of the "
+                                                         "headline line")
     return ap.parse_args()
 
 
@@ -389,6 +401,169 @@ def run_b200(args, rank, world, local_rank):
         dist.destroy_process_group()
 
 
+def _gemv_call(lib, Nt, x, w, ids, top_k, qtype, rows, tokens, y, ws, stream):
+    Nt.check(lib.kt_moe_a8_vec_multi(Nt.ptr(x), Nt.dtype_code(x), tokens, x.shape[1], Nt.ptr(w), 0, w.shape[0],
+                                     Nt.ptr(ids), top_k, qtype, rows, Nt.ptr(y), Nt.ptr(ws), ws.numel(), stream),
+             "kt_moe_a8_vec_multi")
+
+
+def run_sweep(args, cfg_id):
+    """Decode GEMV points (HBM roofline, L2 flushed before every call) and prefill points
+    (tensor roofline) on one config's layer: config 3 (IQ3_S, 512 experts all resident,
+    top-10) or config 2 (Q4_K/Q6_K, 64 of 256 experts resident, top-8)."""
+    import numpy as np
+    import torch
+
+    from kt_gguf_b200 import _native as Nt
+    from kt_gguf_b200 import kernels as Kn
+    from kt_gguf_b200 import kt_gguf_moe_multi as M
+    from kt_gguf_b200 import synth
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    cfg = synth.CONFIGS[cfg_id]
+    L = synth.make_layer(args.seed, **cfg)
+    K, N, k = cfg["hidden"], cfg["inter"], cfg["top_k"]
+    E = L.w13.shape[0]  # resident slots
+    t13, t2 = L.type13, L.type2
+    w13 = torch.from_numpy(L.w13).to(dev)
+    w2 = torch.from_numpy(L.w2).to(dev)
+    x_all = L.x.to(dev)
+    ids_all = L.topk_ids.to(dev)
+    w_all = L.topk_weights.to(dev)
+    lib = Nt.load()
+    stream = torch.cuda.current_stream(dev)
+    hbm, tf_burst, tf_sust, peak_kind = load_peaks()
+    b13 = w13.shape[1] * w13.shape[2]  # bytes of one expert's gate/up rows
+    b2 = w2.shape[1] * w2.shape[2]
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)  # 2x the L2
+    names = {3: "flash-next-like IQ3_S MoE layer (BASELINE configs[2])", 2: CONFIG_NAME}
+    base = {"metric": f"config {cfg_id} point", "config": {"workload": names[cfg_id], "hidden": K, "inter": N,
+                                                           "experts": cfg["n_experts"], "resident": E, "top_k": k,
+                                                           "types": f"ggml {t13} gate/up, {t2} down"},
+            "data": "synthetic (seeded)"}
+    iters = max(20, min(args.steps, 200))
+    m_list = [int(v) for v in args.m_list.split(",") if v]
+    for Mtok in [m for m in m_list if m < 128]:
+        ws13 = Nt.workspace(lib.kt_moe_a8_vec_workspace_size(Mtok, K, Mtok * k, E), dev)
+        ws2 = Nt.workspace(lib.kt_moe_a8_vec_workspace_size(Mtok * k, N, Mtok * k, E), dev)
+        h13 = torch.empty((Mtok * k, 2 * N), dtype=torch.bfloat16, device=dev)
+        y = torch.empty((Mtok * k, K), dtype=torch.bfloat16, device=dev)
+        s13, s2, tl, uniq = [], [], [], []
+        for it in range(args.warmup + iters):
+            r0 = (it * Mtok) % (x_all.shape[0] - Mtok)  # a different window each call: different experts
+            x = x_all[r0:r0 + Mtok]
+            ids = ids_all[r0:r0 + Mtok].reshape(-1).contiguous()
+            flush.zero_()
+            ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+            ev[0].record(stream)
+            _gemv_call(lib, Nt, x, w13, ids, k, t13, 2 * N, Mtok, h13, ws13, stream.cuda_stream)
+            ev[1].record(stream)
+            h = Kn.silu_and_mul(h13)
+            ev[2].record(stream)
+            _gemv_call(lib, Nt, h, w2, ids, 1, t2, K, Mtok * k, y, ws2, stream.cuda_stream)
+            ev[3].record(stream)
+            Kn.combine(y.view(Mtok, k, K), w_all[r0:r0 + Mtok])
+            torch.cuda.synchronize()
+            if it >= args.warmup:
+                s13.append(ev[0].elapsed_time(ev[1]))
+                s2.append(ev[2].elapsed_time(ev[3]))
+                tl.append(ev[0].elapsed_time(ev[3]))
+                u_ids = torch.unique(ids)
+                uniq.append(int((u_ids >= 0).sum()))
+        u = statistics.mean(uniq)
+        g13 = u * b13 / (statistics.median(s13) * 1e-3) / 1e9
+        g2 = u * b2 / (statistics.median(s2) * 1e-3) / 1e9
+        line = dict(base, path="decode GEMV (q8_1 x GGUF, reference arithmetic)", M=Mtok,
+                    unique_experts=u, ms_gate_up=statistics.median(s13), ms_down=statistics.median(s2),
+                    ms_layer_without_combine=statistics.median(tl),
+                    roofline={"bound": "hbm", "gate_up_GBps": g13, "down_GBps": g2, "peak": hbm, "unit": "GB/s",
+                              "gate_up_frac": g13 / hbm, "down_frac": g2 / hbm, "peak_kind": f"{peak_kind} copy",
+                              "bytes": "unique experts' GGUF bytes per call (gate/up %d B, down %d B per expert)" % (b13, b2)},
+                    l2="256 MB buffer written before every call", iters=iters)
+        print(json.dumps(line), flush=True)
+    for Mtok in [m for m in m_list if m >= 128]:
+        x = x_all[:Mtok].contiguous()
+        ids = ids_all[:Mtok].contiguous()
+        wts = w_all[:Mtok].contiguous()
+        ws = Nt.workspace(lib.kt_moe_prefill_workspace_size(Mtok, k, K, N, E), dev)
+        out = torch.empty((Mtok, K), dtype=torch.bfloat16, device=dev)
+        n = max(4, min(20, args.steps))
+        evs = [[torch.cuda.Event(enable_timing=True) for _ in range(5)] for _ in range(args.warmup + n)]
+        for e in (e for es in evs for e in es):
+            e.record(stream)
+        hs = [(ctypes.c_void_p * 4)(*[e.cuda_event for e in es[1:]]) for es in evs]
+        for i in range(args.warmup + n):
+            evs[i][0].record(stream)
+            Nt.check(lib.kt_moe_prefill_timed(Nt.ptr(x), Mtok, K, N, Nt.ptr(ids), Nt.ptr(wts), k, Nt.ptr(w13), t13,
+                                              Nt.ptr(w2), t2, 0, E, Nt.ptr(out), Nt.ptr(ws), ws.numel(),
+                                              stream.cuda_stream, hs[i]), "kt_moe_prefill")
+        torch.cuda.synchronize()
+        assert Nt.workspace_status(ws) == Nt.KT_DEV_OK
+        st = [statistics.median(evs[i][j].elapsed_time(evs[i][j + 1]) for i in range(args.warmup, args.warmup + n))
+              for j in range(4)]
+        R = int((L.topk_ids[:Mtok] >= 0).sum())  # resident routes
+        tf13 = 4.0 * K * N * R / (st[1] * 1e-3) / 1e12
+        tf2 = 2.0 * K * N * R / (st[2] * 1e-3) / 1e12
+        line = dict(base, path="prefill (tcgen05 GEMMs)", M=Mtok, value=Mtok / (sum(st) * 1e-3), unit="tokens/s",
+                    stage_ms={"permute": st[0], "gate_up_gemm": st[1], "down_gemm": st[2], "combine": st[3]},
+                    roofline={"bound": "tensor", "gate_up_tflops": tf13, "down_tflops": tf2, "peak": tf_burst,
+                              "unit": "TFLOP/s", "gate_up_frac": tf13 / tf_burst, "down_frac": tf2 / tf_burst,
+                              "peak_kind": f"{peak_kind} bf16 burst (cuBLAS)"})
+        print(json.dumps(line), flush=True)
+
+
+def run_config1(args):
+    """Q8_0, 16 experts top-4, 256 tokens: GPU layer, CPU baseline on the whole chunk, parity."""
+    import numpy as np
+    import torch
+
+    from kt_gguf_b200 import _native as Nt
+    from kt_gguf_b200 import kt_gguf_moe_multi as M
+    from kt_gguf_b200 import synth
+    from oracle import oracle as O
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    cfg = synth.CONFIGS[1]
+    L = synth.make_layer(args.seed, **cfg)
+    K, N, k = cfg["hidden"], cfg["inter"], cfg["top_k"]
+    x, ids, wts = L.x.to(dev), L.topk_ids.to(dev), L.topk_weights.to(dev)
+    w13, w2 = torch.from_numpy(L.w13).to(dev), torch.from_numpy(L.w2).to(dev)
+    lib = Nt.load()
+    T = x.shape[0]
+    ws = Nt.workspace(lib.kt_moe_prefill_workspace_size(T, k, K, N, w13.shape[0]), dev)
+    out = torch.empty((T, K), dtype=torch.bfloat16, device=dev)
+    for _ in range(args.warmup):
+        M.moe_prefill(x, w13, w2, ids, wts, 8, 8, N, out=out, workspace=ws)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        M.moe_prefill(x, w13, w2, ids, wts, 8, 8, N, out=out, workspace=ws)
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    xb = L.x.view(torch.int16).numpy().view(np.uint16)
+    want = O.moe_fp32(xb, L.topk_ids.numpy(), L.topk_weights.numpy(), 8, L.w13, 8, L.w2, N)
+    err = O.rel_l2(out.float().cpu().numpy(), want)
+    O.build()
+    threads = host_threads()
+    os.environ["OMP_NUM_THREADS"] = str(threads)
+    O.moe_ref_bf16(xb[:8], L.topk_ids.numpy()[:8], L.topk_weights.numpy()[:8], 8, L.w13, 8, L.w2, N)
+    t = time.perf_counter()
+    O.moe_ref_bf16(xb, L.topk_ids.numpy(), L.topk_weights.numpy(), 8, L.w13, 8, L.w2, N)
+    cpu_s = time.perf_counter() - t
+    line = {"metric": "config 1 layer", "value": T / (ms * 1e-3), "unit": "tokens/s", "ms_per_step": ms,
+            "steps": args.steps, "config": {"workload": "Q8_0 MoE layer (BASELINE configs[0])", "tokens": T,
+                                             "hidden": K, "inter": N, "experts": cfg["n_experts"], "top_k": k},
+            "rel_l2_vs_fp32_oracle": err, "tolerance": 5e-3,
+            "cpu_baseline": {"value": T / cpu_s, "unit": "tokens/s", "cores": threads, "kind": "port",
+                             "sample": "the whole 256-token chunk"},
+            "data": "synthetic (seeded)"}
+    print(json.dumps(line), flush=True)
+
+
 def main():
     args = parse()
     rank = int(os.environ.get("RANK", "0"))
@@ -396,6 +571,12 @@ def main():
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
         run_reference(args, rank)
+        return
+    if args.config == 3 or (args.config == 2 and args.sweep):
+        run_sweep(args, args.config)
+        return
+    if args.config == 1:
+        run_config1(args)
         return
     run_b200(args, rank, world, local_rank)
 

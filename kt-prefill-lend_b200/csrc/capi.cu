@@ -77,13 +77,13 @@ int moe_vec(const void* x, int x_dtype, int64_t tokens, int64_t cols, const void
   if (ws_bytes < v.bytes) return KT_ERR_WORKSPACE;
   cudaStream_t s = S(stream);
   if (cudaMemsetAsync(v.status, 0, sizeof(int), s) != cudaSuccess) return KT_ERR_CUDA;
-  int rc = kt_launch_quantize_q8_1(x, x_dtype, tokens, cols, v.qx, s);
+  int rc = kt_launch_quantize_q8_1_split(x, x_dtype, tokens, cols, v.qx, s);
   if (rc) return launch_rc(rc);
   rc = kt_launch_group_routes(ids, routes, n_slots, v.groups, v.order, s);
   if (rc) return launch_rc(rc);
   const int max_groups = (int)(routes < (int64_t)n_slots + 1 ? routes : (int64_t)n_slots + 1);
   rc = kt_launch_moe_vec(type, w, table, v.qx, kt_q8_1_row_bytes(cols), v.groups, v.order, max_groups, (int)top_k,
-                         (int)rows, (int)cols, x_dtype, y, s);
+                         (int)rows, (int)cols, x_dtype, y, v.status, s);
   return launch_rc(rc);
 }
 

@@ -31,20 +31,25 @@ struct KtChunk<KT_IQ3_S> {
   static constexpr int QK = 256, BYTES = 110, CPB = 8, VDR = 1;
 };
 
-__device__ __forceinline__ float kt_q8_1_d(const uint8_t* b8) { return __low2float(*reinterpret_cast<const half2*>(b8)); }
+// Activations reach the dot products in the GEMV's split q8_1 layout: per token row, the
+// int8 values of all 32-value blocks (block b at byte 32*b, 16-byte aligned rows), then the
+// (d, s) half2 of every block (block b at byte kpad + 4*b). Values and scales are those of
+// the reference's q8_1 blocks; only their placement differs. yq / yd point at the first
+// q8_1 block a chunk uses.
+__device__ __forceinline__ float kt_q8_1_dd(const uint8_t* yd) { return __low2float(*reinterpret_cast<const half2*>(yd)); }
 
 // ---- Q8_0: d_w * d_a * sum(q_w * q_a) over 8 values (iqs in {0,2,4,6})
-__device__ __forceinline__ float kt_vd_q8_0(const uint8_t* bx, const uint8_t* by, int iqs) {
+__device__ __forceinline__ float kt_vd_q8_0(const uint8_t* bx, const uint8_t* yq, const uint8_t* yd, int iqs) {
   int sumi = 0;
 #pragma unroll
-  for (int i = 0; i < 2; ++i) sumi = __dp4a(kt_ld_b2(bx + 2 + 4 * (iqs + i)), kt_ld_b4(by + 4 + 4 * (iqs + i)), sumi);
+  for (int i = 0; i < 2; ++i) sumi = __dp4a(kt_ld_b2(bx + 2 + 4 * (iqs + i)), kt_ld_b4(yq + 4 * (iqs + i)), sumi);
   const float d80 = kt_h2f(*reinterpret_cast<const uint16_t*>(bx));
-  const float d81 = kt_q8_1_d(by);
+  const float d81 = kt_q8_1_dd(yd);
   return d80 * d81 * sumi;
 }
 
 // ---- Q4_K: 16 values from sub-blocks (bq8_offset, bq8_offset + 1); iqs in {0,2,...,30}
-__device__ __forceinline__ float kt_vd_q4_k(const uint8_t* bx, const uint8_t* by0, int iqs) {
+__device__ __forceinline__ float kt_vd_q4_k(const uint8_t* bx, const uint8_t* yq, const uint8_t* yd, int iqs) {
   const int bq8_offset = 2 * ((iqs / 2) / 4);
   const uint8_t* q4 = bx + 16 + 16 * bq8_offset + 4 * ((iqs / 2) % 4);
   const int v0 = kt_ld_b4(q4), v1 = kt_ld_b4(q4 + 16);
@@ -61,10 +66,10 @@ __device__ __forceinline__ float kt_vd_q4_k(const uint8_t* bx, const uint8_t* by
   float sumf_d = 0.0f, sumf_m = 0.0f;
 #pragma unroll
   for (int i = 0; i < 2; ++i) {
-    const uint8_t* b8 = by0 + KT_Q8_1_BYTES * (bq8_offset + i);
-    const float d8 = kt_q8_1_d(b8);
-    const int u0 = kt_ld_b4(b8 + 4 + 4 * ((iqs / 2) % 4));
-    const int u1 = kt_ld_b4(b8 + 4 + 4 * ((iqs / 2) % 4) + 16);
+    const uint8_t* q8 = yq + 32 * (bq8_offset + i);
+    const float d8 = kt_q8_1_dd(yd + 4 * (bq8_offset + i));
+    const int u0 = kt_ld_b4(q8 + 4 * ((iqs / 2) % 4));
+    const int u1 = kt_ld_b4(q8 + 4 * ((iqs / 2) % 4) + 16);
     const int v0i = (v0 >> (4 * i)) & 0x0F0F0F0F;
     const int v1i = (v1 >> (4 * i)) & 0x0F0F0F0F;
     const int dot1 = __dp4a(v1i, u1, __dp4a(v0i, u0, 0));
@@ -78,8 +83,10 @@ __device__ __forceinline__ float kt_vd_q4_k(const uint8_t* bx, const uint8_t* by
   return dm.x * sumf_d - dm.y * sumf_m;
 }
 
-// ---- Q6_K: 8 values; iqs in 0..31
-__device__ __forceinline__ float kt_vd_q6_k(const uint8_t* bx, const uint8_t* by0, int iqs) {
+// ---- Q6_K: 8 values; iqs in 0..31. The reference's per-byte (code - 32) with __vsubss4
+// never saturates (codes are 0..63), so the integer dot is dp4a(code, u) - 32 * sum(u),
+// computed here with two dp4a instead of the emulated SIMD subtract.
+__device__ __forceinline__ float kt_vd_q6_k(const uint8_t* bx, const uint8_t* yq, const uint8_t* yd, int iqs) {
   const int bq8_offset = 4 * (iqs / 16) + (iqs % 16) / 8;
   const int scale_offset = 8 * (iqs / 16) + (iqs % 16) / 4;
   const int vh_shift = 2 * ((iqs % 16) / 8);
@@ -89,49 +96,62 @@ __device__ __forceinline__ float kt_vd_q6_k(const uint8_t* bx, const uint8_t* by
   float sumf = 0.0f;
 #pragma unroll
   for (int i = 0; i < 2; ++i) {
-    const uint8_t* b8 = by0 + KT_Q8_1_BYTES * (bq8_offset + 2 * i);
-    const int u = kt_ld_b4(b8 + 4 + 4 * (iqs % 8));
-    const float d8 = kt_q8_1_d(b8);
+    const int u = kt_ld_b4(yq + 32 * (bq8_offset + 2 * i) + 4 * (iqs % 8));
+    const float d8 = kt_q8_1_dd(yd + 4 * (bq8_offset + 2 * i));
     const int sc = scales[4 * i];
     const int vil = (vl >> (4 * i)) & 0x0F0F0F0F;
     const int vih = ((vh >> (4 * i)) << 4) & 0x30303030;
-    const int vi = __vsubss4((vil | vih), 0x20202020);
-    sumf += d8 * (__dp4a(vi, u, 0) * sc);
+    const int dot = __dp4a(vil | vih, u, 0) - 32 * __dp4a(0x01010101, u, 0);
+    sumf += d8 * (dot * sc);
   }
   return kt_h2f(*reinterpret_cast<const uint16_t*>(bx + 208)) * sumf;
 }
 
-// ---- IQ3_S: one 32-value sub-block (ib32 = iqs in 0..7); grid from shared memory
-__device__ __forceinline__ float kt_vd_iq3_s(const uint8_t* bx, const uint8_t* by0, int ib32, const uint32_t* grid) {
-  const uint8_t* qs = bx + 2 + 8 * ib32;
-  const int qh = bx[66 + ib32];
-  const uint8_t* signs = bx + 74 + 4 * ib32;
-  const uint8_t* b8 = by0 + KT_Q8_1_BYTES * ib32;
-  const uint8_t* q8 = b8 + 4;
-  int sumi = 0;
+// byte j of the result is 0xFF when bit j of the nibble n is set (n < 16): the multiply
+// moves bit j to bit 8j, no carries
+__device__ __forceinline__ uint32_t kt_nibble_mask(uint32_t n) { return ((n * 0x00204081u) & 0x01010101u) * 0xffu; }
+
+// ---- IQ3_S: one 32-value sub-block (ib32 = iqs in 0..7); `grid` is the 512-entry codebook
+// in shared memory. The reference applies the signs per byte ((g ^ s) - s) before one dp4a
+// chain; the same integer is sum(g * q) - 2 * sum((g & s) * q), two plain dp4a chains
+// (grid magnitudes are < 128), with the byte masks s built from the sign bits in registers.
+__device__ __forceinline__ float kt_vd_iq3_s(const uint8_t* bx, const uint8_t* yq, const uint8_t* yd, int ib32,
+                                             const uint32_t* grid) {
+  yq += 32 * ib32;
+  yd += 4 * ib32;
+  const uint32_t qs0 = (uint32_t)kt_ld_b2(bx + 2 + 8 * ib32), qs1 = (uint32_t)kt_ld_b2(bx + 6 + 8 * ib32);
+  const uint32_t qh = bx[66 + ib32];
+  const uint32_t sg = (uint32_t)kt_ld_b2(bx + 74 + 4 * ib32);
+  const int4 a0 = *reinterpret_cast<const int4*>(yq);
+  const int4 a1 = *reinterpret_cast<const int4*>(yq + 16);
+  const int q[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+  int sum_all = 0, sum_neg = 0;
 #pragma unroll
   for (int l = 0; l < 4; ++l) {
-    const uint32_t g1 = grid[qs[2 * l + 0] | ((qh << (8 - 2 * l)) & 256)];
-    const uint32_t g2 = grid[qs[2 * l + 1] | ((qh << (7 - 2 * l)) & 256)];
-    const uint32_t s0 = __vcmpeq4(((signs[l] & 0xf) * 0x01010101u) & 0x08040201u, 0x08040201u);
-    const uint32_t s1 = __vcmpeq4(((signs[l] >> 4) * 0x01010101u) & 0x08040201u, 0x08040201u);
-    const int gl = (int)__vsub4(g1 ^ s0, s0);
-    const int gh = (int)__vsub4(g2 ^ s1, s1);
-    sumi = __dp4a(gl, kt_ld_b4(q8 + 0), sumi);
-    sumi = __dp4a(gh, kt_ld_b4(q8 + 4), sumi);
-    q8 += 8;
+    const uint32_t w = l < 2 ? qs0 : qs1;
+    const uint32_t b1 = (w >> (16 * (l & 1))) & 0xff, b2 = (w >> (16 * (l & 1) + 8)) & 0xff;
+    const int g1 = (int)grid[b1 | ((qh << (8 - 2 * l)) & 256)];
+    const int g2 = (int)grid[b2 | ((qh << (7 - 2 * l)) & 256)];
+    const uint32_t sb = sg >> (8 * l);
+    const int m1 = (int)kt_nibble_mask(sb & 15), m2 = (int)kt_nibble_mask((sb >> 4) & 15);
+    sum_all = __dp4a(g1, q[2 * l], sum_all);
+    sum_all = __dp4a(g2, q[2 * l + 1], sum_all);
+    sum_neg = __dp4a(g1 & m1, q[2 * l], sum_neg);
+    sum_neg = __dp4a(g2 & m2, q[2 * l + 1], sum_neg);
   }
-  const float d =
-      kt_h2f(*reinterpret_cast<const uint16_t*>(bx)) * (1 + 2 * ((bx[106 + ib32 / 2] >> 4 * (ib32 % 2)) & 0xf)) * kt_q8_1_d(b8);
+  const int sumi = sum_all - 2 * sum_neg;
+  const float d = kt_h2f(*reinterpret_cast<const uint16_t*>(bx)) * (1 + 2 * ((bx[106 + ib32 / 2] >> 4 * (ib32 % 2)) & 0xf)) *
+                  kt_q8_1_dd(yd);
   return d * sumi;
 }
 
 template <int TYPE>
-__device__ __forceinline__ float kt_vec_dot(const uint8_t* bx, const uint8_t* by, int iqs, const uint32_t* grid) {
-  if constexpr (TYPE == KT_Q8_0) return kt_vd_q8_0(bx, by, iqs);
-  if constexpr (TYPE == KT_Q4_K) return kt_vd_q4_k(bx, by, iqs);
-  if constexpr (TYPE == KT_Q6_K) return kt_vd_q6_k(bx, by, iqs);
-  if constexpr (TYPE == KT_IQ3_S) return kt_vd_iq3_s(bx, by, iqs, grid);
+__device__ __forceinline__ float kt_vec_dot(const uint8_t* bx, const uint8_t* yq, const uint8_t* yd, int iqs,
+                                            const uint32_t* grid) {
+  if constexpr (TYPE == KT_Q8_0) return kt_vd_q8_0(bx, yq, yd, iqs);
+  if constexpr (TYPE == KT_Q4_K) return kt_vd_q4_k(bx, yq, yd, iqs);
+  if constexpr (TYPE == KT_Q6_K) return kt_vd_q6_k(bx, yq, yd, iqs);
+  if constexpr (TYPE == KT_IQ3_S) return kt_vd_iq3_s(bx, yq, yd, iqs, grid);
   return 0.0f;
 }
 

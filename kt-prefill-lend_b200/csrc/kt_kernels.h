@@ -23,11 +23,13 @@ struct KtGemmArgs {
 };
 
 int kt_launch_quantize_q8_1(const void* x, int dtype, int64_t rows, int64_t cols, void* qx, cudaStream_t s);
+// the same values in the GEMV's split layout: a row's int8 values, then its half2 (d, s) per block
+int kt_launch_quantize_q8_1_split(const void* x, int dtype, int64_t rows, int64_t cols, void* qx, cudaStream_t s);
 int kt_launch_group_routes(const int32_t* ids, int64_t routes, int n_slots, int32_t* groups, int32_t* order,
                            cudaStream_t s);
 int kt_launch_moe_vec(int type, const void* w, int table, const void* qx, int64_t qrow, const int32_t* groups,
                       const int32_t* order, int max_groups, int top_k, int rows, int cols, int dtype, void* y,
-                      cudaStream_t s);
+                      int* status, cudaStream_t s);
 
 int kt_launch_dequant(int type, const void* w, int64_t rows, int64_t cols, void* out, int out_dtype, cudaStream_t s);
 int kt_launch_silu_and_mul(const void* h13, int dtype, int64_t rows, int64_t n, void* h, cudaStream_t s);

@@ -19,7 +19,9 @@
 
 // ------------------------------------------------------------------ q8_1 quantizer
 
-template <int DT>
+// SPLIT = false: the reference's q8_1 blocks (half2 ds, 32 int8) back to back; SPLIT = true:
+// the GEMV's split layout (a row's int8 values, then its half2 ds per block), same values.
+template <int DT, bool SPLIT>
 __global__ void __launch_bounds__(256) kt_quantize_q8_1_kernel(const void* __restrict__ x, uint8_t* __restrict__ qx,
                                                                int64_t rows, int64_t cols, int64_t kpad) {
   const int64_t ix = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;  // column in the padded row
@@ -34,26 +36,39 @@ __global__ void __launch_bounds__(256) kt_quantize_q8_1_kernel(const void* __res
   }
   const float d = amax / 127;
   const int8_t q = amax == 0.0f ? 0 : (int8_t)roundf(xi / d);
-  uint8_t* blk = qx + row * (kpad / 32 * KT_Q8_1_BYTES) + (ix / 32) * KT_Q8_1_BYTES;
-  blk[4 + (ix % 32)] = (uint8_t)q;
-  if (ix % 32 == 0) {
-    half2 ds = __halves2half2(__float2half(d), __float2half(sum));
-    *reinterpret_cast<half2*>(blk) = ds;
+  uint8_t* rowp = qx + row * (kpad / 32 * KT_Q8_1_BYTES);
+  const half2 ds = __halves2half2(__float2half(d), __float2half(sum));
+  if constexpr (SPLIT) {
+    rowp[ix] = (uint8_t)q;
+    if (ix % 32 == 0) *reinterpret_cast<half2*>(rowp + kpad + 4 * (ix / 32)) = ds;
+  } else {
+    uint8_t* blk = rowp + (ix / 32) * KT_Q8_1_BYTES;
+    blk[4 + (ix % 32)] = (uint8_t)q;
+    if (ix % 32 == 0) *reinterpret_cast<half2*>(blk) = ds;
   }
 }
 
-int kt_launch_quantize_q8_1(const void* x, int dtype, int64_t rows, int64_t cols, void* qx, cudaStream_t s) {
+template <bool SPLIT>
+static int launch_quantize(const void* x, int dtype, int64_t rows, int64_t cols, void* qx, cudaStream_t s) {
   if (rows <= 0) return 0;
   const int64_t kpad = (cols + 511) / 512 * 512;
   const int64_t zr = (rows + 65534) / 65535;
   dim3 grid((unsigned)((kpad + 255) / 256), (unsigned)(rows < 65535 ? rows : 65535), (unsigned)zr);
   switch (dtype) {
-    case KT_DT_F32: kt_quantize_q8_1_kernel<KT_DT_F32><<<grid, 256, 0, s>>>(x, (uint8_t*)qx, rows, cols, kpad); break;
-    case KT_DT_F16: kt_quantize_q8_1_kernel<KT_DT_F16><<<grid, 256, 0, s>>>(x, (uint8_t*)qx, rows, cols, kpad); break;
-    case KT_DT_BF16: kt_quantize_q8_1_kernel<KT_DT_BF16><<<grid, 256, 0, s>>>(x, (uint8_t*)qx, rows, cols, kpad); break;
+    case KT_DT_F32: kt_quantize_q8_1_kernel<KT_DT_F32, SPLIT><<<grid, 256, 0, s>>>(x, (uint8_t*)qx, rows, cols, kpad); break;
+    case KT_DT_F16: kt_quantize_q8_1_kernel<KT_DT_F16, SPLIT><<<grid, 256, 0, s>>>(x, (uint8_t*)qx, rows, cols, kpad); break;
+    case KT_DT_BF16: kt_quantize_q8_1_kernel<KT_DT_BF16, SPLIT><<<grid, 256, 0, s>>>(x, (uint8_t*)qx, rows, cols, kpad); break;
     default: return -1;
   }
   return 0;
+}
+
+int kt_launch_quantize_q8_1(const void* x, int dtype, int64_t rows, int64_t cols, void* qx, cudaStream_t s) {
+  return launch_quantize<false>(x, dtype, rows, cols, qx, s);
+}
+
+int kt_launch_quantize_q8_1_split(const void* x, int dtype, int64_t rows, int64_t cols, void* qx, cudaStream_t s) {
+  return launch_quantize<true>(x, dtype, rows, cols, qx, s);
 }
 
 // ------------------------------------------------------------------ route grouping
@@ -116,7 +131,8 @@ struct KtVecArgs {
   const uint8_t* w;            // slot base (plain layout) or int64 table of slot addresses
   int table;                   // 1: w is the table
   const uint8_t* qx;           // q8_1 activations [tokens, qrow] bytes
-  int64_t qrow;                // bytes per q8_1 row
+  int64_t qrow;                // bytes per q8_1 row (split layout: kpad int8, then kpad/32 half2)
+  int64_t kpad;                // padded columns of a q8_1 row
   const int32_t* groups;       // from kt_group_routes
   const int32_t* order;
   int top_k;
@@ -125,6 +141,8 @@ struct KtVecArgs {
   int rows_per_cta;
   int members_per_pass;
   void* y;                     // [routes, rows]
+  int* status;                 // workspace status word (bounded waits)
+  int tiles_per_group;         // pipelined kernel: row tiles of rows_per_cta rows per group
 };
 
 // LPR lanes per row: 32, or 16 when a row has at most 16 chunks (two rows per warp).
@@ -199,10 +217,13 @@ __global__ void __launch_bounds__(256) kt_moe_vec_kernel(const KtVecArgs a) {
           for (int c = sl; c < nchunks; c += LPR) {
             const int i = c / C::CPB, iqs = C::VDR * (c % C::CPB);
             const uint8_t* bx = wrow + (int64_t)i * C::BYTES;
-            const int64_t yoff = (int64_t)i * (C::QK / 32) * KT_Q8_1_BYTES;
+            const int64_t qb = (int64_t)i * (C::QK / 32);  // first q8_1 block of the chunk
 #pragma unroll
             for (int m = 0; m < 8; ++m)
-              if (mb + m < nm) acc[m] += kt_vec_dot<TYPE>(bx, act + (int64_t)(mb + m) * a.qrow + yoff, iqs, grid_s);
+              if (mb + m < nm) {
+                const uint8_t* yr = act + (int64_t)(mb + m) * a.qrow;
+                acc[m] += kt_vec_dot<TYPE>(bx, yr + 32 * qb, yr + a.kpad + 4 * qb, iqs, grid_s);
+              }
           }
         }
 #pragma unroll
@@ -220,8 +241,162 @@ __global__ void __launch_bounds__(256) kt_moe_vec_kernel(const KtVecArgs a) {
   }
 }
 
+// One row (this lane's share) against W consecutive members of a group: per-lane sums in the
+// reference's chunk order, xor butterfly over the LPR lanes of the row, one store per member.
+// W is a compile-time width so that no work is issued for absent members.
+template <int TYPE, int DT, int LPR, int W>
+__device__ __forceinline__ void kt_vec_row_members(const KtVecArgs& a, const uint8_t* wrow, bool live, int nchunks,
+                                                   int sl, int start, int mb, int64_t out_row,
+                                                   const uint32_t* grid) {
+  using C = KtChunk<TYPE>;
+  const uint8_t* yrow[W];
+#pragma unroll
+  for (int m = 0; m < W; ++m) yrow[m] = a.qx + (int64_t)(a.order[start + mb + m] / a.top_k) * a.qrow;
+  float acc[W];
+#pragma unroll
+  for (int m = 0; m < W; ++m) acc[m] = 0.0f;
+  if (live) {
+    for (int c = sl; c < nchunks; c += LPR) {
+      const int i = c / C::CPB, iqs = C::VDR * (c % C::CPB);
+      const uint8_t* bx = wrow + (int64_t)i * C::BYTES;
+      const int64_t qb = (int64_t)i * (C::QK / 32);  // first q8_1 block of the chunk
+#pragma unroll
+      for (int m = 0; m < W; ++m) acc[m] += kt_vec_dot<TYPE>(bx, yrow[m] + 32 * qb, yrow[m] + a.kpad + 4 * qb, iqs, grid);
+    }
+  }
+#pragma unroll
+  for (int m = 0; m < W; ++m) {
+    float t = acc[m];
+#pragma unroll
+    for (int mask = LPR / 2; mask > 0; mask >>= 1) t += __shfl_xor_sync(0xffffffffu, t, mask);
+    if (live && sl == 0) kt_store_act<DT>(a.y, (int64_t)a.order[start + mb + m] * a.rows + out_row, t);
+  }
+}
+
+// Pipelined variant for bandwidth: a persistent grid walks (group, row tile) items; one
+// thread streams each item's raw rows into a ring of kVecStages shared-memory stages with a
+// single 1-D bulk copy (the rows of a tile are contiguous in HBM), so several tiles per SM
+// are in flight while the warps compute. The per-row arithmetic (lane-to-chunk assignment,
+// per-lane sums in chunk order, xor butterfly) is the kernel's above, so every route's sum is
+// the same. Activations are read from the q8_1 buffer in global memory (L1/L2 resident).
+constexpr int kVecStages = 4;
+
+template <int TYPE, int DT, int LPR>
+__global__ void __launch_bounds__(256) kt_moe_vec_pipe_kernel(const KtVecArgs a) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  __shared__ uint32_t grid_s[512];
+  __shared__ __align__(8) uint64_t full[kVecStages];
+  using C = KtChunk<TYPE>;
+  const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
+  const int n_items = a.groups[0] * a.tiles_per_group;
+  const int64_t tile_cap = ((int64_t)a.rows_per_cta * a.row_bytes + 127) & ~(int64_t)127;
+  if (tid == 0) {
+    for (int i = 0; i < kVecStages; ++i) kt_mbar_init(&full[i], 1);
+    kt_fence_mbar_init();
+  }
+  if constexpr (TYPE == KT_IQ3_S) {
+    for (int i = tid; i < 512; i += blockDim.x) grid_s[i] = kt_iq3s_grid_dev[i];
+  }
+  __syncthreads();
+  // stage the raw rows of the CTA's j-th item
+  auto issue = [&](int j) {
+    const int item = blockIdx.x + j * gridDim.x;
+    if (item >= n_items) return;
+    uint64_t* bar = &full[j % kVecStages];
+    const int g = item / a.tiles_per_group, r0 = (item % a.tiles_per_group) * a.rows_per_cta;
+    const int slot = a.groups[1 + 3 * g + 0];
+    if (slot < 0) {
+      kt_mbar_arrive(bar);
+      return;
+    }
+    const int nr = min(a.rows_per_cta, a.rows - r0);
+    const uint8_t* wbase = a.table ? reinterpret_cast<const uint8_t*>(reinterpret_cast<const int64_t*>(a.w)[slot])
+                                   : a.w + (int64_t)slot * a.rows * a.row_bytes;
+    const uint32_t bytes = (uint32_t)((int64_t)nr * a.row_bytes);
+    kt_mbar_arrive_expect_tx(bar, bytes);
+    kt_bulk_g2s(smem + (j % kVecStages) * tile_cap, wbase + (int64_t)r0 * a.row_bytes, bytes, bar);
+  };
+  if (tid == 0)
+    for (int j = 0; j < kVecStages; ++j) issue(j);
+  const int nblocks = a.cols / C::QK;
+  const int nchunks = nblocks * C::CPB;
+  constexpr int RPW = 32 / LPR;
+  const int sub = lane / LPR, sl = lane % LPR;
+  bool ok = true;
+  for (int j = 0; blockIdx.x + j * gridDim.x < n_items; ++j) {
+    const int item = blockIdx.x + j * gridDim.x;
+    const int g = item / a.tiles_per_group, r0 = (item % a.tiles_per_group) * a.rows_per_cta;
+    const int slot = a.groups[1 + 3 * g + 0];
+    const int start = a.groups[1 + 3 * g + 1];
+    const int count = a.groups[1 + 3 * g + 2];
+    const int nr = min(a.rows_per_cta, a.rows - r0);
+    if (!kt_mbar_wait(&full[j % kVecStages], (j / kVecStages) & 1, a.status, nullptr)) {
+      // a copy that never landed (recorded in the status word): wait, bounded, for the other
+      // copies this CTA issued, then leave
+      ok = false;
+      if (tid == 0)
+        for (int jj = j + 1; jj < j + kVecStages && blockIdx.x + jj * gridDim.x < n_items; ++jj)
+          kt_mbar_wait(&full[jj % kVecStages], (jj / kVecStages) & 1, nullptr, nullptr);
+      break;
+    }
+    if (slot < 0) {  // routes not on this device: zero rows
+      for (int64_t i = tid; i < (int64_t)count * nr; i += blockDim.x) {
+        const int p = a.order[start + i / nr];
+        kt_store_act<DT>(a.y, (int64_t)p * a.rows + r0 + i % nr, 0.0f);
+      }
+    } else {
+      const uint8_t* wt = smem + (j % kVecStages) * tile_cap;
+      for (int rr = warp * RPW; rr < nr; rr += (blockDim.x / 32) * RPW) {
+        const int r = rr + sub;
+        const bool live = r < nr;
+        const uint8_t* wrow = wt + (int64_t)(live ? r : 0) * a.row_bytes;
+        for (int mb = 0; mb < count;) {
+          const int left = count - mb;
+          if (left >= 4) {
+            kt_vec_row_members<TYPE, DT, LPR, 4>(a, wrow, live, nchunks, sl, start, mb, r0 + r, grid_s);
+            mb += 4;
+          } else if (left >= 2) {
+            kt_vec_row_members<TYPE, DT, LPR, 2>(a, wrow, live, nchunks, sl, start, mb, r0 + r, grid_s);
+            mb += 2;
+          } else {
+            kt_vec_row_members<TYPE, DT, LPR, 1>(a, wrow, live, nchunks, sl, start, mb, r0 + r, grid_s);
+            mb += 1;
+          }
+        }
+      }
+    }
+    __syncthreads();  // every warp is done with the stage
+    if (tid == 0) issue(j + kVecStages);
+  }
+  (void)ok;
+}
+
+static int vec_num_sms() {
+  static int n = 0;
+  if (!n) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+  }
+  return n;
+}
+
+template <int TYPE, int DT, int LPR>
+static int launch_pipe(const KtVecArgs& a, int max_groups, cudaStream_t s) {
+  const int64_t tile_cap = ((int64_t)a.rows_per_cta * a.row_bytes + 127) & ~(int64_t)127;
+  const size_t smem = (size_t)(kVecStages * tile_cap);
+  auto k = kt_moe_vec_pipe_kernel<TYPE, DT, LPR>;
+  if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess) return -3;
+  const int64_t max_items = (int64_t)max_groups * a.tiles_per_group;
+  const int64_t ctas = 3 * (int64_t)vec_num_sms();
+  k<<<(unsigned)(max_items < ctas ? max_items : ctas), 256, smem, s>>>(a);
+  return 0;
+}
+
 template <int TYPE, int DT>
 static int launch_vec_t(const KtVecArgs& a, int max_groups, int lpr, size_t smem, cudaStream_t s) {
+  if (a.tiles_per_group > 0) return lpr == 16 ? launch_pipe<TYPE, DT, 16>(a, max_groups, s)
+                                              : launch_pipe<TYPE, DT, 32>(a, max_groups, s);
   dim3 grid((a.rows + a.rows_per_cta - 1) / a.rows_per_cta, max_groups);
   if (lpr == 16) {
     auto k = kt_moe_vec_kernel<TYPE, DT, 16>;
@@ -252,9 +427,19 @@ static int pick_rows_per_cta(int64_t row_bytes, int rows) {
   return rpc;
 }
 
+// Pipelined path: tiles of at most 16 KB whose bytes are a 16-byte multiple (1-D bulk copies
+// need 16-byte aligned addresses and sizes), a whole number of tiles per slot, and a
+// 16-byte aligned weight base (or slot table). Returns the rows per tile, or 0.
+static int pick_pipe_rows(int64_t row_bytes, int rows, const void* w, int table) {
+  if (!table && (((uintptr_t)w) & 15)) return 0;
+  for (int rpt = 64; rpt >= 8; rpt /= 2)
+    if ((int64_t)rpt * row_bytes <= 16 * 1024 && ((int64_t)rpt * row_bytes) % 16 == 0 && rows % rpt == 0) return rpt;
+  return 0;
+}
+
 int kt_launch_moe_vec(int type, const void* w, int table, const void* qx, int64_t qrow, const int32_t* groups,
                       const int32_t* order, int max_groups, int top_k, int rows, int cols, int dtype, void* y,
-                      cudaStream_t s) {
+                      int* status, cudaStream_t s) {
   const KtBlockInfo bi = kt_block_info(type);
   if (!bi.qk || cols % bi.qk) return -1;
   KtVecArgs a;
@@ -262,13 +447,17 @@ int kt_launch_moe_vec(int type, const void* w, int table, const void* qx, int64_
   a.table = table;
   a.qx = (const uint8_t*)qx;
   a.qrow = qrow;
+  a.kpad = (cols + 511) / 512 * 512;
   a.groups = groups;
   a.order = order;
   a.top_k = top_k;
   a.rows = rows;
   a.cols = cols;
   a.row_bytes = (int64_t)cols / bi.qk * bi.bytes;
-  a.rows_per_cta = pick_rows_per_cta(a.row_bytes, rows);
+  a.status = status;
+  const int pipe_rows = pick_pipe_rows(a.row_bytes, rows, w, table);
+  a.rows_per_cta = pipe_rows ? pipe_rows : pick_rows_per_cta(a.row_bytes, rows);
+  a.tiles_per_group = pipe_rows ? rows / pipe_rows : 0;
   const int64_t wt_bytes = ((int64_t)a.rows_per_cta * a.row_bytes + 15) & ~(int64_t)15;
   int mpp = 8;
   while (mpp > 1 && wt_bytes + mpp * qrow > 200 * 1024) mpp /= 2;
