@@ -53,11 +53,12 @@ def parse():
     ap.add_argument("--cpu-sample", type=int, default=256, help="tokens per CPU-baseline sample")
     ap.add_argument("--tokens", type=int, default=16384, help="chunk size (profiling runs use smaller chunks)")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end pass (profiling)")
-    ap.add_argument("--config", type=int, default=2, choices=[1, 2, 3],
+    ap.add_argument("--config", type=int, default=2, choices=[1, 2, 3, 4, 5],
                     help="2: the headline line (default); 1 and 3: the other BASELINE configs, one JSON line per point")
     ap.add_argument("--m-list", default="1,4,16,64,2048,16384",
                     help="sweep token counts (config 3, or config 2 with --sweep): below 128 the decode GEMV, "
                          "from 128 the prefill GEMMs")
+    ap.add_argument("--tokens-c4", type=int, default=32768, help="config 4: tokens per rank")
     ap.add_argument("--sweep", action="store_true", help="config 2: run the decode/prefill sweep instead of the "
                                                          "headline line")
     return ap.parse_args()
@@ -401,6 +402,332 @@ def run_b200(args, rank, world, local_rank):
         dist.destroy_process_group()
 
 
+def _ep_setup_config2(args, rank, world, dev):
+    """Config 2: the 64 resident experts dealt hottest first in snake order; each rank its own
+    16K-token chunk (same experts, different tokens)."""
+    import torch
+
+    from kt_gguf_b200 import ep as EP
+    from kt_gguf_b200 import kt_gguf_moe_multi as M
+    from kt_gguf_b200 import synth
+
+    cfg = dict(synth.CONFIGS[2], tokens=args.tokens)
+    L = synth.make_layer(args.seed, token_seed=args.seed + 1 + rank, **cfg)
+    K, N = cfg["hidden"], cfg["inter"]
+    S = L.w13.shape[0]
+    owner, local = EP.snake_placement(S, world)
+    mine = (owner == rank).nonzero().flatten()
+    mine = mine[torch.argsort(local[mine])]
+    w13_all = torch.from_numpy(L.w13).to(dev)
+    w2_all = torch.from_numpy(L.w2).to(dev)
+    w13 = w13_all[mine.to(dev)].contiguous()
+    w2 = w2_all[mine.to(dev)].contiguous()
+    x, ids, wts = L.x.to(dev), L.topk_ids.to(dev), L.topk_weights.to(dev)
+    layer = EP.ExpertParallelMoE(owner, local, EP.prefill_expert_fn(w13, w2, L.type13, L.type2, N))
+
+    def ref_fn(n):  # the whole layer on this GPU (all 64 slots) for this rank's first n tokens
+        return M.moe_prefill(x[:n].contiguous(), w13_all, w2_all, ids[:n].contiguous(), wts[:n].contiguous(),
+                             L.type13, L.type2, N)
+
+    r_all = int((L.topk_ids >= 0).sum())
+    return dict(x=x, ids=ids, wts=wts, layer=layer, w13=w13, w2=w2, types=(L.type13, L.type2), K=K, N=N,
+                ref_fn=ref_fn, flops=6.0 * K * N * r_all, metric=METRIC, workload=CONFIG_NAME,
+                config={"experts": 256, "top_k": cfg["top_k"], "resident_experts": S,
+                        "types": "Q4_K gate/up, Q6_K down",
+                        "placement": "64 resident experts dealt hottest first in snake order"},
+                host=(L.x, L.topk_ids, L.topk_weights))
+
+
+def _ep_setup_config4(args, rank, world, dev):
+    """Config 4: DeepSeek-V3-like layer, hidden 7168, expert intermediate 2048, 256 routed
+    experts + 1 shared, grouped top-8 (8 groups, top-4 groups, sigmoid scores, renormalised,
+    scale 2.5), Q4_K everywhere, 32768 tokens per rank; experts contiguous over the ranks.
+    Weights: 16 distinct N(0,0.02) experts quantized to Q4_K, expert e holds copy e % 16 (the
+    256 slots are distinct memory; generating 256 distinct experts on the host takes minutes)."""
+    import numpy as np
+    import torch
+
+    from kt_gguf_b200 import ep as EP
+    from kt_gguf_b200 import kernels as Kn
+    from kt_gguf_b200 import kt_gguf_moe_multi as M
+    from kt_gguf_b200 import synth
+
+    K, N, E, k, T = 7168, 2048, 256, 8, args.tokens_c4
+    rng = np.random.default_rng(args.seed)
+    w13_16, w2_16 = synth.expert_weights(rng, 17, K, N, 12, 12)  # 16 routed + 1 shared
+    w13_16 = torch.from_numpy(w13_16).to(dev)
+    w2_16 = torch.from_numpy(w2_16).to(dev)
+    owner, local = EP.contiguous_placement(E, world)
+    per = E // world
+    gids = torch.arange(rank * per, (rank + 1) * per)
+    w13 = w13_16[(gids % 16).to(dev)].contiguous()
+    w2 = w2_16[(gids % 16).to(dev)].contiguous()
+    sw13, sw2 = w13_16[16:17].contiguous(), w2_16[16:17].contiguous()
+    g = torch.Generator().manual_seed(args.seed + 1 + rank)
+    x = torch.randn((T, K), generator=g).to(torch.bfloat16).to(dev)
+    logits = torch.randn((T, E), generator=g).to(dev)
+    bias = (torch.randn(E, generator=g) * 0.1).to(dev)
+    wts, ids = Kn.topk_grouped(logits, bias, 8, 4, k, renormalize=True, scale=2.5)
+    ones = torch.ones((T, 1), dtype=torch.float32, device=dev)
+    zeros = torch.zeros((T, 1), dtype=torch.int32, device=dev)
+    sh_ws = {}
+
+    def shared_fn(xx):
+        n = xx.shape[0]
+        if "ws" not in sh_ws:
+            from kt_gguf_b200 import _native as Nt
+
+            sh_ws["ws"] = Nt.workspace(Nt.load().kt_moe_prefill_workspace_size(n, 1, K, N, 1), dev)
+        return M.moe_prefill(xx, sw13, sw2, zeros[:n], ones[:n], 12, 12, N, workspace=sh_ws["ws"])
+
+    layer = EP.ExpertParallelMoE(owner, local, EP.prefill_expert_fn(w13, w2, 12, 12, N), shared_fn=shared_fn)
+
+    def ref_fn(n):  # the whole layer on this GPU: expert e is copy e % 16, plus the shared expert
+        r = M.moe_prefill(x[:n].contiguous(), w13_16[:16], w2_16[:16], (ids[:n] % 16).to(torch.int32).contiguous(),
+                          wts[:n].contiguous(), 12, 12, N)
+        return (r.float() + shared_fn(x[:n].contiguous()).float()).to(torch.bfloat16)
+
+    return dict(x=x, ids=ids, wts=wts, layer=layer, w13=w13, w2=w2, types=(12, 12), K=K, N=N, ref_fn=ref_fn,
+                flops=6.0 * K * N * (T * k + T), metric="DeepSeek-V3-like MoE layer tok/s @32K chunk",
+                workload="deepseek-v3-like MoE layer (BASELINE configs[3])",
+                config={"experts": E, "shared_experts": 1, "top_k": k, "routing": "grouped: 8 groups, top-4 groups",
+                        "types": "Q4_K", "placement": "contiguous, %d experts per rank" % per,
+                        "weights": "16 distinct experts, expert e holds copy e % 16"},
+                host=(x.cpu(), ids.cpu(), wts.cpu()))
+
+
+def run_ep(args, rank, world, local_rank, cfg_id=2):
+    """Expert-parallel layer on `world` GPUs (kt_gguf_b200.ep): tokens go to the ranks owning
+    their experts and the partial outputs come back by NCCL all-to-all. Each rank processes
+    its own chunk, so per-rank work stays fixed as ranks are added ("weak")."""
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    from kt_gguf_b200 import _native as Nt
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+    st = (_ep_setup_config2 if cfg_id == 2 else _ep_setup_config4)(args, rank, world, dev)
+    x, ids, wts, layer, w13, w2 = st["x"], st["ids"], st["wts"], st["layer"], st["w13"], st["w2"]
+    K, N = st["K"], st["N"]
+    T = x.shape[0]
+    stream = torch.cuda.current_stream(dev)
+
+    for _ in range(args.warmup):
+        out = layer(x, ids, wts)
+    torch.cuda.synchronize()
+    n_chk = min(512, T)
+    ref = st["ref_fn"](n_chk)
+    err = float((out[:n_chk].float() - ref.float()).norm() / ref.float().norm())
+    # phases of one call (events around dispatch, local experts, combine)
+    ph = []
+    for _ in range(5):
+        e = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+        e[0].record(stream)
+        xr, ir, wr, plan = layer.dispatch(x, ids, wts)
+        e[1].record(stream)
+        yr = layer.expert_fn(xr, ir, wr)
+        e[2].record(stream)
+        layer.combine(yr, plan, T)
+        e[3].record(stream)
+        torch.cuda.synchronize()
+        ph.append([e[j].elapsed_time(e[j + 1]) for j in range(3)])
+    phases = [statistics.median(p[j] for p in ph) for j in range(3)]
+    n_recv = int(xr.shape[0])
+    # local GEMM stages on the received rows (for the roofline)
+    lib = Nt.load()
+    ws = Nt.workspace(lib.kt_moe_prefill_workspace_size(n_recv, ir.shape[1], K, N, w13.shape[0]), dev)
+    yl = torch.empty((n_recv, K), dtype=torch.bfloat16, device=dev)
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(5)] for _ in range(6)]
+    for ee in (ee for es in evs for ee in es):
+        ee.record(stream)
+    hs = [(ctypes.c_void_p * 4)(*[ee.cuda_event for ee in es[1:]]) for es in evs]
+    for i in range(6):
+        evs[i][0].record(stream)
+        Nt.check(lib.kt_moe_prefill_timed(Nt.ptr(xr), n_recv, K, N, Nt.ptr(ir), Nt.ptr(wr), ir.shape[1], Nt.ptr(w13),
+                                          st["types"][0], Nt.ptr(w2), st["types"][1], 0, w13.shape[0], Nt.ptr(yl),
+                                          Nt.ptr(ws), ws.numel(), stream.cuda_stream, hs[i]), "kt_moe_prefill")
+    torch.cuda.synchronize()
+    stage_ms = [statistics.median(evs[i][j].elapsed_time(evs[i][j + 1]) for i in range(1, 6)) for j in range(4)]
+    r_local = int((ir >= 0).sum())
+
+    uuid = torch.cuda.get_device_properties(dev).uuid
+    sampler = ClockSampler(f"GPU-{uuid}") if rank == 0 else None
+    if sampler:
+        sampler.start()
+        time.sleep(0.3)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    wall0 = time.time()
+    t0.record(stream)
+    for _ in range(args.steps):
+        out = layer(x, ids, wts)
+    t1.record(stream)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    wall1 = time.time()
+    m = torch.tensor([t0.elapsed_time(t1)], device=dev)
+    if world > 1:
+        dist.all_reduce(m, op=dist.ReduceOp.MAX)
+    ms = float(m.item())
+    clocks = sampler.stop(wall0, wall1) if sampler else None
+
+    e2e = None
+    if not args.no_e2e:
+        x_h, ids_h, w_h = (t.pin_memory() for t in st["host"])
+        out_h = torch.empty((T, K), dtype=torch.bfloat16).pin_memory()
+
+        def e2e_step():
+            o = layer(x_h.to(dev, non_blocking=True), ids_h.to(dev, non_blocking=True), w_h.to(dev, non_blocking=True))
+            out_h.copy_(o, non_blocking=True)
+
+        for _ in range(2):
+            e2e_step()
+        torch.cuda.synchronize()
+        e_steps = max(5, args.steps // 4)
+        if world > 1:
+            dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(e_steps):
+            e2e_step()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        me = torch.tensor([e0.elapsed_time(e1)], device=dev)
+        if world > 1:
+            dist.all_reduce(me, op=dist.ReduceOp.MAX)
+        e2e = {"value": world * T * e_steps / (float(me.item()) * 1e-3), "unit": "tokens/s",
+               "h2d_bytes_per_step": x_h.numel() * 2 + ids_h.numel() * 4 + w_h.numel() * 4,
+               "d2h_bytes_per_step": out_h.numel() * 2, "overlap": "none (sequential copies around each call)"}
+    errs = [torch.tensor([err], device=dev)]
+    recvs = [torch.tensor([float(n_recv)], device=dev)]
+    if world > 1:
+        errs = [torch.zeros(1, device=dev) for _ in range(world)]
+        dist.all_gather(errs, torch.tensor([err], device=dev))
+        recvs = [torch.zeros(1, device=dev) for _ in range(world)]
+        dist.all_gather(recvs, torch.tensor([float(n_recv)], device=dev))
+    if rank == 0:
+        hbm, tf_burst, tf_sust, peak_kind = load_peaks()
+        tf13 = 4.0 * K * N * r_local / (stage_ms[1] * 1e-3) / 1e12
+        line = {
+            "metric": st["metric"], "value": world * T * args.steps / (ms * 1e-3), "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None,
+            "dtype": "bf16 (GGUF weights dequantized in-kernel, fp32 accumulate)", "data": "synthetic (seeded)",
+            "config": dict({"workload": st["workload"], "tokens_per_gpu": T, "hidden": K, "inter": N,
+                            "parallelism": f"ep{world}",
+                            "l2": "no flush: one step's working set exceeds the 126 MB L2"}, **st["config"]),
+            "layer_tflops": world * st["flops"] * args.steps / (ms * 1e-3) / 1e12,
+            "ep": {"phase_ms": {"dispatch": phases[0], "local_experts": phases[1], "combine": phases[2]},
+                   "rows_received_per_rank": [int(v.item()) for v in recvs],
+                   "check_rel_l2_vs_single_gpu_layer": max(float(v.item()) for v in errs),
+                   "collective": "torch.distributed.all_to_all_single over NCCL (counts, rows, metadata; "
+                                 "partials back)"},
+            "stage_ms_local": {"permute": stage_ms[0], "gate_up_gemm": stage_ms[1], "down_gemm": stage_ms[2],
+                               "combine": stage_ms[3]},
+            "roofline": {"bound": "tensor", "kernel": "kt_moe_gemm_kernel<Q4_K, gate/up> (rank 0's received rows)",
+                         "achieved": tf13, "peak": tf_burst, "unit": "TFLOP/s", "frac": tf13 / tf_burst,
+                         "peak_kind": f"{peak_kind} bf16 burst (cuBLAS)",
+                         "traffic": None},
+            "cpu_baseline": None,
+            "e2e": e2e,
+            "gpu_launches": 6 * args.steps,
+            "clocks": clocks,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def run_config5(args):
+    """Config 5: a 48-layer prefill of a 65536-token prompt in 16384-token chunks. Each layer
+    runs one dense bf16 projection [4096 x 2048] (cuBLAS through torch.matmul) and the
+    config-2 MoE layer (tcgen05 path, x += moe(x)); the dense weights live in pinned host
+    memory and come back one layer ahead on a side stream (kt_gguf_b200.lend.LayerStreamer:
+    two device slots, event-ordered copies). Reported: tokens/s of the whole prompt, the H2D
+    rate of the copies, the fraction of copy time hidden under compute, and the same pass
+    with the dense weights resident (the cost of streaming). One expert set serves all 48
+    layers (per-layer work and bytes are those of distinct layers)."""
+    import torch
+
+    from kt_gguf_b200 import _native as Nt
+    from kt_gguf_b200 import kt_gguf_moe_multi as M
+    from kt_gguf_b200 import lend
+    from kt_gguf_b200 import synth
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    n_layers, prompt, chunk, dense_rows = 48, 65536, 16384, 4096
+    cfg = dict(synth.CONFIGS[2], tokens=prompt)
+    L = synth.make_layer(args.seed, **cfg)
+    K, N = cfg["hidden"], cfg["inter"]
+    w13, w2 = torch.from_numpy(L.w13).to(dev), torch.from_numpy(L.w2).to(dev)
+    x_all = L.x.to(dev)
+    ids_all, w_all = L.topk_ids.to(dev), L.topk_weights.to(dev)
+    g = torch.Generator().manual_seed(args.seed + 5)
+    host = [(torch.randn((dense_rows, K), generator=g) * 0.02).to(torch.bfloat16).pin_memory() for _ in range(n_layers)]
+    resident = [h.to(dev) for h in host]
+    lib = Nt.load()
+    ws = Nt.workspace(lib.kt_moe_prefill_workspace_size(chunk, ids_all.shape[1], K, N, w13.shape[0]), dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def prompt_pass(weights_for):
+        for c0 in range(0, prompt, chunk):
+            x = x_all[c0:c0 + chunk].clone()
+            ids, wts = ids_all[c0:c0 + chunk].contiguous(), w_all[c0:c0 + chunk].contiguous()
+            for li in range(n_layers):
+                wd = weights_for(li)
+                h = torch.matmul(x, wd.t())  # the layer's dense projection
+                del h
+                x += M.moe_prefill(x, w13, w2, ids, wts, L.type13, L.type2, N, workspace=ws)
+            if hasattr(weights_for, "finish"):
+                weights_for.finish()
+
+    class Streamed:
+        def __init__(self, timing):
+            self.s = lend.LayerStreamer(host, dev, timing=timing)
+
+        def __call__(self, li):
+            return self.s.enter(li)
+
+        def finish(self):
+            self.s.finish()
+
+    def timed(fn):
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        fn()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1)
+
+    warm = Streamed(False)
+    prompt_pass(warm)  # warm-up (cuBLAS heuristics, library state)
+    ms_res = timed(lambda: prompt_pass(lambda li: resident[li]))
+    sw = Streamed(True)
+    ms_str = timed(lambda: prompt_pass(sw))
+    stt = sw.s.stats()
+    line = {"metric": "config 5 prompt", "value": prompt / (ms_str * 1e-3), "unit": "tokens/s",
+            "ms_prompt_streamed": ms_str, "ms_prompt_resident": ms_res,
+            "streaming_overhead_frac": ms_str / ms_res - 1.0,
+            "lend": {"copies": stt["copies"], "bytes": stt["bytes"], "h2d_GBps": stt["h2d_GBps"],
+                     "copy_ms": stt["copy_ms"], "compute_wait_ms": stt["wait_ms"], "hidden_frac": stt["hidden_frac"]},
+            "config": {"workload": "48-layer lend pipeline (BASELINE configs[4])", "layers": n_layers,
+                       "prompt_tokens": prompt, "chunk": chunk, "dense_weight": [dense_rows, K],
+                       "moe": "config 2 layer (Q4_K/Q6_K, 64 resident experts), one expert set for all layers"},
+            "data": "synthetic (seeded)"}
+    print(json.dumps(line), flush=True)
+
+
 def _gemv_call(lib, Nt, x, w, ids, top_k, qtype, rows, tokens, y, ws, stream):
     Nt.check(lib.kt_moe_a8_vec_multi(Nt.ptr(x), Nt.dtype_code(x), tokens, x.shape[1], Nt.ptr(w), 0, w.shape[0],
                                      Nt.ptr(ids), top_k, qtype, rows, Nt.ptr(y), Nt.ptr(ws), ws.numel(), stream),
@@ -577,6 +904,15 @@ def main():
         return
     if args.config == 1:
         run_config1(args)
+        return
+    if args.config == 4:
+        run_ep(args, rank, world, local_rank, cfg_id=4)
+        return
+    if args.config == 5:
+        run_config5(args)
+        return
+    if world > 1:
+        run_ep(args, rank, world, local_rank)
         return
     run_b200(args, rank, world, local_rank)
 

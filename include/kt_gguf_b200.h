@@ -185,6 +185,31 @@ int kt_moe_prefill_timed(const void* x, int64_t tokens, int64_t hidden, int64_t 
                          int w_is_table, int n_slots, void* out, void* workspace, size_t workspace_bytes, void* stream,
                          void* const* stage_events);
 
+/* ---- Expert-parallel plumbing (no counterpart in the reference, which runs the hot experts on
+ * one GPU per tensor-parallel rank). Around an all-to-all of bf16 rows over n_ranks <= 8
+ * ranks: owner[e] / local[e] give, for each of n_experts logical experts, its rank (< 0: none)
+ * and its slot there. */
+
+/* Scratch for kt_ep_plan (per block of 256 tokens and rank). */
+size_t kt_ep_plan_workspace_size(int64_t tokens, int n_ranks);
+
+/* Dispatch plan: each token goes once to every rank owning at least one of its experts; send
+ * rows are grouped by destination rank, tokens ascending. Writes counts [n_ranks],
+ * send_token [rows] (rows <= tokens*n_ranks), meta [rows][2*top_k] (the row's local slots,
+ * -1 where the expert is elsewhere, then its weights as fp32 bits, 0 there) and
+ * row_of [tokens][n_ranks] (send row of token t for rank r, or -1). */
+int kt_ep_plan(const int32_t* topk_ids, const float* topk_weights, int64_t tokens, int64_t top_k, const int32_t* owner,
+               const int32_t* local, int n_experts, int n_ranks, int32_t* counts, int32_t* send_token, int32_t* meta,
+               int32_t* row_of, void* workspace, size_t workspace_bytes, void* stream);
+
+/* out[i] = x[send_token[i]] for i < rows; x, out bf16 rows of `hidden` values, 16-byte aligned. */
+int kt_ep_pack(const void* x, int64_t hidden, const int32_t* send_token, int64_t rows, void* out, void* stream);
+
+/* out[t] = bf16(shared[t] + sum over r = 0..n_ranks-1 of back[row_of[t][r]]) with fp32 sums in
+ * rank order; rows of -1 are skipped; shared may be NULL. bf16 rows of `hidden` values. */
+int kt_ep_combine(const void* back, const int32_t* row_of, int n_ranks, const void* shared, int64_t tokens,
+                  int64_t hidden, void* out, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

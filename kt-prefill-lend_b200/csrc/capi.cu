@@ -314,6 +314,41 @@ KT_EXPORT int kt_moe_prefill(const void* x, int64_t tokens, int64_t hidden, int6
                               w_is_table, n_slots, out, workspace, workspace_bytes, stream, nullptr);
 }
 
+// ------------------------------------------------------------------ expert-parallel plumbing
+
+KT_EXPORT size_t kt_ep_plan_workspace_size(int64_t tokens, int n_ranks) {
+  if (tokens < 0 || n_ranks < 1) return 0;
+  return align_up((size_t)kt_ep_plan_ints(tokens, n_ranks) * sizeof(int32_t) + 256, 256);
+}
+
+KT_EXPORT int kt_ep_plan(const int32_t* topk_ids, const float* topk_weights, int64_t tokens, int64_t top_k,
+                         const int32_t* owner, const int32_t* local, int n_experts, int n_ranks, int32_t* counts,
+                         int32_t* send_token, int32_t* meta, int32_t* row_of, void* workspace, size_t workspace_bytes,
+                         void* stream) {
+  if (tokens < 0 || top_k < 1 || top_k > 64 || n_experts < 1 || n_ranks < 1 || n_ranks > 8) return KT_ERR_ARG;
+  if (!counts || !owner || !local || !workspace) return KT_ERR_ARG;
+  if (tokens > 0 && (!topk_ids || !topk_weights || !send_token || !meta || !row_of)) return KT_ERR_ARG;
+  if (workspace_bytes < kt_ep_plan_workspace_size(tokens, n_ranks)) return KT_ERR_WORKSPACE;
+  return launch_rc(kt_launch_ep_plan(topk_ids, topk_weights, tokens, (int)top_k, owner, local, n_experts, n_ranks,
+                                     (int32_t*)workspace, counts, send_token, meta, row_of, S(stream)));
+}
+
+KT_EXPORT int kt_ep_pack(const void* x, int64_t hidden, const int32_t* send_token, int64_t rows, void* out,
+                         void* stream) {
+  if (hidden <= 0 || rows < 0) return KT_ERR_ARG;
+  if (rows == 0) return KT_OK;
+  if (!x || !send_token || !out) return KT_ERR_ARG;
+  return launch_rc(kt_launch_ep_pack(x, hidden, send_token, rows, out, S(stream)));
+}
+
+KT_EXPORT int kt_ep_combine(const void* back, const int32_t* row_of, int n_ranks, const void* shared, int64_t tokens,
+                            int64_t hidden, void* out, void* stream) {
+  if (tokens < 0 || hidden <= 0 || n_ranks < 1 || n_ranks > 8) return KT_ERR_ARG;
+  if (tokens == 0) return KT_OK;
+  if (!row_of || !out || (!back && !shared)) return KT_ERR_ARG;
+  return launch_rc(kt_launch_ep_combine(back, row_of, n_ranks, shared, tokens, hidden, out, S(stream)));
+}
+
 // ------------------------------------------------------------------ allocation-free decode GEMV
 // Some callers cannot hand this library device memory on every call: code that runs while a
 // CUDA graph is being captured under a frozen memory pool, plugins whose host framework owns

@@ -59,3 +59,12 @@ int kt_launch_gemm_down(int type, const void* h, int64_t R, int K, int N, const 
                         const int32_t* tiles,
                         const int32_t* n_tiles, void* y, int* status, int grid, cudaStream_t s);
 int kt_gemm_tile_tokens();
+
+// expert-parallel plumbing (ep.cu): dispatch plan, row packing, combine of partials (bf16 rows)
+int64_t kt_ep_plan_ints(int64_t T, int P);
+int kt_launch_ep_plan(const int32_t* ids, const float* w, int64_t T, int k, const int32_t* owner, const int32_t* local,
+                      int n_experts, int P, int32_t* block_scratch, int32_t* counts, int32_t* send_token, int32_t* meta,
+                      int32_t* row_of, cudaStream_t s);
+int kt_launch_ep_pack(const void* x, int64_t K, const int32_t* send_token, int64_t n, void* rows, cudaStream_t s);
+int kt_launch_ep_combine(const void* back, const int32_t* row_of, int P, const void* shared, int64_t T, int64_t K,
+                         void* out, cudaStream_t s);

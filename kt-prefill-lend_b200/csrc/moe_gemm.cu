@@ -35,7 +35,8 @@
 // copies complete a local barrier, and one warp forwards each completed stage with a single
 // remote arrival.
 // TMEM (per CTA): two 256-column fp32 accumulators, so the epilogue of one tile overlaps the
-// MMAs of the next. No TMA or bulk copy uses .multicast::cluster.
+// MMAs of the next. Every TMA and bulk copy lands in the issuing CTA only (no cluster-wide
+// delivery of loaded data).
 #include <string.h>
 
 #include "gguf_dot.cuh"

@@ -32,6 +32,10 @@ SIGNATURES = {
     "kt_moe_a8_vec_multi": (_I, [_P, _I, _I64, _I64, _P, _I, _I, _P, _I64, _I, _I64, _P, _P, _SZ, _P]),
     "kt_moe_a8_vec_routes": (_I, [_P, _I, _I64, _I64, _P, _I, _I, _P, _I64, _I, _I64, _P, _P, _SZ, _P]),
     "kt_moe_a8_vec_multi_static": (_I, [_P, _I, _I64, _I64, _P, _I, _I, _P, _I64, _I, _I64, _P, _P]),
+    "kt_ep_plan_workspace_size": (_SZ, [_I64, _I]),
+    "kt_ep_plan": (_I, [_P, _P, _I64, _I64, _P, _P, _I, _I, _P, _P, _P, _P, _P, _SZ, _P]),
+    "kt_ep_pack": (_I, [_P, _I64, _P, _I64, _P, _P]),
+    "kt_ep_combine": (_I, [_P, _P, _I, _P, _I64, _I64, _P, _P]),
     "kt_dense_a8_vec_workspace_size": (_SZ, [_I64, _I64]),
     "kt_dense_a8_vec": (_I, [_P, _I, _I64, _I64, _P, _I, _I64, _P, _P, _SZ, _P]),
     "kt_gguf_dequantize": (_I, [_P, _I, _I64, _I64, _P, _I, _P]),

@@ -20,7 +20,7 @@ PKG = Path(__file__).resolve().parent
 CSRC = PKG.parent / "csrc"
 INCLUDE = PKG.parent.parent / "include"
 LIB = PKG / "lib"
-CUDA_SOURCES = ["capi.cu", "moe_vec.cu", "moe_misc.cu", "moe_gemm.cu"]
+CUDA_SOURCES = ["capi.cu", "moe_vec.cu", "moe_misc.cu", "moe_gemm.cu", "ep.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

@@ -1,0 +1,229 @@
+"""Expert-parallel MoE layer over a process group (one process per GPU, NCCL over NVLink).
+
+Each rank owns a set of expert slots and its own chunk of tokens. A layer call:
+  1. routes: owner rank and local slot of every (token, k) route from the placement tables;
+     routes to experts no rank owns (ids < 0, or experts left on the CPU) are dropped;
+  2. dispatch: each token goes once to every rank that owns at least one of its experts
+     (the rank's local expert list and weights travel with it: k slots, -1 padded);
+     per-destination counts by one all-to-all, then the rows and the metadata by two more;
+  3. local experts: `expert_fn(x_rows, local_ids, local_weights)` -> bf16 rows, the weighted
+     sum over the rank's experts of each received token (on the GPU: the tcgen05 prefill
+     layer, kt_gguf_moe_multi.moe_prefill, on the rank's slots);
+  4. combine: the partial rows go back by the reverse all-to-all and each token's partials
+     are summed in fp32 in rank order (deterministic) and rounded once to bf16, together with
+     an optional shared expert computed locally.
+
+Placement: `owner[e]` (rank, or -1) and `local[e]` (slot on that rank) for every logical
+expert e. `contiguous_placement(E, P)` gives rank g the experts [g*E/P, (g+1)*E/P);
+`round_robin_placement(hot, E, P)` spreads a hot list over the ranks; `snake_placement`
+deals experts listed hottest first to ranks 0..P-1, P-1..0, ... (config 2 of the benchmark:
+the 64 hot experts of a Zipf-skewed router, 8 per rank at 8 ranks).
+
+The exchange uses torch.distributed.all_to_all_single (NCCL on GPUs, gloo in the CPU tests).
+The split sizes need one device-to-host copy of the counts per call. On GPUs the plan, the row
+packing and the combine are the library's kernels (kt_ep_plan / kt_ep_pack / kt_ep_combine,
+csrc/ep.cu); `plan_dispatch` restates the same plan with PyTorch ops, which the CPU tests of the
+exchange run on gloo ranks.
+"""
+from dataclasses import dataclass
+from typing import Callable, List, Optional, Tuple
+
+import torch
+import torch.distributed as dist
+
+
+def contiguous_placement(n_experts: int, world: int) -> Tuple[torch.Tensor, torch.Tensor]:
+    if n_experts % world:
+        raise ValueError(f"{n_experts} experts do not split over {world} ranks")
+    per = n_experts // world
+    e = torch.arange(n_experts, dtype=torch.int32)
+    return (e // per).to(torch.int32), (e % per).to(torch.int32)
+
+
+def round_robin_placement(hot: torch.Tensor, n_experts: int, world: int) -> Tuple[torch.Tensor, torch.Tensor]:
+    """Hot expert hot[i] goes to rank i % world, slot i // world; the others to no rank."""
+    owner = torch.full((n_experts,), -1, dtype=torch.int32)
+    local = torch.full((n_experts,), -1, dtype=torch.int32)
+    i = torch.arange(hot.numel(), dtype=torch.int32)
+    owner[hot.long()] = i % world
+    local[hot.long()] = i // world
+    return owner, local
+
+
+def snake_placement(n_experts: int, world: int) -> Tuple[torch.Tensor, torch.Tensor]:
+    """Experts listed hottest first go to ranks 0..P-1, then P-1..0, and so on (slot = round),
+    which balances a skewed load better than plain round-robin."""
+    i = torch.arange(n_experts, dtype=torch.int32)
+    rnd, pos = i // world, i % world
+    owner = torch.where(rnd % 2 == 0, pos, world - 1 - pos).to(torch.int32)
+    return owner, rnd.to(torch.int32)
+
+
+@dataclass
+class Dispatch:
+    """Host and device bookkeeping of one call (kept for the combine)."""
+    send_counts: List[int]
+    recv_counts: List[int]
+    token_of_row: Optional[torch.Tensor] = None  # CPU path: [n_send] source token of each sent row
+    row_of: Optional[torch.Tensor] = None        # GPU path: [T, P] send row of token t for rank r, or -1
+
+
+def plan_dispatch(topk_ids: torch.Tensor, topk_weights: torch.Tensor, owner: torch.Tensor, local: torch.Tensor,
+                  world: int):
+    """Rows to send, grouped by destination rank (rank-major, tokens ascending).
+
+    Returns (token_of_row [n], dest_of_row [n], local_ids [n, k] int32, local_w [n, k] fp32,
+    send_counts [world] int64 tensor)."""
+    T, k = topk_ids.shape
+    ids = topk_ids.long()
+    valid = ids >= 0
+    safe = torch.where(valid, ids, torch.zeros_like(ids))
+    dest = torch.where(valid, owner[safe].long(), torch.full_like(ids, -1))  # [T, k]
+    lslot = torch.where(valid, local[safe].long(), torch.full_like(ids, -1))
+    # sends[r, t]: token t has at least one expert on rank r
+    sends = torch.zeros((world, T), dtype=torch.bool, device=topk_ids.device)
+    ok = dest >= 0
+    rows_t = torch.arange(T, device=topk_ids.device).unsqueeze(1).expand(T, k)
+    sends[dest[ok], rows_t[ok]] = True
+    dest_of_row, token_of_row = sends.nonzero(as_tuple=True)  # rank-major, tokens ascending
+    send_counts = sends.sum(dim=1)
+    d = dest[token_of_row]  # [n, k]
+    same = d == dest_of_row.unsqueeze(1)
+    local_ids = torch.where(same, lslot[token_of_row], torch.full_like(d, -1)).to(torch.int32)
+    local_w = torch.where(same, topk_weights[token_of_row].to(torch.float32), torch.zeros_like(d, dtype=torch.float32))
+    return token_of_row, dest_of_row, local_ids, local_w, send_counts
+
+
+class ExpertParallelMoE:
+    """One MoE layer, experts sharded over the ranks of `group` (see the module docstring)."""
+
+    def __init__(self, owner: torch.Tensor, local: torch.Tensor, expert_fn: Callable, group=None,
+                 shared_fn: Optional[Callable] = None):
+        self.group = group
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        self.owner, self.local = owner, local
+        self.expert_fn, self.shared_fn = expert_fn, shared_fn
+
+    def _a2a(self, out: torch.Tensor, inp: torch.Tensor, out_splits: List[int], in_splits: List[int]):
+        if self.world == 1:
+            out.copy_(inp)
+        else:
+            dist.all_to_all_single(out, inp, out_splits, in_splits, group=self.group)
+
+    def _plan_cuda(self, x, topk_ids, topk_weights):
+        from . import _native as N
+
+        lib = N.load()
+        dev = x.device
+        T, k = topk_ids.shape
+        P = self.world
+        if getattr(self, "_dev_tables", None) is None or self._dev_tables[0].device != dev:
+            self._dev_tables = (self.owner.to(dev, torch.int32).contiguous(), self.local.to(dev, torch.int32).contiguous())
+        owner, local = self._dev_tables
+        ids = topk_ids.to(torch.int32).contiguous()
+        w = topk_weights.to(torch.float32).contiguous()
+        ws = N.workspace(lib.kt_ep_plan_workspace_size(T, P), dev)
+        counts = torch.empty(P, dtype=torch.int32, device=dev)
+        send_token = torch.empty(T * P, dtype=torch.int32, device=dev)
+        meta = torch.empty((T * P, 2 * k), dtype=torch.int32, device=dev)
+        row_of = torch.empty((T, P), dtype=torch.int32, device=dev)
+        N.check(lib.kt_ep_plan(N.ptr(ids), N.ptr(w), T, k, N.ptr(owner), N.ptr(local), owner.numel(), P, N.ptr(counts),
+                               N.ptr(send_token), N.ptr(meta), N.ptr(row_of), N.ptr(ws), ws.numel(), N.stream_of(x)),
+                "kt_ep_plan")
+        return send_token, meta, counts, row_of
+
+    def dispatch(self, x: torch.Tensor, topk_ids: torch.Tensor, topk_weights: torch.Tensor):
+        """-> (x_recv [n_recv, K], ids_recv [n_recv, k] int32, w_recv [n_recv, k] fp32, Dispatch)"""
+        dev = x.device
+        k = topk_ids.shape[1]
+        if x.is_cuda:
+            from . import _native as N
+
+            send_token, meta, counts, row_of = self._plan_cuda(x, topk_ids, topk_weights)
+            tok = None
+        else:  # the CPU tests of the exchange
+            owner, local = self.owner.to(dev), self.local.to(dev)
+            tok, _, lid, lw, counts = plan_dispatch(topk_ids, topk_weights, owner, local, self.world)
+            row_of = None
+        recv_counts_t = torch.empty_like(counts)
+        self._a2a(recv_counts_t, counts, [1] * self.world, [1] * self.world)
+        both = torch.stack([counts, recv_counts_t]).cpu()  # the one host sync of the call
+        send_counts, recv_counts = both[0].tolist(), both[1].tolist()
+        n_send, n_recv = sum(send_counts), sum(recv_counts)
+        if x.is_cuda:
+            x = x.contiguous()
+            x_send = torch.empty((n_send, x.shape[1]), dtype=x.dtype, device=dev)
+            N.check(N.load().kt_ep_pack(N.ptr(x), x.shape[1], N.ptr(send_token), n_send, N.ptr(x_send), N.stream_of(x)),
+                    "kt_ep_pack")
+            meta_send = meta[:n_send]
+        else:
+            x_send = x[tok].contiguous()
+            meta_send = torch.cat([lid, lw.view(torch.int32)], dim=1).contiguous()  # [n, 2k] int32
+        x_recv = torch.empty((n_recv, x.shape[1]), dtype=x.dtype, device=dev)
+        meta_recv = torch.empty((n_recv, 2 * k), dtype=torch.int32, device=dev)
+        self._a2a(x_recv, x_send, recv_counts, send_counts)
+        self._a2a(meta_recv, meta_send, recv_counts, send_counts)
+        ids_recv = meta_recv[:, :k].contiguous()
+        w_recv = meta_recv[:, k:].contiguous().view(torch.float32)
+        return x_recv, ids_recv, w_recv, Dispatch(send_counts, recv_counts, tok, row_of)
+
+    def combine(self, y_recv: torch.Tensor, plan: Dispatch, T: int, shared: Optional[torch.Tensor] = None):
+        """partial rows back to their tokens: out[t] = bf16(shared[t] + sum over ranks, in rank order)"""
+        dev = y_recv.device
+        y_back = torch.empty((sum(plan.send_counts), y_recv.shape[1]), dtype=y_recv.dtype, device=dev)
+        self._a2a(y_back, y_recv, plan.send_counts, plan.recv_counts)
+        if plan.row_of is not None:
+            from . import _native as N
+
+            out = torch.empty((T, y_recv.shape[1]), dtype=y_recv.dtype, device=dev)
+            sh = shared.to(y_recv.dtype).contiguous() if shared is not None else None
+            N.check(N.load().kt_ep_combine(N.ptr(y_back) if y_back.numel() else None, N.ptr(plan.row_of), self.world,
+                                           N.ptr(sh) if sh is not None else None, T, y_recv.shape[1], N.ptr(out),
+                                           N.stream_of(y_back)), "kt_ep_combine")
+            return out
+        acc = torch.zeros((T, y_recv.shape[1]), dtype=torch.float32, device=dev)
+        if shared is not None:
+            acc += shared.float()
+        start = 0
+        for c in plan.send_counts:  # rank r's rows: each token at most once
+            if c:
+                idx = plan.token_of_row[start:start + c]
+                acc[idx] += y_back[start:start + c].float()
+            start += c
+        return acc.to(y_recv.dtype)
+
+    def __call__(self, x: torch.Tensor, topk_ids: torch.Tensor, topk_weights: torch.Tensor) -> torch.Tensor:
+        if self.world == 1 and x.is_cuda and self.shared_fn is None:
+            # one rank: no exchange; the local slots straight from the logical ids
+            local = self.local.to(x.device, torch.int32)
+            owned = (self.owner.to(x.device) == 0)
+            ids = topk_ids.long()
+            valid = (ids >= 0) & owned[ids.clamp(min=0)]
+            lid = torch.where(valid, local[ids.clamp(min=0)], torch.full_like(topk_ids, -1, dtype=torch.int32))
+            return self.expert_fn(x.contiguous(), lid.to(torch.int32).contiguous(), topk_weights.to(torch.float32).contiguous())
+        x_recv, ids_recv, w_recv, plan = self.dispatch(x, topk_ids, topk_weights)
+        if x_recv.shape[0]:
+            y_recv = self.expert_fn(x_recv, ids_recv, w_recv)
+        else:
+            y_recv = torch.empty((0, x.shape[1]), dtype=x.dtype, device=x.device)
+        shared = self.shared_fn(x) if self.shared_fn is not None else None
+        return self.combine(y_recv, plan, x.shape[0], shared)
+
+
+def prefill_expert_fn(w13: torch.Tensor, w2: torch.Tensor, type13: int, type2: int, inter: int):
+    """The rank's slots through the tcgen05 prefill layer (bf16 rows)."""
+    from . import kt_gguf_moe_multi as M
+    from . import _native as N
+
+    cache = {}
+
+    def fn(x, ids, w):
+        T, k = ids.shape
+        need = N.load().kt_moe_prefill_workspace_size(T, k, x.shape[1], inter, w13.shape[0])
+        ws = cache.get("ws")
+        if ws is None or ws.numel() < need:
+            ws = cache["ws"] = N.workspace(max(need, int(need * 1.25)), x.device)
+        return M.moe_prefill(x, w13, w2, ids, w, type13, type2, inter, workspace=ws)
+
+    return fn

@@ -109,12 +109,15 @@ def zipf_bias(rng: np.random.Generator, n_experts: int, s: float = 1.1) -> np.nd
 
 
 def make_layer(seed: int, tokens: int, hidden: int, inter: int, n_experts: int, top_k: int, type13: int, type2: int,
-               n_hot: Optional[int] = None, zipf: Optional[float] = None, renormalize: bool = False) -> MoELayer:
+               n_hot: Optional[int] = None, zipf: Optional[float] = None, renormalize: bool = False,
+               token_seed: Optional[int] = None) -> MoELayer:
     """Config generator: router logits N(0,1) (+ Zipf bias), softmax top-k; the n_hot experts
-    with the largest bias (or the first n_hot) are resident in slots 0..n_hot-1; the
-    others map to -1 like HotCache.route's slot ids."""
+    with the largest bias (or the first n_hot) are resident in slots 0..n_hot-1 (hottest
+    first); the others map to -1 like HotCache.route's slot ids. Weights and the bias come
+    from `seed`, activations and logits from `token_seed` (default: seed), so ranks can share
+    the experts and differ in tokens."""
     rng = np.random.default_rng(seed)
-    g = torch.Generator().manual_seed(seed)
+    g = torch.Generator().manual_seed(seed if token_seed is None else token_seed)
     logits = torch.randn((tokens, n_experts), generator=g)
     hot = np.arange(n_experts) if n_hot is None else None
     if zipf is not None:
