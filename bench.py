@@ -10,8 +10,11 @@ package's encoders. All data synthetic and seeded (no checkpoint is available he
 A step = one kt_moe_prefill call over the chunk (routing permutation, tcgen05 gate/up
 GEMM with SwiGLU, tcgen05 down GEMM, combine), inputs resident in HBM. With --gpus N each
 rank processes its own 16K-token chunk against its own replica of the resident experts
-(token-parallel, no data-path collective: "scaling": "weak"); the time is the max over
-ranks of CUDA-event time.
+(token-parallel, no data-path collective: "scaling": "weak"; the 130 MB resident set
+replicates trivially in 180 GB); the time is the max over ranks of CUDA-event time. --ep
+runs the same chunks expert-parallel instead (the 64 experts dealt over the ranks, tokens
+and partial outputs exchanged by NCCL all-to-all), and --config 4 the DeepSeek-V3-like
+layer expert-parallel.
 
 --config 1 / 3 print the other BASELINE configurations (one JSON line per point): config 1
 (Q8_0, 256 tokens, with the CPU baseline on the whole chunk and the rel-L2 against the fp32
@@ -59,6 +62,10 @@ def parse():
                     help="sweep token counts (config 3, or config 2 with --sweep): below 128 the decode GEMV, "
                          "from 128 the prefill GEMMs")
     ap.add_argument("--tokens-c4", type=int, default=32768, help="config 4: tokens per rank")
+    ap.add_argument("--ep", action="store_true", help="config 2 on N GPUs expert-parallel (NCCL all-to-all) "
+                                                      "instead of token-parallel replicas")
+    ap.add_argument("--ep-chunks", type=int, default=1, help="expert-parallel runs: token chunks per call whose "
+                                                             "all-to-alls overlap the other chunks' GEMMs")
     ap.add_argument("--sweep", action="store_true", help="config 2: run the decode/prefill sweep instead of the "
                                                          "headline line")
     return ap.parse_args()
@@ -423,7 +430,8 @@ def _ep_setup_config2(args, rank, world, dev):
     w13 = w13_all[mine.to(dev)].contiguous()
     w2 = w2_all[mine.to(dev)].contiguous()
     x, ids, wts = L.x.to(dev), L.topk_ids.to(dev), L.topk_weights.to(dev)
-    layer = EP.ExpertParallelMoE(owner, local, EP.prefill_expert_fn(w13, w2, L.type13, L.type2, N))
+    layer = EP.ExpertParallelMoE(owner, local, EP.prefill_expert_fn(w13, w2, L.type13, L.type2, N),
+                                 chunks=args.ep_chunks)
 
     def ref_fn(n):  # the whole layer on this GPU (all 64 slots) for this rank's first n tokens
         return M.moe_prefill(x[:n].contiguous(), w13_all, w2_all, ids[:n].contiguous(), wts[:n].contiguous(),
@@ -480,7 +488,8 @@ def _ep_setup_config4(args, rank, world, dev):
             sh_ws["ws"] = Nt.workspace(Nt.load().kt_moe_prefill_workspace_size(n, 1, K, N, 1), dev)
         return M.moe_prefill(xx, sw13, sw2, zeros[:n], ones[:n], 12, 12, N, workspace=sh_ws["ws"])
 
-    layer = EP.ExpertParallelMoE(owner, local, EP.prefill_expert_fn(w13, w2, 12, 12, N), shared_fn=shared_fn)
+    layer = EP.ExpertParallelMoE(owner, local, EP.prefill_expert_fn(w13, w2, 12, 12, N), shared_fn=shared_fn,
+                                 chunks=args.ep_chunks)
 
     def ref_fn(n):  # the whole layer on this GPU: expert e is copy e % 16, plus the shared expert
         r = M.moe_prefill(x[:n].contiguous(), w13_16[:16], w2_16[:16], (ids[:n] % 16).to(torch.int32).contiguous(),
@@ -625,7 +634,8 @@ def run_ep(args, rank, world, local_rank, cfg_id=2):
                             "parallelism": f"ep{world}",
                             "l2": "no flush: one step's working set exceeds the 126 MB L2"}, **st["config"]),
             "layer_tflops": world * st["flops"] * args.steps / (ms * 1e-3) / 1e12,
-            "ep": {"phase_ms": {"dispatch": phases[0], "local_experts": phases[1], "combine": phases[2]},
+            "ep": {"phase_ms_unpipelined": {"dispatch": phases[0], "local_experts": phases[1], "combine": phases[2]},
+                   "chunks": args.ep_chunks,
                    "rows_received_per_rank": [int(v.item()) for v in recvs],
                    "check_rel_l2_vs_single_gpu_layer": max(float(v.item()) for v in errs),
                    "collective": "torch.distributed.all_to_all_single over NCCL (counts, rows, metadata; "
@@ -911,7 +921,7 @@ def main():
     if args.config == 5:
         run_config5(args)
         return
-    if world > 1:
+    if args.ep:
         run_ep(args, rank, world, local_rank)
         return
     run_b200(args, rank, world, local_rank)

@@ -2,6 +2,8 @@
 // carving, and the launch sequences of the decode GEMV and the prefill layer.
 #include <string.h>
 
+#include <stdlib.h>
+
 #include <mutex>
 
 #include "kt_gguf_b200.h"
@@ -290,7 +292,15 @@ KT_EXPORT int kt_moe_prefill_timed(const void* x, int64_t tokens, int64_t hidden
                              p.n_tiles, p.sorted_token, p.route_pos, s);
   if (rc) return launch_rc(rc);
   mark(0);
-  const int grid = num_sms();
+  // SMs left to concurrent kernels (e.g. NCCL's while an expert-parallel layer overlaps its
+  // all-to-alls with these GEMMs): KT_B200_RESERVE_SMS, read once; the GEMMs are persistent
+  // grids and would otherwise hold every SM until they end
+  static const int reserve = [] {
+    const char* e = getenv("KT_B200_RESERVE_SMS");
+    const int v = e ? atoi(e) : 0;
+    return v > 0 ? v : 0;
+  }();
+  const int grid = num_sms() - reserve >= 2 ? num_sms() - reserve : 2;
   rc = kt_launch_gemm_gate_up(type13, x, tokens, (int)hidden, (int)inter, w13, w_is_table, n_slots, p.tiles, p.n_tiles,
                               p.sorted_token, p.h, p.status, grid, s);
   if (rc) return launch_rc(rc);

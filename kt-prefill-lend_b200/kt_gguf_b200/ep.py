@@ -95,120 +95,180 @@ def plan_dispatch(topk_ids: torch.Tensor, topk_weights: torch.Tensor, owner: tor
 
 
 class ExpertParallelMoE:
-    """One MoE layer, experts sharded over the ranks of `group` (see the module docstring)."""
+    """One MoE layer, experts sharded over the ranks of `group` (see the module docstring).
+
+    chunks > 1 pipelines the call: the tokens are split into chunks whose all-to-alls run
+    asynchronously (NCCL's stream) while other chunks compute, so the exchange hides behind
+    the expert GEMMs except for the first dispatch and the last combine."""
 
     def __init__(self, owner: torch.Tensor, local: torch.Tensor, expert_fn: Callable, group=None,
-                 shared_fn: Optional[Callable] = None):
+                 shared_fn: Optional[Callable] = None, chunks: int = 1):
         self.group = group
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
         self.owner, self.local = owner, local
         self.expert_fn, self.shared_fn = expert_fn, shared_fn
+        self.chunks = max(1, int(chunks))
+        self._dev_tables = None
 
-    def _a2a(self, out: torch.Tensor, inp: torch.Tensor, out_splits: List[int], in_splits: List[int]):
+    # ---- exchange primitives
+    def _a2a(self, out: torch.Tensor, inp: torch.Tensor, out_splits: List[int], in_splits: List[int], async_op=False):
         if self.world == 1:
             out.copy_(inp)
-        else:
-            dist.all_to_all_single(out, inp, out_splits, in_splits, group=self.group)
+            return None
+        return dist.all_to_all_single(out, inp, out_splits, in_splits, group=self.group, async_op=async_op)
 
-    def _plan_cuda(self, x, topk_ids, topk_weights):
-        from . import _native as N
+    @staticmethod
+    def _wait(work):
+        if work is not None:
+            work.wait()
 
-        lib = N.load()
+    # ---- per-chunk steps
+    def _plan(self, x, topk_ids, topk_weights):
+        """-> dict with counts (device, [P]) and what packing and combining need"""
         dev = x.device
         T, k = topk_ids.shape
         P = self.world
-        if getattr(self, "_dev_tables", None) is None or self._dev_tables[0].device != dev:
-            self._dev_tables = (self.owner.to(dev, torch.int32).contiguous(), self.local.to(dev, torch.int32).contiguous())
-        owner, local = self._dev_tables
-        ids = topk_ids.to(torch.int32).contiguous()
-        w = topk_weights.to(torch.float32).contiguous()
-        ws = N.workspace(lib.kt_ep_plan_workspace_size(T, P), dev)
-        counts = torch.empty(P, dtype=torch.int32, device=dev)
-        send_token = torch.empty(T * P, dtype=torch.int32, device=dev)
-        meta = torch.empty((T * P, 2 * k), dtype=torch.int32, device=dev)
-        row_of = torch.empty((T, P), dtype=torch.int32, device=dev)
-        N.check(lib.kt_ep_plan(N.ptr(ids), N.ptr(w), T, k, N.ptr(owner), N.ptr(local), owner.numel(), P, N.ptr(counts),
-                               N.ptr(send_token), N.ptr(meta), N.ptr(row_of), N.ptr(ws), ws.numel(), N.stream_of(x)),
-                "kt_ep_plan")
-        return send_token, meta, counts, row_of
-
-    def dispatch(self, x: torch.Tensor, topk_ids: torch.Tensor, topk_weights: torch.Tensor):
-        """-> (x_recv [n_recv, K], ids_recv [n_recv, k] int32, w_recv [n_recv, k] fp32, Dispatch)"""
-        dev = x.device
-        k = topk_ids.shape[1]
         if x.is_cuda:
             from . import _native as N
 
-            send_token, meta, counts, row_of = self._plan_cuda(x, topk_ids, topk_weights)
-            tok = None
-        else:  # the CPU tests of the exchange
-            owner, local = self.owner.to(dev), self.local.to(dev)
-            tok, _, lid, lw, counts = plan_dispatch(topk_ids, topk_weights, owner, local, self.world)
-            row_of = None
-        recv_counts_t = torch.empty_like(counts)
-        self._a2a(recv_counts_t, counts, [1] * self.world, [1] * self.world)
-        both = torch.stack([counts, recv_counts_t]).cpu()  # the one host sync of the call
-        send_counts, recv_counts = both[0].tolist(), both[1].tolist()
-        n_send, n_recv = sum(send_counts), sum(recv_counts)
+            lib = N.load()
+            if self._dev_tables is None or self._dev_tables[0].device != dev:
+                self._dev_tables = (self.owner.to(dev, torch.int32).contiguous(),
+                                    self.local.to(dev, torch.int32).contiguous())
+            owner, local = self._dev_tables
+            ids = topk_ids.to(torch.int32).contiguous()
+            w = topk_weights.to(torch.float32).contiguous()
+            ws = N.workspace(lib.kt_ep_plan_workspace_size(T, P), dev)
+            counts = torch.empty(P, dtype=torch.int32, device=dev)
+            send_token = torch.empty(T * P, dtype=torch.int32, device=dev)
+            meta = torch.empty((T * P, 2 * k), dtype=torch.int32, device=dev)
+            row_of = torch.empty((T, P), dtype=torch.int32, device=dev)
+            N.check(lib.kt_ep_plan(N.ptr(ids), N.ptr(w), T, k, N.ptr(owner), N.ptr(local), owner.numel(), P,
+                                   N.ptr(counts), N.ptr(send_token), N.ptr(meta), N.ptr(row_of), N.ptr(ws), ws.numel(),
+                                   N.stream_of(x)), "kt_ep_plan")
+            return {"counts": counts, "send_token": send_token, "meta": meta, "row_of": row_of, "tok": None}
+        owner, local = self.owner.to(dev), self.local.to(dev)
+        tok, _, lid, lw, counts = plan_dispatch(topk_ids, topk_weights, owner, local, P)  # the CPU tests
+        meta = torch.cat([lid, lw.view(torch.int32)], dim=1).contiguous()
+        return {"counts": counts, "send_token": None, "meta": meta, "row_of": None, "tok": tok}
+
+    def _pack(self, x, plan, n_send):
         if x.is_cuda:
+            from . import _native as N
+
             x = x.contiguous()
-            x_send = torch.empty((n_send, x.shape[1]), dtype=x.dtype, device=dev)
-            N.check(N.load().kt_ep_pack(N.ptr(x), x.shape[1], N.ptr(send_token), n_send, N.ptr(x_send), N.stream_of(x)),
-                    "kt_ep_pack")
-            meta_send = meta[:n_send]
-        else:
-            x_send = x[tok].contiguous()
-            meta_send = torch.cat([lid, lw.view(torch.int32)], dim=1).contiguous()  # [n, 2k] int32
-        x_recv = torch.empty((n_recv, x.shape[1]), dtype=x.dtype, device=dev)
-        meta_recv = torch.empty((n_recv, 2 * k), dtype=torch.int32, device=dev)
-        self._a2a(x_recv, x_send, recv_counts, send_counts)
-        self._a2a(meta_recv, meta_send, recv_counts, send_counts)
-        ids_recv = meta_recv[:, :k].contiguous()
-        w_recv = meta_recv[:, k:].contiguous().view(torch.float32)
-        return x_recv, ids_recv, w_recv, Dispatch(send_counts, recv_counts, tok, row_of)
+            out = torch.empty((n_send, x.shape[1]), dtype=x.dtype, device=x.device)
+            N.check(N.load().kt_ep_pack(N.ptr(x), x.shape[1], N.ptr(plan["send_token"]), n_send, N.ptr(out),
+                                        N.stream_of(x)), "kt_ep_pack")
+            return out, plan["meta"][:n_send]
+        return x[plan["tok"]].contiguous(), plan["meta"]
 
-    def combine(self, y_recv: torch.Tensor, plan: Dispatch, T: int, shared: Optional[torch.Tensor] = None):
-        """partial rows back to their tokens: out[t] = bf16(shared[t] + sum over ranks, in rank order)"""
-        dev = y_recv.device
-        y_back = torch.empty((sum(plan.send_counts), y_recv.shape[1]), dtype=y_recv.dtype, device=dev)
-        self._a2a(y_back, y_recv, plan.send_counts, plan.recv_counts)
-        if plan.row_of is not None:
+    def _combine_rows(self, y_back, plan, send_counts, out, shared):
+        """out[t] = bf16(shared[t] + the token's partial rows, fp32 in rank order)"""
+        if plan["row_of"] is not None:
             from . import _native as N
 
-            out = torch.empty((T, y_recv.shape[1]), dtype=y_recv.dtype, device=dev)
-            sh = shared.to(y_recv.dtype).contiguous() if shared is not None else None
-            N.check(N.load().kt_ep_combine(N.ptr(y_back) if y_back.numel() else None, N.ptr(plan.row_of), self.world,
-                                           N.ptr(sh) if sh is not None else None, T, y_recv.shape[1], N.ptr(out),
-                                           N.stream_of(y_back)), "kt_ep_combine")
-            return out
-        acc = torch.zeros((T, y_recv.shape[1]), dtype=torch.float32, device=dev)
+            sh = shared.to(out.dtype).contiguous() if shared is not None else None
+            N.check(N.load().kt_ep_combine(N.ptr(y_back) if y_back.numel() else None, N.ptr(plan["row_of"]), self.world,
+                                           N.ptr(sh), out.shape[0], out.shape[1], N.ptr(out), N.stream_of(out)),
+                    "kt_ep_combine")
+            return
+        acc = torch.zeros(out.shape, dtype=torch.float32, device=out.device)
         if shared is not None:
             acc += shared.float()
         start = 0
-        for c in plan.send_counts:  # rank r's rows: each token at most once
+        for c in send_counts:  # rank r's rows: each token at most once
             if c:
-                idx = plan.token_of_row[start:start + c]
+                idx = plan["tok"][start:start + c]
                 acc[idx] += y_back[start:start + c].float()
             start += c
-        return acc.to(y_recv.dtype)
+        out.copy_(acc.to(out.dtype))
 
+    # ---- one call, split into phases (for timing) ...
+    def dispatch(self, x: torch.Tensor, topk_ids: torch.Tensor, topk_weights: torch.Tensor):
+        """-> (x_recv [n_recv, K], ids_recv [n_recv, k] int32, w_recv [n_recv, k] fp32, Dispatch)"""
+        k = topk_ids.shape[1]
+        plan = self._plan(x, topk_ids, topk_weights)
+        counts = plan["counts"]
+        recv_t = torch.empty_like(counts)
+        self._a2a(recv_t, counts, [1] * self.world, [1] * self.world)
+        both = torch.stack([counts, recv_t]).cpu()  # the one host sync of the call
+        send_counts, recv_counts = both[0].tolist(), both[1].tolist()
+        x_send, meta_send = self._pack(x, plan, sum(send_counts))
+        x_recv = torch.empty((sum(recv_counts), x.shape[1]), dtype=x.dtype, device=x.device)
+        meta_recv = torch.empty((sum(recv_counts), 2 * k), dtype=torch.int32, device=x.device)
+        self._a2a(x_recv, x_send, recv_counts, send_counts)
+        self._a2a(meta_recv, meta_send, recv_counts, send_counts)
+        d = Dispatch(send_counts, recv_counts, plan["tok"], plan["row_of"])
+        d.plan = plan
+        return x_recv, meta_recv[:, :k].contiguous(), meta_recv[:, k:].contiguous().view(torch.float32), d
+
+    def combine(self, y_recv: torch.Tensor, plan: Dispatch, T: int, shared: Optional[torch.Tensor] = None):
+        """partial rows back to their tokens: out[t] = bf16(shared[t] + sum over ranks, in rank order)"""
+        y_back = torch.empty((sum(plan.send_counts), y_recv.shape[1]), dtype=y_recv.dtype, device=y_recv.device)
+        self._a2a(y_back, y_recv, plan.send_counts, plan.recv_counts)
+        out = torch.empty((T, y_recv.shape[1]), dtype=y_recv.dtype, device=y_recv.device)
+        self._combine_rows(y_back, plan.plan, plan.send_counts, out, shared)
+        return out
+
+    # ---- ... or pipelined over chunks
     def __call__(self, x: torch.Tensor, topk_ids: torch.Tensor, topk_weights: torch.Tensor) -> torch.Tensor:
+        T, K = x.shape
+        k = topk_ids.shape[1]
         if self.world == 1 and x.is_cuda and self.shared_fn is None:
             # one rank: no exchange; the local slots straight from the logical ids
             local = self.local.to(x.device, torch.int32)
-            owned = (self.owner.to(x.device) == 0)
+            owned = self.owner.to(x.device) == 0
             ids = topk_ids.long()
             valid = (ids >= 0) & owned[ids.clamp(min=0)]
             lid = torch.where(valid, local[ids.clamp(min=0)], torch.full_like(topk_ids, -1, dtype=torch.int32))
-            return self.expert_fn(x.contiguous(), lid.to(torch.int32).contiguous(), topk_weights.to(torch.float32).contiguous())
-        x_recv, ids_recv, w_recv, plan = self.dispatch(x, topk_ids, topk_weights)
-        if x_recv.shape[0]:
-            y_recv = self.expert_fn(x_recv, ids_recv, w_recv)
-        else:
-            y_recv = torch.empty((0, x.shape[1]), dtype=x.dtype, device=x.device)
+            return self.expert_fn(x.contiguous(), lid.to(torch.int32).contiguous(),
+                                  topk_weights.to(torch.float32).contiguous())
+        C = min(self.chunks, max(1, T))
+        bounds = [(T * c // C, T * (c + 1) // C) for c in range(C)]
+        # 1. plans and counts of every chunk, one host sync for all
+        plans, recvs, works = [], [], []
+        for a, b in bounds:
+            p = self._plan(x[a:b], topk_ids[a:b], topk_weights[a:b])
+            r = torch.empty_like(p["counts"])
+            works.append(self._a2a(r, p["counts"], [1] * self.world, [1] * self.world, async_op=True))
+            plans.append(p)
+            recvs.append(r)
+        for w in works:
+            self._wait(w)
+        allc = torch.stack([torch.cat([p["counts"], r]) for p, r in zip(plans, recvs)]).cpu()
+        sends = [row[:self.world].tolist() for row in allc]
+        recvc = [row[self.world:].tolist() for row in allc]
+        # 2. pack and dispatch every chunk (asynchronous all-to-alls)
+        rx, rmeta, wd = [], [], []
+        for c, (a, b) in enumerate(bounds):
+            xs, ms = self._pack(x[a:b], plans[c], sum(sends[c]))
+            xr = torch.empty((sum(recvc[c]), K), dtype=x.dtype, device=x.device)
+            mr = torch.empty((sum(recvc[c]), 2 * k), dtype=torch.int32, device=x.device)
+            wd.append((self._a2a(xr, xs, recvc[c], sends[c], async_op=True),
+                       self._a2a(mr, ms, recvc[c], sends[c], async_op=True), xs, ms))
+            rx.append(xr)
+            rmeta.append(mr)
+        # 3. experts of chunk c once its rows are here; its partials go back asynchronously
+        backs, wb = [], []
+        for c in range(C):
+            self._wait(wd[c][0])
+            self._wait(wd[c][1])
+            if rx[c].shape[0]:
+                y = self.expert_fn(rx[c], rmeta[c][:, :k].contiguous(), rmeta[c][:, k:].contiguous().view(torch.float32))
+            else:
+                y = torch.empty((0, K), dtype=x.dtype, device=x.device)
+            yb = torch.empty((sum(sends[c]), K), dtype=x.dtype, device=x.device)
+            wb.append((self._a2a(yb, y, sends[c], recvc[c], async_op=True), y))
+            backs.append(yb)
         shared = self.shared_fn(x) if self.shared_fn is not None else None
-        return self.combine(y_recv, plan, x.shape[0], shared)
+        # 4. combine
+        out = torch.empty((T, K), dtype=x.dtype, device=x.device)
+        for c, (a, b) in enumerate(bounds):
+            self._wait(wb[c][0])
+            self._combine_rows(backs[c], plans[c], sends[c], out[a:b], shared[a:b] if shared is not None else None)
+        return out
 
 
 def prefill_expert_fn(w13: torch.Tensor, w2: torch.Tensor, type13: int, type2: int, inter: int):

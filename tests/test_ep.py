@@ -81,7 +81,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _rank_main(rank, world, port, placement, q):
+def _rank_main(rank, world, port, placement, q, chunks=1):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world)
@@ -102,7 +102,7 @@ def _rank_main(rank, world, port, placement, q):
             return out
 
         x, ids, w = make_inputs(rank)
-        layer = ep.ExpertParallelMoE(owner, local, expert_fn, shared_fn=lambda xx: 0.5 * xx)
+        layer = ep.ExpertParallelMoE(owner, local, expert_fn, shared_fn=lambda xx: 0.5 * xx, chunks=chunks)
         out = layer(x, ids, w)
         want = reference(x, ids, w, owner) + 0.5 * x
         q.put((rank, float((out - want).abs().max())))
@@ -110,12 +110,12 @@ def _rank_main(rank, world, port, placement, q):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("placement", ["contiguous", "round_robin"])
-def test_two_gloo_ranks_match_reference(placement):
+@pytest.mark.parametrize("placement,chunks", [("contiguous", 1), ("round_robin", 1), ("contiguous", 3)])
+def test_two_gloo_ranks_match_reference(placement, chunks):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_rank_main, args=(r, 2, port, placement, q)) for r in range(2)]
+    procs = [ctx.Process(target=_rank_main, args=(r, 2, port, placement, q, chunks)) for r in range(2)]
     for p in procs:
         p.start()
     for p in procs:
