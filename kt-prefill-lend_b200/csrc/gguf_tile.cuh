@@ -74,7 +74,7 @@ struct KtTileDq<KT_Q4_K> {
     }
   }
   __device__ __forceinline__ void kstep_quarter(const uint8_t* slot, int off, int kk, int qt, uint32_t (&pk)[8],
-                                                const uint32_t*) const {
+                                                const uint32_t*) {
     const int hf = qt >> 1;
     uint32_t q[4];
     kt_ld_words<4>(slot, off + 16 + 32 * kk + 16 * (qt & 1), q);
@@ -102,19 +102,24 @@ template <>
 struct KtTileDq<KT_Q6_K> {
   static constexpr int KPU = 4;
   float d;
+  // k-steps 2n and 2n+1 read the same ql / qh / scale bytes (nibble part kk%2 picks the
+  // bits): they are loaded and re-aligned once, at the even k-step (kk is a compile-time
+  // constant in the producers' unrolled loop)
+  uint32_t ql[4], qh[4], sc[2];
   __device__ __forceinline__ void unit(const uint8_t* slot, int off) {
     uint32_t w[1];
     kt_ld_words<1>(slot, off + 208, w);
     d = kt_lo_half(w[0]);
   }
   __device__ __forceinline__ void kstep_quarter(const uint8_t* slot, int off, int kk, int qt, uint32_t (&pk)[8],
-                                                const uint32_t*) const {
+                                                const uint32_t*) {
     const int n = kk >> 1, part = kk & 1, hf = qt >> 1, sub = qt & 1;
-    uint32_t ql[4], qh[4], sc[1];
-    kt_ld_words<4>(slot, off + 64 * n + 32 * hf + 16 * sub, ql);
-    kt_ld_words<4>(slot, off + 128 + 32 * n + 16 * sub, qh);
-    kt_ld_words<1>(slot, off + 192 + 8 * n + 4 * part, sc);
-    const float sa = d * (float)(int8_t)(sc[0] >> (8 * (2 * hf + sub)));
+    if (part == 0) {
+      kt_ld_words<4>(slot, off + 64 * n + 32 * hf + 16 * sub, ql);
+      kt_ld_words<4>(slot, off + 128 + 32 * n + 16 * sub, qh);
+      kt_ld_words<2>(slot, off + 192 + 8 * n, sc);
+    }
+    const float sa = d * (float)(int8_t)(sc[part] >> (8 * (2 * hf + sub)));
     constexpr float M = 8388640.0f;  // 2^23 + 32: magic(code) - M = code - 32
     const int ls = 4 * part, hs = 4 * part + 2 * hf;
 #pragma unroll
@@ -143,7 +148,7 @@ struct KtTileDq<KT_IQ3_S> {
     sc = s4[0];
   }
   __device__ __forceinline__ void kstep_quarter(const uint8_t* slot, int off, int kk, int qt, uint32_t (&pk)[8],
-                                                const uint32_t* grid) const {
+                                                const uint32_t* grid) {
     const int hf = qt >> 1, ib = 2 * kk + hf, l0 = 2 * (qt & 1);
     uint32_t qs[2], qh[1], sg[1];
     kt_ld_words<2>(slot, off + 2 + 8 * ib, qs);
@@ -177,7 +182,7 @@ struct KtTileDq<KT_Q8_0> {
   static constexpr int KPU = 2;
   __device__ __forceinline__ void unit(const uint8_t*, int) {}
   __device__ __forceinline__ void kstep_quarter(const uint8_t* slot, int off, int kk, int qt, uint32_t (&pk)[8],
-                                                const uint32_t*) const {
+                                                const uint32_t*) {
     constexpr float M = 8388736.0f;
     const int bo = off + 34 * (2 * kk + (qt >> 1));
     uint32_t dw[1], q[4];

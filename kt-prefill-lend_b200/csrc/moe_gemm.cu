@@ -225,8 +225,10 @@ __global__ void __launch_bounds__(Roles<PHASE>::kThreads, 1) kt_moe_gemm_kernel(
         // slot; the unit starts at the alignment remainder of its global address
         const int off = (int)(((uintptr_t)(grow_ptr + (int64_t)u * R::UNIT_BYTES)) & 15);
         const uint8_t* slotp = sRaw + su * R::STAGE_BYTES + slot_off;
-        KtTileDq<TYPE> dq;
-        dq.unit(slotp, off);
+        // one decoder per k-step quarter of this thread (decoders may keep bytes across k-steps)
+        KtTileDq<TYPE> dq[RL::kQuarters];
+#pragma unroll
+        for (int j = 0; j < RL::kQuarters; ++j) dq[j].unit(slotp, off);
         bool ok = true;
 #pragma unroll
         for (int kk = 0; kk < R::KPU; ++kk) {
@@ -238,7 +240,7 @@ __global__ void __launch_bounds__(Roles<PHASE>::kThreads, 1) kt_moe_gemm_kernel(
 #pragma unroll
             for (int j = 0; j < RL::kQuarters; ++j) {
               uint32_t pk[8];
-              dq.kstep_quarter(slotp, off, kk, qt0 + j, pk, sGrid);
+              dq[j].kstep_quarter(slotp, off, kk, qt0 + j, pk, sGrid);
 #pragma unroll
               for (int c = 0; c < 2; ++c)
                 *reinterpret_cast<uint4*>(arow + kt_swz128(rh, 16 * (qt0 + j) + 8 * c)) =
