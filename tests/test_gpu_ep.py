@@ -39,7 +39,8 @@ def test_plan_pack_combine_kernels_match_torch_plan(cuda_device, P):
     layer = EP.ExpertParallelMoE(owner, local, None)
     layer.world = P  # plan for P ranks inside one process
     x = torch.randn((T, K), generator=g).to(torch.bfloat16).to(cuda_device)
-    send_token, meta, counts_d, row_of = layer._plan_cuda(x, ids.to(cuda_device), w.to(cuda_device))
+    plan = layer._plan(x, ids.to(cuda_device), w.to(cuda_device))
+    send_token, meta, counts_d, row_of = plan["send_token"], plan["meta"], plan["counts"], plan["row_of"]
     n = int(counts.sum())
     assert torch.equal(counts_d.cpu().long(), counts)
     assert torch.equal(send_token[:n].cpu().long(), tok)
