@@ -25,8 +25,8 @@
 //                 map that views G consecutive weight rows as one (G = rows whose bytes make a
 //                 16-byte multiple); slot tables fall back to one 1-D bulk copy per row
 //   warp P+1      B loader: phase 1 gathers this CTA's token rows of X with 16-byte cp.async
-//                 copies into the swizzled stage, together with warp P+7 (one warp's copies
-//                 alone cannot keep up); phase 2 loads H rows with one 2-D TMA per k-step
+//                 copies into the swizzled stage, 32 rows each, together with warps P+7..P+9;
+//                 phase 2 loads H rows with one 2-D TMA per k-step
 //   warp P+2      even CTA: MMA issuer (tcgen05.mma.cta_group::2, commits multicast to both
 //                 CTAs); odd CTA: forwards its stage completions to the even CTA's barrier
 //   warps P+3..P+6 epilogue: tcgen05.ld of the accumulator; phase 1 SwiGLU -> H (bf16),
@@ -45,23 +45,30 @@
 
 namespace {
 
-#ifndef KT_GATHER_WARPS
-#define KT_GATHER_WARPS 2
-#endif
-constexpr int kGatherWarps = KT_GATHER_WARPS;  // phase 1: warps gathering token rows
-
-// Warp roles per phase. Phase 1 runs 8 producer warps (two threads per A row) beside its two
-// gather warps: more producers take issue slots from the gathers, which bound phase 1.
-// Phase 2 loads B with one TMA per k-step and runs 16 producer warps (four threads per A
-// row), which shortens each producer's per-k-step latency, the bound of phase 2.
+// Warp roles per phase. Phase 1 runs 8 producer warps (two threads per A row) and four warps
+// gathering token rows (32 rows each): the gather rate grows with the number of gathering
+// warps, not with the copies per warp, and four outrun the dequant producers. Phase 2 loads B
+// with one TMA per k-step and runs 16 producer warps (four threads per A row), which shortens
+// each producer's per-k-step latency, the bound of phase 2. The epilogue warps' index modulo 4
+// is the TMEM lane quadrant they may read.
 template <int PHASE>
 struct Roles {
-  static constexpr int kProd = PHASE == 1 ? 8 : 16;           // producer warps
-  static constexpr int kRaw = kProd, kB = kProd + 1, kMma = kProd + 2, kEpi0 = kProd + 3;
-  static constexpr int kB2 = PHASE == 1 ? kProd + 7 : -1;     // further gather warps: kB2, kB2 + 1, ...
-  static constexpr int kThreads = 32 * (PHASE == 1 ? kProd + 6 + kGatherWarps : kProd + 7);
+  static constexpr int kProd = PHASE == 1 ? 8 : 16;  // producer warps
+  static constexpr int kRaw = kProd, kMma = kProd + 2, kEpi0 = kProd + 3;
+  static constexpr int kGather = PHASE == 1 ? 4 : 1;  // B loader warps: P+1, then P+7, P+8, ...
+  static constexpr int kThreads = 32 * (kProd + 6 + kGather);
   static constexpr int kQuarters = 4 * 128 / (32 * kProd);  // k-step quarters per producer thread (2 or 1)
   static_assert(kQuarters == 1 || kQuarters == 2, "two or four producer threads per A row");
+  // B loader index of a warp, or -1
+  static __device__ __forceinline__ int gather_index(int warp) {
+    if (warp == kProd + 1) return 0;
+    if (warp >= kProd + 7 && warp < kProd + 6 + kGather) return warp - kProd - 6;
+    return -1;
+  }
+};
+template <bool B>
+struct KtBool {
+  static constexpr bool value = B;
 };
 constexpr int kTN = 256;           // tokens per tile (MMA N, split between the pair)
 constexpr int kHalfN = kTN / 2;    // B rows held by each CTA
@@ -138,8 +145,8 @@ __global__ void __launch_bounds__(Roles<PHASE>::kThreads, 1) kt_moe_gemm_kernel(
                                                                   const KtGemmArgs a) {
   extern __shared__ uint8_t smem_raw[];
   using RL = Roles<PHASE>;
-  constexpr int kProdWarps = RL::kProd, kWarpRaw = RL::kRaw, kWarpB = RL::kB, kWarpMma = RL::kMma,
-                kWarpEpi0 = RL::kEpi0, kWarpB2 = RL::kB2;
+  constexpr int kProdWarps = RL::kProd, kWarpRaw = RL::kRaw, kWarpMma = RL::kMma, kWarpEpi0 = RL::kEpi0,
+                kGatherWarps = RL::kGather;
   uint8_t* smem = reinterpret_cast<uint8_t*>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   using R = Raw<TYPE>;
   uint8_t* sA = smem;
@@ -210,7 +217,7 @@ __global__ void __launch_bounds__(Roles<PHASE>::kThreads, 1) kt_moe_gemm_kernel(
     const int seg = rh >> 6, rr = rh & 63;
     const int slot_off = seg * R::SEG_BYTES + (rr / (64 / G)) * sub_pitch<TYPE>(G) + (rr % (64 / G)) * R::SLOT;
     const int wr = seg * 64 + wrow(rr, G);
-    uint64_t* stage_bar = leader ? full : bfull;  // local; the odd CTA's warp 10 forwards
+    uint64_t* stage_bar = leader ? full : bfull;  // local; the odd CTA's forwarder warp relays
     uint32_t kit = 0, uit = 0;
     for (int item = first_item; item < n_items && !*abort_flag; item += item_stride) {
       const int tile = item / n_wt, wt = item % n_wt;
@@ -225,31 +232,42 @@ __global__ void __launch_bounds__(Roles<PHASE>::kThreads, 1) kt_moe_gemm_kernel(
         // slot; the unit starts at the alignment remainder of its global address
         const int off = (int)(((uintptr_t)(grow_ptr + (int64_t)u * R::UNIT_BYTES)) & 15);
         const uint8_t* slotp = sRaw + su * R::STAGE_BYTES + slot_off;
-        // one decoder per k-step quarter of this thread (decoders may keep bytes across k-steps)
-        KtTileDq<TYPE> dq[RL::kQuarters];
+        // the unit's k-steps; A16: the unit starts on a 16-byte boundary of its slot
+        auto run_unit = [&](auto a16) -> bool {
+          constexpr bool A16 = decltype(a16)::value;
+          // one decoder per k-step quarter of this thread (decoders may keep bytes across k-steps)
+          KtTileDq<TYPE> dq[RL::kQuarters];
 #pragma unroll
-        for (int j = 0; j < RL::kQuarters; ++j) dq[j].unit(slotp, off);
-        bool ok = true;
+          for (int j = 0; j < RL::kQuarters; ++j) dq[j].template unit<A16>(slotp, off, qt0 + j);
+          bool ok = true;
 #pragma unroll
-        for (int kk = 0; kk < R::KPU; ++kk) {
-          const int s = (kit + kk) % kStages;
-          if (ok && !kt_mbar_wait(&empty[s], (((kit + kk) / kStages) & 1) ^ 1, a.status, abort_flag)) ok = false;
-          if (ok) {
-            uint8_t* arow = sA + s * kAStageBytes;
-            // quarters beat one wider half per thread here: more independent loads in flight
+          for (int kk = 0; kk < R::KPU; ++kk) {
+            const int s = (kit + kk) % kStages;
+            if (ok && !kt_mbar_wait(&empty[s], (((kit + kk) / kStages) & 1) ^ 1, a.status, abort_flag)) ok = false;
+            if (ok) {
+              uint8_t* arow = sA + s * kAStageBytes;
+              // quarters beat one wider half per thread here: more independent loads in flight
 #pragma unroll
-            for (int j = 0; j < RL::kQuarters; ++j) {
-              uint32_t pk[8];
-              dq[j].kstep_quarter(slotp, off, kk, qt0 + j, pk, sGrid);
+              for (int j = 0; j < RL::kQuarters; ++j) {
+                uint32_t pk[8];
+                dq[j].template kstep_quarter<A16>(slotp, off, kk, qt0 + j, pk, sGrid);
 #pragma unroll
-              for (int c = 0; c < 2; ++c)
-                *reinterpret_cast<uint4*>(arow + kt_swz128(rh, 16 * (qt0 + j) + 8 * c)) =
-                    make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
+                for (int c = 0; c < 2; ++c)
+                  *reinterpret_cast<uint4*>(arow + kt_swz128(rh, 16 * (qt0 + j) + 8 * c)) =
+                      make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
+              }
+              kt_fence_proxy_async_smem();
+              __syncwarp();
+              if (lane == 0) kt_mbar_arrive(&stage_bar[s]);
             }
-            kt_fence_proxy_async_smem();
-            __syncwarp();
-            if (lane == 0) kt_mbar_arrive(&stage_bar[s]);
           }
+          return ok;
+        };
+        bool ok;
+        if constexpr (KtTileDq<TYPE>::kAlignable) {
+          ok = off == 0 ? run_unit(KtBool<true>()) : run_unit(KtBool<false>());
+        } else {
+          ok = run_unit(KtBool<false>());
         }
         kit += R::KPU;
         if (!ok) break;
@@ -306,9 +324,9 @@ __global__ void __launch_bounds__(Roles<PHASE>::kThreads, 1) kt_moe_gemm_kernel(
                       reinterpret_cast<const void*>(src[i]), len[i], &raw_full[su]);
       }
     }
-  } else if (warp == kWarpB || (PHASE == 1 && warp >= kWarpB2)) {
+  } else if (RL::gather_index(warp) >= 0) {
     // ---------------------------------------------------------------- B loaders
-    const int gw = warp == kWarpB ? 0 : 1 + (warp - kWarpB2);
+    const int gw = RL::gather_index(warp);
     constexpr int NR = kHalfN / (4 * kGatherWarps);  // rows per lane per k-step (phase 1)
     uint32_t kit = 0;
     for (int item = first_item; item < n_items && !*abort_flag; item += item_stride) {
