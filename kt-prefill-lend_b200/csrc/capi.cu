@@ -96,6 +96,7 @@ struct PreWs {
   int32_t* hist;  // per permute block and slot: route count, then first sorted position
   int32_t* tiles;
   int32_t* n_tiles;
+  int32_t* chunks;
   int32_t* sorted_token;
   int32_t* route_pos;
   uint16_t* h;
@@ -113,6 +114,7 @@ PreWs pre_ws(void* ws, int64_t tokens, int64_t top_k, int64_t hidden, int64_t in
   p.hist = c.take<int32_t>((size_t)kt_permute_hist_ints(R, n_slots));
   p.tiles = c.take<int32_t>(3 * (size_t)(R / tn + n_slots + 1));
   p.n_tiles = c.take<int32_t>(4);
+  p.chunks = c.take<int32_t>(3 * (size_t)(R / tn + n_slots + 1));
   p.sorted_token = c.take<int32_t>(R);
   p.route_pos = c.take<int32_t>(R);
   p.h = c.take<uint16_t>((size_t)R * inter, 1024);
@@ -288,8 +290,8 @@ KT_EXPORT int kt_moe_prefill_timed(const void* x, int64_t tokens, int64_t hidden
   };
   const int64_t R = tokens * top_k;
   if (cudaMemsetAsync(p.status, 0, sizeof(int), s) != cudaSuccess) return KT_ERR_CUDA;
-  int rc = kt_launch_permute(topk_ids, R, (int)top_k, n_slots, kt_gemm_tile_tokens(), p.counts, p.hist, p.tiles,
-                             p.n_tiles, p.sorted_token, p.route_pos, s);
+  int rc = kt_launch_permute(topk_ids, R, (int)top_k, n_slots, kt_gemm_tile_tokens(), kt_gemm_chunk_tiles(), p.counts,
+                             p.hist, p.tiles, p.n_tiles, p.chunks, p.sorted_token, p.route_pos, s);
   if (rc) return launch_rc(rc);
   mark(0);
   // SMs left to concurrent kernels (e.g. NCCL's while an expert-parallel layer overlaps its
@@ -305,9 +307,8 @@ KT_EXPORT int kt_moe_prefill_timed(const void* x, int64_t tokens, int64_t hidden
                               p.sorted_token, p.h, p.status, grid, s);
   if (rc) return launch_rc(rc);
   mark(1);
-  rc = kt_launch_gemm_down(type2, p.h, R, (int)hidden, (int)inter, w2, w_is_table, n_slots, p.tiles, p.n_tiles, p.y,
-                           p.status,
-                           grid, s);
+  rc = kt_launch_gemm_down(type2, p.h, R, (int)hidden, (int)inter, w2, w_is_table, n_slots, p.tiles, p.n_tiles,
+                           p.chunks, p.y, p.status, grid, s);
   if (rc) return launch_rc(rc);
   mark(2);
   rc = kt_launch_combine_sorted(p.y, p.route_pos, topk_weights, tokens, top_k, hidden, (uint16_t*)out, s);

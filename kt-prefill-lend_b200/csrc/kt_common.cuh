@@ -198,6 +198,11 @@ __device__ __forceinline__ void kt_tma_2d(void* dst, const CUtensorMap* map, int
       : "memory");
 }
 
+// L2 prefetch of one box of a 2-D tensor map (coordinates past the tensor are ignored)
+__device__ __forceinline__ void kt_tma_prefetch_2d(const CUtensorMap* map, int x, int y) {
+  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(map), "r"(x), "r"(y) : "memory");
+}
+
 // four rows (y0..y3) of a 2-D tensor map whose box is one row high, columns x..x+box-1
 __device__ __forceinline__ void kt_tma_gather4(void* dst, const CUtensorMap* map, int x, int y0, int y1, int y2, int y3,
                                                uint64_t* bar) {

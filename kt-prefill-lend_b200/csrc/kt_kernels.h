@@ -14,7 +14,8 @@ struct KtGemmArgs {
   int N;                        // expert intermediate size
   int K_out;                    // rows of W2 (hidden size); phase 1: unused
   const int32_t* tiles;         // [n_tiles][3]: slot, first sorted position, tokens (<= 256)
-  const int32_t* n_tiles;       // device scalar
+  const int32_t* n_tiles;       // device scalars: tiles, resident routes, chunks
+  const int32_t* chunks;        // [n_chunks][3]: slot, first sorted row, rows (down projection, resident A)
   int n_wtiles;                 // weight tiles per token tile
   const int32_t* sorted_token;  // token of each sorted position (phase 1)
   uint16_t* out;                // bf16 output rows (H or Y), row = sorted position
@@ -45,20 +46,23 @@ int kt_launch_topk_grouped(const float* logits, const float* bias, int64_t T, in
                            int renorm, float scale, float* weights, int32_t* ids, cudaStream_t s);
 
 // prefill permutation: routes sorted by slot, token tiles of kt_gemm_tile_tokens() rows;
-// hist holds kt_permute_hist_ints() ints; n_tiles[0] = tiles, n_tiles[1] = resident routes
+// hist holds kt_permute_hist_ints() ints; n_tiles[0] = tiles, n_tiles[1] = resident routes,
+// n_tiles[2] = chunks: runs of at most chunk_tiles consecutive tiles of one slot, as
+// chunks[3c..3c+2] = slot, first sorted row, rows (capacity: that of the tile list)
 constexpr int kPermMaxSlots = 8192;
 int64_t kt_permute_hist_ints(int64_t routes, int n_slots);
-int kt_launch_permute(const int32_t* ids, int64_t routes, int top_k, int n_slots, int tile_tokens, int32_t* counts,
-                      int32_t* hist, int32_t* tiles, int32_t* n_tiles, int32_t* sorted_token, int32_t* route_pos,
-                      cudaStream_t s);
+int kt_launch_permute(const int32_t* ids, int64_t routes, int top_k, int n_slots, int tile_tokens, int chunk_tiles,
+                      int32_t* counts, int32_t* hist, int32_t* tiles, int32_t* n_tiles, int32_t* chunks,
+                      int32_t* sorted_token, int32_t* route_pos, cudaStream_t s);
 
 int kt_launch_gemm_gate_up(int type, const void* x, int64_t T, int K, int N, const void* w13, int table, int n_slots,
                            const int32_t* tiles, const int32_t* n_tiles, const int32_t* sorted_token, void* h,
                            int* status, int grid, cudaStream_t s);
 int kt_launch_gemm_down(int type, const void* h, int64_t R, int K, int N, const void* w2, int table, int n_slots,
-                        const int32_t* tiles,
-                        const int32_t* n_tiles, void* y, int* status, int grid, cudaStream_t s);
+                        const int32_t* tiles, const int32_t* n_tiles, const int32_t* chunks, void* y, int* status,
+                        int grid, cudaStream_t s);
 int kt_gemm_tile_tokens();
+int kt_gemm_chunk_tiles();  // tiles per chunk of the down projection's work units
 
 // expert-parallel plumbing (ep.cu): dispatch plan, row packing, combine of partials (bf16 rows)
 int64_t kt_ep_plan_ints(int64_t T, int P);

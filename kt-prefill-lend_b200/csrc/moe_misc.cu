@@ -460,9 +460,11 @@ __device__ __forceinline__ int32_t kt_block_exclusive_scan(int32_t v, int32_t* w
 
 // warp w handles slots w, w + 32, ...; lanes walk the blocks (independent loads in flight)
 __global__ void __launch_bounds__(kPermBlock) kt_perm_scan_kernel(int32_t* __restrict__ hist, int n_blocks, int n_slots,
-                                                                  int tile_tokens, int32_t* __restrict__ counts,
+                                                                  int tile_tokens, int chunk_tiles,
+                                                                  int32_t* __restrict__ counts,
                                                                   int32_t* __restrict__ tiles,
-                                                                  int32_t* __restrict__ n_tiles) {
+                                                                  int32_t* __restrict__ n_tiles,
+                                                                  int32_t* __restrict__ chunks) {
   __shared__ int32_t warp_sums[32];
   __shared__ int32_t sbase[kPermMaxSlots];
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
@@ -478,16 +480,25 @@ __global__ void __launch_bounds__(kPermBlock) kt_perm_scan_kernel(int32_t* __res
   // 2. slot bases and tile offsets: exclusive scans over the slots (thread t owns [e0, e1))
   const int per = (n_slots + blockDim.x - 1) / blockDim.x;
   const int e0 = min(n_slots, (int)threadIdx.x * per), e1 = min(n_slots, e0 + per);
-  int32_t my_routes = 0, my_tiles = 0;
+  int32_t my_routes = 0, my_tiles = 0, my_chunks = 0;
   for (int e = e0; e < e1; ++e) {
+    const int32_t nt = (counts[e] + tile_tokens - 1) / tile_tokens;
     my_routes += counts[e];
-    my_tiles += (counts[e] + tile_tokens - 1) / tile_tokens;
+    my_tiles += nt;
+    my_chunks += (nt + chunk_tiles - 1) / chunk_tiles;
   }
-  int32_t total_routes, total_tiles;
+  int32_t total_routes, total_tiles, total_chunks;
   int32_t off = kt_block_exclusive_scan(my_routes, warp_sums, &total_routes);
   int32_t t = kt_block_exclusive_scan(my_tiles, warp_sums, &total_tiles);
+  int32_t ch = kt_block_exclusive_scan(my_chunks, warp_sums, &total_chunks);
   for (int e = e0; e < e1; ++e) {
     const int32_t c = counts[e];
+    const int32_t nt = (c + tile_tokens - 1) / tile_tokens;
+    for (int32_t k = 0; k < nt; k += chunk_tiles, ++ch) {
+      chunks[3 * ch + 0] = e;
+      chunks[3 * ch + 1] = off + k * tile_tokens;
+      chunks[3 * ch + 2] = min(chunk_tiles * tile_tokens, c - k * tile_tokens);
+    }
     for (int32_t r = 0; r < c; r += tile_tokens, ++t) {
       tiles[3 * t + 0] = e;
       tiles[3 * t + 1] = off + r;
@@ -516,6 +527,7 @@ __global__ void __launch_bounds__(kPermBlock) kt_perm_scan_kernel(int32_t* __res
   if (threadIdx.x == 0) {
     n_tiles[0] = total_tiles;
     n_tiles[1] = total_routes;
+    n_tiles[2] = total_chunks;
   }
 }
 
@@ -538,14 +550,15 @@ __global__ void __launch_bounds__(kPermBlock) kt_perm_scatter_kernel(const int32
 
 int64_t kt_permute_hist_ints(int64_t routes, int n_slots) { return ((routes + kPermBlock - 1) / kPermBlock) * n_slots; }
 
-int kt_launch_permute(const int32_t* ids, int64_t routes, int top_k, int n_slots, int tile_tokens, int32_t* counts,
-                      int32_t* hist, int32_t* tiles, int32_t* n_tiles, int32_t* sorted_token, int32_t* route_pos,
-                      cudaStream_t s) {
-  if (n_slots <= 0 || n_slots > kPermMaxSlots) return -1;
+int kt_launch_permute(const int32_t* ids, int64_t routes, int top_k, int n_slots, int tile_tokens, int chunk_tiles,
+                      int32_t* counts, int32_t* hist, int32_t* tiles, int32_t* n_tiles, int32_t* chunks,
+                      int32_t* sorted_token, int32_t* route_pos, cudaStream_t s) {
+  if (n_slots <= 0 || n_slots > kPermMaxSlots || chunk_tiles <= 0) return -1;
   const int nb = (int)((routes + kPermBlock - 1) / kPermBlock);
   if (nb > 0)
     kt_perm_hist_kernel<<<nb, kPermBlock, n_slots * sizeof(int32_t), s>>>(ids, routes, n_slots, hist, route_pos);
-  kt_perm_scan_kernel<<<1, kPermBlock, 0, s>>>(hist, nb, n_slots, tile_tokens, counts, tiles, n_tiles);
+  kt_perm_scan_kernel<<<1, kPermBlock, 0, s>>>(hist, nb, n_slots, tile_tokens, chunk_tiles, counts, tiles, n_tiles,
+                                               chunks);
   if (nb > 0)
     kt_perm_scatter_kernel<<<nb, kPermBlock, 0, s>>>(ids, routes, top_k, n_slots, hist, sorted_token, route_pos);
   return 0;

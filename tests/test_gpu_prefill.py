@@ -147,3 +147,35 @@ def test_prefill_deterministic(cuda_device):
     a, _, _ = run_prefill(L, cuda_device)
     b, _, _ = run_prefill(L, cuda_device)
     assert torch.equal(a, b)
+
+
+@pytest.mark.parametrize("type13,type2", [(8, 8), (12, 14)])
+def test_prefill_long_reduction(cuda_device, type13, type2):
+    # inter 768: the down projection's reduction (12 k-steps) is too long to keep resident and
+    # runs through the streaming kernel (Q6_K rows of 630 bytes: 8-row raw groups)
+    L = synth.make_layer(seed=type13 + type2, tokens=256, hidden=512, inter=768, n_experts=6, top_k=3,
+                         type13=type13, type2=type2, n_hot=6)
+    check_layer(L, cuda_device)
+
+
+def test_prefill_down_resident_matches_streaming(cuda_device, monkeypatch):
+    # one slot with 6 token tiles (chunks of 4 + 2 tiles), one with a single partial tile, and
+    # others small: the resident-strip down kernel and the streaming one compute each tile
+    # with the same MMA order, so H, Y and the output agree bit for bit
+    T, k = 1600, 2
+    L = synth.make_layer(seed=12, tokens=T, hidden=1024, inter=512, n_experts=5, top_k=k, type13=12, type2=14, n_hot=5)
+    ids = L.topk_ids.clone()
+    ids[:1400, 0] = 0
+    ids[1400:, 0] = 1
+    L.topk_ids = ids
+    out_res, st_res, _ = run_prefill(L, cuda_device)
+    monkeypatch.setenv("KT_B200_DOWN_STREAM", "1")
+    out_str, st_str, _ = run_prefill(L, cuda_device)
+    # Y per route (the order of sorted rows within a slot may differ between calls)
+    def y_of_routes(st):
+        rp = st["route_pos"]
+        return st["y"][rp[rp >= 0].long().to(st["y"].device)]
+
+    assert torch.equal(y_of_routes(st_res), y_of_routes(st_str))
+    assert torch.equal(out_res, out_str)
+    check_layer(L, cuda_device)
