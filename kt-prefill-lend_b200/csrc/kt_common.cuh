@@ -131,6 +131,13 @@ __device__ __forceinline__ bool kt_mbar_wait(uint64_t* bar, uint32_t parity, int
   return false;
 }
 
+// spin for `ns` nanoseconds of wall time (the global timer), bounded by construction
+__device__ __forceinline__ void kt_drain_ns(uint64_t ns) {
+  const uint64_t t0 = kt_globaltimer_ns();
+  while (kt_globaltimer_ns() - t0 < ns) {
+  }
+}
+
 // ------------------------------------------------------------------ clusters (CTA pairs)
 
 __device__ __forceinline__ uint32_t kt_cluster_rank() {

@@ -503,6 +503,9 @@ __global__ void __launch_bounds__(Roles<PHASE>::kThreads, 1) kt_moe_gemm_kernel(
 
   kt_tc_fence_before();
   __syncthreads();
+  // after a timed-out wait the loaders may have copies (TMA, bulk, cp.async) in flight that no
+  // role waited for: let them land in this CTA's shared memory before it can exit
+  if (*abort_flag) kt_drain_ns(200000);
   kt_cluster_sync();  // neither CTA leaves while the pair's MMAs may read its shared memory
   if (warp == kWarpMma) {
     kt_tc_fence_after();
@@ -902,6 +905,9 @@ __global__ void __launch_bounds__(ResRoles::kThreads, 1) kt_moe_down_res_kernel(
 
   kt_tc_fence_before();
   __syncthreads();
+  // after a timed-out wait the loaders may have copies (TMA, bulk, cp.async) in flight that no
+  // role waited for: let them land in this CTA's shared memory before it can exit
+  if (*abort_flag) kt_drain_ns(200000);
   kt_cluster_sync();  // neither CTA leaves while the pair's MMAs may read its shared memory
   if (warp == RL::kMma) {
     kt_tc_fence_after();
