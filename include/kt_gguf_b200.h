@@ -14,7 +14,10 @@
  * reads after the stream has finished.
  *
  * Types: ggml type ids KT_GGML_Q8_0 (8), KT_GGML_Q4_K (12), KT_GGML_Q6_K (14),
- * KT_GGML_IQ3_S (21). Activation dtypes: KT_DTYPE_F32 (0), KT_DTYPE_F16 (1), KT_DTYPE_BF16 (2).
+ * KT_GGML_IQ3_S (21) everywhere; the decode GEMV, the dense GEMV and the dequantizer also
+ * take the 32-value blocks KT_GGML_Q4_0 (2), KT_GGML_Q4_1 (3), KT_GGML_Q5_0 (6),
+ * KT_GGML_Q5_1 (7) and KT_GGML_IQ4_NL (20) (the prefill layer returns KT_ERR_TYPE for them).
+ * Activation dtypes: KT_DTYPE_F32 (0), KT_DTYPE_F16 (1), KT_DTYPE_BF16 (2).
  *
  * Weight layout (as the reference's KTGGUFHotExpertsMethod, hot/kt_gguf_hot.py:17-20):
  *   w13  uint8 [n_slots, 2*inter, row_bytes(hidden)]   rows [gate; up]
@@ -45,7 +48,12 @@ extern "C" {
 #define KT_DEV_OK 0
 #define KT_DEV_TIMEOUT 1
 
+#define KT_GGML_Q4_0 2
+#define KT_GGML_Q4_1 3
+#define KT_GGML_Q5_0 6
+#define KT_GGML_Q5_1 7
 #define KT_GGML_Q8_0 8
+#define KT_GGML_IQ4_NL 20
 #define KT_GGML_Q4_K 12
 #define KT_GGML_Q6_K 14
 #define KT_GGML_IQ3_S 21

@@ -16,7 +16,7 @@ namespace {
 
 inline cudaStream_t S(void* s) { return reinterpret_cast<cudaStream_t>(s); }
 
-inline bool type_ok(int t) { return t == KT_Q8_0 || t == KT_Q4_K || t == KT_Q6_K || t == KT_IQ3_S; }
+inline bool type_ok(int t) { return kt_gemv_type(t); }  // decode GEMV, dequantization, row sizes
 inline bool dtype_ok(int d) { return d == KT_DT_F32 || d == KT_DT_F16 || d == KT_DT_BF16; }
 
 inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
@@ -274,7 +274,7 @@ KT_EXPORT int kt_moe_prefill_timed(const void* x, int64_t tokens, int64_t hidden
                                    const int32_t* topk_ids, const float* topk_weights, int64_t top_k, const void* w13,
                                    int type13, const void* w2, int type2, int w_is_table, int n_slots, void* out,
                                    void* workspace, size_t workspace_bytes, void* stream, void* const* stage_events) {
-  if (!type_ok(type13) || !type_ok(type2)) return KT_ERR_TYPE;
+  if (!kt_prefill_type(type13) || !kt_prefill_type(type2)) return KT_ERR_TYPE;
   if (tokens < 0 || top_k <= 0 || top_k > 32 || n_slots <= 0 || n_slots > kPermMaxSlots || hidden <= 0 || inter <= 0)
     return KT_ERR_ARG;
   if (hidden % 256 || inter % 256 || hidden > (1 << 20) || inter > (1 << 20)) return KT_ERR_ARG;

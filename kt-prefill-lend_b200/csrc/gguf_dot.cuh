@@ -18,6 +18,28 @@ template <>
 struct KtChunk<KT_Q8_0> {
   static constexpr int QK = 32, BYTES = 34, CPB = 4, VDR = 2;
 };
+// 32-value blocks of the legacy family and IQ4_NL: two chunks of 8 nibble pairs per block
+// (the reference's VDR 2 over QI 4 ints: values [8c, 8c+8) and [16+8c, 16+8c+8) of chunk c)
+template <>
+struct KtChunk<KT_Q4_0> {
+  static constexpr int QK = 32, BYTES = 18, CPB = 2, VDR = 2;
+};
+template <>
+struct KtChunk<KT_Q4_1> {
+  static constexpr int QK = 32, BYTES = 20, CPB = 2, VDR = 2;
+};
+template <>
+struct KtChunk<KT_Q5_0> {
+  static constexpr int QK = 32, BYTES = 22, CPB = 2, VDR = 2;
+};
+template <>
+struct KtChunk<KT_Q5_1> {
+  static constexpr int QK = 32, BYTES = 24, CPB = 2, VDR = 2;
+};
+template <>
+struct KtChunk<KT_IQ4_NL> {
+  static constexpr int QK = 32, BYTES = 18, CPB = 2, VDR = 2;
+};
 template <>
 struct KtChunk<KT_Q4_K> {
   static constexpr int QK = 256, BYTES = 144, CPB = 16, VDR = 2;
@@ -46,6 +68,110 @@ __device__ __forceinline__ float kt_vd_q8_0(const uint8_t* bx, const uint8_t* yq
   const float d80 = kt_h2f(*reinterpret_cast<const uint16_t*>(bx));
   const float d81 = kt_q8_1_dd(yd);
   return d80 * d81 * sumi;
+}
+
+// ---- legacy 32-value blocks: chunk iqs in {0, 2} covers the nibble bytes [4iqs, 4iqs+8):
+// low nibbles are values 4iqs.., high nibbles values 16+4iqs.. (q8_1 ints iqs+i and iqs+i+4)
+__device__ __forceinline__ float2 kt_ds8(const uint8_t* yd) { return __half22float2(*reinterpret_cast<const half2*>(yd)); }
+
+// Q4_0 (d, qs[16]): d * (sum(q * u) * d8 - 4 * s8); the 4 is 8 (the code offset) times this
+// chunk's share of the block's sum of activations s8 (2 of 4 ints)
+__device__ __forceinline__ float kt_vd_q4_0(const uint8_t* bx, const uint8_t* yq, const uint8_t* yd, int iqs) {
+  int sumi = 0;
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const int v = kt_ld_b2(bx + 2 + 4 * (iqs + i));
+    sumi = __dp4a(v & 0x0F0F0F0F, kt_ld_b4(yq + 4 * (iqs + i)), sumi);
+    sumi = __dp4a((v >> 4) & 0x0F0F0F0F, kt_ld_b4(yq + 4 * (iqs + i + 4)), sumi);
+  }
+  const float2 ds8 = kt_ds8(yd);
+  return kt_h2f(*reinterpret_cast<const uint16_t*>(bx)) * (sumi * ds8.x - 4 * ds8.y);
+}
+
+// Q4_1 (half2 (d, m), qs[16]): the products d*d8 and m*s8 are formed in half precision, like
+// the reference (__hmul2), then sum(q * u) * (d*d8) + (m*s8) / 2 (this chunk's half of m*s8)
+__device__ __forceinline__ float kt_vd_q4_1(const uint8_t* bx, const uint8_t* yq, const uint8_t* yd, int iqs) {
+  int sumi = 0;
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const int v = kt_ld_b4(bx + 4 + 4 * (iqs + i));
+    sumi = __dp4a(v & 0x0F0F0F0F, kt_ld_b4(yq + 4 * (iqs + i)), sumi);
+    sumi = __dp4a((v >> 4) & 0x0F0F0F0F, kt_ld_b4(yq + 4 * (iqs + i + 4)), sumi);
+  }
+  const float2 t = __half22float2(__hmul2(*reinterpret_cast<const half2*>(bx), *reinterpret_cast<const half2*>(yd)));
+  return sumi * t.x + t.y / 2;
+}
+
+// fifth bits of the 4 low-nibble (vl) and 4 high-nibble (vh) codes of int i of a Q5 block:
+// qh bit 4i+j -> bit 8j+4 of the low word, bit 16+4i+j -> bit 8j+4 of the high word
+__device__ __forceinline__ void kt_q5_codes(int ql, int qh, int i, int& lo, int& hi) {
+  const int h = qh >> (4 * i);
+  lo = (ql & 0x0F0F0F0F) | ((h << 4) & 0x10) | ((h << 11) & 0x1000) | ((h << 18) & 0x100000) | ((h << 25) & 0x10000000);
+  hi = ((ql >> 4) & 0x0F0F0F0F) | ((h >> 12) & 0x10) | ((h >> 5) & 0x1000) | ((h << 2) & 0x100000) |
+       ((h << 9) & 0x10000000);
+}
+
+// Q5_0 (d, qh[4], qs[16]): d * (sum(q * u) * d8 - 8 * s8)
+__device__ __forceinline__ float kt_vd_q5_0(const uint8_t* bx, const uint8_t* yq, const uint8_t* yd, int iqs) {
+  const int qh = kt_ld_b2(bx + 2);
+  int sumi = 0;
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    int lo, hi;
+    kt_q5_codes(kt_ld_b2(bx + 6 + 4 * (iqs + i)), qh, iqs + i, lo, hi);
+    sumi = __dp4a(lo, kt_ld_b4(yq + 4 * (iqs + i)), sumi);
+    sumi = __dp4a(hi, kt_ld_b4(yq + 4 * (iqs + i + 4)), sumi);
+  }
+  const float2 ds8 = kt_ds8(yd);
+  return kt_h2f(*reinterpret_cast<const uint16_t*>(bx)) * (sumi * ds8.x - 8 * ds8.y);
+}
+
+// Q5_1 (half2 (d, m), qh[4], qs[16]): as Q4_1 with 5-bit codes
+__device__ __forceinline__ float kt_vd_q5_1(const uint8_t* bx, const uint8_t* yq, const uint8_t* yd, int iqs) {
+  const int qh = kt_ld_b4(bx + 4);
+  int sumi = 0;
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    int lo, hi;
+    kt_q5_codes(kt_ld_b4(bx + 8 + 4 * (iqs + i)), qh, iqs + i, lo, hi);
+    sumi = __dp4a(lo, kt_ld_b4(yq + 4 * (iqs + i)), sumi);
+    sumi = __dp4a(hi, kt_ld_b4(yq + 4 * (iqs + i + 4)), sumi);
+  }
+  const float2 t = __half22float2(__hmul2(*reinterpret_cast<const half2*>(bx), *reinterpret_cast<const half2*>(yd)));
+  return sumi * t.x + t.y / 2;
+}
+
+// the IQ4_NL code book, 16 signed levels (-127 ... 113), four per word as bytes
+#define KT_IQ4NL_W0 0xBFAD9881u
+#define KT_IQ4NL_W1 0xF6EADDCFu
+#define KT_IQ4NL_W2 0x26190D01u
+#define KT_IQ4NL_W3 0x71594535u
+__device__ __forceinline__ int kt_iq4nl_level(int code) {
+  const uint32_t w = code < 4 ? KT_IQ4NL_W0 : code < 8 ? KT_IQ4NL_W1 : code < 12 ? KT_IQ4NL_W2 : KT_IQ4NL_W3;
+  return (int)(int8_t)(w >> (8 * (code & 3)));
+}
+// four codes (the low nibbles of the bytes of n, high nibbles zero) mapped through the code
+// book into bytes: the low 3 bits of each code select a byte among the first or the last
+// eight levels (two byte permutes), bit 3 picks between them
+__device__ __forceinline__ int kt_iq4nl_bytes(uint32_t n) {
+  const uint32_t x = n & 0x07070707u, y = x | (x >> 4);
+  const uint32_t sel = (y & 0xffu) | ((y >> 8) & 0xff00u);
+  const uint32_t lo = __byte_perm(KT_IQ4NL_W0, KT_IQ4NL_W1, sel), hi = __byte_perm(KT_IQ4NL_W2, KT_IQ4NL_W3, sel);
+  const uint32_t m = ((n >> 3) & 0x01010101u) * 0xffu;
+  return (int)((lo & ~m) | (hi & m));
+}
+
+// IQ4_NL (d, qs[16]): d * d8 * (sum over the low-nibble levels + sum over the high ones)
+__device__ __forceinline__ float kt_vd_iq4_nl(const uint8_t* bx, const uint8_t* yq, const uint8_t* yd, int iqs) {
+  int sumi1 = 0, sumi2 = 0;
+#pragma unroll
+  for (int l = 0; l < 2; ++l) {
+    const uint32_t q = (uint32_t)kt_ld_b2(bx + 2 + 4 * (iqs + l));
+    sumi1 = __dp4a(kt_iq4nl_bytes(q & 0x0F0F0F0Fu), kt_ld_b4(yq + 4 * (iqs + l)), sumi1);
+    sumi2 = __dp4a(kt_iq4nl_bytes((q >> 4) & 0x0F0F0F0Fu), kt_ld_b4(yq + 4 * (iqs + l + 4)), sumi2);
+  }
+  const float d = kt_h2f(*reinterpret_cast<const uint16_t*>(bx)) * kt_q8_1_dd(yd);
+  return d * (sumi1 + sumi2);
 }
 
 // ---- Q4_K: 16 values from sub-blocks (bq8_offset, bq8_offset + 1); iqs in {0,2,...,30}
@@ -149,6 +275,11 @@ template <int TYPE>
 __device__ __forceinline__ float kt_vec_dot(const uint8_t* bx, const uint8_t* yq, const uint8_t* yd, int iqs,
                                             const uint32_t* grid) {
   if constexpr (TYPE == KT_Q8_0) return kt_vd_q8_0(bx, yq, yd, iqs);
+  if constexpr (TYPE == KT_Q4_0) return kt_vd_q4_0(bx, yq, yd, iqs);
+  if constexpr (TYPE == KT_Q4_1) return kt_vd_q4_1(bx, yq, yd, iqs);
+  if constexpr (TYPE == KT_Q5_0) return kt_vd_q5_0(bx, yq, yd, iqs);
+  if constexpr (TYPE == KT_Q5_1) return kt_vd_q5_1(bx, yq, yd, iqs);
+  if constexpr (TYPE == KT_IQ4_NL) return kt_vd_iq4_nl(bx, yq, yd, iqs);
   if constexpr (TYPE == KT_Q4_K) return kt_vd_q4_k(bx, yq, yd, iqs);
   if constexpr (TYPE == KT_Q6_K) return kt_vd_q6_k(bx, yq, yd, iqs);
   if constexpr (TYPE == KT_IQ3_S) return kt_vd_iq3_s(bx, yq, yd, iqs, grid);
@@ -223,11 +354,36 @@ __device__ __forceinline__ void kt_dq32_iq3_s(const uint8_t* b, int sub, float* 
   }
 }
 
+// legacy 32-value blocks: value j < 16 from the low nibble of qs[j], j >= 16 from the high
+// nibble of qs[j-16]; Q5 types add bit j of qh as the fifth bit. ggml: (q - 8) * d, q * d + m,
+// (q - 16) * d, q * d + m, level(q) * d (every product exact in fp32)
+template <int TYPE>
+__device__ __forceinline__ void kt_dq32_legacy(const uint8_t* b, float* y) {
+  const float d = kt_h2f(b[0] | (b[1] << 8));
+  const bool has_m = TYPE == KT_Q4_1 || TYPE == KT_Q5_1;
+  const float m = has_m ? kt_h2f(b[2] | (b[3] << 8)) : 0.0f;
+  const int qs_off = TYPE == KT_Q4_0 || TYPE == KT_IQ4_NL ? 2 : TYPE == KT_Q4_1 ? 4 : TYPE == KT_Q5_0 ? 6 : 8;
+  uint32_t qh = 0;
+  if constexpr (TYPE == KT_Q5_0) qh = (uint32_t)b[2] | ((uint32_t)b[3] << 8) | ((uint32_t)b[4] << 16) | ((uint32_t)b[5] << 24);
+  if constexpr (TYPE == KT_Q5_1) qh = (uint32_t)b[4] | ((uint32_t)b[5] << 8) | ((uint32_t)b[6] << 16) | ((uint32_t)b[7] << 24);
+#pragma unroll
+  for (int j = 0; j < 32; ++j) {
+    const int nib = (b[qs_off + (j & 15)] >> (j < 16 ? 0 : 4)) & 0xF;
+    const int q = nib | (int)(((qh >> j) & 1) << 4);
+    if constexpr (TYPE == KT_Q4_0) y[j] = (float)(nib - 8) * d;
+    if constexpr (TYPE == KT_Q4_1 || TYPE == KT_Q5_1) y[j] = __fadd_rn(__fmul_rn((float)q, d), m);
+    if constexpr (TYPE == KT_Q5_0) y[j] = (float)(q - 16) * d;
+    if constexpr (TYPE == KT_IQ4_NL) y[j] = (float)kt_iq4nl_level(nib) * d;
+  }
+}
+
 // 32 consecutive values starting at element 32*sub32 of a row made of blocks of TYPE
 template <int TYPE>
 __device__ __forceinline__ void kt_dq32(const uint8_t* row, int sub32, float* y, const uint32_t* grid) {
   if constexpr (TYPE == KT_Q8_0) {
     kt_dq32_q8_0(row + sub32 * 34, y);
+  } else if constexpr (KtChunk<TYPE>::QK == 32) {
+    kt_dq32_legacy<TYPE>(row + sub32 * KtChunk<TYPE>::BYTES, y);
   } else {
     constexpr int BS = KtChunk<TYPE>::BYTES;
     const uint8_t* b = row + (sub32 / 8) * BS;

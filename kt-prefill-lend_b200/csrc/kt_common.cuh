@@ -17,9 +17,14 @@
 // the IQ3_S codebook in global memory; kernels copy it to shared memory before use
 static __device__ const uint32_t kt_iq3s_grid_dev[512] = KT_IQ3S_GRID_INIT;
 
+#define KT_Q4_0 2
+#define KT_Q4_1 3
+#define KT_Q5_0 6
+#define KT_Q5_1 7
 #define KT_Q8_0 8
 #define KT_Q4_K 12
 #define KT_Q6_K 14
+#define KT_IQ4_NL 20
 #define KT_IQ3_S 21
 
 // activation / output dtype codes of the C ABI
@@ -42,8 +47,13 @@ struct KtBlockInfo {
 };
 
 __host__ __device__ constexpr KtBlockInfo kt_block_info(int type) {
-  return type == KT_Q8_0   ? KtBlockInfo{32, 34}
-         : type == KT_Q4_K ? KtBlockInfo{256, 144}
+  return type == KT_Q8_0     ? KtBlockInfo{32, 34}
+         : type == KT_Q4_0   ? KtBlockInfo{32, 18}
+         : type == KT_Q4_1   ? KtBlockInfo{32, 20}
+         : type == KT_Q5_0   ? KtBlockInfo{32, 22}
+         : type == KT_Q5_1   ? KtBlockInfo{32, 24}
+         : type == KT_IQ4_NL ? KtBlockInfo{32, 18}
+         : type == KT_Q4_K   ? KtBlockInfo{256, 144}
          : type == KT_Q6_K ? KtBlockInfo{256, 210}
          : type == KT_IQ3_S ? KtBlockInfo{256, 110}
                             : KtBlockInfo{0, 0};
@@ -82,6 +92,14 @@ __device__ __forceinline__ int kt_ld_b2(const uint8_t* p) {
   return (int)((uint32_t)q[0] | ((uint32_t)q[1] << 16));
 }
 __device__ __forceinline__ int kt_ld_b4(const uint8_t* p) { return *reinterpret_cast<const int*>(p); }
+// the GEMV's legacy-block types (prefill GEMM: Q8_0, Q4_K, Q6_K, IQ3_S only)
+__host__ __device__ constexpr bool kt_gemv_type(int t) {
+  return t == KT_Q4_0 || t == KT_Q4_1 || t == KT_Q5_0 || t == KT_Q5_1 || t == KT_Q8_0 || t == KT_IQ4_NL ||
+         t == KT_Q4_K || t == KT_Q6_K || t == KT_IQ3_S;
+}
+__host__ __device__ constexpr bool kt_prefill_type(int t) {
+  return t == KT_Q8_0 || t == KT_Q4_K || t == KT_Q6_K || t == KT_IQ3_S;
+}
 
 __device__ __forceinline__ uint32_t kt_smem_addr(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
 

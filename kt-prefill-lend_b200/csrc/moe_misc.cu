@@ -52,6 +52,11 @@ int kt_launch_dequant(int type, const void* w, int64_t rows, int64_t cols, void*
   if (!bi.qk || cols % bi.qk) return -1;
   switch (type) {
     case KT_Q8_0: return dequant_t<KT_Q8_0>(w, rows, cols, out, out_dtype, s);
+    case KT_Q4_0: return dequant_t<KT_Q4_0>(w, rows, cols, out, out_dtype, s);
+    case KT_Q4_1: return dequant_t<KT_Q4_1>(w, rows, cols, out, out_dtype, s);
+    case KT_Q5_0: return dequant_t<KT_Q5_0>(w, rows, cols, out, out_dtype, s);
+    case KT_Q5_1: return dequant_t<KT_Q5_1>(w, rows, cols, out, out_dtype, s);
+    case KT_IQ4_NL: return dequant_t<KT_IQ4_NL>(w, rows, cols, out, out_dtype, s);
     case KT_Q4_K: return dequant_t<KT_Q4_K>(w, rows, cols, out, out_dtype, s);
     case KT_Q6_K: return dequant_t<KT_Q6_K>(w, rows, cols, out, out_dtype, s);
     case KT_IQ3_S: return dequant_t<KT_IQ3_S>(w, rows, cols, out, out_dtype, s);

@@ -465,11 +465,20 @@ int kt_launch_moe_vec(int type, const void* w, int table, const void* qx, int64_
   a.y = y;
   const size_t smem = (size_t)(wt_bytes + mpp * qrow);
   if (smem > 220 * 1024) return -2;
-  int chunks_per_block = type == KT_Q8_0 ? 4 : type == KT_Q4_K ? 16 : type == KT_Q6_K ? 32 : 8;
+  const int chunks_per_block = type == KT_Q8_0    ? KtChunk<KT_Q8_0>::CPB
+                               : type == KT_Q4_K  ? KtChunk<KT_Q4_K>::CPB
+                               : type == KT_Q6_K  ? KtChunk<KT_Q6_K>::CPB
+                               : type == KT_IQ3_S ? KtChunk<KT_IQ3_S>::CPB
+                                                  : KtChunk<KT_Q4_0>::CPB;  // the 32-value legacy blocks
   const int nchunks = cols / bi.qk * chunks_per_block;
   const int lpr = nchunks <= 16 ? 16 : 32;
   switch (type) {
     case KT_Q8_0: return launch_vec_dt<KT_Q8_0>(a, dtype, max_groups, lpr, smem, s);
+    case KT_Q4_0: return launch_vec_dt<KT_Q4_0>(a, dtype, max_groups, lpr, smem, s);
+    case KT_Q4_1: return launch_vec_dt<KT_Q4_1>(a, dtype, max_groups, lpr, smem, s);
+    case KT_Q5_0: return launch_vec_dt<KT_Q5_0>(a, dtype, max_groups, lpr, smem, s);
+    case KT_Q5_1: return launch_vec_dt<KT_Q5_1>(a, dtype, max_groups, lpr, smem, s);
+    case KT_IQ4_NL: return launch_vec_dt<KT_IQ4_NL>(a, dtype, max_groups, lpr, smem, s);
     case KT_Q4_K: return launch_vec_dt<KT_Q4_K>(a, dtype, max_groups, lpr, smem, s);
     case KT_Q6_K: return launch_vec_dt<KT_Q6_K>(a, dtype, max_groups, lpr, smem, s);
     case KT_IQ3_S: return launch_vec_dt<KT_IQ3_S>(a, dtype, max_groups, lpr, smem, s);

@@ -56,7 +56,8 @@ GGML_Q8_0 = 8
 GGML_Q2_0 = 42
 # ggml type -> (block elements, block bytes), the reference's table (hot/kt_gguf_hot.py:76-80)
 BLOCK_INFO = {
-    8: (32, 34), 10: (256, 84), 11: (256, 110), 12: (256, 144), 13: (256, 176), 14: (256, 210),
+    2: (32, 18), 3: (32, 20), 6: (32, 22), 7: (32, 24), 8: (32, 34), 10: (256, 84), 11: (256, 110),
+    12: (256, 144), 13: (256, 176), 14: (256, 210),
     16: (256, 66), 19: (256, 74), 20: (32, 18), 21: (256, 110), 22: (256, 82), 23: (256, 136),
     18: (256, 98), 42: (64, 18),
 }

@@ -41,6 +41,7 @@ ROUTES = os.environ.get("KT_GGUF_MOE_ROUTES", "1") == "1"
 # ggml types this build has kernels for (Q8_0, Q4_K, Q6_K, IQ3_S)
 DENSE_TYPES = set(N.SUPPORTED_TYPES)
 SUPPORTED_TYPES = set(N.SUPPORTED_TYPES)
+PREFILL_TYPES = set(N.PREFILL_TYPES)
 
 
 def _load(mmv_y=None, rpw=None, per_route=False, table=False):
@@ -145,8 +146,8 @@ def moe_prefill(x, w13, w2, topk_ids, topk_weights, type13, type2, inter, table=
     N.require_device(x)
     if x.dtype != torch.bfloat16:
         raise TypeError("the prefill path takes bf16 activations")
-    if type13 not in SUPPORTED_TYPES or type2 not in SUPPORTED_TYPES:
-        raise ValueError("unsupported ggml type")
+    if type13 not in PREFILL_TYPES or type2 not in PREFILL_TYPES:
+        raise ValueError(f"ggml types {type13}/{type2}: the prefill layer takes {sorted(PREFILL_TYPES)}")
     if topk_ids.dtype != torch.int32 or topk_weights.dtype != torch.float32:
         raise TypeError("topk ids must be int32 and weights float32")
     x = x.contiguous()

@@ -8,7 +8,12 @@
  * What it restates (paths relative to the reference project root):
  *   - GGUF block layouts and dequantization for Q8_0, Q4_K, Q6_K, IQ3_S
  *     (hot/kt_gguf_moe_multi/ggml-common.h:55-69, 88-94, 105-112, 145-154; ggml's
- *     dequantize_row_* order, which gguf-py 0.19.0 follows as well).
+ *     dequantize_row_* order, which gguf-py 0.19.0 follows as well), and for the 32-value
+ *     blocks Q4_0, Q4_1, Q5_0, Q5_1, IQ4_NL of the GEMV's wider type switch.
+ *   - vec_dot_q4_0/q4_1/q5_0/q5_1_q8_1 (vecdotq.cuh:48-160 and their wrappers, 637-650,
+ *     729-745, 850-865) and vec_dot_iq4_nl_q8_1 (vecdotq.cuh:1995-2015): chunk = 2 ints of
+ *     nibbles (8 low + 8 high codes), the Q4_1 / Q5_1 products d*d8 and m*s8 rounded to
+ *     half precision as the reference's __hmul2 does.
  *   - the q8_1 activation quantizer quantize_q8_1 (hot/kt_gguf_moe_multi/kt_gguf_moe_multi.cu:600-650),
  *     including the lane order of its 32-lane butterfly sum that produces ds.y.
  *   - the per-chunk integer dot products vec_dot_q8_0_q8_1 (vecdotq.cuh:969-982),
@@ -36,6 +41,11 @@
 #include <string.h>
 #include "../kt-prefill-lend_b200/csrc/iq3s_grid.h"
 
+#define KO_Q4_0 2
+#define KO_Q4_1 3
+#define KO_Q5_0 6
+#define KO_Q5_1 7
+#define KO_IQ4_NL 20
 #define KO_Q8_0 8
 #define KO_Q4_K 12
 #define KO_Q6_K 14
@@ -105,9 +115,17 @@ int ko_block_info(int type, int* blck, int* bytes) {
     case KO_Q4_K: *blck = 256; *bytes = 144; return 0;
     case KO_Q6_K: *blck = 256; *bytes = 210; return 0;
     case KO_IQ3_S: *blck = 256; *bytes = 110; return 0;
+    case KO_Q4_0: *blck = 32; *bytes = 18; return 0;
+    case KO_Q4_1: *blck = 32; *bytes = 20; return 0;
+    case KO_Q5_0: *blck = 32; *bytes = 22; return 0;
+    case KO_Q5_1: *blck = 32; *bytes = 24; return 0;
+    case KO_IQ4_NL: *blck = 32; *bytes = 18; return 0;
     default: return -1;
   }
 }
+
+/* the IQ4_NL code book (ggml-common.h kvalues_iq4nl) */
+static const int8_t ko_iq4nl[16] = {-127, -104, -83, -65, -49, -35, -22, -10, 1, 13, 25, 38, 53, 69, 89, 113};
 
 /* ---------------------------------------------------------------- dequant */
 
@@ -198,6 +216,26 @@ static void dq_iq3_s(const uint8_t* b, float* y) {
   }
 }
 
+/* 32-value blocks: code j < 16 is the low nibble of qs[j], j >= 16 the high nibble of
+ * qs[j - 16]; Q5 adds bit j of qh as the fifth bit. ggml: (q-8)*d, q*d+m, (q-16)*d, q*d+m,
+ * level(q)*d */
+static void dq_legacy(int type, const uint8_t* b, float* y) {
+  float d = ko_h2f(rd16(b));
+  float m = (type == KO_Q4_1 || type == KO_Q5_1) ? ko_h2f(rd16(b + 2)) : 0.0f;
+  int qs_off = (type == KO_Q4_0 || type == KO_IQ4_NL) ? 2 : type == KO_Q4_1 ? 4 : type == KO_Q5_0 ? 6 : 8;
+  uint32_t qh = type == KO_Q5_0 ? (uint32_t)rd32(b + 2) : type == KO_Q5_1 ? (uint32_t)rd32(b + 4) : 0u;
+  for (int j = 0; j < 32; ++j) {
+    int nib = (b[qs_off + (j & 15)] >> (j < 16 ? 0 : 4)) & 0xF;
+    int q = nib | (int)(((qh >> j) & 1) << 4);
+    switch (type) {
+      case KO_Q4_0: y[j] = (float)(nib - 8) * d; break;
+      case KO_Q4_1: case KO_Q5_1: y[j] = (float)q * d + m; break;
+      case KO_Q5_0: y[j] = (float)(q - 16) * d; break;
+      case KO_IQ4_NL: y[j] = (float)ko_iq4nl[nib] * d; break;
+    }
+  }
+}
+
 int ko_dequant_rows(int type, const uint8_t* w, int64_t nrows, int64_t cols, float* out) {
   int blck, bs;
   if (ko_block_info(type, &blck, &bs) || cols % blck) return -1;
@@ -212,6 +250,7 @@ int ko_dequant_rows(int type, const uint8_t* w, int64_t nrows, int64_t cols, flo
         case KO_Q4_K: dq_q4_k(b, y); break;
         case KO_Q6_K: dq_q6_k(b, y); break;
         case KO_IQ3_S: dq_iq3_s(b, y); break;
+        default: dq_legacy(type, b, y); break;
       }
     }
   }
@@ -351,6 +390,60 @@ static float vd_iq3_s(const uint8_t* bx, const uint8_t* by0, int ib32) {
   return d * (float)sumi;
 }
 
+/* legacy blocks, chunk iqs in {0, 2}: ints iqs, iqs+1 of the nibble bytes against q8_1 ints
+ * iqs+i (low codes) and iqs+i+4 (high codes) */
+static float ko_h2f_product(uint16_t a, uint16_t b) { return ko_h2f(ko_f2h(ko_h2f(a) * ko_h2f(b))); }
+
+static int32_t q5_lo(uint32_t ql, uint32_t h) {
+  return (int32_t)((ql & 0x0F0F0F0Fu) | ((h << 4) & 0x10u) | ((h << 11) & 0x1000u) | ((h << 18) & 0x100000u) |
+                   ((h << 25) & 0x10000000u));
+}
+static int32_t q5_hi(uint32_t ql, uint32_t h) {
+  return (int32_t)(((ql >> 4) & 0x0F0F0F0Fu) | ((h >> 12) & 0x10u) | ((h >> 5) & 0x1000u) | ((h << 2) & 0x100000u) |
+                   ((h << 9) & 0x10000000u));
+}
+
+static float vd_legacy(int type, const uint8_t* bx, const uint8_t* b8, int iqs) {
+  const uint8_t* q8 = b8 + 4;
+  int32_t sumi = 0, sumi2 = 0;
+  int qs_off = (type == KO_Q4_0 || type == KO_IQ4_NL) ? 2 : type == KO_Q4_1 ? 4 : type == KO_Q5_0 ? 6 : 8;
+  int32_t qh = type == KO_Q5_0 ? rd32(bx + 2) : type == KO_Q5_1 ? rd32(bx + 4) : 0;
+  for (int i = 0; i < 2; ++i) {
+    uint32_t v = (uint32_t)rd32(bx + qs_off + 4 * (iqs + i));
+    int32_t u0 = rd32(q8 + 4 * (iqs + i)), u1 = rd32(q8 + 4 * (iqs + i + 4));
+    if (type == KO_Q5_0 || type == KO_Q5_1) {
+      uint32_t h = (uint32_t)(qh >> (4 * (iqs + i))); /* arithmetic shift, as the reference's int */
+      sumi = dp4a(q5_lo(v, h), u0, sumi);
+      sumi = dp4a(q5_hi(v, h), u1, sumi);
+    } else if (type == KO_IQ4_NL) {
+      uint32_t lo = 0, hi = 0;
+      for (int k = 0; k < 4; ++k) {
+        lo |= (uint32_t)(uint8_t)ko_iq4nl[(v >> (8 * k)) & 0xF] << (8 * k);
+        hi |= (uint32_t)(uint8_t)ko_iq4nl[(v >> (8 * k + 4)) & 0xF] << (8 * k);
+      }
+      sumi = dp4a((int32_t)lo, u0, sumi);
+      sumi2 = dp4a((int32_t)hi, u1, sumi2);
+    } else {
+      sumi = dp4a((int32_t)(v & 0x0F0F0F0Fu), u0, sumi);
+      sumi = dp4a((int32_t)((v >> 4) & 0x0F0F0F0Fu), u1, sumi);
+    }
+  }
+  const float d8 = ko_h2f(rd16(b8)), s8 = ko_h2f(rd16(b8 + 2));
+  switch (type) {
+    case KO_Q4_0: return ko_h2f(rd16(bx)) * ((float)sumi * d8 - 4.0f * s8);
+    case KO_Q5_0: return ko_h2f(rd16(bx)) * ((float)sumi * d8 - 8.0f * s8);
+    case KO_Q4_1:
+    case KO_Q5_1: {
+      float dd = ko_h2f_product(rd16(bx), rd16(b8)), ms = ko_h2f_product(rd16(bx + 2), rd16(b8 + 2));
+      return (float)sumi * dd + ms / 2.0f;
+    }
+    default: { /* IQ4_NL */
+      float d = ko_h2f(rd16(bx)) * d8;
+      return d * (float)(sumi + sumi2);
+    }
+  }
+}
+
 /* chunk geometry of the reference launchers: values per block, chunks per block, vdr */
 static int chunk_geom(int type, int* qk, int* cpb, int* vdr) {
   switch (type) {
@@ -358,13 +451,15 @@ static int chunk_geom(int type, int* qk, int* cpb, int* vdr) {
     case KO_Q4_K: *qk = 256; *cpb = 16; *vdr = 2; return 0; /* qi 32, vdr 2 */
     case KO_Q6_K: *qk = 256; *cpb = 32; *vdr = 1; return 0; /* qi 32, vdr 1 */
     case KO_IQ3_S: *qk = 256; *cpb = 8; *vdr = 1; return 0; /* qi 8, vdr 1 */
+    case KO_Q4_0: case KO_Q4_1: case KO_Q5_0: case KO_Q5_1: case KO_IQ4_NL:
+      *qk = 32; *cpb = 2; *vdr = 2; return 0;               /* qi 4, vdr 2 */
     default: return -1;
   }
 }
 
 /* One output row: lane t takes chunks t, t+32, ... in order; then the xor butterfly. */
 static float row_dot(int type, const uint8_t* wrow, int bs, int nblocks, const uint8_t* yrow) {
-  int qk, cpb, vdr;
+  int qk = 32, cpb = 1, vdr = 1;
   chunk_geom(type, &qk, &cpb, &vdr);
   float lane[32];
   for (int t = 0; t < 32; ++t) lane[t] = 0.0f;
@@ -379,6 +474,7 @@ static float row_dot(int type, const uint8_t* wrow, int bs, int nblocks, const u
       case KO_Q4_K: v = vd_q4_k(bx, by, iqs); break;
       case KO_Q6_K: v = vd_q6_k(bx, by, iqs); break;
       case KO_IQ3_S: v = vd_iq3_s(bx, by, iqs); break;
+      default: v = vd_legacy(type, bx, by, iqs); break;
     }
     lane[c % 32] += v;
   }

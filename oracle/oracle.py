@@ -18,7 +18,8 @@ import numpy as np
 
 HERE = Path(__file__).resolve().parent
 LIB_PATH = HERE / "libkt_oracle.so"
-BLOCK = {8: (32, 34), 12: (256, 144), 14: (256, 210), 21: (256, 110)}
+BLOCK = {8: (32, 34), 12: (256, 144), 14: (256, 210), 21: (256, 110),
+         2: (32, 18), 3: (32, 20), 6: (32, 22), 7: (32, 24), 20: (32, 18)}
 
 _lib = None
 

@@ -2,12 +2,14 @@
 
 The reference ships no fixtures for this path, so the known answers come from gguf-py
 0.19.0 (`gguf.quants.dequantize`, numpy restatements of ggml's dequantize_row_*), an
-implementation independent of this repository. For each hot-path type the file holds
-  <type>_blocks  uint8  : 48 rows of 512 values (2 super-blocks / 16 Q8_0 blocks per row):
-                           rows 0-23 encoded from N(0, 0.02) weights by gguf_encode.c,
+implementation independent of this repository. For each type the file holds
+  <type>_blocks  uint8  : 48 rows of 512 values (2 super-blocks / 16 32-value blocks per row):
+                           rows 0-23 encoded from N(0, 0.02) weights (gguf_encode.c for the
+                           hot-path types, gguf-py's quantizer for Q4_0/Q4_1/Q5_0/Q5_1; IQ4_NL,
+                           which neither encodes, takes random blocks here too),
                            rows 24-47 random bytes with finite scales (every code pattern)
   <type>_values  float32: gguf-py's dequantization of those rows
-plus the IQ3_S codebook as uint32 words.
+plus the IQ3_S codebook as uint32 words and the IQ4_NL levels.
 
 Run from the repository root: python tests/golden/make_golden.py
 """
@@ -20,11 +22,12 @@ ROOT = Path(__file__).resolve().parents[2]
 sys.path.insert(0, str(ROOT / "kt-prefill-lend_b200"))
 
 from gguf import GGMLQuantizationType as Q  # noqa: E402
-from gguf.quants import IQ3_S, dequantize  # noqa: E402
+from gguf.quants import IQ3_S, IQ4_NL, dequantize, quantize  # noqa: E402
 
 from kt_gguf_b200 import synth  # noqa: E402
 
 TYPES = {8: Q.Q8_0, 12: Q.Q4_K, 14: Q.Q6_K, 21: Q.IQ3_S}
+LEGACY = {2: Q.Q4_0, 3: Q.Q4_1, 6: Q.Q5_0, 7: Q.Q5_1, 20: Q.IQ4_NL}
 
 
 def main():
@@ -36,6 +39,14 @@ def main():
         blocks = np.concatenate([enc, rnd])
         out[f"{t}_blocks"] = blocks
         out[f"{t}_values"] = dequantize(blocks, qt).reshape(48, 512).astype(np.float32)
+    for t, qt in LEGACY.items():
+        w = rng.standard_normal((24, 512), dtype=np.float32) * 0.02
+        enc = synth.random_blocks(rng, t, 24, 512) if t == 20 else quantize(w, qt)
+        rnd = synth.random_blocks(rng, t, 24, 512)
+        blocks = np.concatenate([enc, rnd])
+        out[f"{t}_blocks"] = blocks
+        out[f"{t}_values"] = dequantize(blocks, qt).reshape(48, 512).astype(np.float32)
+    out["iq4nl_levels"] = np.array(IQ4_NL.kvalues, dtype=np.int8)
     IQ3_S.init_grid()
     g = IQ3_S.grid.reshape(512, 4).astype(np.uint32)
     out["iq3s_grid"] = g[:, 0] | (g[:, 1] << 8) | (g[:, 2] << 16) | (g[:, 3] << 24)

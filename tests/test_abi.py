@@ -62,6 +62,12 @@ def test_argument_errors_before_any_launch():
                               None) == N.KT_ERR_ARG
     assert lib.kt_moe_prefill(P(16), 16, 2048, 512, P(16), P(16), 8, P(16), 12, P(16), 99, 0, 64, P(16), P(16), 1 << 40,
                               None) == N.KT_ERR_TYPE
+    # the 32-value legacy blocks have a decode GEMV but no prefill GEMM
+    assert lib.kt_moe_prefill(P(16), 16, 2048, 512, P(16), P(16), 8, P(16), 2, P(16), 14, 0, 64, P(16), P(16), 1 << 40,
+                              None) == N.KT_ERR_TYPE
+    rb = ctypes.c_int64()
+    assert lib.kt_gguf_row_bytes(2, 2048, ctypes.byref(rb)) == N.KT_OK and rb.value == 64 * 18
+    assert lib.kt_gguf_row_bytes(7, 512, ctypes.byref(rb)) == N.KT_OK and rb.value == 16 * 24
     assert lib.kt_moe_prefill(P(16), 16, 2048, 512, P(16), P(16), 8, P(16), 12, P(16), 14, 0, 64, P(16), P(16), 64,
                               None) == N.KT_ERR_WORKSPACE
     # the permute keeps a shared-memory histogram over slots: at most 8192 slots

@@ -9,19 +9,21 @@ from oracle import oracle as O
 
 GOLDEN = np.load(Path(__file__).with_name("golden") / "gguf_dequant.npz")
 TYPES = (8, 12, 14, 21)
+LEGACY = (2, 3, 6, 7, 20)  # 32-value blocks of the GEMV's wider type switch
 REF_COMMON = Path("/root/reference/hot/kt_gguf_moe_multi/ggml-common.h")
 
 
 def test_block_sizes_known_answers():
     # hot/kt_gguf_hot.py:76-80 BLOCK_INFO for the hot-path types
-    assert O.BLOCK == {8: (32, 34), 12: (256, 144), 14: (256, 210), 21: (256, 110)}
+    assert O.BLOCK == {8: (32, 34), 12: (256, 144), 14: (256, 210), 21: (256, 110),
+                       2: (32, 18), 3: (32, 20), 6: (32, 22), 7: (32, 24), 20: (32, 18)}
     from kt_gguf_b200 import synth
 
     assert synth.BLOCK == O.BLOCK
     assert O.row_bytes(12, 2048) == 8 * 144 and O.row_bytes(14, 512) == 420 and O.row_bytes(21, 512) == 220
 
 
-@pytest.mark.parametrize("qtype", TYPES)
+@pytest.mark.parametrize("qtype", TYPES + LEGACY)
 def test_oracle_dequant_matches_golden_bit_exact(qtype):
     blocks = GOLDEN[f"{qtype}_blocks"]
     want = GOLDEN[f"{qtype}_values"]
@@ -85,3 +87,12 @@ def test_bf16_helpers_round_to_nearest_even():
 
     want = torch.from_numpy(x).to(torch.bfloat16).to(torch.float32).numpy()
     assert np.array_equal(back.view(np.uint32), want.view(np.uint32))
+
+
+def test_iq4nl_levels_match_gguf_py_and_device_words():
+    # the code book the device packs into four words (gguf_dot.cuh KT_IQ4NL_W0..3)
+    levels = GOLDEN["iq4nl_levels"].astype(np.int8)
+    src = (Path(__file__).resolve().parents[1] / "kt-prefill-lend_b200" / "csrc" / "gguf_dot.cuh").read_text()
+    words = [int(re.search(rf"#define KT_IQ4NL_W{i} (0x[0-9A-Fa-f]+)u", src).group(1), 16) for i in range(4)]
+    packed = np.array(words, dtype=np.uint32).view(np.int8)
+    assert np.array_equal(packed, levels)

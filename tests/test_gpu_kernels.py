@@ -12,6 +12,7 @@ from oracle import oracle as O
 pytestmark = pytest.mark.gpu
 GOLDEN = np.load(__import__("pathlib").Path(__file__).with_name("golden") / "gguf_dequant.npz")
 TYPES = (8, 12, 14, 21)
+LEGACY = (2, 3, 6, 7, 20)  # 32-value blocks: decode GEMV and dequantizer only
 
 
 def bits(t: torch.Tensor) -> np.ndarray:
@@ -27,7 +28,7 @@ def ulp_diff_bf16(a: np.ndarray, b: np.ndarray) -> np.ndarray:
     return np.abs(ia - ib)
 
 
-@pytest.mark.parametrize("qtype", TYPES)
+@pytest.mark.parametrize("qtype", TYPES + LEGACY)
 def test_dequant_bit_exact_vs_golden(cuda_device, qtype):
     blocks = torch.from_numpy(GOLDEN[f"{qtype}_blocks"]).to(cuda_device)
     want = GOLDEN[f"{qtype}_values"]
@@ -61,8 +62,11 @@ def close_enough(got_bits: np.ndarray, want: np.ndarray) -> None:
 
 def _gemv_case(qtype, cols, rows, slots, tokens, top_k, seed, dtype=torch.bfloat16):
     rng = np.random.default_rng(seed)
-    W = np.stack([synth.quantize(rng.standard_normal((rows, cols), dtype=np.float32) * 0.02, qtype)
-                  for _ in range(slots)])
+    if qtype in LEGACY:  # no encoder here for these: arbitrary valid blocks
+        W = np.stack([synth.random_blocks(rng, qtype, rows, cols) for _ in range(slots)])
+    else:
+        W = np.stack([synth.quantize(rng.standard_normal((rows, cols), dtype=np.float32) * 0.02, qtype)
+                      for _ in range(slots)])
     g = torch.Generator().manual_seed(seed)
     x = torch.randn((tokens, cols), generator=g).to(dtype)
     ids = torch.from_numpy(rng.integers(-1, slots, size=(tokens, top_k)).astype(np.int32))
@@ -75,7 +79,9 @@ def _oracle_gemv(qtype, W, x, ids, top_k, rows, cols):
 
 
 @pytest.mark.parametrize("qtype,cols,rows", [(8, 2048, 96), (8, 768, 2048), (12, 2048, 1024), (14, 512, 2048),
-                                             (21, 2048, 1024), (21, 512, 2048), (12, 7168, 64)])
+                                             (21, 2048, 1024), (21, 512, 2048), (12, 7168, 64),
+                                             (2, 2048, 256), (3, 2048, 256), (6, 512, 512), (7, 2048, 256),
+                                             (20, 2048, 256)])
 @pytest.mark.parametrize("tokens,top_k", [(1, 8), (4, 10), (16, 3)])
 def test_gemv_matches_reference_arithmetic(cuda_device, qtype, cols, rows, tokens, top_k):
     slots = 6
@@ -97,7 +103,7 @@ def test_gemv_matches_reference_arithmetic(cuda_device, qtype, cols, rows, token
     assert np.all(got[zero] == 0)
 
 
-@pytest.mark.parametrize("qtype", TYPES)
+@pytest.mark.parametrize("qtype", TYPES + LEGACY)
 def test_gemv_f32_output_and_table_mode(cuda_device, qtype):
     cols, rows, slots, tokens, top_k = (2048 if qtype != 14 else 512), 256, 5, 3, 4
     W, x, ids = _gemv_case(qtype, cols, rows, slots, tokens, top_k, seed=7 + qtype, dtype=torch.float32)

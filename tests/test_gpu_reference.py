@@ -65,6 +65,32 @@ def test_window_kernel_vs_reference(cuda_device, ref_mods, qtype, cols, rows, to
     assert O.rel_l2(O.bf16_to_f32(gb), O.bf16_to_f32(rb)) < 1e-3
 
 
+@pytest.mark.parametrize("qtype,cols,rows", [(2, 2048, 512), (3, 2048, 512), (6, 512, 1024), (7, 2048, 512),
+                                             (20, 2048, 512)])
+@pytest.mark.parametrize("tokens,top_k", [(1, 8), (4, 4)])
+def test_legacy_blocks_vs_reference(cuda_device, ref_mods, qtype, cols, rows, tokens, top_k):
+    # the 32-value block types of the reference's switch (kt_gguf_moe_multi.cu:672-749, 880-892),
+    # on arbitrary valid blocks
+    win, _ = ref_mods
+    slots = 8
+    rng = np.random.default_rng(qtype * 11 + tokens)
+    W = np.stack([synth.random_blocks(rng, qtype, rows, cols) for _ in range(slots)])
+    x = torch.randn((tokens, cols), generator=torch.Generator().manual_seed(tokens * 3 + cols)).to(torch.bfloat16)
+    ids = np.stack([rng.permutation(slots)[:top_k] for _ in range(tokens)]).astype(np.int32)
+    ids[rng.random(ids.shape) < 0.2] = -1
+    ids_t = torch.from_numpy(ids.reshape(-1)).to(cuda_device)
+    Wd, xd = torch.from_numpy(W).to(cuda_device), x.to(cuda_device)
+    y_ref = win.kt_moe_a8_vec_multi(xd, Wd, ids_t, top_k, qtype, rows, tokens)
+    y = M.moe_a8_vec_multi(xd, Wd, ids_t, top_k, qtype, rows, tokens)
+    torch.cuda.synchronize()
+    want = O.moe_vec(qtype, W, O.quantize_q8_1(x.float().numpy()), ids.reshape(-1), top_k, rows, cols)
+    ob, rb, gb = O.f32_to_bf16(want), bits(y_ref), bits(y)
+    print(f"\nREFPIN type={qtype} cols={cols} rows={rows} tokens={tokens} top_k={top_k}: "
+          f"oracle!=ref {(ob != rb).mean():.2e}  b200!=ref {(gb != rb).mean():.2e}")
+    assert (ob != rb).mean() < 2e-3 and (gb != rb).mean() < 2e-3
+    assert O.rel_l2(O.bf16_to_f32(gb), O.bf16_to_f32(rb)) < 1e-3
+
+
 @pytest.mark.parametrize("qtype,cols,rows", [(12, 2048, 1024), (21, 512, 2048)])
 def test_per_route_build_at_prefill_size(cuda_device, ref_mods, qtype, cols, rows):
     _, routes = ref_mods

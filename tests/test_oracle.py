@@ -33,6 +33,64 @@ def test_gemv_integer_path_equals_dequant_matmul(qtype, cols, rows):
     assert np.all(y[2] == 0)
 
 
+def _legacy_fields(qtype, W):
+    """per 32-value block: codes [.., 32] (int), d, m (float32; m = 0 where absent)"""
+    qk, bs = O.BLOCK[qtype]
+    b = W.reshape(*W.shape[:-1], -1, bs)
+    f16 = lambda o: b[..., o:o + 2].copy().view(np.float16)[..., 0]
+    qs_off = {2: 2, 20: 2, 3: 4, 6: 6, 7: 8}[qtype]
+    qs = b[..., qs_off:qs_off + 16].astype(np.int32)
+    codes = np.concatenate([qs & 15, qs >> 4], axis=-1)
+    if qtype in (6, 7):
+        o = 2 if qtype == 6 else 4
+        qh = b[..., o:o + 4].copy().view(np.uint32)[..., 0].astype(np.int64)
+        codes = codes | (((qh[..., None] >> np.arange(32)) & 1) << 4).astype(np.int32)
+    d = f16(0)
+    m = f16(2) if qtype in (3, 7) else np.zeros_like(d)
+    return codes, d, m
+
+
+@pytest.mark.parametrize("qtype", [2, 3, 6, 7, 20])
+def test_gemv_legacy_blocks_equal_blockwise_formula(qtype):
+    # vec_dot_q4_0/q4_1/q5_0/q5_1/iq4_nl_q8_1 summed over a row: per block,
+    # d*(d8*sum(q*u) - off*s8) (Q4_0 off 8, Q5_0 off 16), (d*d8)*sum(q*u) + m*s8 with the two
+    # products rounded to half (Q4_1, Q5_1), d*d8*sum(level(q)*u) (IQ4_NL); s8 is the q8_1
+    # block's sum of the unquantized activations
+    rng = np.random.default_rng(qtype)
+    rows, cols = 24, 512
+    x = rng.standard_normal((3, cols), dtype=np.float32)
+    W = np.stack([synth.random_blocks(rng, qtype, rows, cols) for _ in range(2)])
+    qx = O.quantize_q8_1(x)
+    ids = np.array([0, 1, -1, 1, 0, 0], dtype=np.int32)  # top_k 2
+    y = O.moe_vec(qtype, W, qx, ids, 2, rows, cols)
+    nb = cols // 32
+    q8 = qx.reshape(3, -1, 36)[:, :nb]
+    d8 = q8[:, :, 0:2].copy().view(np.float16)[..., 0]
+    s8 = q8[:, :, 2:4].copy().view(np.float16)[..., 0]
+    u = q8[:, :, 4:].view(np.int8).astype(np.int64)
+    codes, d, m = _legacy_fields(qtype, W)  # [E, rows, nb, 32], [E, rows, nb]
+    levels = np.array([-127, -104, -83, -65, -49, -35, -22, -10, 1, 13, 25, 38, 53, 69, 89, 113], np.int64)
+    exp = np.zeros((len(ids), rows), np.float64)
+    for p, e in enumerate(ids):
+        if e < 0:
+            continue
+        t = p // 2
+        q = levels[codes[e]] if qtype == 20 else codes[e].astype(np.int64)
+        dot = (q * u[t][None]).sum(-1).astype(np.float64)  # [rows, nb]
+        if qtype in (2, 6):
+            off = 8 if qtype == 2 else 16
+            v = d[e].astype(np.float64) * (d8[t].astype(np.float64) * dot - off * s8[t].astype(np.float64))
+        elif qtype in (3, 7):
+            dd = (d[e] * d8[t]).astype(np.float16).astype(np.float64)  # half products
+            ms = (m[e] * s8[t]).astype(np.float16).astype(np.float64)
+            v = dd * dot + ms
+        else:
+            v = d[e].astype(np.float64) * d8[t].astype(np.float64) * dot
+        exp[p] = v.sum(-1)
+    assert O.rel_l2(y, exp.astype(np.float32)) < 2e-6
+    assert np.all(y[2] == 0)
+
+
 def test_fused_combine_equals_mul_and_sum():
     # hot/kt_gguf_hot.py:297-304: the fused kernel and out.mul_(w) + moe_sum give identical bits
     g = torch.Generator().manual_seed(3)
