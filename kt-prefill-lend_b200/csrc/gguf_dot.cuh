@@ -44,6 +44,24 @@ template <>
 struct KtChunk<KT_Q4_K> {
   static constexpr int QK = 256, BYTES = 144, CPB = 16, VDR = 2;
 };
+// K-quants and IQ4_XS with the reference's split: Q2_K / Q3_K one int of 2-bit codes per
+// chunk (QI 16, VDR 1), Q5_K two ints (QI 32, VDR 2), IQ4_XS one 32-value sub-block (QI 8)
+template <>
+struct KtChunk<KT_Q2_K> {
+  static constexpr int QK = 256, BYTES = 84, CPB = 16, VDR = 1;
+};
+template <>
+struct KtChunk<KT_Q3_K> {
+  static constexpr int QK = 256, BYTES = 110, CPB = 16, VDR = 1;
+};
+template <>
+struct KtChunk<KT_Q5_K> {
+  static constexpr int QK = 256, BYTES = 176, CPB = 16, VDR = 2;
+};
+template <>
+struct KtChunk<KT_IQ4_XS> {
+  static constexpr int QK = 256, BYTES = 136, CPB = 8, VDR = 1;
+};
 template <>
 struct KtChunk<KT_Q6_K> {
   static constexpr int QK = 256, BYTES = 210, CPB = 32, VDR = 1;
@@ -209,6 +227,102 @@ __device__ __forceinline__ float kt_vd_q4_k(const uint8_t* bx, const uint8_t* yq
   return dm.x * sumf_d - dm.y * sumf_m;
 }
 
+// ---- Q2_K (scales[16] (scale | min << 4), qs[64], half2 (d, dmin)); iqs in 0..15: int iqs of
+// qs holds 4 codes of each of the groups 8(iqs/8) + 2i + (iqs%8)/4 (i = 0..3, bits 2i),
+// against int iqs%8 of q8_1 blocks 4(iqs/8) + i
+__device__ __forceinline__ float kt_vd_q2_k(const uint8_t* bx, const uint8_t* yq, const uint8_t* yd, int iqs) {
+  const int bq8_offset = 4 * (iqs / 8);
+  const uint8_t* scales = bx + iqs - iqs % 8 + (iqs % 8) / 4;
+  const int v = kt_ld_b4(bx + 16 + 4 * iqs);
+  float sumf_d = 0.0f, sumf_m = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int u = kt_ld_b4(yq + 32 * (bq8_offset + i) + 4 * (iqs % 8));
+    const float d8 = kt_q8_1_dd(yd + 4 * (bq8_offset + i));
+    const int sc = scales[2 * i];
+    sumf_d += d8 * (__dp4a((v >> (2 * i)) & 0x03030303, u, 0) * (sc & 0xF));
+    sumf_m += d8 * __dp4a((sc >> 4) * 0x01010101, u, 0);  // the min in every byte
+  }
+  const float2 dm = __half22float2(*reinterpret_cast<const half2*>(bx + 80));
+  return dm.x * sumf_d - dm.y * sumf_m;
+}
+
+// ---- Q3_K (hmask[32], qs[64], scales[12] (16 6-bit scales), d); iqs in 0..15: low 2 bits
+// from int iqs of qs, the third bit (inverted: 0 -> -4) from int iqs%8 of hmask
+__device__ __forceinline__ float kt_vd_q3_k(const uint8_t* bx, const uint8_t* yq, const uint8_t* yd, int iqs) {
+  const int bq8_offset = 4 * (iqs / 8);
+  const int scale_offset = iqs - iqs % 8 + (iqs % 8) / 4;
+  const uint8_t* scales = bx + 96;
+  const int vl = kt_ld_b2(bx + 32 + 4 * iqs);
+  const int vh = ~kt_ld_b2(bx + 4 * (iqs % 8)) >> bq8_offset;
+  float sumf = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int isc = scale_offset + 2 * i;
+    const int sc_low = (scales[isc % 8] >> (4 * (isc / 8))) & 0xF;
+    const int sc_high = ((scales[8 + isc % 4] >> (2 * (isc / 4))) & 3) << 4;
+    const int sc = (sc_low | sc_high) - 32;
+    const int vi = __vsubss4((vl >> (2 * i)) & 0x03030303, ((vh >> i) << 2) & 0x04040404);
+    const int u = kt_ld_b4(yq + 32 * (bq8_offset + i) + 4 * (iqs % 8));
+    sumf += kt_q8_1_dd(yd + 4 * (bq8_offset + i)) * (__dp4a(vi, u, 0) * sc);
+  }
+  return kt_h2f(*reinterpret_cast<const uint16_t*>(bx + 108)) * sumf;
+}
+
+// ---- Q5_K (half2 (d, dmin), scales[12], qh[32], qs[128]): as Q4_K, with the fifth bit of
+// each code from qh (bit bq8_offset + i of the byte of the code's position)
+__device__ __forceinline__ float kt_vd_q5_k(const uint8_t* bx, const uint8_t* yq, const uint8_t* yd, int iqs) {
+  const int bq8_offset = 2 * ((iqs / 2) / 4);
+  const uint8_t* ql = bx + 48 + 16 * bq8_offset + 4 * ((iqs / 2) % 4);
+  const uint8_t* qh = bx + 16 + 4 * ((iqs / 2) % 4);
+  const int vl0 = kt_ld_b4(ql), vl1 = kt_ld_b4(ql + 16);
+  const int vh0 = kt_ld_b4(qh) >> bq8_offset, vh1 = kt_ld_b4(qh + 16) >> bq8_offset;
+  const uint16_t* s16 = reinterpret_cast<const uint16_t*>(bx + 4);
+  uint16_t aux0, aux1;
+  const int j = bq8_offset / 2;
+  if (j < 2) {
+    aux0 = s16[j + 0] & 0x3f3f;
+    aux1 = s16[j + 2] & 0x3f3f;
+  } else {
+    aux0 = ((s16[j + 2] >> 0) & 0x0f0f) | ((s16[j - 2] & 0xc0c0) >> 2);
+    aux1 = ((s16[j + 2] >> 4) & 0x0f0f) | ((s16[j - 0] & 0xc0c0) >> 2);
+  }
+  float sumf_d = 0.0f, sumf_m = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const uint8_t* q8 = yq + 32 * (bq8_offset + i) + 4 * ((iqs / 2) % 4);
+    const int u0 = kt_ld_b4(q8), u1 = kt_ld_b4(q8 + 16);
+    const int v0 = ((vl0 >> (4 * i)) & 0x0F0F0F0F) | (((vh0 >> i) << 4) & 0x10101010);
+    const int v1 = ((vl1 >> (4 * i)) & 0x0F0F0F0F) | (((vh1 >> i) << 4) & 0x10101010);
+    const int dot1 = __dp4a(v0, u0, __dp4a(v1, u1, 0));
+    const int dot2 = __dp4a(0x01010101, u0, __dp4a(0x01010101, u1, 0));
+    const float d8 = kt_q8_1_dd(yd + 4 * (bq8_offset + i));
+    const int sc = (aux0 >> (8 * i)) & 0xff, m = (aux1 >> (8 * i)) & 0xff;
+    sumf_d += d8 * (dot1 * sc);
+    sumf_m += d8 * (dot2 * m);
+  }
+  const float2 dm = __half22float2(*reinterpret_cast<const half2*>(bx));
+  return dm.x * sumf_d - dm.y * sumf_m;
+}
+
+// ---- IQ4_XS (d, scales_h (2 bits per sub-block), scales_l[4] (4 bits), qs[128]); chunk =
+// sub-block ib32: d * (ls - 32) * d8 * (sum over the low-nibble levels + the high ones)
+__device__ __forceinline__ float kt_vd_iq4_xs(const uint8_t* bx, const uint8_t* yq, const uint8_t* yd, int ib32) {
+  const uint8_t* q8 = yq + 32 * ib32;
+  const uint8_t* q4 = bx + 8 + 16 * ib32;
+  const int scales_h = bx[2] | (bx[3] << 8);
+  const int ls = ((bx[4 + ib32 / 2] >> (4 * (ib32 % 2))) & 0xf) | (((scales_h >> (2 * ib32)) & 3) << 4);
+  const float d = kt_h2f(*reinterpret_cast<const uint16_t*>(bx)) * (ls - 32) * kt_q8_1_dd(yd + 4 * ib32);
+  int sumi1 = 0, sumi2 = 0;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const uint32_t q = (uint32_t)kt_ld_b4(q4 + 4 * j);
+    sumi1 = __dp4a(kt_iq4nl_bytes(q & 0x0F0F0F0Fu), kt_ld_b4(q8 + 4 * j), sumi1);
+    sumi2 = __dp4a(kt_iq4nl_bytes((q >> 4) & 0x0F0F0F0Fu), kt_ld_b4(q8 + 16 + 4 * j), sumi2);
+  }
+  return d * (sumi1 + sumi2);
+}
+
 // ---- Q6_K: 8 values; iqs in 0..31. The reference's per-byte (code - 32) with __vsubss4
 // never saturates (codes are 0..63), so the integer dot is dp4a(code, u) - 32 * sum(u),
 // computed here with two dp4a instead of the emulated SIMD subtract.
@@ -280,6 +394,10 @@ __device__ __forceinline__ float kt_vec_dot(const uint8_t* bx, const uint8_t* yq
   if constexpr (TYPE == KT_Q5_0) return kt_vd_q5_0(bx, yq, yd, iqs);
   if constexpr (TYPE == KT_Q5_1) return kt_vd_q5_1(bx, yq, yd, iqs);
   if constexpr (TYPE == KT_IQ4_NL) return kt_vd_iq4_nl(bx, yq, yd, iqs);
+  if constexpr (TYPE == KT_Q2_K) return kt_vd_q2_k(bx, yq, yd, iqs);
+  if constexpr (TYPE == KT_Q3_K) return kt_vd_q3_k(bx, yq, yd, iqs);
+  if constexpr (TYPE == KT_Q5_K) return kt_vd_q5_k(bx, yq, yd, iqs);
+  if constexpr (TYPE == KT_IQ4_XS) return kt_vd_iq4_xs(bx, yq, yd, iqs);
   if constexpr (TYPE == KT_Q4_K) return kt_vd_q4_k(bx, yq, yd, iqs);
   if constexpr (TYPE == KT_Q6_K) return kt_vd_q6_k(bx, yq, yd, iqs);
   if constexpr (TYPE == KT_IQ3_S) return kt_vd_iq3_s(bx, yq, yd, iqs, grid);
@@ -377,6 +495,70 @@ __device__ __forceinline__ void kt_dq32_legacy(const uint8_t* b, float* y) {
   }
 }
 
+// K-quant sub-block sub (32 values) of a 256-value block, ggml's order and roundings:
+// Q2_K: half n = sub/4, shift pair j = sub%4; values 0-15 from q[32n + l] >> 2j with group
+// scale 8n+2j, 16-31 from q[32n + 16 + l] with group 8n+2j+1: (d*sc)*q - dmin*m
+__device__ __forceinline__ void kt_dq32_q2_k(const uint8_t* b, int sub, float* y) {
+  const float d = kt_h2f(b[80] | (b[81] << 8)), dmin = kt_h2f(b[82] | (b[83] << 8));
+  const int n = sub / 4, j = sub % 4;
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const int sc = b[8 * n + 2 * j + h];
+    const float dl = __fmul_rn(d, (float)(sc & 0xF)), ml = __fmul_rn(dmin, (float)(sc >> 4));
+    const uint8_t* q = b + 16 + 32 * n + 16 * h;
+#pragma unroll
+    for (int l = 0; l < 16; ++l) y[16 * h + l] = __fsub_rn(__fmul_rn(dl, (float)((q[l] >> (2 * j)) & 3)), ml);
+  }
+}
+// Q3_K: as Q2_K's grouping; the third bit is bit 4n+j of hmask[l] / hmask[16+l] (clear: -4);
+// 6-bit scales minus 32: (d*(s-32))*q
+__device__ __forceinline__ void kt_dq32_q3_k(const uint8_t* b, int sub, float* y) {
+  const float d = kt_h2f(b[108] | (b[109] << 8));
+  const int n = sub / 4, j = sub % 4, m = 1 << (4 * n + j);
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const int is = 8 * n + 2 * j + h;
+    const int sc = (((b[96 + is % 8] >> (4 * (is / 8))) & 0xF) | (((b[104 + is % 4] >> (2 * (is / 4))) & 3) << 4)) - 32;
+    const float dl = __fmul_rn(d, (float)sc);
+    const uint8_t* q = b + 32 + 32 * n + 16 * h;
+    const uint8_t* hm = b + 16 * h;
+#pragma unroll
+    for (int l = 0; l < 16; ++l) {
+      const int v = ((q[l] >> (2 * j)) & 3) - ((hm[l] & m) ? 0 : 4);
+      y[16 * h + l] = __fmul_rn(dl, (float)v);
+    }
+  }
+}
+// Q5_K: group j = sub/2 of 64 values, low (sub even) or high nibbles of ql[32j + l], fifth bit
+// sub of qh[l]: (d*sc)*q - dmin*m
+__device__ __forceinline__ void kt_dq32_q5_k(const uint8_t* b, int sub, float* y) {
+  const float d = kt_h2f(b[0] | (b[1] << 8)), dmin = kt_h2f(b[2] | (b[3] << 8));
+  int sc, m;
+  kt_q4k_scale_min(sub, b + 4, sc, m);
+  const float d1 = __fmul_rn(d, (float)sc), m1 = __fmul_rn(dmin, (float)m);
+  const uint8_t* ql = b + 48 + 32 * (sub / 2);
+  const uint8_t* qh = b + 16;
+  const int sh = 4 * (sub & 1);
+#pragma unroll
+  for (int l = 0; l < 32; ++l) {
+    const int q = ((ql[l] >> sh) & 0xF) | (((qh[l] >> sub) & 1) << 4);
+    y[l] = __fsub_rn(__fmul_rn(d1, (float)q), m1);
+  }
+}
+// IQ4_XS: sub-block ib = sub: (d*(ls-32)) * level(code)
+__device__ __forceinline__ void kt_dq32_iq4_xs(const uint8_t* b, int sub, float* y) {
+  const float d = kt_h2f(b[0] | (b[1] << 8));
+  const int scales_h = b[2] | (b[3] << 8);
+  const int ls = ((b[4 + sub / 2] >> (4 * (sub % 2))) & 0xf) | (((scales_h >> (2 * sub)) & 3) << 4);
+  const float dl = __fmul_rn(d, (float)(ls - 32));
+  const uint8_t* qs = b + 8 + 16 * sub;
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    y[j] = __fmul_rn(dl, (float)kt_iq4nl_level(qs[j] & 0xf));
+    y[j + 16] = __fmul_rn(dl, (float)kt_iq4nl_level(qs[j] >> 4));
+  }
+}
+
 // 32 consecutive values starting at element 32*sub32 of a row made of blocks of TYPE
 template <int TYPE>
 __device__ __forceinline__ void kt_dq32(const uint8_t* row, int sub32, float* y, const uint32_t* grid) {
@@ -390,5 +572,9 @@ __device__ __forceinline__ void kt_dq32(const uint8_t* row, int sub32, float* y,
     if constexpr (TYPE == KT_Q4_K) kt_dq32_q4_k(b, sub32 % 8, y);
     if constexpr (TYPE == KT_Q6_K) kt_dq32_q6_k(b, sub32 % 8, y);
     if constexpr (TYPE == KT_IQ3_S) kt_dq32_iq3_s(b, sub32 % 8, y, grid);
+    if constexpr (TYPE == KT_Q2_K) kt_dq32_q2_k(b, sub32 % 8, y);
+    if constexpr (TYPE == KT_Q3_K) kt_dq32_q3_k(b, sub32 % 8, y);
+    if constexpr (TYPE == KT_Q5_K) kt_dq32_q5_k(b, sub32 % 8, y);
+    if constexpr (TYPE == KT_IQ4_XS) kt_dq32_iq4_xs(b, sub32 % 8, y);
   }
 }

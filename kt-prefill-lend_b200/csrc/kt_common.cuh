@@ -22,10 +22,14 @@ static __device__ const uint32_t kt_iq3s_grid_dev[512] = KT_IQ3S_GRID_INIT;
 #define KT_Q5_0 6
 #define KT_Q5_1 7
 #define KT_Q8_0 8
+#define KT_Q2_K 10
+#define KT_Q3_K 11
 #define KT_Q4_K 12
+#define KT_Q5_K 13
 #define KT_Q6_K 14
 #define KT_IQ4_NL 20
 #define KT_IQ3_S 21
+#define KT_IQ4_XS 23
 
 // activation / output dtype codes of the C ABI
 #define KT_DT_F32 0
@@ -53,6 +57,10 @@ __host__ __device__ constexpr KtBlockInfo kt_block_info(int type) {
          : type == KT_Q5_0   ? KtBlockInfo{32, 22}
          : type == KT_Q5_1   ? KtBlockInfo{32, 24}
          : type == KT_IQ4_NL ? KtBlockInfo{32, 18}
+         : type == KT_Q2_K   ? KtBlockInfo{256, 84}
+         : type == KT_Q3_K   ? KtBlockInfo{256, 110}
+         : type == KT_Q5_K   ? KtBlockInfo{256, 176}
+         : type == KT_IQ4_XS ? KtBlockInfo{256, 136}
          : type == KT_Q4_K   ? KtBlockInfo{256, 144}
          : type == KT_Q6_K ? KtBlockInfo{256, 210}
          : type == KT_IQ3_S ? KtBlockInfo{256, 110}
@@ -92,10 +100,11 @@ __device__ __forceinline__ int kt_ld_b2(const uint8_t* p) {
   return (int)((uint32_t)q[0] | ((uint32_t)q[1] << 16));
 }
 __device__ __forceinline__ int kt_ld_b4(const uint8_t* p) { return *reinterpret_cast<const int*>(p); }
-// the GEMV's legacy-block types (prefill GEMM: Q8_0, Q4_K, Q6_K, IQ3_S only)
+// the decode GEMV's types (prefill GEMM: Q8_0, Q4_K, Q6_K, IQ3_S only)
 __host__ __device__ constexpr bool kt_gemv_type(int t) {
   return t == KT_Q4_0 || t == KT_Q4_1 || t == KT_Q5_0 || t == KT_Q5_1 || t == KT_Q8_0 || t == KT_IQ4_NL ||
-         t == KT_Q4_K || t == KT_Q6_K || t == KT_IQ3_S;
+         t == KT_Q2_K || t == KT_Q3_K || t == KT_Q4_K || t == KT_Q5_K || t == KT_Q6_K || t == KT_IQ3_S ||
+         t == KT_IQ4_XS;
 }
 __host__ __device__ constexpr bool kt_prefill_type(int t) {
   return t == KT_Q8_0 || t == KT_Q4_K || t == KT_Q6_K || t == KT_IQ3_S;

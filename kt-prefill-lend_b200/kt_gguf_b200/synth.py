@@ -17,7 +17,8 @@ import torch
 
 ENC_PATH = Path(__file__).resolve().parent / "lib" / "libkt_gguf_encode.so"
 BLOCK = {8: (32, 34), 12: (256, 144), 14: (256, 210), 21: (256, 110),
-         2: (32, 18), 3: (32, 20), 6: (32, 22), 7: (32, 24), 20: (32, 18)}
+         2: (32, 18), 3: (32, 20), 6: (32, 22), 7: (32, 24), 20: (32, 18),
+         10: (256, 84), 11: (256, 110), 13: (256, 176), 23: (256, 136)}
 _enc = None
 
 
@@ -73,6 +74,16 @@ def random_blocks(rng: np.random.Generator, qtype: int, rows: int, cols: int) ->
     elif qtype in (3, 7):  # d, m
         put_f16(0, 0, 2e-3)
         put_f16(2, -2e-2, 2e-2)
+    elif qtype == 10:  # d, dmin at the block's end
+        put_f16(80, 0, 2e-3)
+        put_f16(82, 0, 2e-3)
+    elif qtype == 11:  # d
+        put_f16(108, -2e-3, 2e-3)
+    elif qtype == 13:  # d, dmin
+        put_f16(0, 0, 2e-3)
+        put_f16(2, 0, 2e-3)
+    elif qtype == 23:  # d
+        put_f16(0, -2e-4, 2e-4)
     return b.reshape(rows, cols // qk * bs)
 
 

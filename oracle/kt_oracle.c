@@ -14,6 +14,10 @@
  *     729-745, 850-865) and vec_dot_iq4_nl_q8_1 (vecdotq.cuh:1995-2015): chunk = 2 ints of
  *     nibbles (8 low + 8 high codes), the Q4_1 / Q5_1 products d*d8 and m*s8 rounded to
  *     half precision as the reference's __hmul2 does.
+ *   - the K-quants Q2_K, Q3_K, Q5_K and IQ4_XS (ggml-common.h block_q2_K / q3_K / q5_K /
+ *     iq4_xs; ggml's dequantize_row order): vec_dot_q2_K_q8_1 (vecdotq.cuh:211-241,
+ *     1057-1076), vec_dot_q3_K_q8_1 (282-317, 1175-1198), vec_dot_q5_K_q8_1 (413-445,
+ *     1467-1509), vec_dot_iq4_xs_q8_1 (2019-2040).
  *   - the q8_1 activation quantizer quantize_q8_1 (hot/kt_gguf_moe_multi/kt_gguf_moe_multi.cu:600-650),
  *     including the lane order of its 32-lane butterfly sum that produces ds.y.
  *   - the per-chunk integer dot products vec_dot_q8_0_q8_1 (vecdotq.cuh:969-982),
@@ -50,6 +54,10 @@
 #define KO_Q4_K 12
 #define KO_Q6_K 14
 #define KO_IQ3_S 21
+#define KO_Q2_K 10
+#define KO_Q3_K 11
+#define KO_Q5_K 13
+#define KO_IQ4_XS 23
 
 /* ---------------------------------------------------------------- numbers */
 
@@ -120,6 +128,10 @@ int ko_block_info(int type, int* blck, int* bytes) {
     case KO_Q5_0: *blck = 32; *bytes = 22; return 0;
     case KO_Q5_1: *blck = 32; *bytes = 24; return 0;
     case KO_IQ4_NL: *blck = 32; *bytes = 18; return 0;
+    case KO_Q2_K: *blck = 256; *bytes = 84; return 0;
+    case KO_Q3_K: *blck = 256; *bytes = 110; return 0;
+    case KO_Q5_K: *blck = 256; *bytes = 176; return 0;
+    case KO_IQ4_XS: *blck = 256; *bytes = 136; return 0;
     default: return -1;
   }
 }
@@ -160,6 +172,89 @@ static void dq_q4_k(const uint8_t* b, float* y) {
     for (int l = 0; l < 32; ++l) *y++ = d2 * (float)(q[l] >> 4) - m2;
     q += 32;
     is += 2;
+  }
+}
+
+/* Q2_K: scales[16] (low nibble scale, high nibble min), qs[64], d, dmin; 128-value halves,
+ * four 2-bit planes each, 16 values per scale */
+static void dq_q2_k(const uint8_t* b, float* y) {
+  float d = ko_h2f(rd16(b + 80)), dmin = ko_h2f(rd16(b + 82));
+  const uint8_t* q = b + 16;
+  int is = 0;
+  for (int n = 0; n < 256; n += 128) {
+    for (int shift = 0; shift < 8; shift += 2) {
+      for (int h = 0; h < 2; ++h) {
+        uint8_t sc = b[is++];
+        float dl = d * (float)(sc & 0xF), ml = dmin * (float)(sc >> 4);
+        for (int l = 0; l < 16; ++l) *y++ = dl * (float)((q[16 * h + l] >> shift) & 3) - ml;
+      }
+    }
+    q += 32;
+  }
+}
+
+/* Q3_K scale i (0..15): 4 low bits from byte i%8 (nibble i/8), 2 high bits from byte 8+i%4
+ * (pair i/4), minus 32 */
+static int q3k_scale(const uint8_t* s, int i) {
+  return (((s[i % 8] >> (4 * (i / 8))) & 0xF) | (((s[8 + i % 4] >> (2 * (i / 4))) & 3) << 4)) - 32;
+}
+
+/* Q3_K: hmask[32], qs[64], scales[12], d; as Q2_K's planes, the hmask bit (clear: -4) */
+static void dq_q3_k(const uint8_t* b, float* y) {
+  float d = ko_h2f(rd16(b + 108));
+  const uint8_t* q = b + 32;
+  const uint8_t* hm = b;
+  int is = 0;
+  uint8_t m = 1;
+  for (int n = 0; n < 256; n += 128) {
+    for (int shift = 0; shift < 8; shift += 2) {
+      for (int h = 0; h < 2; ++h) {
+        float dl = d * (float)q3k_scale(b + 96, is++);
+        for (int l = 0; l < 16; ++l)
+          *y++ = dl * (float)(((q[16 * h + l] >> shift) & 3) - ((hm[16 * h + l] & m) ? 0 : 4));
+      }
+      m <<= 1;
+    }
+    q += 32;
+  }
+}
+
+/* Q5_K: d, dmin, Q4_K's 12-byte scales, qh[32], qs[128]; fifth bit from qh, planes 2j / 2j+1 */
+static void dq_q5_k(const uint8_t* b, float* y) {
+  float d = ko_h2f(rd16(b)), dmin = ko_h2f(rd16(b + 2));
+  const uint8_t* ql = b + 48;
+  const uint8_t* qh = b + 16;
+  int is = 0;
+  uint8_t u1 = 1, u2 = 2;
+  for (int j = 0; j < 256; j += 64) {
+    uint8_t sc, m;
+    q4k_scale_min(is + 0, b + 4, &sc, &m);
+    float d1 = d * sc, m1 = dmin * m;
+    q4k_scale_min(is + 1, b + 4, &sc, &m);
+    float d2 = d * sc, m2 = dmin * m;
+    for (int l = 0; l < 32; ++l) *y++ = d1 * (float)((ql[l] & 0xF) + ((qh[l] & u1) ? 16 : 0)) - m1;
+    for (int l = 0; l < 32; ++l) *y++ = d2 * (float)((ql[l] >> 4) + ((qh[l] & u2) ? 16 : 0)) - m2;
+    ql += 32;
+    is += 2;
+    u1 <<= 2;
+    u2 <<= 2;
+  }
+}
+
+/* IQ4_XS: d, scales_h (2 bits per sub-block), scales_l[4] (4 bits), qs[128]; IQ4_NL levels */
+static void dq_iq4_xs(const uint8_t* b, float* y) {
+  float d = ko_h2f(rd16(b));
+  uint16_t scales_h = rd16(b + 2);
+  const uint8_t* qs = b + 8;
+  for (int ib = 0; ib < 8; ++ib) {
+    int ls = ((b[4 + ib / 2] >> (4 * (ib % 2))) & 0xf) | (((scales_h >> (2 * ib)) & 3) << 4);
+    float dl = d * (float)(ls - 32);
+    for (int j = 0; j < 16; ++j) {
+      y[j] = dl * (float)ko_iq4nl[qs[j] & 0xf];
+      y[j + 16] = dl * (float)ko_iq4nl[qs[j] >> 4];
+    }
+    y += 32;
+    qs += 16;
   }
 }
 
@@ -250,6 +345,10 @@ int ko_dequant_rows(int type, const uint8_t* w, int64_t nrows, int64_t cols, flo
         case KO_Q4_K: dq_q4_k(b, y); break;
         case KO_Q6_K: dq_q6_k(b, y); break;
         case KO_IQ3_S: dq_iq3_s(b, y); break;
+        case KO_Q2_K: dq_q2_k(b, y); break;
+        case KO_Q3_K: dq_q3_k(b, y); break;
+        case KO_Q5_K: dq_q5_k(b, y); break;
+        case KO_IQ4_XS: dq_iq4_xs(b, y); break;
         default: dq_legacy(type, b, y); break;
       }
     }
@@ -444,6 +543,104 @@ static float vd_legacy(int type, const uint8_t* bx, const uint8_t* b8, int iqs) 
   }
 }
 
+/* vec_dot_q2_K_q8_1: iqs 0..15; int iqs of qs has 4 codes of 4 groups (bit pairs), against
+ * int iqs%8 of q8_1 blocks 4(iqs/8) + i; group scales at 2i past scale_offset */
+static float vd_q2_k(const uint8_t* bx, const uint8_t* by0, int iqs) {
+  const int bq8_offset = 4 * (iqs / 8);
+  const uint8_t* scales = bx + iqs - iqs % 8 + (iqs % 8) / 4;
+  const uint32_t v = (uint32_t)rd32(bx + 16 + 4 * iqs);
+  float sumf_d = 0.0f, sumf_m = 0.0f;
+  for (int i = 0; i < 4; ++i) {
+    const uint8_t* b8 = by0 + 36 * (bq8_offset + i);
+    const int32_t u = rd32(b8 + 4 + 4 * (iqs % 8));
+    const float d8 = q8_1_d(b8);
+    const int sc = scales[2 * i];
+    sumf_d += d8 * (float)(dp4a((int32_t)((v >> (2 * i)) & 0x03030303u), u, 0) * (sc & 0xF));
+    sumf_m += d8 * (float)dp4a((sc >> 4) * 0x01010101, u, 0);
+  }
+  const float dmx = ko_h2f(rd16(bx + 80)), dmy = ko_h2f(rd16(bx + 82));
+  return dmx * sumf_d - dmy * sumf_m;
+}
+
+/* vec_dot_q3_K_q8_1: as Q2_K, the code's third bit from hmask int iqs%8 (clear: subtract 4,
+ * a per-byte saturating subtraction that never saturates for 0..3 - 0/4) */
+static float vd_q3_k(const uint8_t* bx, const uint8_t* by0, int iqs) {
+  const int bq8_offset = 4 * (iqs / 8);
+  const int scale_offset = iqs - iqs % 8 + (iqs % 8) / 4;
+  const uint32_t vl = (uint32_t)rd32(bx + 32 + 4 * iqs);
+  const int32_t vh = ~rd32(bx + 4 * (iqs % 8)) >> bq8_offset;
+  float sumf = 0.0f;
+  for (int i = 0; i < 4; ++i) {
+    const int sc = q3k_scale(bx + 96, scale_offset + 2 * i);
+    const uint32_t lo = (vl >> (2 * i)) & 0x03030303u;
+    const uint32_t hi = ((uint32_t)(vh >> i) << 2) & 0x04040404u;
+    uint32_t vi = 0;
+    for (int k = 0; k < 4; ++k) {
+      int8_t a = (int8_t)(lo >> (8 * k)), c = (int8_t)(hi >> (8 * k));
+      vi |= (uint32_t)(uint8_t)(int8_t)(a - c) << (8 * k);
+    }
+    const uint8_t* b8 = by0 + 36 * (bq8_offset + i);
+    const int32_t u = rd32(b8 + 4 + 4 * (iqs % 8));
+    sumf += q8_1_d(b8) * (float)(dp4a((int32_t)vi, u, 0) * sc);
+  }
+  return ko_h2f(rd16(bx + 108)) * sumf;
+}
+
+/* vec_dot_q5_K_q8_1: Q4_K's chunk (iqs even 0..30) with the fifth bit of each code from qh */
+static float vd_q5_k(const uint8_t* bx, const uint8_t* by0, int iqs) {
+  const int bq8_offset = 2 * ((iqs / 2) / 4);
+  const uint8_t* ql = bx + 48 + 16 * bq8_offset + 4 * ((iqs / 2) % 4);
+  const uint8_t* qh = bx + 16 + 4 * ((iqs / 2) % 4);
+  const uint32_t vl0 = (uint32_t)rd32(ql), vl1 = (uint32_t)rd32(ql + 16);
+  const int32_t vh0 = rd32(qh) >> bq8_offset, vh1 = rd32(qh + 16) >> bq8_offset;
+  uint16_t s16[6];
+  for (int i = 0; i < 6; ++i) s16[i] = rd16(bx + 4 + 2 * i);
+  uint16_t aux0, aux1;
+  const int j = bq8_offset / 2;
+  if (j < 2) {
+    aux0 = s16[j + 0] & 0x3f3f;
+    aux1 = s16[j + 2] & 0x3f3f;
+  } else {
+    aux0 = (uint16_t)(((s16[j + 2] >> 0) & 0x0f0f) | ((s16[j - 2] & 0xc0c0) >> 2));
+    aux1 = (uint16_t)(((s16[j + 2] >> 4) & 0x0f0f) | ((s16[j - 0] & 0xc0c0) >> 2));
+  }
+  float sumf_d = 0.0f, sumf_m = 0.0f;
+  for (int i = 0; i < 2; ++i) {
+    const uint8_t* b8 = by0 + 36 * (bq8_offset + i);
+    const int32_t u0 = rd32(b8 + 4 + 4 * ((iqs / 2) % 4)), u1 = rd32(b8 + 4 + 4 * ((iqs / 2) % 4) + 16);
+    const int32_t v0 = (int32_t)(((vl0 >> (4 * i)) & 0x0F0F0F0Fu) | (((uint32_t)(vh0 >> i) << 4) & 0x10101010u));
+    const int32_t v1 = (int32_t)(((vl1 >> (4 * i)) & 0x0F0F0F0Fu) | (((uint32_t)(vh1 >> i) << 4) & 0x10101010u));
+    const int32_t dot1 = dp4a(v0, u0, dp4a(v1, u1, 0));
+    const int32_t dot2 = dp4a(0x01010101, u0, dp4a(0x01010101, u1, 0));
+    const float d8 = q8_1_d(b8);
+    const int sc = (aux0 >> (8 * i)) & 0xff, m = (aux1 >> (8 * i)) & 0xff;
+    sumf_d += d8 * (float)(dot1 * sc);
+    sumf_m += d8 * (float)(dot2 * m);
+  }
+  const float dmx = ko_h2f(rd16(bx)), dmy = ko_h2f(rd16(bx + 2));
+  return dmx * sumf_d - dmy * sumf_m;
+}
+
+/* vec_dot_iq4_xs_q8_1: chunk = sub-block ib32 (0..7) against q8_1 block ib32 */
+static float vd_iq4_xs(const uint8_t* bx, const uint8_t* by0, int ib32) {
+  const uint8_t* b8 = by0 + 36 * ib32;
+  const uint8_t* q4 = bx + 8 + 16 * ib32;
+  const int scales_h = rd16(bx + 2);
+  const int ls = ((bx[4 + ib32 / 2] >> (4 * (ib32 % 2))) & 0xf) | (((scales_h >> (2 * ib32)) & 3) << 4);
+  const float d = ko_h2f(rd16(bx)) * (float)(ls - 32) * q8_1_d(b8);
+  int32_t sumi1 = 0, sumi2 = 0;
+  for (int j = 0; j < 4; ++j) {
+    uint32_t q = (uint32_t)rd32(q4 + 4 * j), lo = 0, hi = 0;
+    for (int k = 0; k < 4; ++k) {
+      lo |= (uint32_t)(uint8_t)ko_iq4nl[(q >> (8 * k)) & 0xF] << (8 * k);
+      hi |= (uint32_t)(uint8_t)ko_iq4nl[(q >> (8 * k + 4)) & 0xF] << (8 * k);
+    }
+    sumi1 = dp4a((int32_t)lo, rd32(b8 + 4 + 4 * j), sumi1);
+    sumi2 = dp4a((int32_t)hi, rd32(b8 + 20 + 4 * j), sumi2);
+  }
+  return d * (float)(sumi1 + sumi2);
+}
+
 /* chunk geometry of the reference launchers: values per block, chunks per block, vdr */
 static int chunk_geom(int type, int* qk, int* cpb, int* vdr) {
   switch (type) {
@@ -451,6 +648,9 @@ static int chunk_geom(int type, int* qk, int* cpb, int* vdr) {
     case KO_Q4_K: *qk = 256; *cpb = 16; *vdr = 2; return 0; /* qi 32, vdr 2 */
     case KO_Q6_K: *qk = 256; *cpb = 32; *vdr = 1; return 0; /* qi 32, vdr 1 */
     case KO_IQ3_S: *qk = 256; *cpb = 8; *vdr = 1; return 0; /* qi 8, vdr 1 */
+    case KO_Q2_K: case KO_Q3_K: *qk = 256; *cpb = 16; *vdr = 1; return 0; /* qi 16, vdr 1 */
+    case KO_Q5_K: *qk = 256; *cpb = 16; *vdr = 2; return 0; /* qi 32, vdr 2 */
+    case KO_IQ4_XS: *qk = 256; *cpb = 8; *vdr = 1; return 0; /* qi 8, vdr 1 */
     case KO_Q4_0: case KO_Q4_1: case KO_Q5_0: case KO_Q5_1: case KO_IQ4_NL:
       *qk = 32; *cpb = 2; *vdr = 2; return 0;               /* qi 4, vdr 2 */
     default: return -1;
@@ -474,6 +674,10 @@ static float row_dot(int type, const uint8_t* wrow, int bs, int nblocks, const u
       case KO_Q4_K: v = vd_q4_k(bx, by, iqs); break;
       case KO_Q6_K: v = vd_q6_k(bx, by, iqs); break;
       case KO_IQ3_S: v = vd_iq3_s(bx, by, iqs); break;
+      case KO_Q2_K: v = vd_q2_k(bx, by, iqs); break;
+      case KO_Q3_K: v = vd_q3_k(bx, by, iqs); break;
+      case KO_Q5_K: v = vd_q5_k(bx, by, iqs); break;
+      case KO_IQ4_XS: v = vd_iq4_xs(bx, by, iqs); break;
       default: v = vd_legacy(type, bx, by, iqs); break;
     }
     lane[c % 32] += v;

@@ -9,6 +9,8 @@ implementation independent of this repository. For each type the file holds
                            which neither encodes, takes random blocks here too),
                            rows 24-47 random bytes with finite scales (every code pattern)
   <type>_values  float32: gguf-py's dequantization of those rows
+and for Q2_K, Q3_K, Q5_K and IQ4_XS, which gguf-py does not encode, 48 rows of random blocks
+with finite scales and their dequantization,
 plus the IQ3_S codebook as uint32 words and the IQ4_NL levels.
 
 Run from the repository root: python tests/golden/make_golden.py
@@ -28,6 +30,7 @@ from kt_gguf_b200 import synth  # noqa: E402
 
 TYPES = {8: Q.Q8_0, 12: Q.Q4_K, 14: Q.Q6_K, 21: Q.IQ3_S}
 LEGACY = {2: Q.Q4_0, 3: Q.Q4_1, 6: Q.Q5_0, 7: Q.Q5_1, 20: Q.IQ4_NL}
+KQUANTS = {10: Q.Q2_K, 11: Q.Q3_K, 13: Q.Q5_K, 23: Q.IQ4_XS}
 
 
 def main():
@@ -44,6 +47,10 @@ def main():
         enc = synth.random_blocks(rng, t, 24, 512) if t == 20 else quantize(w, qt)
         rnd = synth.random_blocks(rng, t, 24, 512)
         blocks = np.concatenate([enc, rnd])
+        out[f"{t}_blocks"] = blocks
+        out[f"{t}_values"] = dequantize(blocks, qt).reshape(48, 512).astype(np.float32)
+    for t, qt in KQUANTS.items():
+        blocks = synth.random_blocks(rng, t, 48, 512)
         out[f"{t}_blocks"] = blocks
         out[f"{t}_values"] = dequantize(blocks, qt).reshape(48, 512).astype(np.float32)
     out["iq4nl_levels"] = np.array(IQ4_NL.kvalues, dtype=np.int8)

@@ -12,7 +12,8 @@ from oracle import oracle as O
 pytestmark = pytest.mark.gpu
 GOLDEN = np.load(__import__("pathlib").Path(__file__).with_name("golden") / "gguf_dequant.npz")
 TYPES = (8, 12, 14, 21)
-LEGACY = (2, 3, 6, 7, 20)  # 32-value blocks: decode GEMV and dequantizer only
+# decode GEMV and dequantizer only: 32-value blocks and the K-quants Q2_K / Q3_K / Q5_K / IQ4_XS
+LEGACY = (2, 3, 6, 7, 20, 10, 11, 13, 23)
 
 
 def bits(t: torch.Tensor) -> np.ndarray:
@@ -81,7 +82,8 @@ def _oracle_gemv(qtype, W, x, ids, top_k, rows, cols):
 @pytest.mark.parametrize("qtype,cols,rows", [(8, 2048, 96), (8, 768, 2048), (12, 2048, 1024), (14, 512, 2048),
                                              (21, 2048, 1024), (21, 512, 2048), (12, 7168, 64),
                                              (2, 2048, 256), (3, 2048, 256), (6, 512, 512), (7, 2048, 256),
-                                             (20, 2048, 256)])
+                                             (20, 2048, 256), (10, 2048, 256), (11, 512, 512), (13, 2048, 256),
+                                             (23, 2048, 256)])
 @pytest.mark.parametrize("tokens,top_k", [(1, 8), (4, 10), (16, 3)])
 def test_gemv_matches_reference_arithmetic(cuda_device, qtype, cols, rows, tokens, top_k):
     slots = 6

@@ -18,11 +18,16 @@ def q8_1_dequant(qx: np.ndarray, cols: int) -> np.ndarray:
 
 
 @pytest.mark.parametrize("qtype,cols,rows", [(8, 2048, 96), (8, 768, 40), (12, 2048, 64), (14, 512, 64),
-                                             (21, 2048, 48), (21, 512, 40)])
+                                             (21, 2048, 48), (21, 512, 40), (10, 2048, 40), (11, 512, 40),
+                                             (13, 2048, 40), (23, 2048, 40)])
 def test_gemv_integer_path_equals_dequant_matmul(qtype, cols, rows):
     rng = np.random.default_rng(qtype * 1000 + cols)
     x = rng.standard_normal((5, cols), dtype=np.float32)
-    W = np.stack([synth.quantize(rng.standard_normal((rows, cols), dtype=np.float32) * 0.02, qtype) for _ in range(3)])
+    if qtype in (10, 11, 13, 23):  # no encoder for these: arbitrary valid blocks
+        W = np.stack([synth.random_blocks(rng, qtype, rows, cols) for _ in range(3)])
+    else:
+        W = np.stack([synth.quantize(rng.standard_normal((rows, cols), dtype=np.float32) * 0.02, qtype)
+                      for _ in range(3)])
     qx = O.quantize_q8_1(x)
     ids = np.array([0, 2, -1, 1, 2, 0, 1, 1, 2, 0], dtype=np.int32)  # top_k 2, a CPU route, repeats
     y = O.moe_vec(qtype, W, qx, ids, 2, rows, cols)
