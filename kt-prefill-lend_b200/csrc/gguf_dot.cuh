@@ -62,6 +62,11 @@ template <>
 struct KtChunk<KT_IQ4_XS> {
   static constexpr int QK = 256, BYTES = 136, CPB = 8, VDR = 1;
 };
+// Q2_0: 4 bytes of codes (16 values) per chunk against half a q8_1 block (QI 4, VDR 1)
+template <>
+struct KtChunk<KT_Q2_0> {
+  static constexpr int QK = 64, BYTES = 18, CPB = 4, VDR = 1;
+};
 template <>
 struct KtChunk<KT_Q6_K> {
   static constexpr int QK = 256, BYTES = 210, CPB = 32, VDR = 1;
@@ -323,6 +328,24 @@ __device__ __forceinline__ float kt_vd_iq4_xs(const uint8_t* bx, const uint8_t* 
   return d * (sumi1 + sumi2);
 }
 
+// ---- Q2_0 (fp16 d, qs[16]: byte b holds elements 4b..4b+3, code s at bits 2s; value
+// d*(code-1)); chunk iqs 0..3 = bytes 4iqs..4iqs+3 against half iqs&1 of q8_1 block iqs/2.
+// The -1 is taken as sum(code*u) - sum(u) so that no byte of a packed int borrows.
+__device__ __forceinline__ float kt_vd_q2_0(const uint8_t* bx, const uint8_t* yq, const uint8_t* yd, int iqs) {
+  const uint8_t* q = bx + 2 + 4 * iqs;
+  const uint8_t* u = yq + 32 * (iqs >> 1) + 16 * (iqs & 1);
+  int sumi = 0, sumy = 0;
+#pragma unroll
+  for (int b = 0; b < 4; ++b) {
+    const int c = q[b];
+    const int codes = (c | (c << 6) | (c << 12) | (c << 18)) & 0x03030303;  // code s -> byte s
+    const int ub = kt_ld_b4(u + 4 * b);
+    sumi = __dp4a(codes, ub, sumi);
+    sumy = __dp4a(0x01010101, ub, sumy);
+  }
+  return kt_h2f(*reinterpret_cast<const uint16_t*>(bx)) * kt_q8_1_dd(yd + 4 * (iqs >> 1)) * (float)(sumi - sumy);
+}
+
 // ---- Q6_K: 8 values; iqs in 0..31. The reference's per-byte (code - 32) with __vsubss4
 // never saturates (codes are 0..63), so the integer dot is dp4a(code, u) - 32 * sum(u),
 // computed here with two dp4a instead of the emulated SIMD subtract.
@@ -398,6 +421,7 @@ __device__ __forceinline__ float kt_vec_dot(const uint8_t* bx, const uint8_t* yq
   if constexpr (TYPE == KT_Q3_K) return kt_vd_q3_k(bx, yq, yd, iqs);
   if constexpr (TYPE == KT_Q5_K) return kt_vd_q5_k(bx, yq, yd, iqs);
   if constexpr (TYPE == KT_IQ4_XS) return kt_vd_iq4_xs(bx, yq, yd, iqs);
+  if constexpr (TYPE == KT_Q2_0) return kt_vd_q2_0(bx, yq, yd, iqs);
   if constexpr (TYPE == KT_Q4_K) return kt_vd_q4_k(bx, yq, yd, iqs);
   if constexpr (TYPE == KT_Q6_K) return kt_vd_q6_k(bx, yq, yd, iqs);
   if constexpr (TYPE == KT_IQ3_S) return kt_vd_iq3_s(bx, yq, yd, iqs, grid);
@@ -566,6 +590,12 @@ __device__ __forceinline__ void kt_dq32(const uint8_t* row, int sub32, float* y,
     kt_dq32_q8_0(row + sub32 * 34, y);
   } else if constexpr (KtChunk<TYPE>::QK == 32) {
     kt_dq32_legacy<TYPE>(row + sub32 * KtChunk<TYPE>::BYTES, y);
+  } else if constexpr (TYPE == KT_Q2_0) {  // half sub32&1 of 64-value block sub32/2: (code-1)*d
+    const uint8_t* b = row + (sub32 / 2) * 18;
+    const float d = kt_h2f(b[0] | (b[1] << 8));
+    const uint8_t* q = b + 2 + 8 * (sub32 & 1);
+#pragma unroll
+    for (int j = 0; j < 32; ++j) y[j] = __fmul_rn((float)(((q[j / 4] >> (2 * (j % 4))) & 3) - 1), d);
   } else {
     constexpr int BS = KtChunk<TYPE>::BYTES;
     const uint8_t* b = row + (sub32 / 8) * BS;

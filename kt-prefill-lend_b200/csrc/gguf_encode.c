@@ -9,6 +9,8 @@
  *   Q6_K  — per 16-value sub-block absmax, int8 scales under an fp16 d.
  *   IQ3_S — per 32-value sub-block scale d*(1+2s), each group of 4 magnitudes snapped
  *           to the nearest grid entry of the 512-word IQ3_S codebook, sign bits apart.
+ *   Q2_0  — the reference's 64-value block (ggml type 42): d = amax/2, code =
+ *           clamp(roundf(x / d) + 1, 0, 3), so the levels are -d, 0, d, 2d.
  * Any bytes these produce are valid blocks of their type; the decoders (GPU kernels and
  * the CPU oracle) do not depend on how the encoder chose them.
  */
@@ -41,6 +43,16 @@ static void enc_q8_0(const float* x, uint8_t* b) {
   const float id = d ? 1.0f / d : 0.0f;
   put16(b, f2h(d));
   for (int j = 0; j < 32; ++j) b[2 + j] = (uint8_t)(int8_t)roundf(x[j] * id);
+}
+
+static void enc_q2_0(const float* x, uint8_t* b) {
+  float amax = 0.0f;
+  for (int j = 0; j < 64; ++j) amax = fmaxf(amax, fabsf(x[j]));
+  const float d = amax / 2;
+  const float id = d ? 1.0f / d : 0.0f;
+  put16(b, f2h(d));
+  memset(b + 2, 0, 16);
+  for (int j = 0; j < 64; ++j) b[2 + j / 4] |= (uint8_t)(clampi((int)roundf(x[j] * id) + 1, 0, 3) << (2 * (j % 4)));
 }
 
 static void enc_q4_k(const float* x, uint8_t* b) {
@@ -182,6 +194,7 @@ int kte_row_bytes(int type, int64_t cols, int64_t* out) {
     case 12: blck = 256; bs = 144; break;
     case 14: blck = 256; bs = 210; break;
     case 21: blck = 256; bs = 110; break;
+    case 42: blck = 64; bs = 18; break;
     default: return -1;
   }
   if (cols % blck) return -2;
@@ -195,8 +208,8 @@ int kte_quantize(int type, const float* x, int64_t rows, int64_t cols, uint8_t* 
   int rc = kte_row_bytes(type, cols, &rb);
   if (rc) return rc;
   if (type == 21 && !iq3s_ready) iq3s_init();
-  const int blck = type == 8 ? 32 : 256;
-  const int bs = type == 8 ? 34 : (type == 12 ? 144 : (type == 14 ? 210 : 110));
+  const int blck = type == 8 ? 32 : (type == 42 ? 64 : 256);
+  const int bs = (int)(rb / (cols / blck));
   const int64_t nb = cols / blck;
 #pragma omp parallel for schedule(static)
   for (int64_t r = 0; r < rows; ++r) {
@@ -208,6 +221,7 @@ int kte_quantize(int type, const float* x, int64_t rows, int64_t cols, uint8_t* 
         case 12: enc_q4_k(xb, bb); break;
         case 14: enc_q6_k(xb, bb); break;
         case 21: enc_iq3_s(xb, bb); break;
+        case 42: enc_q2_0(xb, bb); break;
       }
     }
   }

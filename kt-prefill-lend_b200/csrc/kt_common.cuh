@@ -30,6 +30,7 @@ static __device__ const uint32_t kt_iq3s_grid_dev[512] = KT_IQ3S_GRID_INIT;
 #define KT_IQ4_NL 20
 #define KT_IQ3_S 21
 #define KT_IQ4_XS 23
+#define KT_Q2_0 42  // 64-value blocks: fp16 d, 2-bit codes, value d*(code-1)
 
 // activation / output dtype codes of the C ABI
 #define KT_DT_F32 0
@@ -61,6 +62,7 @@ __host__ __device__ constexpr KtBlockInfo kt_block_info(int type) {
          : type == KT_Q3_K   ? KtBlockInfo{256, 110}
          : type == KT_Q5_K   ? KtBlockInfo{256, 176}
          : type == KT_IQ4_XS ? KtBlockInfo{256, 136}
+         : type == KT_Q2_0   ? KtBlockInfo{64, 18}
          : type == KT_Q4_K   ? KtBlockInfo{256, 144}
          : type == KT_Q6_K ? KtBlockInfo{256, 210}
          : type == KT_IQ3_S ? KtBlockInfo{256, 110}
@@ -104,7 +106,7 @@ __device__ __forceinline__ int kt_ld_b4(const uint8_t* p) { return *reinterpret_
 __host__ __device__ constexpr bool kt_gemv_type(int t) {
   return t == KT_Q4_0 || t == KT_Q4_1 || t == KT_Q5_0 || t == KT_Q5_1 || t == KT_Q8_0 || t == KT_IQ4_NL ||
          t == KT_Q2_K || t == KT_Q3_K || t == KT_Q4_K || t == KT_Q5_K || t == KT_Q6_K || t == KT_IQ3_S ||
-         t == KT_IQ4_XS;
+         t == KT_IQ4_XS || t == KT_Q2_0;
 }
 __host__ __device__ constexpr bool kt_prefill_type(int t) {
   return t == KT_Q8_0 || t == KT_Q4_K || t == KT_Q6_K || t == KT_IQ3_S;

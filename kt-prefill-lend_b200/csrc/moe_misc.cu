@@ -61,6 +61,7 @@ int kt_launch_dequant(int type, const void* w, int64_t rows, int64_t cols, void*
     case KT_Q3_K: return dequant_t<KT_Q3_K>(w, rows, cols, out, out_dtype, s);
     case KT_Q5_K: return dequant_t<KT_Q5_K>(w, rows, cols, out, out_dtype, s);
     case KT_IQ4_XS: return dequant_t<KT_IQ4_XS>(w, rows, cols, out, out_dtype, s);
+    case KT_Q2_0: return dequant_t<KT_Q2_0>(w, rows, cols, out, out_dtype, s);
     case KT_Q4_K: return dequant_t<KT_Q4_K>(w, rows, cols, out, out_dtype, s);
     case KT_Q6_K: return dequant_t<KT_Q6_K>(w, rows, cols, out, out_dtype, s);
     case KT_IQ3_S: return dequant_t<KT_IQ3_S>(w, rows, cols, out, out_dtype, s);

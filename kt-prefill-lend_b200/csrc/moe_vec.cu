@@ -473,6 +473,7 @@ int kt_launch_moe_vec(int type, const void* w, int table, const void* qx, int64_
                                : type == KT_Q3_K   ? KtChunk<KT_Q3_K>::CPB
                                : type == KT_Q5_K   ? KtChunk<KT_Q5_K>::CPB
                                : type == KT_IQ4_XS ? KtChunk<KT_IQ4_XS>::CPB
+                               : type == KT_Q2_0   ? KtChunk<KT_Q2_0>::CPB
                                                    : KtChunk<KT_Q4_0>::CPB;  // the 32-value legacy blocks
   const int nchunks = cols / bi.qk * chunks_per_block;
   const int lpr = nchunks <= 16 ? 16 : 32;
@@ -487,6 +488,7 @@ int kt_launch_moe_vec(int type, const void* w, int table, const void* qx, int64_
     case KT_Q3_K: return launch_vec_dt<KT_Q3_K>(a, dtype, max_groups, lpr, smem, s);
     case KT_Q5_K: return launch_vec_dt<KT_Q5_K>(a, dtype, max_groups, lpr, smem, s);
     case KT_IQ4_XS: return launch_vec_dt<KT_IQ4_XS>(a, dtype, max_groups, lpr, smem, s);
+    case KT_Q2_0: return launch_vec_dt<KT_Q2_0>(a, dtype, max_groups, lpr, smem, s);
     case KT_Q4_K: return launch_vec_dt<KT_Q4_K>(a, dtype, max_groups, lpr, smem, s);
     case KT_Q6_K: return launch_vec_dt<KT_Q6_K>(a, dtype, max_groups, lpr, smem, s);
     case KT_IQ3_S: return launch_vec_dt<KT_IQ3_S>(a, dtype, max_groups, lpr, smem, s);

@@ -17,8 +17,12 @@ reference's layout:
 With KV-lent slots (layer.kt_kv_ptr13 / kt_kv_ptr2) both paths read the weights through the
 per-slot pointer tables.
 
-GGUF types with B200 kernels: Q8_0 (8), Q4_K (12), Q6_K (14), IQ3_S (21); other types raise
-at construction. Q2_0 downs can be repacked losslessly to Q8_0 with q2_0_to_q8_0.
+GGUF types with B200 kernels: the prefill layer takes Q8_0 (8), Q4_K (12), Q6_K (14) and
+IQ3_S (21); the GEMV also Q4_0/Q4_1/Q5_0/Q5_1/IQ4_NL, Q2_K/Q3_K/Q5_K/IQ4_XS and the
+reference's Q2_0 (42); other types raise at construction. As in the reference
+(hot/kt_gguf_hot.py:21-25, 180-190), Q2_0 downs stay 2-bit on the GPU and their layers run
+the GEMV at every length; KT_GGUF_Q2_NATIVE=0 repacks them losslessly into Q8_0 instead
+(q2_0_to_q8_0), which the prefill layer takes.
 """
 import os
 import time
@@ -61,8 +65,9 @@ BLOCK_INFO = {
     16: (256, 66), 19: (256, 74), 20: (32, 18), 21: (256, 110), 22: (256, 82), 23: (256, 136),
     18: (256, 98), 42: (64, 18),
 }
-# types with a B200 kernel (the reference's MMVQ_TYPES lists every sgl-kernel MMVQ type)
-MMVQ_TYPES = set(_multi.SUPPORTED_TYPES)
+# types with a B200 kernel (the reference's MMVQ_TYPES lists every sgl-kernel MMVQ type, which
+# excludes its own Q2_0: that one is allowed through q2_native)
+MMVQ_TYPES = set(_multi.SUPPORTED_TYPES) - {GGML_Q2_0}
 
 
 def _log(msg):
@@ -164,9 +169,14 @@ class KTGGUFHotExpertsMethod(FusedMoEMethodBase):
         if self.types[0] != self.types[1]:
             raise RuntimeError(f"layer {kt_config.layer_idx}: gate {self.types[0]} and up {self.types[1]} differ")
         self.type13 = self.types[0]
-        self.type2 = GGML_Q8_0 if self.types[2] == GGML_Q2_0 else self.types[2]  # Q2_0 repacked exactly
+        # Q2_0 downs stay 2-bit on the GPU (KT_GGUF_Q2_NATIVE=0: the exact 4x Q8_0 repack)
+        self.q2_native = os.environ.get("KT_GGUF_Q2_NATIVE", "1") == "1"
+        if self.types[2] == GGML_Q2_0:
+            self.type2 = GGML_Q2_0 if self.q2_native else GGML_Q8_0
+        else:
+            self.type2 = self.types[2]
         for t in (self.type13, self.type2):
-            if t not in MMVQ_TYPES:
+            if t not in MMVQ_TYPES and not (t == GGML_Q2_0 and self.q2_native):
                 raise RuntimeError(f"layer {kt_config.layer_idx}: ggml type {t} has no B200 kernel "
                                    f"(supported: {sorted(MMVQ_TYPES)})")
         self.moe_runner_config = None
@@ -209,7 +219,7 @@ class KTGGUFHotExpertsMethod(FusedMoEMethodBase):
         layer.w13_qweight.data[:, :N].copy_(self.reader.slice(li, "gate", N, self.rank, p2l))
         layer.w13_qweight.data[:, N:].copy_(self.reader.slice(li, "up", N, self.rank, p2l))
         down = self.reader.slice(li, "down", N, self.rank, p2l)
-        if self.types[2] == GGML_Q2_0:
+        if self.types[2] == GGML_Q2_0 and self.type2 == GGML_Q8_0:
             down = q2_0_to_q8_0(down)
         if tuple(down.shape) != tuple(layer.w2_qweight.shape):
             raise RuntimeError(f"down slice {tuple(down.shape)} vs slots {tuple(layer.w2_qweight.shape)}")
@@ -223,8 +233,11 @@ class KTGGUFHotExpertsMethod(FusedMoEMethodBase):
         self.moe_runner_config = moe_runner_config
 
     def _use_prefill(self, x: torch.Tensor, T: int) -> bool:
+        # layers of other types (a native Q2_0 down, the GEMV-only quantizations) run the GEMV at
+        # every length, as the reference runs its window kernel for its Q2_0 layers
         return (PREFILL_ON_GPU and T >= PREFILL_MIN and x.dtype == torch.bfloat16 and self.K % 256 == 0
-                and self.N % 256 == 0)
+                and self.N % 256 == 0 and self.type13 in _multi.N.PREFILL_TYPES
+                and self.type2 in _multi.N.PREFILL_TYPES)
 
     def apply(self, layer, dispatch_output):
         x = dispatch_output.hidden_states

@@ -18,7 +18,7 @@ import torch
 ENC_PATH = Path(__file__).resolve().parent / "lib" / "libkt_gguf_encode.so"
 BLOCK = {8: (32, 34), 12: (256, 144), 14: (256, 210), 21: (256, 110),
          2: (32, 18), 3: (32, 20), 6: (32, 22), 7: (32, 24), 20: (32, 18),
-         10: (256, 84), 11: (256, 110), 13: (256, 176), 23: (256, 136)}
+         10: (256, 84), 11: (256, 110), 13: (256, 176), 23: (256, 136), 42: (64, 18)}
 _enc = None
 
 
@@ -69,7 +69,7 @@ def random_blocks(rng: np.random.Generator, qtype: int, rows: int, cols: int) ->
         put_f16(208, -2e-4, 2e-4)
     elif qtype == 21:
         put_f16(0, 0, 2e-4)
-    elif qtype in (2, 6, 20):  # d
+    elif qtype in (2, 6, 20, 42):  # d
         put_f16(0, -2e-3, 2e-3)
     elif qtype in (3, 7):  # d, m
         put_f16(0, 0, 2e-3)

@@ -17,7 +17,8 @@
  *   - the K-quants Q2_K, Q3_K, Q5_K and IQ4_XS (ggml-common.h block_q2_K / q3_K / q5_K /
  *     iq4_xs; ggml's dequantize_row order): vec_dot_q2_K_q8_1 (vecdotq.cuh:211-241,
  *     1057-1076), vec_dot_q3_K_q8_1 (282-317, 1175-1198), vec_dot_q5_K_q8_1 (413-445,
- *     1467-1509), vec_dot_iq4_xs_q8_1 (2019-2040).
+ *     1467-1509), vec_dot_iq4_xs_q8_1 (2019-2040); and the reference's own Q2_0 block and
+ *     vec_dot_q2_0_q8_1 (kt_gguf_moe_multi.cu:33-64).
  *   - the q8_1 activation quantizer quantize_q8_1 (hot/kt_gguf_moe_multi/kt_gguf_moe_multi.cu:600-650),
  *     including the lane order of its 32-lane butterfly sum that produces ds.y.
  *   - the per-chunk integer dot products vec_dot_q8_0_q8_1 (vecdotq.cuh:969-982),
@@ -58,6 +59,7 @@
 #define KO_Q3_K 11
 #define KO_Q5_K 13
 #define KO_IQ4_XS 23
+#define KO_Q2_0 42
 
 /* ---------------------------------------------------------------- numbers */
 
@@ -132,6 +134,7 @@ int ko_block_info(int type, int* blck, int* bytes) {
     case KO_Q3_K: *blck = 256; *bytes = 110; return 0;
     case KO_Q5_K: *blck = 256; *bytes = 176; return 0;
     case KO_IQ4_XS: *blck = 256; *bytes = 136; return 0;
+    case KO_Q2_0: *blck = 64; *bytes = 18; return 0;
     default: return -1;
   }
 }
@@ -258,6 +261,13 @@ static void dq_iq4_xs(const uint8_t* b, float* y) {
   }
 }
 
+/* Q2_0 (kt_gguf_moe_multi.cu:33-46): fp16 d, qs[16]; element 4j+s = code s of byte j
+ * (bits 2s); value (code - 1) * d */
+static void dq_q2_0(const uint8_t* b, float* y) {
+  float d = ko_h2f(rd16(b));
+  for (int e = 0; e < 64; ++e) y[e] = (float)(((b[2 + e / 4] >> (2 * (e % 4))) & 3) - 1) * d;
+}
+
 static void dq_q6_k(const uint8_t* b, float* y) {
   const uint8_t* ql = b;
   const uint8_t* qh = b + 128;
@@ -349,6 +359,7 @@ int ko_dequant_rows(int type, const uint8_t* w, int64_t nrows, int64_t cols, flo
         case KO_Q3_K: dq_q3_k(b, y); break;
         case KO_Q5_K: dq_q5_k(b, y); break;
         case KO_IQ4_XS: dq_iq4_xs(b, y); break;
+        case KO_Q2_0: dq_q2_0(b, y); break;
         default: dq_legacy(type, b, y); break;
       }
     }
@@ -641,6 +652,22 @@ static float vd_iq4_xs(const uint8_t* bx, const uint8_t* by0, int ib32) {
   return d * (float)(sumi1 + sumi2);
 }
 
+/* vec_dot_q2_0_q8_1 (kt_gguf_moe_multi.cu:49-64): iqs 0..3, bytes 4iqs..4iqs+3 (16 values)
+ * against half iqs&1 of q8_1 block iqs/2; d * d8 * (sum(code*u) - sum(u)) */
+static float vd_q2_0(const uint8_t* bx, const uint8_t* by0, int iqs) {
+  const uint8_t* b8 = by0 + 36 * (iqs >> 1);
+  const uint8_t* u = b8 + 4 + 16 * (iqs & 1);
+  int32_t sumi = 0, sumy = 0;
+  for (int j = 0; j < 4; ++j) {
+    const int c = bx[2 + 4 * iqs + j];
+    uint32_t codes = 0;
+    for (int s = 0; s < 4; ++s) codes |= (uint32_t)((c >> (2 * s)) & 3) << (8 * s);
+    sumi = dp4a((int32_t)codes, rd32(u + 4 * j), sumi);
+    sumy = dp4a(0x01010101, rd32(u + 4 * j), sumy);
+  }
+  return ko_h2f(rd16(bx)) * q8_1_d(b8) * (float)(sumi - sumy);
+}
+
 /* chunk geometry of the reference launchers: values per block, chunks per block, vdr */
 static int chunk_geom(int type, int* qk, int* cpb, int* vdr) {
   switch (type) {
@@ -651,6 +678,7 @@ static int chunk_geom(int type, int* qk, int* cpb, int* vdr) {
     case KO_Q2_K: case KO_Q3_K: *qk = 256; *cpb = 16; *vdr = 1; return 0; /* qi 16, vdr 1 */
     case KO_Q5_K: *qk = 256; *cpb = 16; *vdr = 2; return 0; /* qi 32, vdr 2 */
     case KO_IQ4_XS: *qk = 256; *cpb = 8; *vdr = 1; return 0; /* qi 8, vdr 1 */
+    case KO_Q2_0: *qk = 64; *cpb = 4; *vdr = 1; return 0;   /* qi 4, vdr 1 */
     case KO_Q4_0: case KO_Q4_1: case KO_Q5_0: case KO_Q5_1: case KO_IQ4_NL:
       *qk = 32; *cpb = 2; *vdr = 2; return 0;               /* qi 4, vdr 2 */
     default: return -1;
@@ -678,6 +706,7 @@ static float row_dot(int type, const uint8_t* wrow, int bs, int nblocks, const u
       case KO_Q3_K: v = vd_q3_k(bx, by, iqs); break;
       case KO_Q5_K: v = vd_q5_k(bx, by, iqs); break;
       case KO_IQ4_XS: v = vd_iq4_xs(bx, by, iqs); break;
+      case KO_Q2_0: v = vd_q2_0(bx, by, iqs); break;
       default: v = vd_legacy(type, bx, by, iqs); break;
     }
     lane[c % 32] += v;

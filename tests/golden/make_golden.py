@@ -10,7 +10,9 @@ implementation independent of this repository. For each type the file holds
                            rows 24-47 random bytes with finite scales (every code pattern)
   <type>_values  float32: gguf-py's dequantization of those rows
 and for Q2_K, Q3_K, Q5_K and IQ4_XS, which gguf-py does not encode, 48 rows of random blocks
-with finite scales and their dequantization,
+with finite scales and their dequantization; for the reference's own Q2_0 (ggml type 42,
+unknown to gguf-py) 24 encoded and 24 random rows with values (code - 1) * d computed here
+in numpy from the block's definition (kt_gguf_moe_multi.cu:33-46 of the reference),
 plus the IQ3_S codebook as uint32 words and the IQ4_NL levels.
 
 Run from the repository root: python tests/golden/make_golden.py
@@ -53,6 +55,13 @@ def main():
         blocks = synth.random_blocks(rng, t, 48, 512)
         out[f"{t}_blocks"] = blocks
         out[f"{t}_values"] = dequantize(blocks, qt).reshape(48, 512).astype(np.float32)
+    enc = synth.quantize(rng.standard_normal((24, 512), dtype=np.float32) * 0.02, 42)
+    blocks = np.concatenate([enc, synth.random_blocks(rng, 42, 24, 512)])
+    b = blocks.reshape(48, 8, 18)
+    d = b[:, :, :2].copy().view(np.float16).astype(np.float32)  # [48, 8, 1]
+    codes = ((b[:, :, 2:, None] >> np.array([0, 2, 4, 6], dtype=np.uint8)) & 3).reshape(48, 8, 64)
+    out["42_blocks"] = blocks
+    out["42_values"] = ((codes.astype(np.float32) - 1) * d).reshape(48, 512)
     out["iq4nl_levels"] = np.array(IQ4_NL.kvalues, dtype=np.int8)
     IQ3_S.init_grid()
     g = IQ3_S.grid.reshape(512, 4).astype(np.uint32)

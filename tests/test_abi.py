@@ -63,9 +63,9 @@ def test_argument_errors_before_any_launch():
                               None) == N.KT_ERR_ARG
     assert lib.kt_moe_prefill(P(16), 16, 2048, 512, P(16), P(16), 8, P(16), 12, P(16), 99, 0, 64, P(16), P(16), 1 << 40,
                               None) == N.KT_ERR_TYPE
-    # the 32-value legacy blocks and Q2_K / Q3_K / Q5_K / IQ4_XS have a decode GEMV but no
+    # the 32-value legacy blocks, Q2_K / Q3_K / Q5_K / IQ4_XS and Q2_0 have a decode GEMV but no
     # prefill GEMM
-    for t in (2, 10, 11, 13, 23):
+    for t in (2, 10, 11, 13, 23, 42):
         assert lib.kt_moe_prefill(P(16), 16, 2048, 512, P(16), P(16), 8, P(16), t, P(16), 14, 0, 64, P(16), P(16),
                                   1 << 40, None) == N.KT_ERR_TYPE
     rb = ctypes.c_int64()

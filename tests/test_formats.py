@@ -10,7 +10,7 @@ from oracle import oracle as O
 GOLDEN = np.load(Path(__file__).with_name("golden") / "gguf_dequant.npz")
 TYPES = (8, 12, 14, 21)
 # the GEMV's wider type switch: 32-value blocks and the K-quants Q2_K / Q3_K / Q5_K / IQ4_XS
-LEGACY = (2, 3, 6, 7, 20, 10, 11, 13, 23)
+LEGACY = (2, 3, 6, 7, 20, 10, 11, 13, 23, 42)  # and the reference's Q2_0
 REF_COMMON = Path("/root/reference/hot/kt_gguf_moe_multi/ggml-common.h")
 
 
@@ -18,7 +18,7 @@ def test_block_sizes_known_answers():
     # hot/kt_gguf_hot.py:76-80 BLOCK_INFO for the hot-path types
     assert O.BLOCK == {8: (32, 34), 12: (256, 144), 14: (256, 210), 21: (256, 110),
                        2: (32, 18), 3: (32, 20), 6: (32, 22), 7: (32, 24), 20: (32, 18),
-                       10: (256, 84), 11: (256, 110), 13: (256, 176), 23: (256, 136)}
+                       10: (256, 84), 11: (256, 110), 13: (256, 176), 23: (256, 136), 42: (64, 18)}
     from kt_gguf_b200 import synth
 
     assert synth.BLOCK == O.BLOCK

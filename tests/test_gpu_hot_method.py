@@ -94,6 +94,35 @@ def test_hot_method_decode_window(cuda_device, tokens):
     assert err <= TOL_REF_LAYER, err
 
 
+@pytest.mark.parametrize("tokens", [4, 384])
+def test_hot_method_q2_0_native_down(cuda_device, monkeypatch, tokens):
+    # hot/kt_gguf_hot.py:21-25, 180-190: a Q2_0 down stays 2-bit and the layer runs the GEMV at
+    # every length (a prefill-sized chunk included)
+    monkeypatch.setenv("KT_GGUF_Q2_NATIVE", "1")
+    L = synth.make_layer(9, tokens, 2048, 512, 32, 8, 12, 42, n_hot=16, zipf=1.1)
+    m, layer = build_method(L, f"fake://q2native{tokens}")
+    assert m.type2 == 42 and not m._use_prefill(L.x, tokens)
+    assert torch.equal(layer.w2_qweight.cpu(), torch.from_numpy(L.w2))
+    out = apply(m, layer, L, cuda_device)
+    x16 = L.x.view(torch.int16).numpy().view(np.uint16)
+    ref = O.bf16_to_f32(O.moe_ref_bf16(x16, L.topk_ids.numpy(), L.topk_weights.numpy(), 12, L.w13, 42, L.w2, L.inter))
+    err = O.rel_l2(out.float().cpu().numpy(), ref)
+    assert err <= TOL_REF_LAYER, err
+
+
+def test_hot_method_q2_0_repacked_down_prefill(cuda_device, monkeypatch):
+    # KT_GGUF_Q2_NATIVE=0: the exact Q8_0 repack, which the tcgen05 prefill layer takes
+    monkeypatch.setenv("KT_GGUF_Q2_NATIVE", "0")
+    L = synth.make_layer(9, 384, 2048, 512, 32, 8, 12, 42, n_hot=16, zipf=1.1)
+    m, layer = build_method(L, "fake://q2repack")
+    assert m.type2 == 8 and m._use_prefill(L.x, 384)
+    out = apply(m, layer, L, cuda_device)
+    want = O.moe_fp32(L.x.view(torch.int16).numpy().view(np.uint16), L.topk_ids.numpy(), L.topk_weights.numpy(),
+                      12, L.w13, 42, L.w2, L.inter)  # the Q2_0 values themselves: the repack is exact
+    err = O.rel_l2(out.float().cpu().numpy(), want)
+    assert err <= TOL_FP32_ORACLE, err
+
+
 def test_hot_cache_route_on_gpu(cuda_device):
     E, NS = 64, 16
     c = C.HotCache(1, E, NS, cuda_device, 0)

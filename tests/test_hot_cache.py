@@ -161,6 +161,35 @@ def test_q2_0_repack_is_exact():
     assert np.array_equal(got, want)
 
 
+def test_q2_0_oracle_dequant_equals_the_q8_0_repack():
+    # the Q2_0 decoder of the oracle against an independent route: the exact Q8_0 repack,
+    # decoded by the Q8_0 path that gguf-py's golden vectors pin
+    rng = np.random.default_rng(5)
+    from kt_gguf_b200 import synth
+
+    w = synth.random_blocks(rng, 42, 6, 1024)
+    q8 = H.q2_0_to_q8_0(torch.from_numpy(w)).numpy()
+    a, b = O.dequant(42, w, 1024), O.dequant(8, q8, 1024)
+    assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
+
+
+@pytest.mark.parametrize("native,type2", [("1", 42), ("0", 8), (None, 42)])
+def test_q2_0_downs_native_or_repacked(monkeypatch, native, type2):
+    # hot/kt_gguf_hot.py:180-190: Q2_0 downs stay 2-bit unless KT_GGUF_Q2_NATIVE=0
+    if native is None:
+        monkeypatch.delenv("KT_GGUF_Q2_NATIVE", raising=False)
+    else:
+        monkeypatch.setenv("KT_GGUF_Q2_NATIVE", native)
+    H._readers["fake://q2"] = SimpleNamespace(types=lambda li: (12, 12, 42))
+    kt = SimpleNamespace(num_gpu_experts=4, weight_path="fake://q2", layer_idx=0)
+    m = H.KTGGUFHotExpertsMethod(kt, SimpleNamespace(moe_tp_rank=0, moe_tp_size=1))
+    assert (m.type13, m.type2, m.q2_native) == (12, type2, native != "0")
+    m.K, m.N = 2048, 512
+    x = torch.zeros((4096, 2048), dtype=torch.bfloat16)
+    # the prefill layer takes the four north-star types: a native Q2_0 layer stays on the GEMV
+    assert m._use_prefill(x, 4096) == (type2 == 8 and H.PREFILL_ON_GPU)
+
+
 def test_row_bytes_and_block_table():
     assert H._row_bytes(2048, 12) == 8 * 144 and H._row_bytes(512, 14) == 420 and H._row_bytes(512, 21) == 220
     with pytest.raises(ValueError):

@@ -19,7 +19,7 @@ def q8_1_dequant(qx: np.ndarray, cols: int) -> np.ndarray:
 
 @pytest.mark.parametrize("qtype,cols,rows", [(8, 2048, 96), (8, 768, 40), (12, 2048, 64), (14, 512, 64),
                                              (21, 2048, 48), (21, 512, 40), (10, 2048, 40), (11, 512, 40),
-                                             (13, 2048, 40), (23, 2048, 40)])
+                                             (13, 2048, 40), (23, 2048, 40), (42, 2048, 40), (42, 512, 40)])
 def test_gemv_integer_path_equals_dequant_matmul(qtype, cols, rows):
     rng = np.random.default_rng(qtype * 1000 + cols)
     x = rng.standard_normal((5, cols), dtype=np.float32)
