@@ -67,6 +67,31 @@ template <>
 struct KtChunk<KT_Q2_0> {
   static constexpr int QK = 64, BYTES = 18, CPB = 4, VDR = 1;
 };
+// the i-quants with a code book: one 32-value sub-block per chunk (QI 8, VDR 1)
+template <>
+struct KtChunk<KT_IQ2_XXS> {
+  static constexpr int QK = 256, BYTES = 66, CPB = 8, VDR = 1;
+};
+template <>
+struct KtChunk<KT_IQ2_XS> {
+  static constexpr int QK = 256, BYTES = 74, CPB = 8, VDR = 1;
+};
+template <>
+struct KtChunk<KT_IQ2_S> {
+  static constexpr int QK = 256, BYTES = 82, CPB = 8, VDR = 1;
+};
+template <>
+struct KtChunk<KT_IQ3_XXS> {
+  static constexpr int QK = 256, BYTES = 98, CPB = 8, VDR = 1;
+};
+template <>
+struct KtChunk<KT_IQ1_S> {
+  static constexpr int QK = 256, BYTES = 50, CPB = 8, VDR = 1;
+};
+template <>
+struct KtChunk<KT_IQ1_M> {
+  static constexpr int QK = 256, BYTES = 56, CPB = 8, VDR = 1;
+};
 template <>
 struct KtChunk<KT_Q6_K> {
   static constexpr int QK = 256, BYTES = 210, CPB = 32, VDR = 1;
@@ -346,6 +371,153 @@ __device__ __forceinline__ float kt_vd_q2_0(const uint8_t* bx, const uint8_t* yq
   return kt_h2f(*reinterpret_cast<const uint16_t*>(bx)) * kt_q8_1_dd(yd + 4 * (iqs >> 1)) * (float)(sumi - sumy);
 }
 
+// ---- i-quants with a code book (grid: the type's book staged in shared memory)
+
+// 7 stored sign bits + the parity bit that makes the count of minus signs even (ggml's
+// ksigns_iq2xs table, computed)
+__device__ __forceinline__ uint32_t kt_signs8(uint32_t s7) { return s7 | ((__popc(s7) & 1u) << 7); }
+// four magnitudes (one per byte) with the signs of bits 0..3 of s4 applied
+__device__ __forceinline__ int kt_signed4(uint32_t mag, uint32_t s4) {
+  const uint32_t m = __vcmpne4((s4 * 0x01010101u) & 0x08040201u, 0u);  // 0xff where negative
+  return (int)__vsub4(mag ^ m, m);
+}
+
+// IQ2_XXS (d, qs[32] u16): sub-block ib32 = 4 grid bytes + a word of 4x7 sign bits and a
+// 4-bit scale: d * (0.5 + s) * d8 / 4 * sum(+-grid * u)
+__device__ __forceinline__ float kt_vd_iq2_xxs(const uint8_t* bx, const uint8_t* yq, const uint8_t* yd, int ib32,
+                                               const uint32_t* grid) {
+  const uint8_t* q2 = bx + 2 + 8 * ib32;
+  const uint8_t* q8 = yq + 32 * ib32;
+  const uint32_t aux32 = (uint32_t)kt_ld_b2(q2 + 4);
+  int sumi = 0;
+#pragma unroll
+  for (int l = 0; l < 4; ++l) {
+    const uint32_t* g = grid + 2 * q2[l];
+    const uint32_t s = kt_signs8((aux32 >> (7 * l)) & 127u);
+    sumi = __dp4a(kt_signed4(g[0], s & 15u), kt_ld_b4(q8 + 8 * l), sumi);
+    sumi = __dp4a(kt_signed4(g[1], s >> 4), kt_ld_b4(q8 + 8 * l + 4), sumi);
+  }
+  const float d = kt_h2f(*reinterpret_cast<const uint16_t*>(bx)) * (0.5f + (aux32 >> 28)) * kt_q8_1_dd(yd + 4 * ib32) *
+                  0.25f;
+  return d * sumi;
+}
+
+// IQ2_XS (d, qs[32] u16: 9-bit grid index | 7 sign bits << 9, scales[8] two 4-bit scales)
+__device__ __forceinline__ float kt_vd_iq2_xs(const uint8_t* bx, const uint8_t* yq, const uint8_t* yd, int ib32,
+                                              const uint32_t* grid) {
+  const uint8_t* q2 = bx + 2 + 8 * ib32;
+  const uint8_t* q8 = yq + 32 * ib32;
+  const uint8_t ls1 = bx[66 + ib32] & 0xf, ls2 = bx[66 + ib32] >> 4;
+  int sumi1 = 0, sumi2 = 0;
+#pragma unroll
+  for (int l = 0; l < 4; ++l) {
+    const uint32_t code = q2[2 * l] | (q2[2 * l + 1] << 8);
+    const uint32_t* g = grid + 2 * (code & 511u);
+    const uint32_t s = kt_signs8(code >> 9);
+    int& sumi = l < 2 ? sumi1 : sumi2;
+    sumi = __dp4a(kt_signed4(g[0], s & 15u), kt_ld_b4(q8 + 8 * l), sumi);
+    sumi = __dp4a(kt_signed4(g[1], s >> 4), kt_ld_b4(q8 + 8 * l + 4), sumi);
+  }
+  const float d = kt_h2f(*reinterpret_cast<const uint16_t*>(bx)) * kt_q8_1_dd(yd + 4 * ib32) * 0.25f;
+  return d * ((0.5f + ls1) * sumi1 + (0.5f + ls2) * sumi2);
+}
+
+// IQ2_S (d, qs[32] grid low bits, signs[32], qh[8] 2 high bits per group, scales[8])
+__device__ __forceinline__ float kt_vd_iq2_s(const uint8_t* bx, const uint8_t* yq, const uint8_t* yd, int ib32,
+                                             const uint32_t* grid) {
+  const uint8_t* qs = bx + 2 + 4 * ib32;
+  const uint8_t* signs = bx + 34 + 4 * ib32;
+  const uint8_t* q8 = yq + 32 * ib32;
+  const int qh = bx[66 + ib32];
+  const uint8_t ls1 = bx[74 + ib32] & 0xf, ls2 = bx[74 + ib32] >> 4;
+  int sumi1 = 0, sumi2 = 0;
+#pragma unroll
+  for (int l = 0; l < 4; ++l) {
+    const uint32_t* g = grid + 2 * (qs[l] | ((qh << (8 - 2 * l)) & 0x300));
+    const uint32_t s = signs[l];
+    int& sumi = l < 2 ? sumi1 : sumi2;
+    sumi = __dp4a(kt_signed4(g[0], s & 15u), kt_ld_b4(q8 + 8 * l), sumi);
+    sumi = __dp4a(kt_signed4(g[1], s >> 4), kt_ld_b4(q8 + 8 * l + 4), sumi);
+  }
+  const float d = kt_h2f(*reinterpret_cast<const uint16_t*>(bx)) * kt_q8_1_dd(yd + 4 * ib32) * 0.25f;
+  return d * ((0.5f + ls1) * sumi1 + (0.5f + ls2) * sumi2);
+}
+
+// IQ3_XXS (d, qs[64] grid indices, 8 words of 4x7 sign bits | 4-bit scale << 28)
+__device__ __forceinline__ float kt_vd_iq3_xxs(const uint8_t* bx, const uint8_t* yq, const uint8_t* yd, int ib32,
+                                               const uint32_t* grid) {
+  const uint8_t* q3 = bx + 2 + 8 * ib32;
+  const uint8_t* q8 = yq + 32 * ib32;
+  const uint32_t aux32 = (uint32_t)kt_ld_b2(bx + 66 + 4 * ib32);
+  int sumi = 0;
+#pragma unroll
+  for (int l = 0; l < 4; ++l) {
+    const uint32_t s = kt_signs8((aux32 >> (7 * l)) & 127u);
+    sumi = __dp4a(kt_signed4(grid[q3[2 * l]], s & 15u), kt_ld_b4(q8 + 8 * l), sumi);
+    sumi = __dp4a(kt_signed4(grid[q3[2 * l + 1]], s >> 4), kt_ld_b4(q8 + 8 * l + 4), sumi);
+  }
+  const float d = kt_h2f(*reinterpret_cast<const uint16_t*>(bx)) * (0.5f + (aux32 >> 28)) * kt_q8_1_dd(yd + 4 * ib32) *
+                  0.5f;
+  return d * sumi;
+}
+
+// IQ1 delta: values are grid + delta, delta = +-1/8 by a sign bit
+#define KT_IQ1_DELTA 0.125f
+
+// IQ1_S (d, qs[32], qh[8] u16: 3 high index bits per group, 3-bit scale, delta sign). The
+// book holds v + 1 in nibbles, so sum(v*u) = sum((v+1)*u) - sum(u): the q8_1 block's s
+// (sum of the unquantized activations) times delta - 1 stands for the -sum(u) + delta*sum(u)
+__device__ __forceinline__ float kt_vd_iq1_s(const uint8_t* bx, const uint8_t* yq, const uint8_t* yd, int ib32,
+                                             const uint32_t* grid) {
+  const uint8_t* qs = bx + 2 + 4 * ib32;
+  const uint8_t* q8 = yq + 32 * ib32;
+  const int qh = bx[34 + 2 * ib32] | (bx[35 + 2 * ib32] << 8);
+  int sumi = 0;
+#pragma unroll
+  for (int l = 0; l < 4; ++l) {
+    const uint32_t w = grid[qs[l] | (((qh >> (3 * l)) & 7) << 8)];
+    sumi = __dp4a((int)(w & 0x0F0F0F0Fu), kt_ld_b4(q8 + 8 * l), sumi);
+    sumi = __dp4a((int)((w >> 4) & 0x0F0F0F0Fu), kt_ld_b4(q8 + 8 * l + 4), sumi);
+  }
+  const float d1q = kt_h2f(*reinterpret_cast<const uint16_t*>(bx)) * (((qh >> 11) & 0x0E) + 1);
+  const float delta = -1.0f + KT_IQ1_DELTA - (qh & 0x8000) * (2.0f * KT_IQ1_DELTA / 0x8000);
+  const float2 ds = __half22float2(*reinterpret_cast<const half2*>(yd + 4 * ib32));
+  return d1q * (ds.x * sumi + ds.y * delta);
+}
+
+// IQ1_M (qs[32], qh[16]: per group 3 high index bits + delta sign, scales[8]: 3-bit scales
+// per 16 values, and the fp16 d spread over the top nibbles of the four scale words)
+__device__ __forceinline__ float kt_vd_iq1_m(const uint8_t* bx, const uint8_t* yq, const uint8_t* yd, int ib32,
+                                             const uint32_t* grid) {
+  const uint8_t* qs = bx + 4 * ib32;
+  const uint8_t* q8 = yq + 32 * ib32;
+  int sumi[2] = {0, 0};
+  float sumf[2] = {0.0f, 0.0f};
+#pragma unroll
+  for (int l = 0; l < 4; ++l) {
+    const int qhl = bx[32 + 2 * ib32 + l / 2] >> (4 * (l % 2));
+    const uint32_t w = grid[qs[l] | ((qhl & 7) << 8)];
+    const int u0 = kt_ld_b4(q8 + 8 * l), u1 = kt_ld_b4(q8 + 8 * l + 4);
+    sumi[l / 2] = __dp4a((int)(w & 0x0F0F0F0Fu), u0, sumi[l / 2]);
+    sumi[l / 2] = __dp4a((int)((w >> 4) & 0x0F0F0F0Fu), u1, sumi[l / 2]);
+    const float delta = -1.0f + KT_IQ1_DELTA - (qhl & 0x08) * (2.0f * KT_IQ1_DELTA / 0x08);
+    int sumy = 0;
+    sumy = __dp4a(u0, 0x01010101, sumy);
+    sumy = __dp4a(u1, 0x01010101, sumy);
+    sumf[l / 2] += delta * sumy;
+  }
+  const uint8_t* s8 = bx + 48;
+  uint16_t sc[4];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) sc[k] = (uint16_t)(s8[2 * k] | (s8[2 * k + 1] << 8));
+  const uint16_t dbits = (sc[0] >> 12) | ((sc[1] >> 8) & 0x00F0) | ((sc[2] >> 4) & 0x0F00) | (sc[3] & 0xF000);
+  const float d = kt_h2f(dbits) * kt_q8_1_dd(yd + 4 * ib32);
+  const int tmp = sc[ib32 / 2] >> (6 * (ib32 % 2));
+  const int sc0 = 2 * ((tmp >> 0) & 0x07) + 1;
+  const int sc1 = 2 * ((tmp >> 3) & 0x07) + 1;
+  return d * ((sumi[0] + sumf[0]) * sc0 + (sumi[1] + sumf[1]) * sc1);
+}
+
 // ---- Q6_K: 8 values; iqs in 0..31. The reference's per-byte (code - 32) with __vsubss4
 // never saturates (codes are 0..63), so the integer dot is dp4a(code, u) - 32 * sum(u),
 // computed here with two dp4a instead of the emulated SIMD subtract.
@@ -422,6 +594,12 @@ __device__ __forceinline__ float kt_vec_dot(const uint8_t* bx, const uint8_t* yq
   if constexpr (TYPE == KT_Q5_K) return kt_vd_q5_k(bx, yq, yd, iqs);
   if constexpr (TYPE == KT_IQ4_XS) return kt_vd_iq4_xs(bx, yq, yd, iqs);
   if constexpr (TYPE == KT_Q2_0) return kt_vd_q2_0(bx, yq, yd, iqs);
+  if constexpr (TYPE == KT_IQ2_XXS) return kt_vd_iq2_xxs(bx, yq, yd, iqs, grid);
+  if constexpr (TYPE == KT_IQ2_XS) return kt_vd_iq2_xs(bx, yq, yd, iqs, grid);
+  if constexpr (TYPE == KT_IQ2_S) return kt_vd_iq2_s(bx, yq, yd, iqs, grid);
+  if constexpr (TYPE == KT_IQ3_XXS) return kt_vd_iq3_xxs(bx, yq, yd, iqs, grid);
+  if constexpr (TYPE == KT_IQ1_S) return kt_vd_iq1_s(bx, yq, yd, iqs, grid);
+  if constexpr (TYPE == KT_IQ1_M) return kt_vd_iq1_m(bx, yq, yd, iqs, grid);
   if constexpr (TYPE == KT_Q4_K) return kt_vd_q4_k(bx, yq, yd, iqs);
   if constexpr (TYPE == KT_Q6_K) return kt_vd_q6_k(bx, yq, yd, iqs);
   if constexpr (TYPE == KT_IQ3_S) return kt_vd_iq3_s(bx, yq, yd, iqs, grid);
@@ -583,6 +761,93 @@ __device__ __forceinline__ void kt_dq32_iq4_xs(const uint8_t* b, int sub, float*
   }
 }
 
+// i-quant sub-block sub (32 values), gguf-py's / ggml's order: db = d * (0.5 + s) * 1/4 (1/2
+// for IQ3_XXS), value = (db * grid) with the sign applied; IQ1: dl * (v + delta)
+__device__ __forceinline__ float kt_signed_mul(float db, uint32_t mag, uint32_t neg) {
+  const float v = __fmul_rn(db, (float)mag);
+  return neg ? -v : v;
+}
+__device__ __forceinline__ float kt_iq_db(float d, int s, float quarter_or_half) {
+  return __fmul_rn(__fmul_rn(d, __fadd_rn(0.5f, (float)s)), quarter_or_half);
+}
+// 8 values from two book words (IQ2 families): element j = byte j%4 of word j/4
+__device__ __forceinline__ void kt_dq8_iq2(float db, const uint32_t* g, uint32_t s8, float* y) {
+#pragma unroll
+  for (int j = 0; j < 8; ++j) y[j] = kt_signed_mul(db, (g[j / 4] >> (8 * (j % 4))) & 0xffu, (s8 >> j) & 1u);
+}
+__device__ __forceinline__ void kt_dq32_iq2_xxs(const uint8_t* b, int sub, float* y, const uint32_t* grid) {
+  const float d = kt_h2f(b[0] | (b[1] << 8));
+  const uint8_t* q2 = b + 2 + 8 * sub;
+  const uint32_t aux32 = (uint32_t)(q2[4] | (q2[5] << 8) | (q2[6] << 16)) | ((uint32_t)q2[7] << 24);
+  const float db = kt_iq_db(d, (int)(aux32 >> 28), 0.25f);
+#pragma unroll
+  for (int l = 0; l < 4; ++l) kt_dq8_iq2(db, grid + 2 * q2[l], kt_signs8((aux32 >> (7 * l)) & 127u), y + 8 * l);
+}
+__device__ __forceinline__ void kt_dq32_iq2_xs(const uint8_t* b, int sub, float* y, const uint32_t* grid) {
+  const float d = kt_h2f(b[0] | (b[1] << 8));
+  const uint8_t* q2 = b + 2 + 8 * sub;
+  const float db0 = kt_iq_db(d, b[66 + sub] & 0xf, 0.25f), db1 = kt_iq_db(d, b[66 + sub] >> 4, 0.25f);
+#pragma unroll
+  for (int l = 0; l < 4; ++l) {
+    const uint32_t code = q2[2 * l] | (q2[2 * l + 1] << 8);
+    kt_dq8_iq2(l < 2 ? db0 : db1, grid + 2 * (code & 511u), kt_signs8(code >> 9), y + 8 * l);
+  }
+}
+__device__ __forceinline__ void kt_dq32_iq2_s(const uint8_t* b, int sub, float* y, const uint32_t* grid) {
+  const float d = kt_h2f(b[0] | (b[1] << 8));
+  const float db0 = kt_iq_db(d, b[74 + sub] & 0xf, 0.25f), db1 = kt_iq_db(d, b[74 + sub] >> 4, 0.25f);
+  const int qh = b[66 + sub];
+#pragma unroll
+  for (int l = 0; l < 4; ++l) {
+    const int idx = b[2 + 4 * sub + l] | ((qh << (8 - 2 * l)) & 0x300);
+    kt_dq8_iq2(l < 2 ? db0 : db1, grid + 2 * idx, b[34 + 4 * sub + l], y + 8 * l);
+  }
+}
+__device__ __forceinline__ void kt_dq32_iq3_xxs(const uint8_t* b, int sub, float* y, const uint32_t* grid) {
+  const float d = kt_h2f(b[0] | (b[1] << 8));
+  const uint8_t* q3 = b + 2 + 8 * sub;
+  const uint8_t* a = b + 66 + 4 * sub;
+  const uint32_t aux32 = (uint32_t)(a[0] | (a[1] << 8) | (a[2] << 16)) | ((uint32_t)a[3] << 24);
+  const float db = kt_iq_db(d, (int)(aux32 >> 28), 0.5f);
+#pragma unroll
+  for (int l = 0; l < 4; ++l) {
+    const uint32_t s8 = kt_signs8((aux32 >> (7 * l)) & 127u);
+    const uint32_t g[2] = {grid[q3[2 * l]], grid[q3[2 * l + 1]]};
+    kt_dq8_iq2(db, g, s8, y + 8 * l);
+  }
+}
+// 8 values v + delta (v from the nibble book: element j<4 low nibble of byte j, j>=4 high
+// nibble of byte j-4, stored as v + 1)
+__device__ __forceinline__ void kt_dq8_iq1(float dl, uint32_t w, float delta, float* y) {
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const int v = (int)((w >> (8 * (j % 4) + 4 * (j / 4))) & 0xfu) - 1;
+    y[j] = __fmul_rn(dl, __fadd_rn((float)v, delta));
+  }
+}
+__device__ __forceinline__ void kt_dq32_iq1_s(const uint8_t* b, int sub, float* y, const uint32_t* grid) {
+  const float d = kt_h2f(b[0] | (b[1] << 8));
+  const int qh = b[34 + 2 * sub] | (b[35 + 2 * sub] << 8);
+  const float dl = __fmul_rn(d, (float)(2 * ((qh >> 12) & 7) + 1));
+  const float delta = (qh & 0x8000) ? -KT_IQ1_DELTA : KT_IQ1_DELTA;
+#pragma unroll
+  for (int l = 0; l < 4; ++l) kt_dq8_iq1(dl, grid[b[2 + 4 * sub + l] | (((qh >> (3 * l)) & 7) << 8)], delta, y + 8 * l);
+}
+__device__ __forceinline__ void kt_dq32_iq1_m(const uint8_t* b, int sub, float* y, const uint32_t* grid) {
+  uint16_t sc[4];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) sc[k] = (uint16_t)(b[48 + 2 * k] | (b[49 + 2 * k] << 8));
+  const float d = kt_h2f((sc[0] >> 12) | ((sc[1] >> 8) & 0x00F0) | ((sc[2] >> 4) & 0x0F00) | (sc[3] & 0xF000));
+  const int tmp = sc[sub / 2] >> (6 * (sub % 2));
+  const float dl0 = __fmul_rn(d, (float)(2 * (tmp & 7) + 1)), dl1 = __fmul_rn(d, (float)(2 * ((tmp >> 3) & 7) + 1));
+#pragma unroll
+  for (int l = 0; l < 4; ++l) {
+    const int qhl = b[32 + 2 * sub + l / 2] >> (4 * (l % 2));
+    kt_dq8_iq1(l < 2 ? dl0 : dl1, grid[b[4 * sub + l] | ((qhl & 7) << 8)], (qhl & 8) ? -KT_IQ1_DELTA : KT_IQ1_DELTA,
+               y + 8 * l);
+  }
+}
+
 // 32 consecutive values starting at element 32*sub32 of a row made of blocks of TYPE
 template <int TYPE>
 __device__ __forceinline__ void kt_dq32(const uint8_t* row, int sub32, float* y, const uint32_t* grid) {
@@ -606,5 +871,11 @@ __device__ __forceinline__ void kt_dq32(const uint8_t* row, int sub32, float* y,
     if constexpr (TYPE == KT_Q3_K) kt_dq32_q3_k(b, sub32 % 8, y);
     if constexpr (TYPE == KT_Q5_K) kt_dq32_q5_k(b, sub32 % 8, y);
     if constexpr (TYPE == KT_IQ4_XS) kt_dq32_iq4_xs(b, sub32 % 8, y);
+    if constexpr (TYPE == KT_IQ2_XXS) kt_dq32_iq2_xxs(b, sub32 % 8, y, grid);
+    if constexpr (TYPE == KT_IQ2_XS) kt_dq32_iq2_xs(b, sub32 % 8, y, grid);
+    if constexpr (TYPE == KT_IQ2_S) kt_dq32_iq2_s(b, sub32 % 8, y, grid);
+    if constexpr (TYPE == KT_IQ3_XXS) kt_dq32_iq3_xxs(b, sub32 % 8, y, grid);
+    if constexpr (TYPE == KT_IQ1_S) kt_dq32_iq1_s(b, sub32 % 8, y, grid);
+    if constexpr (TYPE == KT_IQ1_M) kt_dq32_iq1_m(b, sub32 % 8, y, grid);
   }
 }

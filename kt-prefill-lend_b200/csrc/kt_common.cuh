@@ -13,9 +13,16 @@
 #include <stdint.h>
 
 #include "iq3s_grid.h"
+#include "iquant_grids.h"
 
-// the IQ3_S codebook in global memory; kernels copy it to shared memory before use
+// the i-quant code books in global memory; kernels copy their type's book to shared memory
+// before use (kt_stage_grid)
 static __device__ const uint32_t kt_iq3s_grid_dev[512] = KT_IQ3S_GRID_INIT;
+static __device__ const uint32_t kt_iq2xxs_grid_dev[KT_IQ2XXS_GRID_WORDS] = KT_IQ2XXS_GRID_INIT;
+static __device__ const uint32_t kt_iq2xs_grid_dev[KT_IQ2XS_GRID_WORDS] = KT_IQ2XS_GRID_INIT;
+static __device__ const uint32_t kt_iq2s_grid_dev[KT_IQ2S_GRID_WORDS] = KT_IQ2S_GRID_INIT;
+static __device__ const uint32_t kt_iq3xxs_grid_dev[KT_IQ3XXS_GRID_WORDS] = KT_IQ3XXS_GRID_INIT;
+static __device__ const uint32_t kt_iq1s_grid_dev[KT_IQ1S_GRID_WORDS] = KT_IQ1S_GRID_INIT;
 
 #define KT_Q4_0 2
 #define KT_Q4_1 3
@@ -30,6 +37,12 @@ static __device__ const uint32_t kt_iq3s_grid_dev[512] = KT_IQ3S_GRID_INIT;
 #define KT_IQ4_NL 20
 #define KT_IQ3_S 21
 #define KT_IQ4_XS 23
+#define KT_IQ2_XXS 16
+#define KT_IQ2_XS 17
+#define KT_IQ3_XXS 18
+#define KT_IQ1_S 19
+#define KT_IQ2_S 22
+#define KT_IQ1_M 29
 #define KT_Q2_0 42  // 64-value blocks: fp16 d, 2-bit codes, value d*(code-1)
 
 // activation / output dtype codes of the C ABI
@@ -63,6 +76,12 @@ __host__ __device__ constexpr KtBlockInfo kt_block_info(int type) {
          : type == KT_Q5_K   ? KtBlockInfo{256, 176}
          : type == KT_IQ4_XS ? KtBlockInfo{256, 136}
          : type == KT_Q2_0   ? KtBlockInfo{64, 18}
+         : type == KT_IQ2_XXS ? KtBlockInfo{256, 66}
+         : type == KT_IQ2_XS ? KtBlockInfo{256, 74}
+         : type == KT_IQ3_XXS ? KtBlockInfo{256, 98}
+         : type == KT_IQ1_S  ? KtBlockInfo{256, 50}
+         : type == KT_IQ2_S  ? KtBlockInfo{256, 82}
+         : type == KT_IQ1_M  ? KtBlockInfo{256, 56}
          : type == KT_Q4_K   ? KtBlockInfo{256, 144}
          : type == KT_Q6_K ? KtBlockInfo{256, 210}
          : type == KT_IQ3_S ? KtBlockInfo{256, 110}
@@ -106,7 +125,38 @@ __device__ __forceinline__ int kt_ld_b4(const uint8_t* p) { return *reinterpret_
 __host__ __device__ constexpr bool kt_gemv_type(int t) {
   return t == KT_Q4_0 || t == KT_Q4_1 || t == KT_Q5_0 || t == KT_Q5_1 || t == KT_Q8_0 || t == KT_IQ4_NL ||
          t == KT_Q2_K || t == KT_Q3_K || t == KT_Q4_K || t == KT_Q5_K || t == KT_Q6_K || t == KT_IQ3_S ||
-         t == KT_IQ4_XS || t == KT_Q2_0;
+         t == KT_IQ4_XS || t == KT_Q2_0 || t == KT_IQ2_XXS || t == KT_IQ2_XS || t == KT_IQ3_XXS || t == KT_IQ1_S ||
+         t == KT_IQ2_S || t == KT_IQ1_M;
+}
+// words of the code book a type's kernels stage in shared memory (0: none)
+__host__ __device__ constexpr int kt_grid_words(int t) {
+  return t == KT_IQ3_S     ? 512
+         : t == KT_IQ2_XXS ? KT_IQ2XXS_GRID_WORDS
+         : t == KT_IQ2_XS  ? KT_IQ2XS_GRID_WORDS
+         : t == KT_IQ2_S   ? KT_IQ2S_GRID_WORDS
+         : t == KT_IQ3_XXS ? KT_IQ3XXS_GRID_WORDS
+         : (t == KT_IQ1_S || t == KT_IQ1_M) ? KT_IQ1S_GRID_WORDS
+                                            : 0;
+}
+// size of a static shared array holding TYPE's code book (one word for types without one)
+template <int TYPE>
+struct KtGridSmem {
+  static constexpr int WORDS = kt_grid_words(TYPE) > 0 ? kt_grid_words(TYPE) : 1;
+};
+// copies TYPE's code book into shared memory (nothing for types without one); the caller
+// synchronises before the first read
+template <int TYPE>
+__device__ __forceinline__ void kt_stage_grid(uint32_t* dst, int tid, int nthreads) {
+  constexpr int W = kt_grid_words(TYPE);
+  if constexpr (W > 0) {
+    const uint32_t* src = TYPE == KT_IQ3_S     ? kt_iq3s_grid_dev
+                          : TYPE == KT_IQ2_XXS ? kt_iq2xxs_grid_dev
+                          : TYPE == KT_IQ2_XS  ? kt_iq2xs_grid_dev
+                          : TYPE == KT_IQ2_S   ? kt_iq2s_grid_dev
+                          : TYPE == KT_IQ3_XXS ? kt_iq3xxs_grid_dev
+                                               : kt_iq1s_grid_dev;
+    for (int i = tid; i < W; i += nthreads) dst[i] = src[i];
+  }
 }
 __host__ __device__ constexpr bool kt_prefill_type(int t) {
   return t == KT_Q8_0 || t == KT_Q4_K || t == KT_Q6_K || t == KT_IQ3_S;

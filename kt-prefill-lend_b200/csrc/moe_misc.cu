@@ -16,9 +16,9 @@
 template <int TYPE, int DT>
 __global__ void kt_dequant_kernel(const uint8_t* __restrict__ w, int64_t rows, int64_t cols, int64_t row_bytes,
                                   void* __restrict__ out) {
-  __shared__ uint32_t grid_s[512];
-  if constexpr (TYPE == KT_IQ3_S) {
-    for (int i = threadIdx.x; i < 512; i += blockDim.x) grid_s[i] = kt_iq3s_grid_dev[i];
+  __shared__ uint32_t grid_s[KtGridSmem<TYPE>::WORDS];
+  if constexpr (kt_grid_words(TYPE) > 0) {
+    kt_stage_grid<TYPE>(grid_s, threadIdx.x, blockDim.x);
     __syncthreads();
   }
   const int64_t subs = cols / 32;
@@ -62,6 +62,12 @@ int kt_launch_dequant(int type, const void* w, int64_t rows, int64_t cols, void*
     case KT_Q5_K: return dequant_t<KT_Q5_K>(w, rows, cols, out, out_dtype, s);
     case KT_IQ4_XS: return dequant_t<KT_IQ4_XS>(w, rows, cols, out, out_dtype, s);
     case KT_Q2_0: return dequant_t<KT_Q2_0>(w, rows, cols, out, out_dtype, s);
+    case KT_IQ2_XXS: return dequant_t<KT_IQ2_XXS>(w, rows, cols, out, out_dtype, s);
+    case KT_IQ2_XS: return dequant_t<KT_IQ2_XS>(w, rows, cols, out, out_dtype, s);
+    case KT_IQ2_S: return dequant_t<KT_IQ2_S>(w, rows, cols, out, out_dtype, s);
+    case KT_IQ3_XXS: return dequant_t<KT_IQ3_XXS>(w, rows, cols, out, out_dtype, s);
+    case KT_IQ1_S: return dequant_t<KT_IQ1_S>(w, rows, cols, out, out_dtype, s);
+    case KT_IQ1_M: return dequant_t<KT_IQ1_M>(w, rows, cols, out, out_dtype, s);
     case KT_Q4_K: return dequant_t<KT_Q4_K>(w, rows, cols, out, out_dtype, s);
     case KT_Q6_K: return dequant_t<KT_Q6_K>(w, rows, cols, out, out_dtype, s);
     case KT_IQ3_S: return dequant_t<KT_IQ3_S>(w, rows, cols, out, out_dtype, s);

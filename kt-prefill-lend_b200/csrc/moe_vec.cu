@@ -149,7 +149,7 @@ struct KtVecArgs {
 template <int TYPE, int DT, int LPR>
 __global__ void __launch_bounds__(256) kt_moe_vec_kernel(const KtVecArgs a) {
   extern __shared__ __align__(16) uint8_t smem[];
-  __shared__ uint32_t grid_s[512];
+  __shared__ uint32_t grid_s[KtGridSmem<TYPE>::WORDS];
   using C = KtChunk<TYPE>;
   const int g = blockIdx.y;
   const int ngroups = a.groups[0];
@@ -169,9 +169,7 @@ __global__ void __launch_bounds__(256) kt_moe_vec_kernel(const KtVecArgs a) {
     }
     return;
   }
-  if constexpr (TYPE == KT_IQ3_S) {
-    for (int i = tid; i < 512; i += blockDim.x) grid_s[i] = kt_iq3s_grid_dev[i];
-  }
+  kt_stage_grid<TYPE>(grid_s, tid, blockDim.x);
   // raw rows [r0, r0 + nr) of the slot into shared memory
   const uint8_t* wbase = a.table ? reinterpret_cast<const uint8_t*>(reinterpret_cast<const int64_t*>(a.w)[slot])
                                  : a.w + (int64_t)slot * a.rows * a.row_bytes;
@@ -284,7 +282,7 @@ constexpr int kVecStages = 4;
 template <int TYPE, int DT, int LPR>
 __global__ void __launch_bounds__(256) kt_moe_vec_pipe_kernel(const KtVecArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
-  __shared__ uint32_t grid_s[512];
+  __shared__ uint32_t grid_s[KtGridSmem<TYPE>::WORDS];
   __shared__ __align__(8) uint64_t full[kVecStages];
   using C = KtChunk<TYPE>;
   const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
@@ -294,9 +292,7 @@ __global__ void __launch_bounds__(256) kt_moe_vec_pipe_kernel(const KtVecArgs a)
     for (int i = 0; i < kVecStages; ++i) kt_mbar_init(&full[i], 1);
     kt_fence_mbar_init();
   }
-  if constexpr (TYPE == KT_IQ3_S) {
-    for (int i = tid; i < 512; i += blockDim.x) grid_s[i] = kt_iq3s_grid_dev[i];
-  }
+  kt_stage_grid<TYPE>(grid_s, tid, blockDim.x);
   __syncthreads();
   // stage the raw rows of the CTA's j-th item
   auto issue = [&](int j) {
@@ -464,7 +460,7 @@ int kt_launch_moe_vec(int type, const void* w, int table, const void* qx, int64_
   a.members_per_pass = mpp;
   a.y = y;
   const size_t smem = (size_t)(wt_bytes + mpp * qrow);
-  if (smem > 220 * 1024) return -2;
+  if (smem + 4 * (size_t)kt_grid_words(type) > 222 * 1024) return -2;  // + the static code book
   const int chunks_per_block = type == KT_Q8_0     ? KtChunk<KT_Q8_0>::CPB
                                : type == KT_Q4_K   ? KtChunk<KT_Q4_K>::CPB
                                : type == KT_Q6_K   ? KtChunk<KT_Q6_K>::CPB
@@ -474,6 +470,7 @@ int kt_launch_moe_vec(int type, const void* w, int table, const void* qx, int64_
                                : type == KT_Q5_K   ? KtChunk<KT_Q5_K>::CPB
                                : type == KT_IQ4_XS ? KtChunk<KT_IQ4_XS>::CPB
                                : type == KT_Q2_0   ? KtChunk<KT_Q2_0>::CPB
+                               : kt_grid_words(type) > 0 ? 8  // the i-quants: one sub-block a chunk
                                                    : KtChunk<KT_Q4_0>::CPB;  // the 32-value legacy blocks
   const int nchunks = cols / bi.qk * chunks_per_block;
   const int lpr = nchunks <= 16 ? 16 : 32;
@@ -489,6 +486,12 @@ int kt_launch_moe_vec(int type, const void* w, int table, const void* qx, int64_
     case KT_Q5_K: return launch_vec_dt<KT_Q5_K>(a, dtype, max_groups, lpr, smem, s);
     case KT_IQ4_XS: return launch_vec_dt<KT_IQ4_XS>(a, dtype, max_groups, lpr, smem, s);
     case KT_Q2_0: return launch_vec_dt<KT_Q2_0>(a, dtype, max_groups, lpr, smem, s);
+    case KT_IQ2_XXS: return launch_vec_dt<KT_IQ2_XXS>(a, dtype, max_groups, lpr, smem, s);
+    case KT_IQ2_XS: return launch_vec_dt<KT_IQ2_XS>(a, dtype, max_groups, lpr, smem, s);
+    case KT_IQ2_S: return launch_vec_dt<KT_IQ2_S>(a, dtype, max_groups, lpr, smem, s);
+    case KT_IQ3_XXS: return launch_vec_dt<KT_IQ3_XXS>(a, dtype, max_groups, lpr, smem, s);
+    case KT_IQ1_S: return launch_vec_dt<KT_IQ1_S>(a, dtype, max_groups, lpr, smem, s);
+    case KT_IQ1_M: return launch_vec_dt<KT_IQ1_M>(a, dtype, max_groups, lpr, smem, s);
     case KT_Q4_K: return launch_vec_dt<KT_Q4_K>(a, dtype, max_groups, lpr, smem, s);
     case KT_Q6_K: return launch_vec_dt<KT_Q6_K>(a, dtype, max_groups, lpr, smem, s);
     case KT_IQ3_S: return launch_vec_dt<KT_IQ3_S>(a, dtype, max_groups, lpr, smem, s);

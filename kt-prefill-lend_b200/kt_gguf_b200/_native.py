@@ -19,11 +19,13 @@ GGML_Q4_0, GGML_Q4_1, GGML_Q5_0, GGML_Q5_1, GGML_IQ4_NL = 2, 3, 6, 7, 20
 GGML_Q8_0, GGML_Q4_K, GGML_Q6_K, GGML_IQ3_S = 8, 12, 14, 21
 GGML_Q2_K, GGML_Q3_K, GGML_Q5_K, GGML_IQ4_XS = 10, 11, 13, 23
 GGML_Q2_0 = 42  # the reference's 64-value 2-bit block (kt_gguf_moe_multi.cu:33-46)
+GGML_IQ2_XXS, GGML_IQ2_XS, GGML_IQ3_XXS, GGML_IQ1_S, GGML_IQ2_S, GGML_IQ1_M = 16, 17, 18, 19, 22, 29
 # types of the prefill layer (tcgen05 GEMMs) ...
 PREFILL_TYPES = (GGML_Q8_0, GGML_Q4_K, GGML_Q6_K, GGML_IQ3_S)
 # ... and of the decode GEMV, the dense GEMV and the dequantizer
 SUPPORTED_TYPES = PREFILL_TYPES + (GGML_Q4_0, GGML_Q4_1, GGML_Q5_0, GGML_Q5_1, GGML_IQ4_NL,
-                                   GGML_Q2_K, GGML_Q3_K, GGML_Q5_K, GGML_IQ4_XS, GGML_Q2_0)
+                                   GGML_Q2_K, GGML_Q3_K, GGML_Q5_K, GGML_IQ4_XS, GGML_Q2_0,
+                                   GGML_IQ2_XXS, GGML_IQ2_XS, GGML_IQ3_XXS, GGML_IQ1_S, GGML_IQ2_S, GGML_IQ1_M)
 DTYPE_CODES = {torch.float32: 0, torch.float16: 1, torch.bfloat16: 2}
 
 _P, _I, _I64, _SZ, _F = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_size_t, ctypes.c_float

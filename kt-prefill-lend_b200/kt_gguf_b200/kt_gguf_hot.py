@@ -18,8 +18,9 @@ With KV-lent slots (layer.kt_kv_ptr13 / kt_kv_ptr2) both paths read the weights 
 per-slot pointer tables.
 
 GGUF types with B200 kernels: the prefill layer takes Q8_0 (8), Q4_K (12), Q6_K (14) and
-IQ3_S (21); the GEMV also Q4_0/Q4_1/Q5_0/Q5_1/IQ4_NL, Q2_K/Q3_K/Q5_K/IQ4_XS and the
-reference's Q2_0 (42); other types raise at construction. As in the reference
+IQ3_S (21); the GEMV also Q4_0/Q4_1/Q5_0/Q5_1/IQ4_NL, Q2_K/Q3_K/Q5_K/IQ4_XS,
+IQ2_XXS/IQ2_XS/IQ2_S/IQ3_XXS/IQ1_S/IQ1_M and the reference's Q2_0 (42); other types raise at
+construction. As in the reference
 (hot/kt_gguf_hot.py:21-25, 180-190), Q2_0 downs stay 2-bit on the GPU and their layers run
 the GEMV at every length; KT_GGUF_Q2_NATIVE=0 repacks them losslessly into Q8_0 instead
 (q2_0_to_q8_0), which the prefill layer takes.
@@ -59,11 +60,13 @@ PREFILL_ON_GPU = os.environ.get("KT_B200_PREFILL", "1") == "1"
 GGML_Q8_0 = 8
 GGML_Q2_0 = 42
 # ggml type -> (block elements, block bytes), the reference's table (hot/kt_gguf_hot.py:76-80)
+# (19 is IQ1_S's 50-byte block here, as in the reference kernel's block_iq1_s; the reference's
+# Python table gives it 74 bytes, IQ2_XS's size, and lacks 17 and 29)
 BLOCK_INFO = {
     2: (32, 18), 3: (32, 20), 6: (32, 22), 7: (32, 24), 8: (32, 34), 10: (256, 84), 11: (256, 110),
     12: (256, 144), 13: (256, 176), 14: (256, 210),
-    16: (256, 66), 19: (256, 74), 20: (32, 18), 21: (256, 110), 22: (256, 82), 23: (256, 136),
-    18: (256, 98), 42: (64, 18),
+    16: (256, 66), 17: (256, 74), 19: (256, 50), 20: (32, 18), 21: (256, 110), 22: (256, 82), 23: (256, 136),
+    18: (256, 98), 29: (256, 56), 42: (64, 18),
 }
 # types with a B200 kernel (the reference's MMVQ_TYPES lists every sgl-kernel MMVQ type, which
 # excludes its own Q2_0: that one is allowed through q2_native)

@@ -18,7 +18,8 @@ import torch
 ENC_PATH = Path(__file__).resolve().parent / "lib" / "libkt_gguf_encode.so"
 BLOCK = {8: (32, 34), 12: (256, 144), 14: (256, 210), 21: (256, 110),
          2: (32, 18), 3: (32, 20), 6: (32, 22), 7: (32, 24), 20: (32, 18),
-         10: (256, 84), 11: (256, 110), 13: (256, 176), 23: (256, 136), 42: (64, 18)}
+         10: (256, 84), 11: (256, 110), 13: (256, 176), 23: (256, 136), 42: (64, 18),
+         16: (256, 66), 17: (256, 74), 18: (256, 98), 19: (256, 50), 22: (256, 82), 29: (256, 56)}
 _enc = None
 
 
@@ -84,6 +85,17 @@ def random_blocks(rng: np.random.Generator, qtype: int, rows: int, cols: int) ->
         put_f16(2, 0, 2e-3)
     elif qtype == 23:  # d
         put_f16(0, -2e-4, 2e-4)
+    elif qtype in (16, 17, 22):  # d of the IQ2 families
+        put_f16(0, 0, 5e-4)
+    elif qtype == 18:
+        put_f16(0, 0, 3e-4)
+    elif qtype == 19:
+        put_f16(0, 0, 3e-3)
+    elif qtype == 29:  # the fp16 d spread over the top nibbles of the four scale words
+        d = rng.uniform(0, 3e-3, size=nb).astype(np.float16).view(np.uint16).astype(np.uint16)
+        for k in range(4):
+            hi = ((d >> (4 * k)) & 0xF).astype(np.uint8) << 4
+            b[:, 49 + 2 * k] = (b[:, 49 + 2 * k] & 0x0F) | hi
     return b.reshape(rows, cols // qk * bs)
 
 

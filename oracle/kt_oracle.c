@@ -19,6 +19,9 @@
  *     1057-1076), vec_dot_q3_K_q8_1 (282-317, 1175-1198), vec_dot_q5_K_q8_1 (413-445,
  *     1467-1509), vec_dot_iq4_xs_q8_1 (2019-2040); and the reference's own Q2_0 block and
  *     vec_dot_q2_0_q8_1 (kt_gguf_moe_multi.cu:33-64).
+ *   - the i-quants with a code book, IQ2_XXS / IQ2_XS / IQ2_S / IQ3_XXS / IQ1_S / IQ1_M:
+ *     ggml's dequantize_row order and vec_dot_*_q8_1 (vecdotq.cuh:1755-1977); code books
+ *     from iquant_grids.h.
  *   - the q8_1 activation quantizer quantize_q8_1 (hot/kt_gguf_moe_multi/kt_gguf_moe_multi.cu:600-650),
  *     including the lane order of its 32-lane butterfly sum that produces ds.y.
  *   - the per-chunk integer dot products vec_dot_q8_0_q8_1 (vecdotq.cuh:969-982),
@@ -45,6 +48,7 @@
 #include <stdlib.h>
 #include <string.h>
 #include "../kt-prefill-lend_b200/csrc/iq3s_grid.h"
+#include "../kt-prefill-lend_b200/csrc/iquant_grids.h"
 
 #define KO_Q4_0 2
 #define KO_Q4_1 3
@@ -60,6 +64,13 @@
 #define KO_Q5_K 13
 #define KO_IQ4_XS 23
 #define KO_Q2_0 42
+#define KO_IQ2_XXS 16
+#define KO_IQ2_XS 17
+#define KO_IQ3_XXS 18
+#define KO_IQ1_S 19
+#define KO_IQ2_S 22
+#define KO_IQ1_M 29
+#define KO_IQ1_DELTA 0.125f
 
 /* ---------------------------------------------------------------- numbers */
 
@@ -135,6 +146,12 @@ int ko_block_info(int type, int* blck, int* bytes) {
     case KO_Q5_K: *blck = 256; *bytes = 176; return 0;
     case KO_IQ4_XS: *blck = 256; *bytes = 136; return 0;
     case KO_Q2_0: *blck = 64; *bytes = 18; return 0;
+    case KO_IQ2_XXS: *blck = 256; *bytes = 66; return 0;
+    case KO_IQ2_XS: *blck = 256; *bytes = 74; return 0;
+    case KO_IQ3_XXS: *blck = 256; *bytes = 98; return 0;
+    case KO_IQ1_S: *blck = 256; *bytes = 50; return 0;
+    case KO_IQ2_S: *blck = 256; *bytes = 82; return 0;
+    case KO_IQ1_M: *blck = 256; *bytes = 56; return 0;
     default: return -1;
   }
 }
@@ -268,6 +285,101 @@ static void dq_q2_0(const uint8_t* b, float* y) {
   for (int e = 0; e < 64; ++e) y[e] = (float)(((b[2 + e / 4] >> (2 * (e % 4))) & 3) - 1) * d;
 }
 
+/* ---- i-quants with a code book (ggml's dequantize_row_iq2_xxs / iq2_xs / iq2_s / iq3_xxs /
+ * iq1_s / iq1_m order, which gguf-py restates). Code books: iquant_grids.h (byte j of an
+ * IQ2 entry e is byte j%4 of word 2e + j/4; IQ3_XXS entries are one word; IQ1 entries hold
+ * v + 1 in nibbles, element j<4 in the low nibble of byte j, j>=4 in the high nibble of
+ * byte j-4). Sign bytes: 7 stored bits + an even-parity eighth (ksigns_iq2xs). */
+static uint32_t ko_signs8(uint32_t s7) {
+  uint32_t p = 0;
+  for (int i = 0; i < 7; ++i) p ^= (s7 >> i) & 1u;
+  return s7 | (p << 7);
+}
+static int ko_iq2_mag(const uint32_t* grid, int entry, int j) { return (int)((grid[2 * entry + j / 4] >> (8 * (j % 4))) & 0xffu); }
+static int ko_iq1_val(int entry, int j) {
+  return (int)((kt_iq1s_grid_host[entry] >> (8 * (j % 4) + 4 * (j / 4))) & 0xfu) - 1;
+}
+static uint32_t rd32u(const uint8_t* p) { return (uint32_t)p[0] | ((uint32_t)p[1] << 8) | ((uint32_t)p[2] << 16) | ((uint32_t)p[3] << 24); }
+
+static void dq_iq2_xxs(const uint8_t* b, float* y) {
+  float d = ko_h2f(rd16(b));
+  for (int ib = 0; ib < 8; ++ib) {
+    const uint8_t* q2 = b + 2 + 8 * ib;
+    uint32_t aux = rd32u(q2 + 4);
+    float db = d * (0.5f + (float)(aux >> 28)) * 0.25f;
+    for (int l = 0; l < 4; ++l) {
+      uint32_t s = ko_signs8((aux >> (7 * l)) & 127u);
+      for (int j = 0; j < 8; ++j) *y++ = db * (float)ko_iq2_mag(kt_iq2xxs_grid_host, q2[l], j) * ((s >> j) & 1 ? -1.0f : 1.0f);
+    }
+  }
+}
+static void dq_iq2_xs(const uint8_t* b, float* y) {
+  float d = ko_h2f(rd16(b));
+  for (int ib = 0; ib < 8; ++ib) {
+    const uint8_t* q2 = b + 2 + 8 * ib;
+    float db[2] = {d * (0.5f + (float)(b[66 + ib] & 0xf)) * 0.25f, d * (0.5f + (float)(b[66 + ib] >> 4)) * 0.25f};
+    for (int l = 0; l < 4; ++l) {
+      uint32_t code = rd16(q2 + 2 * l), s = ko_signs8(code >> 9);
+      for (int j = 0; j < 8; ++j)
+        *y++ = db[l / 2] * (float)ko_iq2_mag(kt_iq2xs_grid_host, (int)(code & 511u), j) * ((s >> j) & 1 ? -1.0f : 1.0f);
+    }
+  }
+}
+static void dq_iq2_s(const uint8_t* b, float* y) {
+  float d = ko_h2f(rd16(b));
+  for (int ib = 0; ib < 8; ++ib) {
+    float db[2] = {d * (0.5f + (float)(b[74 + ib] & 0xf)) * 0.25f, d * (0.5f + (float)(b[74 + ib] >> 4)) * 0.25f};
+    for (int l = 0; l < 4; ++l) {
+      int idx = b[2 + 4 * ib + l] | ((b[66 + ib] << (8 - 2 * l)) & 0x300);
+      uint32_t s = b[34 + 4 * ib + l];
+      for (int j = 0; j < 8; ++j)
+        *y++ = db[l / 2] * (float)ko_iq2_mag(kt_iq2s_grid_host, idx, j) * ((s >> j) & 1 ? -1.0f : 1.0f);
+    }
+  }
+}
+static void dq_iq3_xxs(const uint8_t* b, float* y) {
+  float d = ko_h2f(rd16(b));
+  for (int ib = 0; ib < 8; ++ib) {
+    const uint8_t* q3 = b + 2 + 8 * ib;
+    uint32_t aux = rd32u(b + 66 + 4 * ib);
+    float db = d * (0.5f + (float)(aux >> 28)) * 0.5f;
+    for (int l = 0; l < 4; ++l) {
+      uint32_t s = ko_signs8((aux >> (7 * l)) & 127u);
+      for (int j = 0; j < 8; ++j) {
+        int mag = (int)((kt_iq3xxs_grid_host[q3[2 * l + j / 4]] >> (8 * (j % 4))) & 0xffu);
+        *y++ = db * (float)mag * ((s >> j) & 1 ? -1.0f : 1.0f);
+      }
+    }
+  }
+}
+static void dq_iq1_s(const uint8_t* b, float* y) {
+  float d = ko_h2f(rd16(b));
+  for (int ib = 0; ib < 8; ++ib) {
+    int qh = rd16(b + 34 + 2 * ib);
+    float dl = d * (float)(2 * ((qh >> 12) & 7) + 1);
+    float delta = (qh & 0x8000) ? -KO_IQ1_DELTA : KO_IQ1_DELTA;
+    for (int l = 0; l < 4; ++l) {
+      int e = b[2 + 4 * ib + l] | (((qh >> (3 * l)) & 7) << 8);
+      for (int j = 0; j < 8; ++j) *y++ = dl * ((float)ko_iq1_val(e, j) + delta);
+    }
+  }
+}
+static void dq_iq1_m(const uint8_t* b, float* y) {
+  uint16_t sc[4];
+  for (int k = 0; k < 4; ++k) sc[k] = rd16(b + 48 + 2 * k);
+  float d = ko_h2f((uint16_t)((sc[0] >> 12) | ((sc[1] >> 8) & 0x00F0) | ((sc[2] >> 4) & 0x0F00) | (sc[3] & 0xF000)));
+  for (int ib = 0; ib < 8; ++ib) {
+    int tmp = sc[ib / 2] >> (6 * (ib % 2));
+    float dl[2] = {d * (float)(2 * (tmp & 7) + 1), d * (float)(2 * ((tmp >> 3) & 7) + 1)};
+    for (int l = 0; l < 4; ++l) {
+      int qhl = b[32 + 2 * ib + l / 2] >> (4 * (l % 2));
+      int e = b[4 * ib + l] | ((qhl & 7) << 8);
+      float delta = (qhl & 8) ? -KO_IQ1_DELTA : KO_IQ1_DELTA;
+      for (int j = 0; j < 8; ++j) *y++ = dl[l / 2] * ((float)ko_iq1_val(e, j) + delta);
+    }
+  }
+}
+
 static void dq_q6_k(const uint8_t* b, float* y) {
   const uint8_t* ql = b;
   const uint8_t* qh = b + 128;
@@ -360,6 +472,12 @@ int ko_dequant_rows(int type, const uint8_t* w, int64_t nrows, int64_t cols, flo
         case KO_Q5_K: dq_q5_k(b, y); break;
         case KO_IQ4_XS: dq_iq4_xs(b, y); break;
         case KO_Q2_0: dq_q2_0(b, y); break;
+        case KO_IQ2_XXS: dq_iq2_xxs(b, y); break;
+        case KO_IQ2_XS: dq_iq2_xs(b, y); break;
+        case KO_IQ2_S: dq_iq2_s(b, y); break;
+        case KO_IQ3_XXS: dq_iq3_xxs(b, y); break;
+        case KO_IQ1_S: dq_iq1_s(b, y); break;
+        case KO_IQ1_M: dq_iq1_m(b, y); break;
         default: dq_legacy(type, b, y); break;
       }
     }
@@ -668,6 +786,99 @@ static float vd_q2_0(const uint8_t* bx, const uint8_t* by0, int iqs) {
   return ko_h2f(rd16(bx)) * q8_1_d(b8) * (float)(sumi - sumy);
 }
 
+/* ---- i-quant dot products (vecdotq.cuh:1755-1776 iq2_xxs, 1778-1806 iq2_xs, 1809-1845 iq2_s,
+ * 1848-1872 iq3_xxs, 1903-1932 iq1_s, 1935-1977 iq1_m): chunk = sub-block ib32 against q8_1
+ * block ib32. The integer sums are exact whatever the evaluation; the fp32 combinations
+ * follow the reference's expressions. */
+static int32_t ko_sdot8(const uint8_t* q8, int mag_of_j[8], uint32_t s8) {
+  int32_t sum = 0;
+  for (int j = 0; j < 8; ++j) sum += (int32_t)(int8_t)q8[j] * mag_of_j[j] * ((s8 >> j) & 1 ? -1 : 1);
+  return sum;
+}
+static float vd_iq2_xxs(const uint8_t* bx, const uint8_t* by0, int ib32) {
+  const uint8_t* b8 = by0 + 36 * ib32;
+  const uint8_t* q2 = bx + 2 + 8 * ib32;
+  uint32_t aux = rd32u(q2 + 4);
+  int32_t sumi = 0;
+  for (int l = 0; l < 4; ++l) {
+    int m[8];
+    for (int j = 0; j < 8; ++j) m[j] = ko_iq2_mag(kt_iq2xxs_grid_host, q2[l], j);
+    sumi += ko_sdot8(b8 + 4 + 8 * l, m, ko_signs8((aux >> (7 * l)) & 127u));
+  }
+  const float d = ko_h2f(rd16(bx)) * (0.5f + (float)(aux >> 28)) * q8_1_d(b8) * 0.25f;
+  return d * (float)sumi;
+}
+static float vd_iq2_xs_s(int type, const uint8_t* bx, const uint8_t* by0, int ib32) {
+  const uint8_t* b8 = by0 + 36 * ib32;
+  const int ls = type == KO_IQ2_XS ? bx[66 + ib32] : bx[74 + ib32];
+  int32_t sumi[2] = {0, 0};
+  for (int l = 0; l < 4; ++l) {
+    int m[8];
+    uint32_t s;
+    if (type == KO_IQ2_XS) {
+      uint32_t code = rd16(bx + 2 + 8 * ib32 + 2 * l);
+      for (int j = 0; j < 8; ++j) m[j] = ko_iq2_mag(kt_iq2xs_grid_host, (int)(code & 511u), j);
+      s = ko_signs8(code >> 9);
+    } else {
+      int idx = bx[2 + 4 * ib32 + l] | ((bx[66 + ib32] << (8 - 2 * l)) & 0x300);
+      for (int j = 0; j < 8; ++j) m[j] = ko_iq2_mag(kt_iq2s_grid_host, idx, j);
+      s = bx[34 + 4 * ib32 + l];
+    }
+    sumi[l / 2] += ko_sdot8(b8 + 4 + 8 * l, m, s);
+  }
+  const float d = ko_h2f(rd16(bx)) * q8_1_d(b8) * 0.25f;
+  return d * ((0.5f + (float)(ls & 0xf)) * (float)sumi[0] + (0.5f + (float)(ls >> 4)) * (float)sumi[1]);
+}
+static float vd_iq3_xxs(const uint8_t* bx, const uint8_t* by0, int ib32) {
+  const uint8_t* b8 = by0 + 36 * ib32;
+  const uint8_t* q3 = bx + 2 + 8 * ib32;
+  uint32_t aux = rd32u(bx + 66 + 4 * ib32);
+  int32_t sumi = 0;
+  for (int l = 0; l < 4; ++l) {
+    int m[8];
+    for (int j = 0; j < 8; ++j) m[j] = (int)((kt_iq3xxs_grid_host[q3[2 * l + j / 4]] >> (8 * (j % 4))) & 0xffu);
+    sumi += ko_sdot8(b8 + 4 + 8 * l, m, ko_signs8((aux >> (7 * l)) & 127u));
+  }
+  const float d = ko_h2f(rd16(bx)) * (0.5f + (float)(aux >> 28)) * q8_1_d(b8) * 0.5f;
+  return d * (float)sumi;
+}
+/* IQ1: sum((v+1)*u) over a group, the book's stored values */
+static int32_t ko_iq1_dot8(const uint8_t* q8, int e) {
+  int32_t sum = 0;
+  for (int j = 0; j < 8; ++j) sum += (int32_t)(int8_t)q8[j] * (ko_iq1_val(e, j) + 1);
+  return sum;
+}
+static float vd_iq1_s(const uint8_t* bx, const uint8_t* by0, int ib32) {
+  const uint8_t* b8 = by0 + 36 * ib32;
+  const int qh = rd16(bx + 34 + 2 * ib32);
+  int32_t sumi = 0;
+  for (int l = 0; l < 4; ++l) sumi += ko_iq1_dot8(b8 + 4 + 8 * l, bx[2 + 4 * ib32 + l] | (((qh >> (3 * l)) & 7) << 8));
+  const float d1q = ko_h2f(rd16(bx)) * (float)(((qh >> 11) & 0x0E) + 1);
+  const float delta = (qh & 0x8000) ? -1.0f - KO_IQ1_DELTA : -1.0f + KO_IQ1_DELTA;
+  const float dx = ko_h2f(rd16(b8)), dy = ko_h2f(rd16(b8 + 2));
+  return d1q * (dx * (float)sumi + dy * delta);
+}
+static float vd_iq1_m(const uint8_t* bx, const uint8_t* by0, int ib32) {
+  const uint8_t* b8 = by0 + 36 * ib32;
+  int32_t sumi[2] = {0, 0};
+  float sumf[2] = {0.0f, 0.0f};
+  for (int l = 0; l < 4; ++l) {
+    const int qhl = bx[32 + 2 * ib32 + l / 2] >> (4 * (l % 2));
+    sumi[l / 2] += ko_iq1_dot8(b8 + 4 + 8 * l, bx[4 * ib32 + l] | ((qhl & 7) << 8));
+    const float delta = (qhl & 8) ? -1.0f - KO_IQ1_DELTA : -1.0f + KO_IQ1_DELTA;
+    int32_t sumy = 0;
+    for (int j = 0; j < 8; ++j) sumy += (int8_t)b8[4 + 8 * l + j];
+    sumf[l / 2] += delta * (float)sumy;
+  }
+  uint16_t sc[4];
+  for (int k = 0; k < 4; ++k) sc[k] = rd16(bx + 48 + 2 * k);
+  const float d = ko_h2f((uint16_t)((sc[0] >> 12) | ((sc[1] >> 8) & 0x00F0) | ((sc[2] >> 4) & 0x0F00) | (sc[3] & 0xF000))) *
+                  q8_1_d(b8);
+  const int tmp = sc[ib32 / 2] >> (6 * (ib32 % 2));
+  const int sc0 = 2 * (tmp & 7) + 1, sc1 = 2 * ((tmp >> 3) & 7) + 1;
+  return d * (((float)sumi[0] + sumf[0]) * (float)sc0 + ((float)sumi[1] + sumf[1]) * (float)sc1);
+}
+
 /* chunk geometry of the reference launchers: values per block, chunks per block, vdr */
 static int chunk_geom(int type, int* qk, int* cpb, int* vdr) {
   switch (type) {
@@ -679,6 +890,8 @@ static int chunk_geom(int type, int* qk, int* cpb, int* vdr) {
     case KO_Q5_K: *qk = 256; *cpb = 16; *vdr = 2; return 0; /* qi 32, vdr 2 */
     case KO_IQ4_XS: *qk = 256; *cpb = 8; *vdr = 1; return 0; /* qi 8, vdr 1 */
     case KO_Q2_0: *qk = 64; *cpb = 4; *vdr = 1; return 0;   /* qi 4, vdr 1 */
+    case KO_IQ2_XXS: case KO_IQ2_XS: case KO_IQ2_S: case KO_IQ3_XXS: case KO_IQ1_S: case KO_IQ1_M:
+      *qk = 256; *cpb = 8; *vdr = 1; return 0;              /* qi 8, vdr 1 */
     case KO_Q4_0: case KO_Q4_1: case KO_Q5_0: case KO_Q5_1: case KO_IQ4_NL:
       *qk = 32; *cpb = 2; *vdr = 2; return 0;               /* qi 4, vdr 2 */
     default: return -1;
@@ -707,6 +920,11 @@ static float row_dot(int type, const uint8_t* wrow, int bs, int nblocks, const u
       case KO_Q5_K: v = vd_q5_k(bx, by, iqs); break;
       case KO_IQ4_XS: v = vd_iq4_xs(bx, by, iqs); break;
       case KO_Q2_0: v = vd_q2_0(bx, by, iqs); break;
+      case KO_IQ2_XXS: v = vd_iq2_xxs(bx, by, iqs); break;
+      case KO_IQ2_XS: case KO_IQ2_S: v = vd_iq2_xs_s(type, bx, by, iqs); break;
+      case KO_IQ3_XXS: v = vd_iq3_xxs(bx, by, iqs); break;
+      case KO_IQ1_S: v = vd_iq1_s(bx, by, iqs); break;
+      case KO_IQ1_M: v = vd_iq1_m(bx, by, iqs); break;
       default: v = vd_legacy(type, bx, by, iqs); break;
     }
     lane[c % 32] += v;

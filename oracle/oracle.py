@@ -20,7 +20,8 @@ HERE = Path(__file__).resolve().parent
 LIB_PATH = HERE / "libkt_oracle.so"
 BLOCK = {8: (32, 34), 12: (256, 144), 14: (256, 210), 21: (256, 110),
          2: (32, 18), 3: (32, 20), 6: (32, 22), 7: (32, 24), 20: (32, 18),
-         10: (256, 84), 11: (256, 110), 13: (256, 176), 23: (256, 136), 42: (64, 18)}
+         10: (256, 84), 11: (256, 110), 13: (256, 176), 23: (256, 136), 42: (64, 18),
+         16: (256, 66), 17: (256, 74), 18: (256, 98), 19: (256, 50), 22: (256, 82), 29: (256, 56)}
 
 _lib = None
 

@@ -9,8 +9,9 @@ implementation independent of this repository. For each type the file holds
                            which neither encodes, takes random blocks here too),
                            rows 24-47 random bytes with finite scales (every code pattern)
   <type>_values  float32: gguf-py's dequantization of those rows
-and for Q2_K, Q3_K, Q5_K and IQ4_XS, which gguf-py does not encode, 48 rows of random blocks
-with finite scales and their dequantization; for the reference's own Q2_0 (ggml type 42,
+and for Q2_K, Q3_K, Q5_K, IQ4_XS and the code-book i-quants IQ2_XXS, IQ2_XS, IQ2_S, IQ3_XXS,
+IQ1_S, IQ1_M, which gguf-py does not encode, 48 rows of random blocks with finite scales and
+their dequantization; for the reference's own Q2_0 (ggml type 42,
 unknown to gguf-py) 24 encoded and 24 random rows with values (code - 1) * d computed here
 in numpy from the block's definition (kt_gguf_moe_multi.cu:33-46 of the reference),
 plus the IQ3_S codebook as uint32 words and the IQ4_NL levels.
@@ -33,6 +34,7 @@ from kt_gguf_b200 import synth  # noqa: E402
 TYPES = {8: Q.Q8_0, 12: Q.Q4_K, 14: Q.Q6_K, 21: Q.IQ3_S}
 LEGACY = {2: Q.Q4_0, 3: Q.Q4_1, 6: Q.Q5_0, 7: Q.Q5_1, 20: Q.IQ4_NL}
 KQUANTS = {10: Q.Q2_K, 11: Q.Q3_K, 13: Q.Q5_K, 23: Q.IQ4_XS}
+IQUANTS = {16: Q.IQ2_XXS, 17: Q.IQ2_XS, 18: Q.IQ3_XXS, 19: Q.IQ1_S, 22: Q.IQ2_S, 29: Q.IQ1_M}
 
 
 def main():
@@ -62,6 +64,10 @@ def main():
     codes = ((b[:, :, 2:, None] >> np.array([0, 2, 4, 6], dtype=np.uint8)) & 3).reshape(48, 8, 64)
     out["42_blocks"] = blocks
     out["42_values"] = ((codes.astype(np.float32) - 1) * d).reshape(48, 512)
+    for t, qt in IQUANTS.items():
+        blocks = synth.random_blocks(rng, t, 48, 512)
+        out[f"{t}_blocks"] = blocks
+        out[f"{t}_values"] = dequantize(blocks, qt).reshape(48, 512).astype(np.float32)
     out["iq4nl_levels"] = np.array(IQ4_NL.kvalues, dtype=np.int8)
     IQ3_S.init_grid()
     g = IQ3_S.grid.reshape(512, 4).astype(np.uint32)

@@ -34,7 +34,7 @@ def test_host_only_queries():
     assert lib.kt_status_string(N.KT_ERR_WORKSPACE) == b"workspace too small"
     assert N.row_bytes(12, 2048) == 1152 and N.row_bytes(14, 512) == 420 and N.row_bytes(21, 2048) == 880
     out = ctypes.c_int64()
-    assert lib.kt_gguf_row_bytes(16, 256, ctypes.byref(out)) == N.KT_ERR_TYPE  # IQ2_XXS: no kernel
+    assert lib.kt_gguf_row_bytes(1, 256, ctypes.byref(out)) == N.KT_ERR_TYPE  # F16: not a GGUF block type here
     assert lib.kt_gguf_row_bytes(11, 256, ctypes.byref(out)) == 0 and out.value == 110
     assert lib.kt_gguf_row_bytes(12, 100, ctypes.byref(out)) == N.KT_ERR_ARG
     assert lib.kt_moe_a8_vec_workspace_size(4, 2048, 40, 512) > 4 * 2304
@@ -49,7 +49,7 @@ def test_argument_errors_before_any_launch():
     lib = N.load()
     P = ctypes.c_void_p
     # unsupported ggml type, bad dtype, bad shapes, tiny workspace: rejected on the host
-    assert lib.kt_moe_a8_vec_multi(P(16), 2, 1, 2048, P(16), 0, 4, P(16), 1, 16, 64, P(16), P(16), 1 << 20,
+    assert lib.kt_moe_a8_vec_multi(P(16), 2, 1, 2048, P(16), 0, 4, P(16), 1, 1, 64, P(16), P(16), 1 << 20,
                                    None) == N.KT_ERR_TYPE
     assert lib.kt_moe_a8_vec_multi(P(16), 7, 1, 2048, P(16), 0, 4, P(16), 1, 12, 64, P(16), P(16), 1 << 20,
                                    None) == N.KT_ERR_ARG
@@ -65,7 +65,7 @@ def test_argument_errors_before_any_launch():
                               None) == N.KT_ERR_TYPE
     # the 32-value legacy blocks, Q2_K / Q3_K / Q5_K / IQ4_XS and Q2_0 have a decode GEMV but no
     # prefill GEMM
-    for t in (2, 10, 11, 13, 23, 42):
+    for t in (2, 10, 11, 13, 23, 42, 16, 17, 18, 19, 22, 29):
         assert lib.kt_moe_prefill(P(16), 16, 2048, 512, P(16), P(16), 8, P(16), t, P(16), 14, 0, 64, P(16), P(16),
                                   1 << 40, None) == N.KT_ERR_TYPE
     rb = ctypes.c_int64()

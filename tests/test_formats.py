@@ -10,7 +10,7 @@ from oracle import oracle as O
 GOLDEN = np.load(Path(__file__).with_name("golden") / "gguf_dequant.npz")
 TYPES = (8, 12, 14, 21)
 # the GEMV's wider type switch: 32-value blocks and the K-quants Q2_K / Q3_K / Q5_K / IQ4_XS
-LEGACY = (2, 3, 6, 7, 20, 10, 11, 13, 23, 42)  # and the reference's Q2_0
+LEGACY = (2, 3, 6, 7, 20, 10, 11, 13, 23, 42, 16, 17, 18, 19, 22, 29)  # Q2_0 and the code-book i-quants too
 REF_COMMON = Path("/root/reference/hot/kt_gguf_moe_multi/ggml-common.h")
 
 
@@ -18,7 +18,8 @@ def test_block_sizes_known_answers():
     # hot/kt_gguf_hot.py:76-80 BLOCK_INFO for the hot-path types
     assert O.BLOCK == {8: (32, 34), 12: (256, 144), 14: (256, 210), 21: (256, 110),
                        2: (32, 18), 3: (32, 20), 6: (32, 22), 7: (32, 24), 20: (32, 18),
-                       10: (256, 84), 11: (256, 110), 13: (256, 176), 23: (256, 136), 42: (64, 18)}
+                       10: (256, 84), 11: (256, 110), 13: (256, 176), 23: (256, 136), 42: (64, 18),
+                       16: (256, 66), 17: (256, 74), 18: (256, 98), 19: (256, 50), 22: (256, 82), 29: (256, 56)}
     from kt_gguf_b200 import synth
 
     assert synth.BLOCK == O.BLOCK
@@ -51,6 +52,49 @@ def test_iq3s_grid_matches_reference_table():
     body = re.search(r"iq3s_grid\[512\]\s*=\s*\{(.*?)\};", src, re.S).group(1)
     ref = np.array([int(x, 16) for x in re.findall(r"0x[0-9a-fA-F]+", body)], dtype=np.uint32)
     assert np.array_equal(ref, GOLDEN["iq3s_grid"])
+
+
+def _header_words(name):
+    header = Path(__file__).resolve().parents[1] / "kt-prefill-lend_b200" / "csrc" / "iquant_grids.h"
+    body = re.search(r"#define KT_" + name + r"_GRID_INIT \{(.*?)\}", header.read_text(), re.S).group(1)
+    return np.array([int(x, 16) for x in re.findall(r"0x([0-9a-f]{8})u", body)], dtype=np.uint32)
+
+
+def test_iquant_books_match_gguf_py():
+    # iquant_grids.h as committed against gguf-py's code books (the generator's source)
+    from gguf.quants import IQ1_S, IQ2_S, IQ2_XS, IQ2_XXS, IQ3_XXS
+
+    def entries(cls):
+        cls.init_grid()
+        return cls.grid.reshape(cls.grid_shape).astype(np.int64)
+
+    for name, cls in (("IQ2XXS", IQ2_XXS), ("IQ2XS", IQ2_XS), ("IQ2S", IQ2_S), ("IQ3XXS", IQ3_XXS)):
+        w = _header_words(name)
+        got = np.stack([(w >> (8 * k)) & 0xff for k in range(4)], axis=-1).reshape(entries(cls).shape)
+        assert np.array_equal(got, entries(cls)), name
+    w = _header_words("IQ1S")
+    nib = np.stack([(w >> (8 * k + 4 * h)) & 0xf for h in range(2) for k in range(4)], axis=-1).astype(np.int64) - 1
+    assert np.array_equal(nib, entries(IQ1_S))
+    # the sign table the kernels compute: 7 bits + even parity
+    ks = np.frombuffer(IQ2_XXS.ksigns, dtype=np.uint8)
+    assert all(int(ks[i]) == i | ((bin(i).count("1") & 1) << 7) for i in range(128))
+
+
+@pytest.mark.skipif(not REF_COMMON.exists(), reason="reference tree not mounted")
+def test_iquant_books_match_reference_tables():
+    # the reference's ggml-common.h tables (read as text): iq2xxs_grid, iq2xs_grid, iq2s_grid
+    # (uint64, byte j = element j), iq3xxs_grid, and iq1s_grid_gpu (the nibble form)
+    src = REF_COMMON.read_text()
+
+    def ref(name, dt):
+        body = re.search(name + r"\[\d+\]\s*=\s*\{(.*?)\};", src, re.S).group(1)
+        return np.array([int(x, 16) for x in re.findall(r"0x[0-9a-fA-F]+", body)], dtype=dt)
+
+    assert np.array_equal(ref("iq2xxs_grid", np.uint64).view(np.uint32), _header_words("IQ2XXS"))
+    assert np.array_equal(ref("iq2xs_grid", np.uint64).view(np.uint32), _header_words("IQ2XS"))
+    assert np.array_equal(ref("iq2s_grid", np.uint64).view(np.uint32), _header_words("IQ2S"))
+    assert np.array_equal(ref("iq3xxs_grid", np.uint32), _header_words("IQ3XXS"))
+    assert np.array_equal(ref("iq1s_grid_gpu", np.uint64).astype(np.uint32), _header_words("IQ1S"))
 
 
 @pytest.mark.parametrize("qtype,tol", [(8, 0.01), (12, 0.12), (14, 0.03), (21, 0.25)])

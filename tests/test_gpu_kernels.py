@@ -13,7 +13,7 @@ pytestmark = pytest.mark.gpu
 GOLDEN = np.load(__import__("pathlib").Path(__file__).with_name("golden") / "gguf_dequant.npz")
 TYPES = (8, 12, 14, 21)
 # decode GEMV and dequantizer only: 32-value blocks and the K-quants Q2_K / Q3_K / Q5_K / IQ4_XS
-LEGACY = (2, 3, 6, 7, 20, 10, 11, 13, 23, 42)  # and the reference's Q2_0
+LEGACY = (2, 3, 6, 7, 20, 10, 11, 13, 23, 42, 16, 17, 18, 19, 22, 29)  # Q2_0 and the code-book i-quants too
 
 
 def bits(t: torch.Tensor) -> np.ndarray:
@@ -83,7 +83,9 @@ def _oracle_gemv(qtype, W, x, ids, top_k, rows, cols):
                                              (21, 2048, 1024), (21, 512, 2048), (12, 7168, 64),
                                              (2, 2048, 256), (3, 2048, 256), (6, 512, 512), (7, 2048, 256),
                                              (20, 2048, 256), (10, 2048, 256), (11, 512, 512), (13, 2048, 256),
-                                             (23, 2048, 256), (42, 2048, 256), (42, 512, 1024)])
+                                             (23, 2048, 256), (42, 2048, 256), (42, 512, 1024),
+                                             (16, 2048, 256), (17, 2048, 256), (18, 2048, 256), (19, 2048, 256),
+                                             (22, 2048, 256), (29, 2048, 256), (22, 7168, 64)])
 @pytest.mark.parametrize("tokens,top_k", [(1, 8), (4, 10), (16, 3)])
 def test_gemv_matches_reference_arithmetic(cuda_device, qtype, cols, rows, tokens, top_k):
     slots = 6

@@ -67,7 +67,9 @@ def test_window_kernel_vs_reference(cuda_device, ref_mods, qtype, cols, rows, to
 
 @pytest.mark.parametrize("qtype,cols,rows", [(2, 2048, 512), (3, 2048, 512), (6, 512, 1024), (7, 2048, 512),
                                              (20, 2048, 512), (10, 2048, 512), (11, 512, 1024), (13, 2048, 512),
-                                             (23, 2048, 512), (42, 2048, 512), (42, 512, 2048)])
+                                             (23, 2048, 512), (42, 2048, 512), (42, 512, 2048),
+                                             (16, 2048, 512), (17, 2048, 512), (18, 2048, 512), (19, 2048, 512),
+                                             (22, 2048, 512), (29, 2048, 512)])
 @pytest.mark.parametrize("tokens,top_k", [(1, 8), (4, 4)])
 def test_legacy_blocks_vs_reference(cuda_device, ref_mods, qtype, cols, rows, tokens, top_k):
     # the 32-value block types and the K-quants Q2_K / Q3_K / Q5_K / IQ4_XS of the reference's

@@ -194,4 +194,5 @@ def test_row_bytes_and_block_table():
     assert H._row_bytes(2048, 12) == 8 * 144 and H._row_bytes(512, 14) == 420 and H._row_bytes(512, 21) == 220
     with pytest.raises(ValueError):
         H._row_bytes(100, 12)
-    assert H.MMVQ_TYPES == {2, 3, 6, 7, 8, 10, 11, 12, 13, 14, 20, 21, 23}
+    assert H.MMVQ_TYPES == {2, 3, 6, 7, 8, 10, 11, 12, 13, 14, 16, 17, 18, 19, 20, 21, 22, 23, 29}
+    assert all(H.BLOCK_INFO[t] == O.BLOCK[t] for t in H.MMVQ_TYPES | {42})

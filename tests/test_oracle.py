@@ -19,11 +19,13 @@ def q8_1_dequant(qx: np.ndarray, cols: int) -> np.ndarray:
 
 @pytest.mark.parametrize("qtype,cols,rows", [(8, 2048, 96), (8, 768, 40), (12, 2048, 64), (14, 512, 64),
                                              (21, 2048, 48), (21, 512, 40), (10, 2048, 40), (11, 512, 40),
-                                             (13, 2048, 40), (23, 2048, 40), (42, 2048, 40), (42, 512, 40)])
+                                             (13, 2048, 40), (23, 2048, 40), (42, 2048, 40), (42, 512, 40),
+                                             (16, 2048, 40), (17, 2048, 40), (18, 2048, 40), (19, 2048, 40),
+                                             (22, 2048, 40), (29, 2048, 40)])
 def test_gemv_integer_path_equals_dequant_matmul(qtype, cols, rows):
     rng = np.random.default_rng(qtype * 1000 + cols)
     x = rng.standard_normal((5, cols), dtype=np.float32)
-    if qtype in (10, 11, 13, 23):  # no encoder for these: arbitrary valid blocks
+    if qtype in (10, 11, 13, 23, 16, 17, 18, 19, 22, 29):  # no encoder for these: arbitrary valid blocks
         W = np.stack([synth.random_blocks(rng, qtype, rows, cols) for _ in range(3)])
     else:
         W = np.stack([synth.quantize(rng.standard_normal((rows, cols), dtype=np.float32) * 0.02, qtype)
@@ -34,6 +36,21 @@ def test_gemv_integer_path_equals_dequant_matmul(qtype, cols, rows):
     xd = q8_1_dequant(qx, cols)
     Wd = O.dequant(qtype, W, cols)
     exp = np.stack([Wd[e] @ xd[p // 2] if e >= 0 else np.zeros(rows, np.float32) for p, e in enumerate(ids)])
+    if qtype == 19:
+        # vec_dot_iq1_s_q8_1 takes the delta term against the q8_1 block's s (the sum of the
+        # unquantized activations) instead of d8*sum(u): per sub-block it adds
+        # dl * (delta - 1) * (s - d8*sum(u)) to the dequantized product
+        b = W.reshape(3, rows, cols // 256, 50)
+        d = b[..., 0:2].copy().view(np.float16)[..., 0].astype(np.float64)
+        qh = b[..., 34:50].copy().view(np.uint16).astype(np.int64)  # [3, rows, nb, 8]
+        dl_dm1 = d[..., None] * (2 * ((qh >> 12) & 7) + 1) * np.where(qh & 0x8000, -1.125, -0.875)
+        q8 = qx.reshape(qx.shape[0], -1, 36)[:, :cols // 32]
+        d8 = q8[..., 0:2].copy().view(np.float16)[..., 0].astype(np.float64)
+        s8 = q8[..., 2:4].copy().view(np.float16)[..., 0].astype(np.float64)
+        su = q8[..., 4:].view(np.int8).astype(np.int64).sum(-1)
+        gap = s8 - d8 * su  # [tokens, sub-blocks]
+        corr = dl_dm1.reshape(3, rows, -1)
+        exp = np.stack([exp[p] + (corr[e] @ gap[p // 2] if e >= 0 else 0) for p, e in enumerate(ids)])
     assert O.rel_l2(y, exp) < 2e-6
     assert np.all(y[2] == 0)
 
