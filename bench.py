@@ -68,6 +68,9 @@ def parse():
                                                              "all-to-alls overlap the other chunks' GEMMs")
     ap.add_argument("--sweep", action="store_true", help="config 2: run the decode/prefill sweep instead of the "
                                                          "headline line")
+    ap.add_argument("--stream", action="store_true", help="config 2 with the 192 non-resident experts streamed "
+                                                          "from pinned host banks (kt_stream_prefill_gguf)")
+    ap.add_argument("--group", type=int, default=0, help="--stream: experts per group (0: KT_GPU_STREAM_GROUP)")
     return ap.parse_args()
 
 
@@ -738,6 +741,102 @@ def run_config5(args):
     print(json.dumps(line), flush=True)
 
 
+def run_stream(args):
+    """Config 2 with its non-resident experts streamed instead of left to the CPU: the 64 hottest
+    experts stay in their slots (tcgen05 prefill layer), the other 192 come from pinned host
+    banks in groups, copied on a side stream while the previous group computes
+    (kt_stream_prefill_gguf.KTStreamPrefillGGUF, the reference's KT_GPU_STREAM_PREFILL path).
+    A step is the GPU side of one 16K-token chunk: resident layer + streamed groups + their sum.
+    Reported: tokens/s, the H2D rate of the staged bytes over the step, and a plain pinned
+    H2D copy of the same bytes (no compute) measured in this run as the bound (PCIe)."""
+    from types import SimpleNamespace
+
+    import numpy as np
+    import torch
+
+    from kt_gguf_b200 import _native as Nt
+    from kt_gguf_b200 import kt_gguf_moe_multi as M
+    from kt_gguf_b200 import kt_stream_prefill_gguf as SP
+    from kt_gguf_b200 import synth
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    cfg = dict(synth.CONFIGS[2], tokens=args.tokens)
+    n_res = cfg.pop("n_hot")
+    E = cfg["n_experts"]
+    # every expert with weights, physical order = hotness order: slots 0..63 are the resident
+    # experts and the router's physical ids index the bank directly
+    L = synth.make_layer(args.seed, n_hot=E, **cfg)
+    K, Nn = cfg["hidden"], cfg["inter"]
+
+    class Reader:
+        def __init__(self):
+            self.E = E
+
+        def types(self, li):
+            return (L.type13, L.type13, L.type2)
+
+        def slice(self, li, proj, n, rank, experts):
+            e = experts.numpy()
+            v = {"gate": L.w13[e, :n], "up": L.w13[e, n:], "down": L.w2[e]}[proj]
+            return torch.from_numpy(np.ascontiguousarray(v))
+
+    method = SimpleNamespace(reader=Reader(), rank=0, world=1, N=Nn, K=K, num_gpu_experts=n_res,
+                             kt_config=SimpleNamespace(layer_idx=0), streams_hot_experts=False)
+    sp = SP.KTStreamPrefillGGUF(method, group_size=args.group or None)
+    w13r, w2r = torch.from_numpy(L.w13[:n_res]).to(dev), torch.from_numpy(L.w2[:n_res]).to(dev)
+    x, ids, wts = L.x.to(dev), L.topk_ids.to(dev), L.topk_weights.to(dev)
+    slot_ids = torch.where(ids < n_res, ids, torch.full_like(ids, -1))
+    d = SimpleNamespace(hidden_states=x, topk_output=SimpleNamespace(topk_weights=wts))
+    lib = Nt.load()
+    ws = Nt.workspace(lib.kt_moe_prefill_workspace_size(args.tokens, ids.shape[1], K, Nn, n_res), dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def hot_only():
+        return M.moe_prefill(x, w13r, w2r, slot_ids, wts, L.type13, L.type2, Nn, workspace=ws)
+
+    def step():
+        return hot_only().add_(sp.run(method, None, d, ids))
+
+    def timed(fn, n):
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(n):
+            fn()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / n
+
+    for _ in range(max(3, args.warmup)):  # builds the bank, library state
+        step()
+    steps = max(1, min(args.steps, 20))
+    b0 = sp.bytes_staged
+    ms = timed(step, steps)
+    bytes_step = (sp.bytes_staged - b0) / steps
+    ms_hot = timed(hot_only, steps)
+    # the bound: the same bytes as plain pinned H2D copies, no compute
+    banks = sp._bank(0)
+    dst = [torch.empty(b[n_res:].numel(), dtype=torch.uint8, device=dev) for b in banks]
+
+    def copy_only():
+        for b, t in zip(banks, dst):
+            t.copy_(b[n_res:].reshape(-1), non_blocking=True)
+
+    ms_copy = timed(copy_only, 5)
+    peak = bytes_step / (ms_copy * 1e-3) / 1e9
+    got = bytes_step / (ms * 1e-3) / 1e9
+    line = {"metric": "config 2 streamed prefill", "value": args.tokens / (ms * 1e-3), "unit": "tokens/s",
+            "ms_per_step": ms, "ms_resident_only": ms_hot, "steps": steps,
+            "stream": {"experts": E - n_res, "group": sp.G, "groups": len(sp.groups(n_res)),
+                       "bytes_per_step": bytes_step, "h2d_GBps": got, "h2d_copy_only_GBps": peak,
+                       "frac_of_copy_only": got / peak, "ms_copy_only": ms_copy},
+            "config": {"workload": "config 2 (BASELINE configs[1]) with the 192 non-resident experts streamed",
+                       "tokens": args.tokens, "resident_experts": n_res, "streamed_experts": E - n_res},
+            "data": "synthetic (seeded)"}
+    print(json.dumps(line), flush=True)
+
+
 def _gemv_call(lib, Nt, x, w, ids, top_k, qtype, rows, tokens, y, ws, stream):
     Nt.check(lib.kt_moe_a8_vec_multi(Nt.ptr(x), Nt.dtype_code(x), tokens, x.shape[1], Nt.ptr(w), 0, w.shape[0],
                                      Nt.ptr(ids), top_k, qtype, rows, Nt.ptr(y), Nt.ptr(ws), ws.numel(), stream),
@@ -923,6 +1022,9 @@ def main():
         return
     if args.ep:
         run_ep(args, rank, world, local_rank)
+        return
+    if args.stream:
+        run_stream(args)
         return
     run_b200(args, rank, world, local_rank)
 

@@ -185,6 +185,26 @@ int kt_moe_prefill(const void* x, int64_t tokens, int64_t hidden, int64_t inter,
                    const float* topk_weights, int64_t top_k, const void* w13, int type13, const void* w2, int type2,
                    int w_is_table, int n_slots, void* out, void* workspace, size_t workspace_bytes, void* stream);
 
+/* kt_moe_prefill over an expert group, for the streamed prefill of experts that are not
+ * resident (the reference's KTStreamPrefillGGUF._group_body, kt_stream_prefill_gguf.py in
+ * its SGLang tree: dequant to bf16 + cutlass_fused_moe on the group, acc += out per group).
+ * Routes whose id lies in [id_base, id_base + n_slots) run on slot id - id_base of w13 / w2
+ * (the group's staged experts); every other route contributes nothing. acc_flags:
+ *   KT_ACC_LOAD   each token's weighted sum starts from acc[t] (fp32 [tokens, hidden]);
+ *   KT_ACC_STORE  the fp32 sum is written to acc (out unused, may be NULL); tokens with no
+ *                 route in the group are skipped when KT_ACC_LOAD is set too;
+ *   neither       as kt_moe_prefill: out = bf16(sum).
+ * A group loop runs the first group with KT_ACC_STORE, the middle ones with both flags and
+ * the last with KT_ACC_LOAD, so the sum over all groups is rounded to bf16 once. acc is
+ * 16-byte aligned. Errors as kt_moe_prefill, and KT_ERR_ARG for id_base < 0 or unknown
+ * flags. */
+#define KT_ACC_LOAD 1
+#define KT_ACC_STORE 2
+int kt_moe_prefill_ex(const void* x, int64_t tokens, int64_t hidden, int64_t inter, const int32_t* topk_ids,
+                      const float* topk_weights, int64_t top_k, const void* w13, int type13, const void* w2, int type2,
+                      int w_is_table, int n_slots, int32_t id_base, float* acc, int acc_flags, void* out,
+                      void* workspace, size_t workspace_bytes, void* stream);
+
 /* kt_moe_prefill that also records four caller-created CUDA events (cudaEvent_t as void*)
  * on `stream` after its stages: [0] routing permutation, [1] gate/up GEMM, [2] down GEMM,
  * [3] combine. For per-stage timing; stage_events may be NULL. */

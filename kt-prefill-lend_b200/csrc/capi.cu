@@ -270,18 +270,21 @@ KT_EXPORT int kt_moe_prefill_workspace_layout(int64_t tokens, int64_t top_k, int
   return KT_OK;
 }
 
-KT_EXPORT int kt_moe_prefill_timed(const void* x, int64_t tokens, int64_t hidden, int64_t inter,
-                                   const int32_t* topk_ids, const float* topk_weights, int64_t top_k, const void* w13,
-                                   int type13, const void* w2, int type2, int w_is_table, int n_slots, void* out,
-                                   void* workspace, size_t workspace_bytes, void* stream, void* const* stage_events) {
+static int prefill_run(const void* x, int64_t tokens, int64_t hidden, int64_t inter, const int32_t* topk_ids,
+                       const float* topk_weights, int64_t top_k, const void* w13, int type13, const void* w2, int type2,
+                       int w_is_table, int n_slots, int32_t id_base, float* acc, int acc_flags, void* out,
+                       void* workspace, size_t workspace_bytes, void* stream, void* const* stage_events) {
   if (!kt_prefill_type(type13) || !kt_prefill_type(type2)) return KT_ERR_TYPE;
   if (tokens < 0 || top_k <= 0 || top_k > 32 || n_slots <= 0 || n_slots > kPermMaxSlots || hidden <= 0 || inter <= 0)
     return KT_ERR_ARG;
   if (hidden % 256 || inter % 256 || hidden > (1 << 20) || inter > (1 << 20)) return KT_ERR_ARG;
   if (tokens * top_k > (int64_t)1 << 30) return KT_ERR_ARG;
+  if (id_base < 0 || (acc_flags & ~(KT_ACC_LOAD | KT_ACC_STORE))) return KT_ERR_ARG;
   if (tokens == 0) return KT_OK;
-  if (!x || !topk_ids || !topk_weights || !w13 || !w2 || !out || !workspace) return KT_ERR_ARG;
-  if (((uintptr_t)x | (uintptr_t)out) & 15) return KT_ERR_ARG;
+  const bool to_acc = acc_flags & KT_ACC_STORE;
+  if (!x || !topk_ids || !topk_weights || !w13 || !w2 || !workspace || (!to_acc && !out)) return KT_ERR_ARG;
+  if (acc_flags && (!acc || ((uintptr_t)acc & 15))) return KT_ERR_ARG;
+  if (((uintptr_t)x | (uintptr_t)(to_acc ? nullptr : out)) & 15) return KT_ERR_ARG;
   PreWs p = pre_ws(workspace, tokens, top_k, hidden, inter, n_slots);
   if (workspace_bytes < p.bytes) return KT_ERR_WORKSPACE;
   cudaStream_t s = S(stream);
@@ -291,7 +294,7 @@ KT_EXPORT int kt_moe_prefill_timed(const void* x, int64_t tokens, int64_t hidden
   const int64_t R = tokens * top_k;
   if (cudaMemsetAsync(p.status, 0, sizeof(int), s) != cudaSuccess) return KT_ERR_CUDA;
   int rc = kt_launch_permute(topk_ids, R, (int)top_k, n_slots, kt_gemm_tile_tokens(), kt_gemm_chunk_tiles(), p.counts,
-                             p.hist, p.tiles, p.n_tiles, p.chunks, p.sorted_token, p.route_pos, s);
+                             p.hist, p.tiles, p.n_tiles, p.chunks, p.sorted_token, p.route_pos, s, id_base);
   if (rc) return launch_rc(rc);
   mark(0);
   // SMs left to concurrent kernels (e.g. NCCL's while an expert-parallel layer overlaps its
@@ -311,18 +314,35 @@ KT_EXPORT int kt_moe_prefill_timed(const void* x, int64_t tokens, int64_t hidden
                            p.chunks, p.y, p.status, grid, s);
   if (rc) return launch_rc(rc);
   mark(2);
-  rc = kt_launch_combine_sorted(p.y, p.route_pos, topk_weights, tokens, top_k, hidden, (uint16_t*)out, s);
+  rc = kt_launch_combine_sorted(p.y, p.route_pos, topk_weights, tokens, top_k, hidden, (uint16_t*)out, s, acc,
+                                acc_flags);
   if (rc) return launch_rc(rc);
   mark(3);
   return launch_rc(0);
+}
+
+KT_EXPORT int kt_moe_prefill_timed(const void* x, int64_t tokens, int64_t hidden, int64_t inter,
+                                   const int32_t* topk_ids, const float* topk_weights, int64_t top_k, const void* w13,
+                                   int type13, const void* w2, int type2, int w_is_table, int n_slots, void* out,
+                                   void* workspace, size_t workspace_bytes, void* stream, void* const* stage_events) {
+  return prefill_run(x, tokens, hidden, inter, topk_ids, topk_weights, top_k, w13, type13, w2, type2, w_is_table,
+                     n_slots, 0, nullptr, 0, out, workspace, workspace_bytes, stream, stage_events);
 }
 
 KT_EXPORT int kt_moe_prefill(const void* x, int64_t tokens, int64_t hidden, int64_t inter, const int32_t* topk_ids,
                              const float* topk_weights, int64_t top_k, const void* w13, int type13, const void* w2,
                              int type2, int w_is_table, int n_slots, void* out, void* workspace, size_t workspace_bytes,
                              void* stream) {
-  return kt_moe_prefill_timed(x, tokens, hidden, inter, topk_ids, topk_weights, top_k, w13, type13, w2, type2,
-                              w_is_table, n_slots, out, workspace, workspace_bytes, stream, nullptr);
+  return prefill_run(x, tokens, hidden, inter, topk_ids, topk_weights, top_k, w13, type13, w2, type2, w_is_table,
+                     n_slots, 0, nullptr, 0, out, workspace, workspace_bytes, stream, nullptr);
+}
+
+KT_EXPORT int kt_moe_prefill_ex(const void* x, int64_t tokens, int64_t hidden, int64_t inter, const int32_t* topk_ids,
+                                const float* topk_weights, int64_t top_k, const void* w13, int type13, const void* w2,
+                                int type2, int w_is_table, int n_slots, int32_t id_base, float* acc, int acc_flags,
+                                void* out, void* workspace, size_t workspace_bytes, void* stream) {
+  return prefill_run(x, tokens, hidden, inter, topk_ids, topk_weights, top_k, w13, type13, w2, type2, w_is_table,
+                     n_slots, id_base, acc, acc_flags, out, workspace, workspace_bytes, stream, nullptr);
 }
 
 // ------------------------------------------------------------------ expert-parallel plumbing

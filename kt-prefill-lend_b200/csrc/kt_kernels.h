@@ -36,8 +36,10 @@ int kt_launch_dequant(int type, const void* w, int64_t rows, int64_t cols, void*
 int kt_launch_silu_and_mul(const void* h13, int dtype, int64_t rows, int64_t n, void* h, cudaStream_t s);
 int kt_launch_combine(const void* out, int dtype, const float* w, int64_t T, int64_t top_k, int64_t K, void* res,
                       cudaStream_t s);
+// acc_flags bit 0: start each token's sum from acc (fp32 [T, K]); bit 1: write the fp32 sum to
+// acc instead of bf16 to res (tokens with no present route are then skipped)
 int kt_launch_combine_sorted(const uint16_t* y, const int32_t* route_pos, const float* w, int64_t T, int64_t top_k,
-                             int64_t K, uint16_t* res, cudaStream_t s);
+                             int64_t K, uint16_t* res, cudaStream_t s, float* acc = nullptr, int acc_flags = 0);
 int kt_launch_route(const int32_t* ids, int64_t n, const int32_t* slot_tab, const int32_t* cpu_tab, float* counts,
                     int32_t* slot_out, int32_t* cpu_out, cudaStream_t s);
 int kt_launch_topk_softmax(const float* logits, int64_t T, int E, int k, int renorm, float* weights, int32_t* ids,
@@ -51,9 +53,10 @@ int kt_launch_topk_grouped(const float* logits, const float* bias, int64_t T, in
 // chunks[3c..3c+2] = slot, first sorted row, rows (capacity: that of the tile list)
 constexpr int kPermMaxSlots = 8192;
 int64_t kt_permute_hist_ints(int64_t routes, int n_slots);
+// ids outside [id_base, id_base + n_slots) (and negative ids) are not present; slot = id - id_base
 int kt_launch_permute(const int32_t* ids, int64_t routes, int top_k, int n_slots, int tile_tokens, int chunk_tiles,
                       int32_t* counts, int32_t* hist, int32_t* tiles, int32_t* n_tiles, int32_t* chunks,
-                      int32_t* sorted_token, int32_t* route_pos, cudaStream_t s);
+                      int32_t* sorted_token, int32_t* route_pos, cudaStream_t s, int id_base = 0);
 
 int kt_launch_gemm_gate_up(int type, const void* x, int64_t T, int K, int N, const void* w13, int table, int n_slots,
                            const int32_t* tiles, const int32_t* n_tiles, const int32_t* sorted_token, void* h,

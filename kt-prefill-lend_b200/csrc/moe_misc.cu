@@ -144,10 +144,13 @@ int kt_launch_combine(const void* out, int dtype, const float* w, int64_t T, int
 // the fp32 router weight and fp32 accumulation in k order, rounded once (the finalize of the
 // CUTLASS fused MoE that the reference's streamed prefill runs; the decode combine above keeps
 // the hot method's per-route bf16 roundings). Each thread produces 8 consecutive columns.
-template <int KMAX>
+// LOAD: the sum starts from acc[t] (fp32) instead of 0; STORE: the fp32 sum goes back to acc
+// instead of bf16 into res. With both, a token none of whose routes is present keeps its acc
+// untouched and is skipped (the expert-group loop of a streamed prefill).
+template <int KMAX, bool LOAD, bool STORE>
 __global__ void kt_combine_sorted_kernel(const uint16_t* __restrict__ y, const int32_t* __restrict__ route_pos,
                                          const float* __restrict__ w, int64_t T, int top_k, int64_t K,
-                                         uint16_t* __restrict__ res) {
+                                         uint16_t* __restrict__ res, float* __restrict__ acc_f32) {
   const int64_t t = blockIdx.x;
   // the token's routes: positions and weights (KMAX >= top_k), then all row loads in flight
   int32_t pos[KMAX];
@@ -157,14 +160,27 @@ __global__ void kt_combine_sorted_kernel(const uint16_t* __restrict__ y, const i
     pos[k] = k < top_k ? route_pos[t * top_k + k] : -1;
     wk[k] = k < top_k ? w[t * top_k + k] : 0.0f;
   }
+  if constexpr (LOAD && STORE) {
+    bool any = false;
+#pragma unroll
+    for (int k = 0; k < KMAX; ++k) any |= pos[k] >= 0;
+    if (!any) return;
+  }
   for (int64_t c = (int64_t)threadIdx.x * 8; c < K; c += (int64_t)blockDim.x * 8) {
     uint4 v[KMAX];
 #pragma unroll
     for (int k = 0; k < KMAX; ++k)
       v[k] = pos[k] >= 0 ? __ldcs(reinterpret_cast<const uint4*>(y + (int64_t)pos[k] * K + c)) : make_uint4(0, 0, 0, 0);
     float acc[8];
+    if constexpr (LOAD) {
+      const float4 a0 = *reinterpret_cast<const float4*>(acc_f32 + t * K + c);
+      const float4 a1 = *reinterpret_cast<const float4*>(acc_f32 + t * K + c + 4);
+      acc[0] = a0.x, acc[1] = a0.y, acc[2] = a0.z, acc[3] = a0.w;
+      acc[4] = a1.x, acc[5] = a1.y, acc[6] = a1.z, acc[7] = a1.w;
+    } else {
 #pragma unroll
-    for (int j = 0; j < 8; ++j) acc[j] = 0.0f;
+      for (int j = 0; j < 8; ++j) acc[j] = 0.0f;
+    }
 #pragma unroll
     for (int k = 0; k < KMAX; ++k) {
       if (pos[k] < 0) continue;  // bf16(0 * w) adds an exact zero
@@ -175,30 +191,50 @@ __global__ void kt_combine_sorted_kernel(const uint16_t* __restrict__ y, const i
         acc[2 * j + 1] += kt_bf2f((uint16_t)(u[j] >> 16)) * wk[k];
       }
     }
-    uint4 o;
-    o.x = kt_pack_bf2(acc[0], acc[1]);
-    o.y = kt_pack_bf2(acc[2], acc[3]);
-    o.z = kt_pack_bf2(acc[4], acc[5]);
-    o.w = kt_pack_bf2(acc[6], acc[7]);
-    *reinterpret_cast<uint4*>(res + t * K + c) = o;
+    if constexpr (STORE) {
+      *reinterpret_cast<float4*>(acc_f32 + t * K + c) = make_float4(acc[0], acc[1], acc[2], acc[3]);
+      *reinterpret_cast<float4*>(acc_f32 + t * K + c + 4) = make_float4(acc[4], acc[5], acc[6], acc[7]);
+    } else {
+      uint4 o;
+      o.x = kt_pack_bf2(acc[0], acc[1]);
+      o.y = kt_pack_bf2(acc[2], acc[3]);
+      o.z = kt_pack_bf2(acc[4], acc[5]);
+      o.w = kt_pack_bf2(acc[6], acc[7]);
+      *reinterpret_cast<uint4*>(res + t * K + c) = o;
+    }
   }
 }
 
+template <bool LOAD, bool STORE>
+static void launch_combine_sorted_mode(const uint16_t* y, const int32_t* route_pos, const float* w, int64_t T, int k,
+                                       int64_t K, uint16_t* res, float* acc, int threads, cudaStream_t s) {
+  if (k <= 4)
+    kt_combine_sorted_kernel<4, LOAD, STORE><<<(unsigned)T, threads, 0, s>>>(y, route_pos, w, T, k, K, res, acc);
+  else if (k <= 8)
+    kt_combine_sorted_kernel<8, LOAD, STORE><<<(unsigned)T, threads, 0, s>>>(y, route_pos, w, T, k, K, res, acc);
+  else if (k <= 16)
+    kt_combine_sorted_kernel<16, LOAD, STORE><<<(unsigned)T, threads, 0, s>>>(y, route_pos, w, T, k, K, res, acc);
+  else
+    kt_combine_sorted_kernel<32, LOAD, STORE><<<(unsigned)T, threads, 0, s>>>(y, route_pos, w, T, k, K, res, acc);
+}
+
 int kt_launch_combine_sorted(const uint16_t* y, const int32_t* route_pos, const float* w, int64_t T, int64_t top_k,
-                             int64_t K, uint16_t* res, cudaStream_t s) {
+                             int64_t K, uint16_t* res, cudaStream_t s, float* acc, int acc_flags) {
   if (T == 0) return 0;
   if (K % 8 || T > 0x7fffffff || top_k > 32) return -1;
+  const bool load = acc_flags & 1, store = acc_flags & 2;
+  if ((load || store) && (!acc || ((uintptr_t)acc & 15))) return -1;
   const int64_t vec = K / 8;
   const int threads = (int)(vec < 256 ? (vec + 31) / 32 * 32 : 256);
   const int k = (int)top_k;
-  if (k <= 4)
-    kt_combine_sorted_kernel<4><<<(unsigned)T, threads, 0, s>>>(y, route_pos, w, T, k, K, res);
-  else if (k <= 8)
-    kt_combine_sorted_kernel<8><<<(unsigned)T, threads, 0, s>>>(y, route_pos, w, T, k, K, res);
-  else if (k <= 16)
-    kt_combine_sorted_kernel<16><<<(unsigned)T, threads, 0, s>>>(y, route_pos, w, T, k, K, res);
+  if (load && store)
+    launch_combine_sorted_mode<true, true>(y, route_pos, w, T, k, K, res, acc, threads, s);
+  else if (load)
+    launch_combine_sorted_mode<true, false>(y, route_pos, w, T, k, K, res, acc, threads, s);
+  else if (store)
+    launch_combine_sorted_mode<false, true>(y, route_pos, w, T, k, K, res, acc, threads, s);
   else
-    kt_combine_sorted_kernel<32><<<(unsigned)T, threads, 0, s>>>(y, route_pos, w, T, k, K, res);
+    launch_combine_sorted_mode<false, false>(y, route_pos, w, T, k, K, res, acc, threads, s);
   return 0;
 }
 
@@ -428,13 +464,14 @@ int kt_launch_topk_grouped(const float* logits, const float* bias, int64_t T, in
 constexpr int kPermBlock = 1024;
 
 __global__ void __launch_bounds__(kPermBlock) kt_perm_hist_kernel(const int32_t* __restrict__ ids, int64_t routes,
-                                                                  int n_slots, int32_t* __restrict__ hist,
+                                                                  int n_slots, int id_base, int32_t* __restrict__ hist,
                                                                   int32_t* __restrict__ rank) {
   extern __shared__ int32_t sh[];
   for (int e = threadIdx.x; e < n_slots; e += blockDim.x) sh[e] = 0;
   __syncthreads();
   const int64_t p = (int64_t)blockIdx.x * kPermBlock + threadIdx.x;
-  const int32_t e = p < routes ? ids[p] : -1;
+  const int32_t e0 = p < routes ? ids[p] : -1;
+  const int32_t e = e0 >= id_base ? e0 - id_base : -1;  // slot of the id window [id_base, id_base + n_slots)
   const bool valid = e >= 0 && e < n_slots;
   const int lane = threadIdx.x & 31;
   const uint32_t peers = __match_any_sync(0xffffffffu, valid ? e : -1);
@@ -548,13 +585,13 @@ __global__ void __launch_bounds__(kPermBlock) kt_perm_scan_kernel(int32_t* __res
 }
 
 __global__ void __launch_bounds__(kPermBlock) kt_perm_scatter_kernel(const int32_t* __restrict__ ids, int64_t routes,
-                                                                     int top_k, int n_slots,
+                                                                     int top_k, int n_slots, int id_base,
                                                                      const int32_t* __restrict__ hist,
                                                                      int32_t* __restrict__ sorted_token,
                                                                      int32_t* __restrict__ route_pos) {
   const int64_t p = (int64_t)blockIdx.x * kPermBlock + threadIdx.x;
   if (p >= routes) return;
-  const int32_t e = ids[p];
+  const int32_t e = ids[p] >= id_base ? ids[p] - id_base : -1;
   if (e >= 0 && e < n_slots) {
     const int32_t pos = hist[(int64_t)blockIdx.x * n_slots + e] + route_pos[p];
     sorted_token[pos] = (int32_t)(p / top_k);
@@ -568,14 +605,16 @@ int64_t kt_permute_hist_ints(int64_t routes, int n_slots) { return ((routes + kP
 
 int kt_launch_permute(const int32_t* ids, int64_t routes, int top_k, int n_slots, int tile_tokens, int chunk_tiles,
                       int32_t* counts, int32_t* hist, int32_t* tiles, int32_t* n_tiles, int32_t* chunks,
-                      int32_t* sorted_token, int32_t* route_pos, cudaStream_t s) {
-  if (n_slots <= 0 || n_slots > kPermMaxSlots || chunk_tiles <= 0) return -1;
+                      int32_t* sorted_token, int32_t* route_pos, cudaStream_t s, int id_base) {
+  if (n_slots <= 0 || n_slots > kPermMaxSlots || chunk_tiles <= 0 || id_base < 0) return -1;
   const int nb = (int)((routes + kPermBlock - 1) / kPermBlock);
   if (nb > 0)
-    kt_perm_hist_kernel<<<nb, kPermBlock, n_slots * sizeof(int32_t), s>>>(ids, routes, n_slots, hist, route_pos);
+    kt_perm_hist_kernel<<<nb, kPermBlock, n_slots * sizeof(int32_t), s>>>(ids, routes, n_slots, id_base, hist,
+                                                                          route_pos);
   kt_perm_scan_kernel<<<1, kPermBlock, 0, s>>>(hist, nb, n_slots, tile_tokens, chunk_tiles, counts, tiles, n_tiles,
                                                chunks);
   if (nb > 0)
-    kt_perm_scatter_kernel<<<nb, kPermBlock, 0, s>>>(ids, routes, top_k, n_slots, hist, sorted_token, route_pos);
+    kt_perm_scatter_kernel<<<nb, kPermBlock, 0, s>>>(ids, routes, top_k, n_slots, id_base, hist, sorted_token,
+                                                     route_pos);
   return 0;
 }

@@ -15,6 +15,7 @@ LIB_PATH = LIB_DIR / "libkt_gguf_b200.so"
 
 KT_OK, KT_ERR_ARG, KT_ERR_TYPE, KT_ERR_WORKSPACE, KT_ERR_CUDA, KT_ERR_DEVICE = range(6)
 KT_DEV_OK, KT_DEV_TIMEOUT = 0, 1
+KT_ACC_LOAD, KT_ACC_STORE = 1, 2  # kt_moe_prefill_ex accumulator flags
 GGML_Q4_0, GGML_Q4_1, GGML_Q5_0, GGML_Q5_1, GGML_IQ4_NL = 2, 3, 6, 7, 20
 GGML_Q8_0, GGML_Q4_K, GGML_Q6_K, GGML_IQ3_S = 8, 12, 14, 21
 GGML_Q2_K, GGML_Q3_K, GGML_Q5_K, GGML_IQ4_XS = 10, 11, 13, 23
@@ -58,6 +59,8 @@ SIGNATURES = {
     "kt_moe_prefill": (_I, [_P, _I64, _I64, _I64, _P, _P, _I64, _P, _I, _P, _I, _I, _I, _P, _P, _SZ, _P]),
     "kt_moe_prefill_timed": (_I, [_P, _I64, _I64, _I64, _P, _P, _I64, _P, _I, _P, _I, _I, _I, _P, _P, _SZ, _P,
                                   ctypes.POINTER(_P)]),
+    "kt_moe_prefill_ex": (_I, [_P, _I64, _I64, _I64, _P, _P, _I64, _P, _I, _P, _I, _I, _I, _I, _P, _I, _P, _P, _SZ,
+                               _P]),
 }
 
 _lib = None

@@ -143,6 +143,16 @@ def moe_prefill(x, w13, w2, topk_ids, topk_weights, type13, type2, inter, table=
     address tables with table=True); topk_ids [T, k] int32 slot ids (-1: not resident);
     topk_weights [T, k] float32. `workspace` (uint8, optional) is reused when large enough.
     """
+    return moe_prefill_ex(x, w13, w2, topk_ids, topk_weights, type13, type2, inter, table=table, out=out,
+                          workspace=workspace)
+
+
+def moe_prefill_ex(x, w13, w2, topk_ids, topk_weights, type13, type2, inter, table=False, id_base=0, acc=None,
+                   acc_flags=0, out=None, workspace=None):
+    """moe_prefill over the expert group [id_base, id_base + S) (C ABI kt_moe_prefill_ex):
+    routes with other ids contribute nothing. acc (fp32 [T, K]) with acc_flags N.KT_ACC_LOAD
+    (start from acc) / N.KT_ACC_STORE (write the fp32 sum to acc, out not written) carries the
+    sum across groups; returns out (bf16) or, with KT_ACC_STORE, acc."""
     N.require_device(x)
     if x.dtype != torch.bfloat16:
         raise TypeError("the prefill path takes bf16 activations")
@@ -159,13 +169,19 @@ def moe_prefill(x, w13, w2, topk_ids, topk_weights, type13, type2, inter, table=
             raise ValueError("w13 shape does not match [S, 2*inter, row_bytes(K)]")
         if w2.shape[1] != K or w2.shape[2] != N.row_bytes(type2, inter):
             raise ValueError("w2 shape does not match [S, K, row_bytes(inter)]")
-    if out is None:
+    to_acc = bool(acc_flags & N.KT_ACC_STORE)
+    if acc_flags:
+        if acc is None or acc.dtype != torch.float32 or tuple(acc.shape) != (T, K) or not acc.is_contiguous():
+            raise ValueError("acc must be a contiguous float32 [tokens, hidden] tensor")
+    if out is None and not to_acc:
         out = torch.empty((T, K), dtype=torch.bfloat16, device=x.device)
     lib = N.load()
     need = lib.kt_moe_prefill_workspace_size(T, top_k, K, inter, n_slots)
     if workspace is None or workspace.numel() < need:
         workspace = N.workspace(need, x.device)
-    N.check(lib.kt_moe_prefill(N.ptr(x), T, K, inter, N.ptr(topk_ids.contiguous()), N.ptr(topk_weights.contiguous()), top_k,
-                               N.ptr(w13), type13, N.ptr(w2), type2, int(table), n_slots, N.ptr(out), N.ptr(workspace),
-                               workspace.numel(), N.stream_of(x)), "kt_moe_prefill")
-    return out
+    ids, wts = topk_ids.contiguous(), topk_weights.contiguous()
+    N.check(lib.kt_moe_prefill_ex(N.ptr(x), T, K, inter, N.ptr(ids), N.ptr(wts), top_k, N.ptr(w13), type13, N.ptr(w2),
+                                  type2, int(table), n_slots, int(id_base), N.ptr(acc) if acc is not None else None,
+                                  int(acc_flags), None if to_acc else N.ptr(out), N.ptr(workspace), workspace.numel(),
+                                  N.stream_of(x)), "kt_moe_prefill_ex")
+    return acc if to_acc else out
