@@ -68,6 +68,15 @@ def test_argument_errors_before_any_launch():
     for t in (2, 10, 11, 13, 23, 42, 16, 17, 18, 19, 22, 29):
         assert lib.kt_moe_prefill(P(16), 16, 2048, 512, P(16), P(16), 8, P(16), t, P(16), 14, 0, 64, P(16), P(16),
                                   1 << 40, None) == N.KT_ERR_TYPE
+    # the group call: negative id_base, unknown flags, a missing or misaligned accumulator
+    ex = lambda id_base, acc, flags, out: lib.kt_moe_prefill_ex(  # noqa: E731
+        P(16), 16, 2048, 512, P(16), P(16), 8, P(16), 12, P(16), 14, 0, 8, id_base, acc, flags, out, P(16), 1 << 40,
+        None)
+    assert ex(-1, None, 0, P(16)) == N.KT_ERR_ARG
+    assert ex(0, P(16), 4, P(16)) == N.KT_ERR_ARG
+    assert ex(0, None, N.KT_ACC_LOAD, P(16)) == N.KT_ERR_ARG
+    assert ex(0, P(8), N.KT_ACC_STORE, None) == N.KT_ERR_ARG
+    assert ex(0, None, 0, None) == N.KT_ERR_ARG  # no accumulator to write: out is needed
     rb = ctypes.c_int64()
     assert lib.kt_gguf_row_bytes(2, 2048, ctypes.byref(rb)) == N.KT_OK and rb.value == 64 * 18
     assert lib.kt_gguf_row_bytes(7, 512, ctypes.byref(rb)) == N.KT_OK and rb.value == 16 * 24
