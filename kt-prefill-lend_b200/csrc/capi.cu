@@ -61,7 +61,8 @@ VecWs vec_ws(void* ws, int64_t tokens, int64_t cols, int64_t routes, int n_slots
   VecWs v;
   v.status = c.take<int>(4);
   v.qx = c.take<uint8_t>((size_t)tokens * kt_q8_1_row_bytes(cols));
-  v.groups = c.take<int32_t>(1 + 3 * (size_t)(n_slots + 1));
+  // groups: at most one per route once slots are cut into pieces, else one per slot (+ zero)
+  v.groups = c.take<int32_t>(1 + 3 * (size_t)(n_slots + 1 + routes));
   v.order = c.take<int32_t>((size_t)routes);
   v.bytes = align_up(c.off, 256);
   return v;
@@ -79,11 +80,10 @@ int moe_vec(const void* x, int x_dtype, int64_t tokens, int64_t cols, const void
   if (ws_bytes < v.bytes) return KT_ERR_WORKSPACE;
   cudaStream_t s = S(stream);
   if (cudaMemsetAsync(v.status, 0, sizeof(int), s) != cudaSuccess) return KT_ERR_CUDA;
-  int rc = kt_launch_quantize_q8_1_split(x, x_dtype, tokens, cols, v.qx, s);
+  const int piece = kt_vec_ms_ok(type, (int)cols, routes) ? kt_vec_ms_piece() : 0;
+  int rc = kt_launch_quantize_group(x, x_dtype, tokens, cols, v.qx, ids, routes, n_slots, piece, v.groups, v.order, s);
   if (rc) return launch_rc(rc);
-  rc = kt_launch_group_routes(ids, routes, n_slots, v.groups, v.order, s);
-  if (rc) return launch_rc(rc);
-  const int max_groups = (int)(routes < (int64_t)n_slots + 1 ? routes : (int64_t)n_slots + 1);
+  const int max_groups = (int)(piece || routes < (int64_t)n_slots + 1 ? routes : (int64_t)n_slots + 1);
   rc = kt_launch_moe_vec(type, w, table, v.qx, kt_q8_1_row_bytes(cols), v.groups, v.order, max_groups, (int)top_k,
                          (int)rows, (int)cols, x_dtype, y, v.status, s);
   return launch_rc(rc);

@@ -606,6 +606,193 @@ __device__ __forceinline__ float kt_vec_dot(const uint8_t* bx, const uint8_t* yq
   return 0.0f;
 }
 
+// ------------------------------------------------------------------ member-stationary split
+// The chunk dot products of the north-star types cut in two: KtAct<TYPE> holds a chunk's
+// activation side for one member (q8_1 ints, the block scale, and the integer sums of the
+// q8_1 values that do not depend on the weights), KtWgt<TYPE> a chunk's weight side for one
+// row (codes, scales). kt_dot_split(w, a) evaluates the chunk's fp32 expression exactly as
+// kt_vec_dot does, so a kernel can load each member's side once for all its rows and each
+// row's side once for all its members and still produce the reference's sums bit for bit.
+template <int TYPE>
+struct KtAct;
+template <int TYPE>
+struct KtWgt;
+template <int TYPE>
+struct KtSplitOk {
+  static constexpr bool value = TYPE == KT_Q8_0 || TYPE == KT_Q4_K || TYPE == KT_Q6_K || TYPE == KT_IQ3_S;
+};
+
+template <>
+struct KtAct<KT_Q8_0> {
+  int u[2];
+  float d;
+};
+template <>
+struct KtWgt<KT_Q8_0> {
+  int v[2];
+  float d;
+};
+__device__ __forceinline__ void kt_act_load(KtAct<KT_Q8_0>& a, const uint8_t* yq, const uint8_t* yd, int iqs) {
+#pragma unroll
+  for (int i = 0; i < 2; ++i) a.u[i] = kt_ld_b4(yq + 4 * (iqs + i));
+  a.d = kt_q8_1_dd(yd);
+}
+__device__ __forceinline__ void kt_wgt_load(KtWgt<KT_Q8_0>& w, const uint8_t* bx, int iqs, const uint32_t*) {
+#pragma unroll
+  for (int i = 0; i < 2; ++i) w.v[i] = kt_ld_b2(bx + 2 + 4 * (iqs + i));
+  w.d = kt_h2f(*reinterpret_cast<const uint16_t*>(bx));
+}
+__device__ __forceinline__ float kt_dot_split(const KtWgt<KT_Q8_0>& w, const KtAct<KT_Q8_0>& a) {
+  int sumi = 0;
+#pragma unroll
+  for (int i = 0; i < 2; ++i) sumi = __dp4a(w.v[i], a.u[i], sumi);
+  return w.d * a.d * sumi;  // kt_vd_q8_0: d80 * d81 * sumi
+}
+
+template <>
+struct KtAct<KT_Q4_K> {
+  int u0[2], u1[2], s[2];  // s: sum of the chunk's 8 q8_1 values of block bq8_offset + i
+  float d8[2];
+};
+template <>
+struct KtWgt<KT_Q4_K> {
+  int v0[2], v1[2], sc[2], m[2];
+  float dx, dy;
+};
+__device__ __forceinline__ void kt_act_load(KtAct<KT_Q4_K>& a, const uint8_t* yq, const uint8_t* yd, int iqs) {
+  const int bq8_offset = 2 * ((iqs / 2) / 4);
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const uint8_t* q8 = yq + 32 * (bq8_offset + i);
+    a.d8[i] = kt_q8_1_dd(yd + 4 * (bq8_offset + i));
+    a.u0[i] = kt_ld_b4(q8 + 4 * ((iqs / 2) % 4));
+    a.u1[i] = kt_ld_b4(q8 + 4 * ((iqs / 2) % 4) + 16);
+    a.s[i] = __dp4a(0x01010101, a.u1[i], __dp4a(0x01010101, a.u0[i], 0));
+  }
+}
+__device__ __forceinline__ void kt_wgt_load(KtWgt<KT_Q4_K>& w, const uint8_t* bx, int iqs, const uint32_t*) {
+  const int bq8_offset = 2 * ((iqs / 2) / 4);
+  const uint8_t* q4 = bx + 16 + 16 * bq8_offset + 4 * ((iqs / 2) % 4);
+  const int v0 = kt_ld_b4(q4), v1 = kt_ld_b4(q4 + 16);
+  const uint16_t* s16 = reinterpret_cast<const uint16_t*>(bx + 4);
+  uint16_t aux0, aux1;
+  const int j = bq8_offset / 2;
+  if (j < 2) {
+    aux0 = s16[j + 0] & 0x3f3f;
+    aux1 = s16[j + 2] & 0x3f3f;
+  } else {
+    aux0 = ((s16[j + 2] >> 0) & 0x0f0f) | ((s16[j - 2] & 0xc0c0) >> 2);
+    aux1 = ((s16[j + 2] >> 4) & 0x0f0f) | ((s16[j - 0] & 0xc0c0) >> 2);
+  }
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    w.v0[i] = (v0 >> (4 * i)) & 0x0F0F0F0F;
+    w.v1[i] = (v1 >> (4 * i)) & 0x0F0F0F0F;
+    w.sc[i] = (i ? (aux0 >> 8) : aux0) & 0xff;
+    w.m[i] = (i ? (aux1 >> 8) : aux1) & 0xff;
+  }
+  const float2 dm = __half22float2(*reinterpret_cast<const half2*>(bx));
+  w.dx = dm.x;
+  w.dy = dm.y;
+}
+__device__ __forceinline__ float kt_dot_split(const KtWgt<KT_Q4_K>& w, const KtAct<KT_Q4_K>& a) {
+  float sumf_d = 0.0f, sumf_m = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const int dot1 = __dp4a(w.v1[i], a.u1[i], __dp4a(w.v0[i], a.u0[i], 0));
+    sumf_d += a.d8[i] * (dot1 * w.sc[i]);
+    sumf_m += a.d8[i] * (a.s[i] * w.m[i]);
+  }
+  return w.dx * sumf_d - w.dy * sumf_m;
+}
+
+template <>
+struct KtAct<KT_Q6_K> {
+  int u[2], s[2];
+  float d8[2];
+};
+template <>
+struct KtWgt<KT_Q6_K> {
+  int q[2], sc[2];
+  float d;
+};
+__device__ __forceinline__ void kt_act_load(KtAct<KT_Q6_K>& a, const uint8_t* yq, const uint8_t* yd, int iqs) {
+  const int bq8_offset = 4 * (iqs / 16) + (iqs % 16) / 8;
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    a.u[i] = kt_ld_b4(yq + 32 * (bq8_offset + 2 * i) + 4 * (iqs % 8));
+    a.d8[i] = kt_q8_1_dd(yd + 4 * (bq8_offset + 2 * i));
+    a.s[i] = __dp4a(0x01010101, a.u[i], 0);
+  }
+}
+__device__ __forceinline__ void kt_wgt_load(KtWgt<KT_Q6_K>& w, const uint8_t* bx, int iqs, const uint32_t*) {
+  const int scale_offset = 8 * (iqs / 16) + (iqs % 16) / 4;
+  const int vh_shift = 2 * ((iqs % 16) / 8);
+  const int vl = kt_ld_b2(bx + 4 * iqs);
+  const int vh = kt_ld_b2(bx + 128 + 4 * (8 * (iqs / 16) + iqs % 8)) >> vh_shift;
+  const int8_t* scales = reinterpret_cast<const int8_t*>(bx + 192 + scale_offset);
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    w.q[i] = ((vl >> (4 * i)) & 0x0F0F0F0F) | (((vh >> (4 * i)) << 4) & 0x30303030);
+    w.sc[i] = scales[4 * i];
+  }
+  w.d = kt_h2f(*reinterpret_cast<const uint16_t*>(bx + 208));
+}
+__device__ __forceinline__ float kt_dot_split(const KtWgt<KT_Q6_K>& w, const KtAct<KT_Q6_K>& a) {
+  float sumf = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const int dot = __dp4a(w.q[i], a.u[i], 0) - 32 * a.s[i];
+    sumf += a.d8[i] * (dot * w.sc[i]);
+  }
+  return w.d * sumf;
+}
+
+template <>
+struct KtAct<KT_IQ3_S> {
+  int q[8];
+  float d8;
+};
+template <>
+struct KtWgt<KT_IQ3_S> {
+  int g[8], m[8];
+  float dsc;  // d * (1 + 2 * scale)
+};
+__device__ __forceinline__ void kt_act_load(KtAct<KT_IQ3_S>& a, const uint8_t* yq, const uint8_t* yd, int ib32) {
+  const int4 a0 = *reinterpret_cast<const int4*>(yq + 32 * ib32);
+  const int4 a1 = *reinterpret_cast<const int4*>(yq + 32 * ib32 + 16);
+  a.q[0] = a0.x, a.q[1] = a0.y, a.q[2] = a0.z, a.q[3] = a0.w;
+  a.q[4] = a1.x, a.q[5] = a1.y, a.q[6] = a1.z, a.q[7] = a1.w;
+  a.d8 = kt_q8_1_dd(yd + 4 * ib32);
+}
+__device__ __forceinline__ void kt_wgt_load(KtWgt<KT_IQ3_S>& w, const uint8_t* bx, int ib32, const uint32_t* grid) {
+  const uint32_t qs0 = (uint32_t)kt_ld_b2(bx + 2 + 8 * ib32), qs1 = (uint32_t)kt_ld_b2(bx + 6 + 8 * ib32);
+  const uint32_t qh = bx[66 + ib32];
+  const uint32_t sg = (uint32_t)kt_ld_b2(bx + 74 + 4 * ib32);
+#pragma unroll
+  for (int l = 0; l < 4; ++l) {
+    const uint32_t wd = l < 2 ? qs0 : qs1;
+    const uint32_t b1 = (wd >> (16 * (l & 1))) & 0xff, b2 = (wd >> (16 * (l & 1) + 8)) & 0xff;
+    w.g[2 * l] = (int)grid[b1 | ((qh << (8 - 2 * l)) & 256)];
+    w.g[2 * l + 1] = (int)grid[b2 | ((qh << (7 - 2 * l)) & 256)];
+    const uint32_t sb = sg >> (8 * l);
+    w.m[2 * l] = (int)kt_nibble_mask(sb & 15);
+    w.m[2 * l + 1] = (int)kt_nibble_mask((sb >> 4) & 15);
+  }
+  w.dsc = kt_h2f(*reinterpret_cast<const uint16_t*>(bx)) * (1 + 2 * ((bx[106 + ib32 / 2] >> 4 * (ib32 % 2)) & 0xf));
+}
+__device__ __forceinline__ float kt_dot_split(const KtWgt<KT_IQ3_S>& w, const KtAct<KT_IQ3_S>& a) {
+  int sum_all = 0, sum_neg = 0;
+#pragma unroll
+  for (int l = 0; l < 8; ++l) {
+    sum_all = __dp4a(w.g[l], a.q[l], sum_all);
+    sum_neg = __dp4a(w.g[l] & w.m[l], a.q[l], sum_neg);
+  }
+  const int sumi = sum_all - 2 * sum_neg;
+  const float d = w.dsc * a.d8;
+  return d * sumi;
+}
+
 // ------------------------------------------------------------------ dequantization
 // Each function writes the fp32 values of 32 consecutive elements [32*sub, 32*sub + 32)
 // of one block, with ggml's operation order (products that are exact in fp32 first, one

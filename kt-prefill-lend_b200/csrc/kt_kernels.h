@@ -26,8 +26,16 @@ struct KtGemmArgs {
 int kt_launch_quantize_q8_1(const void* x, int dtype, int64_t rows, int64_t cols, void* qx, cudaStream_t s);
 // the same values in the GEMV's split layout: a row's int8 values, then its half2 (d, s) per block
 int kt_launch_quantize_q8_1_split(const void* x, int dtype, int64_t rows, int64_t cols, void* qx, cudaStream_t s);
+// piece > 0 (a power of two): a slot's routes are cut into groups of piece, then powers of two
 int kt_launch_group_routes(const int32_t* ids, int64_t routes, int n_slots, int32_t* groups, int32_t* order,
-                           cudaStream_t s);
+                           cudaStream_t s, int piece = 0);
+// the GEMV runs its member-stationary kernel for this type, width and route count (group with
+// piece 8; kt_launch_moe_vec then takes max_groups = routes)
+bool kt_vec_ms_ok(int type, int cols, int64_t routes);
+int kt_vec_ms_piece();
+// split-layout q8_1 quantization and route grouping in one launch
+int kt_launch_quantize_group(const void* x, int dtype, int64_t rows, int64_t cols, void* qx, const int32_t* ids,
+                             int64_t routes, int n_slots, int piece, int32_t* groups, int32_t* order, cudaStream_t s);
 int kt_launch_moe_vec(int type, const void* w, int table, const void* qx, int64_t qrow, const int32_t* groups,
                       const int32_t* order, int max_groups, int top_k, int rows, int cols, int dtype, void* y,
                       int* status, cudaStream_t s);

@@ -73,55 +73,168 @@ int kt_launch_quantize_q8_1_split(const void* x, int dtype, int64_t rows, int64_
 
 // ------------------------------------------------------------------ route grouping
 // One CTA: counting sort of the routes by expert slot. Routes with an id outside
-// [0, n_slots) form the "zero" group (slot -1). Outputs, in the workspace:
+// [0, n_slots) form the "zero" group (slot -1). With piece > 0 (a power of two) a slot's c
+// routes are cut into groups of `piece` routes and then the binary parts of the rest
+// (c = 13, piece 8: 8, 4, 1), so that a kernel can run each group with a compile-time member
+// count; the zero group stays whole. Outputs, in the workspace:
 //   groups[0]            number of groups G
 //   groups[1 + 3g + 0]   slot of group g (-1 for the zero group)
 //   groups[1 + 3g + 1]   first position of the group in `order`
 //   groups[1 + 3g + 2]   routes in the group
-//   order[R]             route indices grouped by slot
-// Order inside a group is not fixed (atomics); every route's result is independent of it.
+//   order[R]             route indices grouped by slot (a slot's groups are consecutive)
+// Order inside a slot is not fixed (atomics); every route's result is independent of it.
 
-__global__ void __launch_bounds__(1024) kt_group_routes_kernel(const int32_t* __restrict__ ids, int64_t routes,
-                                                               int n_slots, int32_t* __restrict__ groups,
-                                                               int32_t* __restrict__ order) {
-  extern __shared__ int32_t cnt[];  // n_slots + 1 counters, then n_slots + 1 cursors
+__device__ __forceinline__ int kt_group_pieces(int i, int c, int piece) {
+  if (c == 0) return 0;
+  if (i == 0 || piece == 0) return 1;
+  return c / piece + __popc(c % piece);
+}
+
+// the whole CTA groups; cnt: 2 * (n_slots + 1) ints of shared memory
+__device__ __forceinline__ void kt_group_routes_body(const int32_t* __restrict__ ids, int64_t routes, int n_slots,
+                                                     int piece, int32_t* __restrict__ groups,
+                                                     int32_t* __restrict__ order, int32_t* cnt) {
+  __shared__ int32_t wsum[2][32];
   int32_t* cur = cnt + (n_slots + 1);
-  for (int i = threadIdx.x; i < n_slots + 1; i += blockDim.x) cnt[i] = 0;
+  const int n = n_slots + 1;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) cnt[i] = 0;
   __syncthreads();
   for (int64_t p = threadIdx.x; p < routes; p += blockDim.x) {
     const int32_t e = ids[p];
     atomicAdd(&cnt[(e >= 0 && e < n_slots) ? e + 1 : 0], 1);
   }
   __syncthreads();
-  if (threadIdx.x == 0) {
-    int32_t off = 0, g = 0;
-    for (int i = 0; i < n_slots + 1; ++i) {
-      const int32_t c = cnt[i];
-      cur[i] = off;
-      if (c) {
-        groups[1 + 3 * g + 0] = i - 1;
-        groups[1 + 3 * g + 1] = off;
-        groups[1 + 3 * g + 2] = c;
-        ++g;
-      }
-      off += c;
+  // each thread owns consecutive counters [b, e): local totals, then block-wide exclusive
+  // scans of the route counts (order offsets) and of the group counts (group indices)
+  const int per = (n + (int)blockDim.x - 1) / (int)blockDim.x;
+  const int b = min(n, (int)threadIdx.x * per), e = min(n, b + per);
+  int c_sum = 0, g_sum = 0;
+  for (int i = b; i < e; ++i) {
+    c_sum += cnt[i];
+    g_sum += kt_group_pieces(i, cnt[i], piece);
+  }
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  int cx = c_sum, gx = g_sum;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int cy = __shfl_up_sync(0xffffffffu, cx, o), gy = __shfl_up_sync(0xffffffffu, gx, o);
+    if (lane >= o) cx += cy, gx += gy;
+  }
+  if (lane == 31) wsum[0][wid] = cx, wsum[1][wid] = gx;
+  __syncthreads();
+  if (wid == 0) {
+    int cw = wsum[0][lane], gw = wsum[1][lane];
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int cy = __shfl_up_sync(0xffffffffu, cw, o), gy = __shfl_up_sync(0xffffffffu, gw, o);
+      if (lane >= o) cw += cy, gw += gy;
     }
-    groups[0] = g;
+    wsum[0][lane] = cw, wsum[1][lane] = gw;
   }
   __syncthreads();
+  int c_off = cx - c_sum + (wid ? wsum[0][wid - 1] : 0);
+  int g_off = gx - g_sum + (wid ? wsum[1][wid - 1] : 0);
+  for (int i = b; i < e; ++i) {
+    const int c = cnt[i];
+    cur[i] = c_off;
+    if (c) {
+      int first = c_off, left = c;
+      auto emit = [&](int k) {
+        groups[1 + 3 * g_off + 0] = i - 1;
+        groups[1 + 3 * g_off + 1] = first;
+        groups[1 + 3 * g_off + 2] = k;
+        ++g_off;
+        first += k;
+        left -= k;
+      };
+      if (i == 0 || piece == 0) {
+        emit(c);
+      } else {
+        while (left >= piece) emit(piece);
+        for (int bit = piece >> 1; bit > 0; bit >>= 1)
+          if (left & bit) emit(bit);
+      }
+    }
+    c_off += c;
+  }
+  if (threadIdx.x == blockDim.x - 1) groups[0] = g_off;
+  __syncthreads();
   for (int64_t p = threadIdx.x; p < routes; p += blockDim.x) {
-    const int32_t e = ids[p];
-    const int k = (e >= 0 && e < n_slots) ? e + 1 : 0;
+    const int32_t e2 = ids[p];
+    const int k = (e2 >= 0 && e2 < n_slots) ? e2 + 1 : 0;
     order[atomicAdd(&cur[k], 1)] = (int32_t)p;
   }
 }
 
-int kt_launch_group_routes(const int32_t* ids, int64_t routes, int n_slots, int32_t* groups, int32_t* order,
-                           cudaStream_t s) {
+__global__ void __launch_bounds__(1024) kt_group_routes_kernel(const int32_t* __restrict__ ids, int64_t routes,
+                                                               int n_slots, int piece, int32_t* __restrict__ groups,
+                                                               int32_t* __restrict__ order) {
+  extern __shared__ int32_t cnt[];  // n_slots + 1 counters, then n_slots + 1 cursors
+  kt_group_routes_body(ids, routes, n_slots, piece, groups, order, cnt);
+}
+
+// The GEMV's two preparation steps in one launch: blocks [0, nqb) quantize the activations
+// into the split q8_1 layout (256 columns of a row each, as kt_quantize_q8_1_kernel), block nqb
+// groups the routes. Saves a launch on the decode path, where the GEMV itself is short.
+template <int DT>
+__global__ void __launch_bounds__(256) kt_quantize_group_kernel(const void* __restrict__ x, uint8_t* __restrict__ qx,
+                                                                int64_t rows, int64_t cols, int64_t kpad, int64_t nqb,
+                                                                const int32_t* __restrict__ ids, int64_t routes,
+                                                                int n_slots, int piece, int32_t* __restrict__ groups,
+                                                                int32_t* __restrict__ order) {
+  extern __shared__ int32_t cnt[];
+  if ((int64_t)blockIdx.x == nqb) {
+    kt_group_routes_body(ids, routes, n_slots, piece, groups, order, cnt);
+    return;
+  }
+  const int64_t cbx = kpad / 256;
+  const int64_t row = (int64_t)blockIdx.x / cbx;
+  const int64_t ix = ((int64_t)blockIdx.x % cbx) * 256 + threadIdx.x;
+  if (row >= rows) return;
+  const float xi = ix < cols ? kt_load_act<DT>(x, row * cols + ix) : 0.0f;
+  float amax = fabsf(xi), sum = xi;
+#pragma unroll
+  for (int mask = 16; mask > 0; mask >>= 1) {
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, mask, 32));
+    sum += __shfl_xor_sync(0xffffffffu, sum, mask, 32);
+  }
+  const float d = amax / 127;
+  const int8_t q = amax == 0.0f ? 0 : (int8_t)roundf(xi / d);
+  uint8_t* rowp = qx + row * (kpad / 32 * KT_Q8_1_BYTES);
+  rowp[ix] = (uint8_t)q;
+  if (ix % 32 == 0) *reinterpret_cast<half2*>(rowp + kpad + 4 * (ix / 32)) = __halves2half2(__float2half(d), __float2half(sum));
+}
+
+int kt_launch_quantize_group(const void* x, int dtype, int64_t rows, int64_t cols, void* qx, const int32_t* ids,
+                             int64_t routes, int n_slots, int piece, int32_t* groups, int32_t* order, cudaStream_t s) {
   const size_t smem = sizeof(int32_t) * 2 * (size_t)(n_slots + 1);
-  if (smem > 200 * 1024) return -1;
+  if (rows <= 0 || smem > 200 * 1024 || piece < 0 || (piece & (piece - 1))) return -1;
+  const int64_t kpad = (cols + 511) / 512 * 512;
+  const int64_t nqb = rows * (kpad / 256);
+  if (nqb + 1 > 0x7fffffff) return -1;
+  switch (dtype) {
+#define KT_QG_LAUNCH(DT)                                                                                          \
+  {                                                                                                               \
+    auto k = kt_quantize_group_kernel<DT>;                                                                        \
+    if (smem > 48 * 1024) cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);        \
+    k<<<(unsigned)(nqb + 1), 256, smem, s>>>(x, (uint8_t*)qx, rows, cols, kpad, nqb, ids, routes, n_slots, piece, \
+                                             groups, order);                                                      \
+    return 0;                                                                                                     \
+  }
+    case KT_DT_F32: KT_QG_LAUNCH(KT_DT_F32)
+    case KT_DT_F16: KT_QG_LAUNCH(KT_DT_F16)
+    case KT_DT_BF16: KT_QG_LAUNCH(KT_DT_BF16)
+#undef KT_QG_LAUNCH
+  }
+  return -1;
+}
+
+int kt_launch_group_routes(const int32_t* ids, int64_t routes, int n_slots, int32_t* groups, int32_t* order,
+                           cudaStream_t s, int piece) {
+  const size_t smem = sizeof(int32_t) * 2 * (size_t)(n_slots + 1);
+  if (smem > 200 * 1024 || piece < 0 || (piece & (piece - 1))) return -1;
   if (smem > 48 * 1024) cudaFuncSetAttribute(kt_group_routes_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  kt_group_routes_kernel<<<1, 1024, smem, s>>>(ids, routes, n_slots, groups, order);
+  kt_group_routes_kernel<<<1, 1024, smem, s>>>(ids, routes, n_slots, piece, groups, order);
   return 0;
 }
 
@@ -367,6 +480,102 @@ __global__ void __launch_bounds__(256) kt_moe_vec_pipe_kernel(const KtVecArgs a)
   (void)ok;
 }
 
+// Member-stationary kernel for the north-star types (KtSplitOk): groups of 1, 2, 4 or 8
+// routes of one slot (kt_group_routes with piece 8) times row tiles of 8R rows are the work
+// items of a persistent grid. A warp owns R rows of the tile; its lanes walk the chunks of a
+// row as the reference does (lane t: chunks t, t+32, ...), but for each chunk they load the
+// members' activation side once (KtAct: q8_1 ints, scales and the row-independent integer
+// sums) and each row's weight side once (KtWgt), and combine every (row, member) pair with the
+// chunk's own fp32 expression (kt_dot_split). Per-lane sums run in chunk order and end in the
+// same xor butterfly, so every route's result is the reference's bit for bit; the saving is
+// the activation work per row and the weight work per member.
+template <int TYPE, int DT, int R, int WM>
+__device__ __forceinline__ void kt_ms_item(const KtVecArgs& a, const uint8_t* wbase, int start, int r0,
+                                           const uint32_t* grid) {
+  using C = KtChunk<TYPE>;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const uint8_t* yrow[WM];
+#pragma unroll
+  for (int m = 0; m < WM; ++m) yrow[m] = a.qx + (int64_t)(a.order[start + m] / a.top_k) * a.qrow;
+  float acc[R][WM];
+#pragma unroll
+  for (int j = 0; j < R; ++j)
+#pragma unroll
+    for (int m = 0; m < WM; ++m) acc[j][m] = 0.0f;
+  const int nchunks = (a.cols / C::QK) * C::CPB;
+  const int rbase = r0 + warp * R;
+  for (int c = lane; c < nchunks; c += 32) {
+    const int i = c / C::CPB, iqs = C::VDR * (c % C::CPB);
+    const int64_t qb = (int64_t)i * (C::QK / 32);  // first q8_1 block of the chunk
+    KtAct<TYPE> act[WM];
+#pragma unroll
+    for (int m = 0; m < WM; ++m) kt_act_load(act[m], yrow[m] + 32 * qb, yrow[m] + a.kpad + 4 * qb, iqs);
+#pragma unroll
+    for (int j = 0; j < R; ++j) {
+      const int r = rbase + j;
+      if (r < a.rows) {
+        KtWgt<TYPE> w;
+        kt_wgt_load(w, wbase + (int64_t)r * a.row_bytes + (int64_t)i * C::BYTES, iqs, grid);
+#pragma unroll
+        for (int m = 0; m < WM; ++m) acc[j][m] += kt_dot_split(w, act[m]);
+      }
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < R; ++j)
+#pragma unroll
+    for (int m = 0; m < WM; ++m) {
+      float t = acc[j][m];
+#pragma unroll
+      for (int mask = 16; mask > 0; mask >>= 1) t += __shfl_xor_sync(0xffffffffu, t, mask);
+      if (lane == 0 && rbase + j < a.rows) kt_store_act<DT>(a.y, (int64_t)a.order[start + m] * a.rows + rbase + j, t);
+    }
+}
+
+// WMAX 8: two CTAs per SM (128 registers); WMAX 4: three (85 registers), more warps to hide
+// the loads
+template <int TYPE, int DT, int R, int WMAX>
+__global__ void __launch_bounds__(256, WMAX >= 8 ? 2 : 3) kt_moe_vec_ms_kernel(const KtVecArgs a) {
+  __shared__ uint32_t grid_s[KtGridSmem<TYPE>::WORDS];
+  if constexpr (kt_grid_words(TYPE) > 0) {
+    kt_stage_grid<TYPE>(grid_s, threadIdx.x, blockDim.x);
+    __syncthreads();
+  }
+  constexpr int kRows = 8 * R;
+  const int tiles = (a.rows + kRows - 1) / kRows;
+  const int n_items = a.groups[0] * tiles;
+  for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
+    const int g = item / tiles, r0 = (item % tiles) * kRows;
+    const int slot = a.groups[1 + 3 * g + 0];
+    const int start = a.groups[1 + 3 * g + 1];
+    const int count = a.groups[1 + 3 * g + 2];
+    if (slot < 0) {  // routes not on this device: zero rows
+      const int nr = min(kRows, a.rows - r0);
+      for (int64_t i = threadIdx.x; i < (int64_t)count * nr; i += blockDim.x) {
+        const int p = a.order[start + i / nr];
+        kt_store_act<DT>(a.y, (int64_t)p * a.rows + r0 + i % nr, 0.0f);
+      }
+      continue;
+    }
+    const uint8_t* wbase = a.table ? reinterpret_cast<const uint8_t*>(reinterpret_cast<const int64_t*>(a.w)[slot])
+                                   : a.w + (int64_t)slot * a.rows * a.row_bytes;
+    switch (count) {
+      case 8:
+        if constexpr (WMAX >= 8) {
+          kt_ms_item<TYPE, DT, R, 8>(a, wbase, start, r0, grid_s);
+        } else {  // not produced with piece WMAX; two halves if it were
+          kt_ms_item<TYPE, DT, R, 4>(a, wbase, start, r0, grid_s);
+          kt_ms_item<TYPE, DT, R, 4>(a, wbase, start + 4, r0, grid_s);
+        }
+        break;
+      case 4: kt_ms_item<TYPE, DT, R, 4>(a, wbase, start, r0, grid_s); break;
+      case 2: kt_ms_item<TYPE, DT, R, 2>(a, wbase, start, r0, grid_s); break;
+      default:  // 1 (any other count only if the groups were not cut in powers of two)
+        for (int m = 0; m < count; ++m) kt_ms_item<TYPE, DT, R, 1>(a, wbase, start + m, r0, grid_s);
+    }
+  }
+}
+
 static int vec_num_sms() {
   static int n = 0;
   if (!n) {
@@ -404,6 +613,70 @@ static int launch_vec_t(const KtVecArgs& a, int max_groups, int lpr, size_t smem
     k<<<grid, 256, smem, s>>>(a);
   }
   return 0;
+}
+
+// routes per group of the member-stationary kernel (4 or 8; KT_B200_VEC_MS_PIECE for tuning)
+int kt_vec_ms_piece() {
+  static const int p = [] {
+    const char* e = getenv("KT_B200_VEC_MS_PIECE");
+    return e && atoi(e) == 4 ? 4 : 8;
+  }();
+  return p;
+}
+
+// the member-stationary kernel: two rows per warp once there are enough routes to share them,
+// for the types whose two-row variant fits the 128-register cap that keeps two CTAs on an SM
+// without spilling (Q8_0, Q4_K; Q6_K and IQ3_S keep one row)
+template <int TYPE, int DT>
+static int launch_ms(const KtVecArgs& a, int max_groups, cudaStream_t s) {
+  static const int forced = [] {  // KT_B200_VEC_MS_R=1|2: rows per warp for tuning runs
+    const char* e = getenv("KT_B200_VEC_MS_R");
+    return e ? atoi(e) : 0;
+  }();
+  const int R = forced == 1 || forced == 2 || forced == 4 ? forced
+                                                          : (max_groups >= 64 && (TYPE == KT_Q8_0 || TYPE == KT_Q4_K)) ? 2 : 1;
+  const int64_t tiles = (a.rows + 8 * R - 1) / (8 * R);
+  const int64_t items = (int64_t)max_groups * tiles, cap = 8 * (int64_t)vec_num_sms();
+  const unsigned grid = (unsigned)(items < cap ? (items > 0 ? items : 1) : cap);
+  const int wmax = kt_vec_ms_piece();
+#define KT_MS_LAUNCH(RR, WW) kt_moe_vec_ms_kernel<TYPE, DT, RR, WW><<<grid, 256, 0, s>>>(a)
+  if (wmax == 4) {
+    if (R == 4) KT_MS_LAUNCH(4, 4);
+    else if (R == 2) KT_MS_LAUNCH(2, 4);
+    else KT_MS_LAUNCH(1, 4);
+  } else {
+    if (R == 4) KT_MS_LAUNCH(4, 8);
+    else if (R == 2) KT_MS_LAUNCH(2, 8);
+    else KT_MS_LAUNCH(1, 8);
+  }
+#undef KT_MS_LAUNCH
+  return 0;
+}
+
+template <int TYPE>
+static int launch_ms_dt(const KtVecArgs& a, int dtype, int max_groups, cudaStream_t s) {
+  switch (dtype) {
+    case KT_DT_F32: return launch_ms<TYPE, KT_DT_F32>(a, max_groups, s);
+    case KT_DT_F16: return launch_ms<TYPE, KT_DT_F16>(a, max_groups, s);
+    case KT_DT_BF16: return launch_ms<TYPE, KT_DT_BF16>(a, max_groups, s);
+  }
+  return -1;
+}
+
+// whether kt_launch_moe_vec runs the member-stationary kernel for this type, width and number
+// of routes (then the routes must be grouped with piece 8): Q8_0 and Q4_K rows of more than 16
+// chunks (32 lanes per row), 64 routes or more, unless KT_B200_VEC_MS=0. Q6_K and IQ3_S (split written, KtSplitOk) measured slower on
+// it than on the staged kernels (one row per warp for them: more rows spill), so they keep those.
+bool kt_vec_ms_ok(int type, int cols, int64_t routes) {
+  if (routes < 64) return false;  // fewer routes: the staged kernels are quicker (measured)
+  static const bool on = [] {
+    const char* e = getenv("KT_B200_VEC_MS");
+    return !(e && e[0] == '0');
+  }();
+  if (!on) return false;
+  const int cpb = type == KT_Q8_0 ? KtChunk<KT_Q8_0>::CPB : type == KT_Q4_K ? KtChunk<KT_Q4_K>::CPB : 0;
+  const KtBlockInfo bi = kt_block_info(type);
+  return cpb > 0 && bi.qk > 0 && cols % bi.qk == 0 && (int64_t)cols / bi.qk * cpb > 16;
 }
 
 template <int TYPE>
@@ -451,6 +724,13 @@ int kt_launch_moe_vec(int type, const void* w, int table, const void* qx, int64_
   a.cols = cols;
   a.row_bytes = (int64_t)cols / bi.qk * bi.bytes;
   a.status = status;
+  a.y = y;
+  if (kt_vec_ms_ok(type, cols, max_groups)) {  // grouped with piece 8: max_groups = routes
+    switch (type) {
+      case KT_Q8_0: return launch_ms_dt<KT_Q8_0>(a, dtype, max_groups, s);
+      case KT_Q4_K: return launch_ms_dt<KT_Q4_K>(a, dtype, max_groups, s);
+    }
+  }
   const int pipe_rows = pick_pipe_rows(a.row_bytes, rows, w, table);
   a.rows_per_cta = pipe_rows ? pipe_rows : pick_rows_per_cta(a.row_bytes, rows);
   a.tiles_per_group = pipe_rows ? rows / pipe_rows : 0;
@@ -458,7 +738,6 @@ int kt_launch_moe_vec(int type, const void* w, int table, const void* qx, int64_
   int mpp = 8;
   while (mpp > 1 && wt_bytes + mpp * qrow > 200 * 1024) mpp /= 2;
   a.members_per_pass = mpp;
-  a.y = y;
   const size_t smem = (size_t)(wt_bytes + mpp * qrow);
   if (smem + 4 * (size_t)kt_grid_words(type) > 222 * 1024) return -2;  // + the static code book
   const int chunks_per_block = type == KT_Q8_0     ? KtChunk<KT_Q8_0>::CPB

@@ -71,6 +71,8 @@ _device_checked = set()
 def load(path=None) -> ctypes.CDLL:
     """Loads the library (once) and declares every C ABI signature."""
     global _lib
+    if _lib is not None and path is None:  # the per-call path: no lock once loaded
+        return _lib
     with _lock:
         if _lib is not None and path is None:
             return _lib
@@ -102,7 +104,13 @@ def ptr(t) -> int:
     return 0 if t is None else t.data_ptr()
 
 
+_raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+
+
 def stream_of(t: torch.Tensor) -> int:
+    """cudaStream_t of the current stream on t's device"""
+    if _raw_stream is not None:
+        return _raw_stream(t.device.index if t.device.index is not None else torch.cuda.current_device())
     return torch.cuda.current_stream(t.device).cuda_stream
 
 
@@ -125,10 +133,17 @@ def dtype_code(t: torch.Tensor) -> int:
         raise TypeError(f"activation dtype {t.dtype} is not float32/float16/bfloat16") from None
 
 
+_row_bytes_cache: dict = {}
+
+
 def row_bytes(qtype: int, cols: int) -> int:
-    out = ctypes.c_int64(0)
-    check(load().kt_gguf_row_bytes(qtype, cols, ctypes.byref(out)), "kt_gguf_row_bytes")
-    return out.value
+    key = (qtype, cols)
+    v = _row_bytes_cache.get(key)
+    if v is None:
+        out = ctypes.c_int64(0)
+        check(load().kt_gguf_row_bytes(qtype, cols, ctypes.byref(out)), "kt_gguf_row_bytes")
+        v = _row_bytes_cache[key] = out.value
+    return v
 
 
 def workspace(nbytes: int, device) -> torch.Tensor:

@@ -72,6 +72,10 @@ def _check_common(X, W, ids, qtype, table):
             raise ValueError("X, W and ids must be on the same device")
 
 
+_ws_sizes: dict = {}
+_entries: dict = {}
+
+
 def _vec(entry, X, W, ids, top_k, qtype, rows, tokens, table):
     _check_common(X, W, ids, qtype, table)
     X = X.contiguous()
@@ -84,15 +88,25 @@ def _vec(entry, X, W, ids, top_k, qtype, rows, tokens, table):
     if not table and W.shape[2] != N.row_bytes(qtype, cols):
         raise ValueError(f"W row bytes {W.shape[2]} do not match type {qtype} at {cols} columns")
     n_slots = W.numel() if table else W.shape[0]
-    Y = torch.empty((tokens * top_k, rows), dtype=X.dtype, device=X.device)
     if tokens == 0:
-        return Y
+        return torch.empty((0, rows), dtype=X.dtype, device=X.device)
     lib = N.load()
-    ws_bytes = lib.kt_moe_a8_vec_workspace_size(tokens, cols, tokens * top_k, n_slots)
-    ws = N.workspace(ws_bytes, X.device)
-    fn = getattr(lib, entry)
-    N.check(fn(N.ptr(X), N.dtype_code(X), tokens, cols, N.ptr(W), int(table), n_slots, N.ptr(ids), top_k, qtype, rows,
-               N.ptr(Y), N.ptr(ws), ws.numel(), N.stream_of(X)), entry)
+    key = (tokens, cols, tokens * top_k, n_slots)
+    ws_bytes = _ws_sizes.get(key)
+    if ws_bytes is None:
+        ws_bytes = _ws_sizes[key] = max(256, int(lib.kt_moe_a8_vec_workspace_size(tokens, cols, tokens * top_k,
+                                                                                 n_slots)))
+    # Y and the call's scratch in one allocation (Y first, the scratch 256-byte aligned after it)
+    y_bytes = tokens * top_k * rows * X.element_size()
+    y_pad = (y_bytes + 255) & ~255
+    buf = torch.empty(y_pad + ws_bytes, dtype=torch.uint8, device=X.device)
+    Y = buf[:y_bytes].view(X.dtype).view(tokens * top_k, rows)
+    fn = _entries.get(entry)
+    if fn is None:
+        fn = _entries[entry] = getattr(lib, entry)
+    base = buf.data_ptr()
+    N.check(fn(X.data_ptr(), N.dtype_code(X), tokens, cols, W.data_ptr(), int(table), n_slots, ids.data_ptr(), top_k,
+               qtype, rows, base, base + y_pad, ws_bytes, N.stream_of(X)), entry)
     return Y
 
 
