@@ -532,8 +532,7 @@ __device__ __forceinline__ void kt_ms_item(const KtVecArgs& a, const uint8_t* wb
     }
 }
 
-// WMAX 8: two CTAs per SM (128 registers); WMAX 4: three (85 registers), more warps to hide
-// the loads
+// WMAX 8: two CTAs per SM (128 registers); WMAX 4: three (80), more warps to hide the loads
 template <int TYPE, int DT, int R, int WMAX>
 __global__ void __launch_bounds__(256, WMAX >= 8 ? 2 : 3) kt_moe_vec_ms_kernel(const KtVecArgs a) {
   __shared__ uint32_t grid_s[KtGridSmem<TYPE>::WORDS];
@@ -563,12 +562,18 @@ __global__ void __launch_bounds__(256, WMAX >= 8 ? 2 : 3) kt_moe_vec_ms_kernel(c
       case 8:
         if constexpr (WMAX >= 8) {
           kt_ms_item<TYPE, DT, R, 8>(a, wbase, start, r0, grid_s);
-        } else {  // not produced with piece WMAX; two halves if it were
-          kt_ms_item<TYPE, DT, R, 4>(a, wbase, start, r0, grid_s);
-          kt_ms_item<TYPE, DT, R, 4>(a, wbase, start + 4, r0, grid_s);
+        } else {  // not produced with piece WMAX; in parts of WMAX if it were
+          for (int m = 0; m < 8; m += WMAX) kt_ms_item<TYPE, DT, R, WMAX>(a, wbase, start + m, r0, grid_s);
         }
         break;
-      case 4: kt_ms_item<TYPE, DT, R, 4>(a, wbase, start, r0, grid_s); break;
+      case 4:
+        if constexpr (WMAX >= 4) {
+          kt_ms_item<TYPE, DT, R, 4>(a, wbase, start, r0, grid_s);
+        } else {
+          kt_ms_item<TYPE, DT, R, 2>(a, wbase, start, r0, grid_s);
+          kt_ms_item<TYPE, DT, R, 2>(a, wbase, start + 2, r0, grid_s);
+        }
+        break;
       case 2: kt_ms_item<TYPE, DT, R, 2>(a, wbase, start, r0, grid_s); break;
       default:  // 1 (any other count only if the groups were not cut in powers of two)
         for (int m = 0; m < count; ++m) kt_ms_item<TYPE, DT, R, 1>(a, wbase, start + m, r0, grid_s);
@@ -615,40 +620,44 @@ static int launch_vec_t(const KtVecArgs& a, int max_groups, int lpr, size_t smem
   return 0;
 }
 
-// routes per group of the member-stationary kernel (4 or 8; KT_B200_VEC_MS_PIECE for tuning)
+// routes per group of the member-stationary kernel: 4 (KT_B200_VEC_MS_PIECE=8 for tuning runs).
+// Measured on config 2's Q4_K gate/up (CUDA-graph replays, B200): groups of 4 at three CTAs per
+// SM beat groups of 8 at two (M=64: 156 vs 186 us with eight rows per warp).
 int kt_vec_ms_piece() {
   static const int p = [] {
     const char* e = getenv("KT_B200_VEC_MS_PIECE");
-    return e && atoi(e) == 4 ? 4 : 8;
+    return e && atoi(e) == 8 ? 8 : 4;
   }();
   return p;
 }
 
-// the member-stationary kernel: two rows per warp once there are enough routes to share them,
-// for the types whose two-row variant fits the 128-register cap that keeps two CTAs on an SM
-// without spilling (Q8_0, Q4_K; Q6_K and IQ3_S keep one row)
+// the member-stationary kernel's rows per warp: 8 from 64 routes, else 4 (KT_B200_VEC_MS_R=1|2|4|8
+// for tuning runs). Measured on config 2's Q4_K gate/up against the reference kernel (graph
+// replays): M=4 (31 routes) 22.6 us with 4 rows (24.7 reference), M=16 51.3 us and M=64 155.8 us
+// with 8 (53.7 and 188.6); 16 rows spill and lose (187 us at M=64).
 template <int TYPE, int DT>
 static int launch_ms(const KtVecArgs& a, int max_groups, cudaStream_t s) {
-  static const int forced = [] {  // KT_B200_VEC_MS_R=1|2: rows per warp for tuning runs
+  static const int forced = [] {
     const char* e = getenv("KT_B200_VEC_MS_R");
     return e ? atoi(e) : 0;
   }();
-  const int R = forced == 1 || forced == 2 || forced == 4 ? forced
-                                                          : (max_groups >= 64 && (TYPE == KT_Q8_0 || TYPE == KT_Q4_K)) ? 2 : 1;
+  const int R = forced == 1 || forced == 2 || forced == 4 || forced == 8 ? forced : max_groups >= 64 ? 8 : 4;
   const int64_t tiles = (a.rows + 8 * R - 1) / (8 * R);
   const int64_t items = (int64_t)max_groups * tiles, cap = 8 * (int64_t)vec_num_sms();
   const unsigned grid = (unsigned)(items < cap ? (items > 0 ? items : 1) : cap);
   const int wmax = kt_vec_ms_piece();
 #define KT_MS_LAUNCH(RR, WW) kt_moe_vec_ms_kernel<TYPE, DT, RR, WW><<<grid, 256, 0, s>>>(a)
+#define KT_MS_ROWS(WW)            \
+  if (R == 8) KT_MS_LAUNCH(8, WW);  \
+  else if (R == 4) KT_MS_LAUNCH(4, WW); \
+  else if (R == 2) KT_MS_LAUNCH(2, WW); \
+  else KT_MS_LAUNCH(1, WW);
   if (wmax == 4) {
-    if (R == 4) KT_MS_LAUNCH(4, 4);
-    else if (R == 2) KT_MS_LAUNCH(2, 4);
-    else KT_MS_LAUNCH(1, 4);
+    KT_MS_ROWS(4)
   } else {
-    if (R == 4) KT_MS_LAUNCH(4, 8);
-    else if (R == 2) KT_MS_LAUNCH(2, 8);
-    else KT_MS_LAUNCH(1, 8);
+    KT_MS_ROWS(8)
   }
+#undef KT_MS_ROWS
 #undef KT_MS_LAUNCH
   return 0;
 }
@@ -668,7 +677,11 @@ static int launch_ms_dt(const KtVecArgs& a, int dtype, int max_groups, cudaStrea
 // chunks (32 lanes per row), 64 routes or more, unless KT_B200_VEC_MS=0. Q6_K and IQ3_S (split written, KtSplitOk) measured slower on
 // it than on the staged kernels (one row per warp for them: more rows spill), so they keep those.
 bool kt_vec_ms_ok(int type, int cols, int64_t routes) {
-  if (routes < 64) return false;  // fewer routes: the staged kernels are quicker (measured)
+  static const int64_t min_routes = [] {  // KT_B200_VEC_MS_MIN_ROUTES for tuning runs
+    const char* e = getenv("KT_B200_VEC_MS_MIN_ROUTES");
+    return e ? (int64_t)atoll(e) : (int64_t)16;
+  }();
+  if (routes < min_routes) return false;  // fewer routes: the staged kernels are quicker (measured)
   static const bool on = [] {
     const char* e = getenv("KT_B200_VEC_MS");
     return !(e && e[0] == '0');
