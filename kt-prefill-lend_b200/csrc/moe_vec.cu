@@ -673,9 +673,12 @@ static int launch_ms_dt(const KtVecArgs& a, int dtype, int max_groups, cudaStrea
 }
 
 // whether kt_launch_moe_vec runs the member-stationary kernel for this type, width and number
-// of routes (then the routes must be grouped with piece 8): Q8_0 and Q4_K rows of more than 16
-// chunks (32 lanes per row), 64 routes or more, unless KT_B200_VEC_MS=0. Q6_K and IQ3_S (split written, KtSplitOk) measured slower on
-// it than on the staged kernels (one row per warp for them: more rows spill), so they keep those.
+// of routes (then the routes are grouped in pieces of kt_vec_ms_piece()): the north-star types
+// (KtSplitOk), rows of more than 16 chunks (32 lanes per row), 16 routes or more, unless
+// KT_B200_VEC_MS=0. Measured against the reference kernel (graph replays, B200): config 2's Q6_K
+// down 45.2 / 141.4 us at 16 / 64 tokens (reference 56.0 / 202.9, the staged kernels 72.2 /
+// 263.3), config 3's IQ3_S gate/up 30.8 / 96.2 / 299.5 us at 4 / 16 / 64 tokens (reference 40.0 /
+// 99.5 / 362.6).
 bool kt_vec_ms_ok(int type, int cols, int64_t routes) {
   static const int64_t min_routes = [] {  // KT_B200_VEC_MS_MIN_ROUTES for tuning runs
     const char* e = getenv("KT_B200_VEC_MS_MIN_ROUTES");
@@ -687,7 +690,16 @@ bool kt_vec_ms_ok(int type, int cols, int64_t routes) {
     return !(e && e[0] == '0');
   }();
   if (!on) return false;
-  const int cpb = type == KT_Q8_0 ? KtChunk<KT_Q8_0>::CPB : type == KT_Q4_K ? KtChunk<KT_Q4_K>::CPB : 0;
+  static const bool all = [] {  // KT_B200_VEC_MS_ALL=0: Q6_K and IQ3_S on the staged kernels (tuning runs)
+    const char* e = getenv("KT_B200_VEC_MS_ALL");
+    return !(e && e[0] == '0');
+  }();
+  const int cpb = type == KT_Q8_0    ? KtChunk<KT_Q8_0>::CPB
+                  : type == KT_Q4_K  ? KtChunk<KT_Q4_K>::CPB
+                  : !all             ? 0
+                  : type == KT_Q6_K  ? KtChunk<KT_Q6_K>::CPB
+                  : type == KT_IQ3_S ? KtChunk<KT_IQ3_S>::CPB
+                                     : 0;
   const KtBlockInfo bi = kt_block_info(type);
   return cpb > 0 && bi.qk > 0 && cols % bi.qk == 0 && (int64_t)cols / bi.qk * cpb > 16;
 }
@@ -742,6 +754,8 @@ int kt_launch_moe_vec(int type, const void* w, int table, const void* qx, int64_
     switch (type) {
       case KT_Q8_0: return launch_ms_dt<KT_Q8_0>(a, dtype, max_groups, s);
       case KT_Q4_K: return launch_ms_dt<KT_Q4_K>(a, dtype, max_groups, s);
+      case KT_Q6_K: return launch_ms_dt<KT_Q6_K>(a, dtype, max_groups, s);
+      case KT_IQ3_S: return launch_ms_dt<KT_IQ3_S>(a, dtype, max_groups, s);
     }
   }
   const int pipe_rows = pick_pipe_rows(a.row_bytes, rows, w, table);

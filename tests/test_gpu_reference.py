@@ -109,58 +109,72 @@ def test_per_route_build_at_prefill_size(cuda_device, ref_mods, qtype, cols, row
     assert (bits(y) != bits(y_ref)).mean() < 2e-3
 
 
-@pytest.mark.parametrize("tokens", [1, 4, 16, 64])
-def test_decode_speed_vs_reference_kernel(cuda_device, ref_mods, tokens):
-    # The config-2 gate/up GEMV (Q4_K, 1024 rows x 2048, 64 resident slots, top-8 with the
-    # Zipf-skewed routing of the benchmark) timed for the reference kernel (its window build up
-    # to 4 tokens, the per-route build above, as hot/kt_gguf_hot.py picks them) and for the B200
-    # kernel on the same inputs, warm L2, CUDA events over 50 calls each. Printed as REFSPEED;
-    # the bound only catches a gross regression.
-    win, routes = ref_mods
-    L = synth.make_layer(0, tokens, 2048, 512, 256, 8, 12, 14, n_hot=64, zipf=1.1)
-    Wd = torch.from_numpy(L.w13).to(cuda_device)
-    xd = L.x.to(cuda_device)
-    ids = L.topk_ids.reshape(-1).contiguous().to(cuda_device)
-    ref = win if tokens <= 4 else routes
-    rows = 1024
+# (name, ggml type of the projection, layer) for the decode timing: config 2's gate/up (Q4_K) and
+# down (Q6_K, one route per row of the silu output), config 3's gate/up (IQ3_S, 512 experts)
+SPEED_CASES = [("config2 gate/up Q4_K", "gate_up", 2), ("config2 down Q6_K", "down", 2),
+               ("config3 gate/up IQ3_S", "gate_up", 3)]
 
-    def timed(fn, n=50):
+
+@pytest.mark.parametrize("case", SPEED_CASES, ids=[c[0] for c in SPEED_CASES])
+@pytest.mark.parametrize("tokens", [1, 4, 16, 64])
+def test_decode_speed_vs_reference_kernel(cuda_device, ref_mods, tokens, case):
+    # A decode projection of the benchmark layers timed for the reference kernel (its window
+    # build up to 4 rows of activations, the per-route build above, as hot/kt_gguf_hot.py picks
+    # them) and for the B200 kernel on the same inputs, warm L2, CUDA events over 50 calls each,
+    # eager and as CUDA-graph replays (the serving engine captures decode in graphs). Printed as
+    # REFSPEED; the bound only catches a gross regression.
+    win, routes = ref_mods
+    name, proj, cfg = case
+    if cfg == 2:
+        L = synth.make_layer(0, tokens, 2048, 512, 256, 8, 12, 14, n_hot=64, zipf=1.1)
+    else:
+        L = synth.make_layer(0, tokens, 2048, 512, 512, 10, 21, 21)
+    top_k = L.topk_ids.shape[1]
+    if proj == "gate_up":
+        Wd, qtype, rows = torch.from_numpy(L.w13).to(cuda_device), L.type13, 2 * L.inter
+        xd = L.x.to(cuda_device)
+        ids, k, n = L.topk_ids.reshape(-1).contiguous().to(cuda_device), top_k, tokens
+    else:  # the down GEMV: one route per row of h
+        Wd, qtype, rows = torch.from_numpy(L.w2).to(cuda_device), L.type2, L.hidden
+        g = torch.Generator().manual_seed(tokens)
+        xd = torch.randn((tokens * top_k, L.inter), generator=g).to(torch.bfloat16).to(cuda_device)
+        ids, k, n = L.topk_ids.reshape(-1).contiguous().to(cuda_device), 1, tokens * top_k
+    ref = win if n <= 4 else routes
+
+    def timed(fn, reps=50):
         for _ in range(5):
             fn()
         torch.cuda.synchronize()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
-        for _ in range(n):
+        for _ in range(reps):
             fn()
         e1.record()
         torch.cuda.synchronize()
-        return e0.elapsed_time(e1) / n * 1e3
+        return e0.elapsed_time(e1) / reps * 1e3
 
-    def graph_timed(fn, n=50):
-        # one call captured in a CUDA graph (as the serving engine runs decode), replays timed:
-        # GPU time without the host's per-call work
+    def graph_timed(fn, reps=50):
         side = torch.cuda.Stream()
         side.wait_stream(torch.cuda.current_stream())
         with torch.cuda.stream(side):
             for _ in range(3):
                 fn()
         torch.cuda.current_stream().wait_stream(side)
-        g = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g):
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr):
             fn()
-        return timed(g.replay, n)
+        return timed(gr.replay, reps)
 
     # the reference kernel indexes by id and reads ids < 0 as CPU routes (skipped)
-    f_ref = lambda: ref.kt_moe_a8_vec_multi(xd, Wd, ids, 8, 12, rows, tokens)  # noqa: E731
-    f_b200 = lambda: M.moe_a8_vec_multi(xd, Wd, ids, 8, 12, rows, tokens)  # noqa: E731
+    f_ref = lambda: ref.kt_moe_a8_vec_multi(xd, Wd, ids, k, qtype, rows, n)  # noqa: E731
+    f_b200 = lambda: M.moe_a8_vec_multi(xd, Wd, ids, k, qtype, rows, n)  # noqa: E731
     us_ref, us_b200 = timed(f_ref), timed(f_b200)
     g_ref, g_b200 = graph_timed(f_ref), graph_timed(f_b200)
-    y_ref = ref.kt_moe_a8_vec_multi(xd, Wd, ids, 8, 12, rows, tokens)
-    y = M.moe_a8_vec_multi(xd, Wd, ids, 8, 12, rows, tokens)
+    y_ref, y = f_ref(), f_b200()
     torch.cuda.synchronize()
     live = (ids >= 0).cpu().numpy()
     assert np.array_equal(bits(y)[live], bits(y_ref)[live])
-    print(f"\nREFSPEED config2 gate/up Q4_K tokens={tokens} routes={int(live.sum())}: "
+    print(f"\nREFSPEED {name} tokens={tokens} routes={int(live.sum())}: "
           f"reference {us_ref:.1f} us  b200 {us_b200:.1f} us  ratio {us_ref / us_b200:.2f} | "
           f"graph replay: reference {g_ref:.1f} us  b200 {g_b200:.1f} us  ratio {g_ref / g_b200:.2f}")
     assert us_b200 < 3.0 * us_ref
