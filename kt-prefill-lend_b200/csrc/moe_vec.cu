@@ -90,6 +90,53 @@ __device__ __forceinline__ int kt_group_pieces(int i, int c, int piece) {
   return c / piece + __popc(c % piece);
 }
 
+// The same grouping for at most 32 routes by the first warp alone (no block barriers): lane p
+// holds route p; lanes of one slot find each other with __match_any_sync, the lowest is the
+// group's leader, and shuffle scans give each group its first position and first group index.
+// Groups come out in the order of their leaders' lanes instead of slot order, which no caller
+// relies on.
+__device__ __forceinline__ void kt_group_routes_warp(const int32_t* __restrict__ ids, int routes, int n_slots,
+                                                     int piece, int32_t* __restrict__ groups,
+                                                     int32_t* __restrict__ order) {
+  const int lane = threadIdx.x & 31;
+  const bool live = lane < routes;
+  const int32_t e = live ? ids[lane] : -1;
+  const int slot = (e >= 0 && e < n_slots) ? e : -1;
+  const uint32_t peers = __match_any_sync(0xffffffffu, live ? slot : -2);
+  const int leader = __ffs(peers) - 1;
+  const bool lead = live && lane == leader;
+  const int cnt = __popc(peers);
+  const int pieces = lead ? (slot < 0 || piece == 0 ? 1 : cnt / piece + __popc(cnt % piece)) : 0;
+  int c_inc = lead ? cnt : 0, g_inc = pieces;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int cy = __shfl_up_sync(0xffffffffu, c_inc, o), gy = __shfl_up_sync(0xffffffffu, g_inc, o);
+    if (lane >= o) c_inc += cy, g_inc += gy;
+  }
+  const int first = c_inc - (lead ? cnt : 0), g_first = g_inc - pieces;
+  const int start = __shfl_sync(0xffffffffu, first, leader);
+  if (live) order[start + __popc(peers & ((1u << lane) - 1))] = lane;
+  if (lead) {
+    int g = g_first, pos = first, left = cnt;
+    auto emit = [&](int k) {
+      groups[1 + 3 * g + 0] = slot;
+      groups[1 + 3 * g + 1] = pos;
+      groups[1 + 3 * g + 2] = k;
+      ++g;
+      pos += k;
+      left -= k;
+    };
+    if (slot < 0 || piece == 0) {
+      emit(cnt);
+    } else {
+      while (left >= piece) emit(piece);
+      for (int bit = piece >> 1; bit > 0; bit >>= 1)
+        if (left & bit) emit(bit);
+    }
+  }
+  if (lane == 31) groups[0] = g_inc;
+}
+
 // the whole CTA groups; cnt: 2 * (n_slots + 1) ints of shared memory
 __device__ __forceinline__ void kt_group_routes_body(const int32_t* __restrict__ ids, int64_t routes, int n_slots,
                                                      int piece, int32_t* __restrict__ groups,
@@ -184,7 +231,11 @@ __global__ void __launch_bounds__(256) kt_quantize_group_kernel(const void* __re
                                                                 int32_t* __restrict__ order) {
   extern __shared__ int32_t cnt[];
   if ((int64_t)blockIdx.x == nqb) {
-    kt_group_routes_body(ids, routes, n_slots, piece, groups, order, cnt);
+    if (routes <= 32) {
+      if (threadIdx.x < 32) kt_group_routes_warp(ids, (int)routes, n_slots, piece, groups, order);
+    } else {
+      kt_group_routes_body(ids, routes, n_slots, piece, groups, order, cnt);
+    }
     return;
   }
   const int64_t cbx = kpad / 256;
@@ -207,8 +258,10 @@ __global__ void __launch_bounds__(256) kt_quantize_group_kernel(const void* __re
 
 int kt_launch_quantize_group(const void* x, int dtype, int64_t rows, int64_t cols, void* qx, const int32_t* ids,
                              int64_t routes, int n_slots, int piece, int32_t* groups, int32_t* order, cudaStream_t s) {
-  const size_t smem = sizeof(int32_t) * 2 * (size_t)(n_slots + 1);
-  if (rows <= 0 || smem > 200 * 1024 || piece < 0 || (piece & (piece - 1))) return -1;
+  // the counters are only needed by the block-wide grouping (more than 32 routes)
+  const size_t smem = routes <= 32 ? 0 : sizeof(int32_t) * 2 * (size_t)(n_slots + 1);
+  if (rows <= 0 || sizeof(int32_t) * 2 * (size_t)(n_slots + 1) > 200 * 1024 || piece < 0 || (piece & (piece - 1)))
+    return -1;
   const int64_t kpad = (cols + 511) / 512 * 512;
   const int64_t nqb = rows * (kpad / 256);
   if (nqb + 1 > 0x7fffffff) return -1;
