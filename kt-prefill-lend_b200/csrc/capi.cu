@@ -79,9 +79,9 @@ int moe_vec(const void* x, int x_dtype, int64_t tokens, int64_t cols, const void
   VecWs v = vec_ws(ws, tokens, cols, routes, n_slots);
   if (ws_bytes < v.bytes) return KT_ERR_WORKSPACE;
   cudaStream_t s = S(stream);
-  if (cudaMemsetAsync(v.status, 0, sizeof(int), s) != cudaSuccess) return KT_ERR_CUDA;
   const int piece = kt_vec_ms_ok(type, (int)cols, routes) ? kt_vec_ms_piece() : 0;
-  int rc = kt_launch_quantize_group(x, x_dtype, tokens, cols, v.qx, ids, routes, n_slots, piece, v.groups, v.order, s);
+  int rc = kt_launch_quantize_group(x, x_dtype, tokens, cols, v.qx, ids, routes, n_slots, piece, v.groups, v.order,
+                                    v.status, s);  // the first launch also resets the status word
   if (rc) return launch_rc(rc);
   const int max_groups = (int)(piece || routes < (int64_t)n_slots + 1 ? routes : (int64_t)n_slots + 1);
   rc = kt_launch_moe_vec(type, w, table, v.qx, kt_q8_1_row_bytes(cols), v.groups, v.order, max_groups, (int)top_k,

@@ -33,9 +33,10 @@ int kt_launch_group_routes(const int32_t* ids, int64_t routes, int n_slots, int3
 // piece 8; kt_launch_moe_vec then takes max_groups = routes)
 bool kt_vec_ms_ok(int type, int cols, int64_t routes);
 int kt_vec_ms_piece();
-// split-layout q8_1 quantization and route grouping in one launch
+// split-layout q8_1 quantization and route grouping in one launch; also resets *status
 int kt_launch_quantize_group(const void* x, int dtype, int64_t rows, int64_t cols, void* qx, const int32_t* ids,
-                             int64_t routes, int n_slots, int piece, int32_t* groups, int32_t* order, cudaStream_t s);
+                             int64_t routes, int n_slots, int piece, int32_t* groups, int32_t* order, int* status,
+                             cudaStream_t s);
 int kt_launch_moe_vec(int type, const void* w, int table, const void* qx, int64_t qrow, const int32_t* groups,
                       const int32_t* order, int max_groups, int top_k, int rows, int cols, int dtype, void* y,
                       int* status, cudaStream_t s);

@@ -228,9 +228,10 @@ __global__ void __launch_bounds__(256) kt_quantize_group_kernel(const void* __re
                                                                 int64_t rows, int64_t cols, int64_t kpad, int64_t nqb,
                                                                 const int32_t* __restrict__ ids, int64_t routes,
                                                                 int n_slots, int piece, int32_t* __restrict__ groups,
-                                                                int32_t* __restrict__ order) {
+                                                                int32_t* __restrict__ order, int* __restrict__ status) {
   extern __shared__ int32_t cnt[];
   if ((int64_t)blockIdx.x == nqb) {
+    if (threadIdx.x == 0 && status) *status = KT_DEV_OK;  // the call's status word, before the GEMV runs
     if (routes <= 32) {
       if (threadIdx.x < 32) kt_group_routes_warp(ids, (int)routes, n_slots, piece, groups, order);
     } else {
@@ -257,7 +258,8 @@ __global__ void __launch_bounds__(256) kt_quantize_group_kernel(const void* __re
 }
 
 int kt_launch_quantize_group(const void* x, int dtype, int64_t rows, int64_t cols, void* qx, const int32_t* ids,
-                             int64_t routes, int n_slots, int piece, int32_t* groups, int32_t* order, cudaStream_t s) {
+                             int64_t routes, int n_slots, int piece, int32_t* groups, int32_t* order, int* status,
+                             cudaStream_t s) {
   // the counters are only needed by the block-wide grouping (more than 32 routes)
   const size_t smem = routes <= 32 ? 0 : sizeof(int32_t) * 2 * (size_t)(n_slots + 1);
   if (rows <= 0 || sizeof(int32_t) * 2 * (size_t)(n_slots + 1) > 200 * 1024 || piece < 0 || (piece & (piece - 1)))
@@ -271,7 +273,7 @@ int kt_launch_quantize_group(const void* x, int dtype, int64_t rows, int64_t col
     auto k = kt_quantize_group_kernel<DT>;                                                                        \
     if (smem > 48 * 1024) cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);        \
     k<<<(unsigned)(nqb + 1), 256, smem, s>>>(x, (uint8_t*)qx, rows, cols, kpad, nqb, ids, routes, n_slots, piece, \
-                                             groups, order);                                                      \
+                                             groups, order, status);                                              \
     return 0;                                                                                                     \
   }
     case KT_DT_F32: KT_QG_LAUNCH(KT_DT_F32)
