@@ -617,10 +617,6 @@ template <int TYPE>
 struct KtAct;
 template <int TYPE>
 struct KtWgt;
-template <int TYPE>
-struct KtSplitOk {
-  static constexpr bool value = TYPE == KT_Q8_0 || TYPE == KT_Q4_K || TYPE == KT_Q6_K || TYPE == KT_IQ3_S;
-};
 
 template <>
 struct KtAct<KT_Q8_0> {

@@ -24,16 +24,12 @@ struct KtGemmArgs {
 };
 
 int kt_launch_quantize_q8_1(const void* x, int dtype, int64_t rows, int64_t cols, void* qx, cudaStream_t s);
-// the same values in the GEMV's split layout: a row's int8 values, then its half2 (d, s) per block
-int kt_launch_quantize_q8_1_split(const void* x, int dtype, int64_t rows, int64_t cols, void* qx, cudaStream_t s);
-// piece > 0 (a power of two): a slot's routes are cut into groups of piece, then powers of two
-int kt_launch_group_routes(const int32_t* ids, int64_t routes, int n_slots, int32_t* groups, int32_t* order,
-                           cudaStream_t s, int piece = 0);
-// the GEMV runs its member-stationary kernel for this type, width and route count (group with
-// piece 8; kt_launch_moe_vec then takes max_groups = routes)
+// the GEMV runs its member-stationary kernel for this type, width and route count (routes grouped
+// in pieces of kt_vec_ms_piece(); kt_launch_moe_vec then takes max_groups = routes)
 bool kt_vec_ms_ok(int type, int cols, int64_t routes);
 int kt_vec_ms_piece();
-// split-layout q8_1 quantization and route grouping in one launch; also resets *status
+// q8_1 quantization in the GEMV's split layout (a row's int8 values, then its half2 (d, s) per
+// block) and route grouping in one launch; also resets *status
 int kt_launch_quantize_group(const void* x, int dtype, int64_t rows, int64_t cols, void* qx, const int32_t* ids,
                              int64_t routes, int n_slots, int piece, int32_t* groups, int32_t* order, int* status,
                              cudaStream_t s);

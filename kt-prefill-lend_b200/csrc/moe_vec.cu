@@ -67,9 +67,6 @@ int kt_launch_quantize_q8_1(const void* x, int dtype, int64_t rows, int64_t cols
   return launch_quantize<false>(x, dtype, rows, cols, qx, s);
 }
 
-int kt_launch_quantize_q8_1_split(const void* x, int dtype, int64_t rows, int64_t cols, void* qx, cudaStream_t s) {
-  return launch_quantize<true>(x, dtype, rows, cols, qx, s);
-}
 
 // ------------------------------------------------------------------ route grouping
 // One CTA: counting sort of the routes by expert slot. Routes with an id outside
@@ -213,13 +210,6 @@ __device__ __forceinline__ void kt_group_routes_body(const int32_t* __restrict__
   }
 }
 
-__global__ void __launch_bounds__(1024) kt_group_routes_kernel(const int32_t* __restrict__ ids, int64_t routes,
-                                                               int n_slots, int piece, int32_t* __restrict__ groups,
-                                                               int32_t* __restrict__ order) {
-  extern __shared__ int32_t cnt[];  // n_slots + 1 counters, then n_slots + 1 cursors
-  kt_group_routes_body(ids, routes, n_slots, piece, groups, order, cnt);
-}
-
 // The GEMV's two preparation steps in one launch: blocks [0, nqb) quantize the activations
 // into the split q8_1 layout (256 columns of a row each, as kt_quantize_q8_1_kernel), block nqb
 // groups the routes. Saves a launch on the decode path, where the GEMV itself is short.
@@ -284,15 +274,6 @@ int kt_launch_quantize_group(const void* x, int dtype, int64_t rows, int64_t col
   return -1;
 }
 
-int kt_launch_group_routes(const int32_t* ids, int64_t routes, int n_slots, int32_t* groups, int32_t* order,
-                           cudaStream_t s, int piece) {
-  const size_t smem = sizeof(int32_t) * 2 * (size_t)(n_slots + 1);
-  if (smem > 200 * 1024 || piece < 0 || (piece & (piece - 1))) return -1;
-  if (smem > 48 * 1024) cudaFuncSetAttribute(kt_group_routes_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  kt_group_routes_kernel<<<1, 1024, smem, s>>>(ids, routes, n_slots, piece, groups, order);
-  return 0;
-}
-
 // ------------------------------------------------------------------ GEMV
 
 struct KtVecArgs {
@@ -301,7 +282,7 @@ struct KtVecArgs {
   const uint8_t* qx;           // q8_1 activations [tokens, qrow] bytes
   int64_t qrow;                // bytes per q8_1 row (split layout: kpad int8, then kpad/32 half2)
   int64_t kpad;                // padded columns of a q8_1 row
-  const int32_t* groups;       // from kt_group_routes
+  const int32_t* groups;       // from the route grouping (kt_launch_quantize_group)
   const int32_t* order;
   int top_k;
   int rows, cols;
@@ -535,8 +516,8 @@ __global__ void __launch_bounds__(256) kt_moe_vec_pipe_kernel(const KtVecArgs a)
   (void)ok;
 }
 
-// Member-stationary kernel for the north-star types (KtSplitOk): groups of 1, 2, 4 or 8
-// routes of one slot (kt_group_routes with piece 8) times row tiles of 8R rows are the work
+// Member-stationary kernel for the north-star types (Q8_0, Q4_K, Q6_K, IQ3_S): groups of 1, 2, 4 or 8
+// routes of one slot (grouped in pieces of kt_vec_ms_piece()) times row tiles of 8R rows are the work
 // items of a persistent grid. A warp owns R rows of the tile; its lanes walk the chunks of a
 // row as the reference does (lane t: chunks t, t+32, ...), but for each chunk they load the
 // members' activation side once (KtAct: q8_1 ints, scales and the row-independent integer
@@ -729,7 +710,7 @@ static int launch_ms_dt(const KtVecArgs& a, int dtype, int max_groups, cudaStrea
 
 // whether kt_launch_moe_vec runs the member-stationary kernel for this type, width and number
 // of routes (then the routes are grouped in pieces of kt_vec_ms_piece()): the north-star types
-// (KtSplitOk), rows of more than 16 chunks (32 lanes per row), 16 routes or more, unless
+// (Q8_0, Q4_K, Q6_K, IQ3_S), rows of more than 16 chunks (32 lanes per row), 16 routes or more, unless
 // KT_B200_VEC_MS=0. Measured against the reference kernel (graph replays, B200): config 2's Q6_K
 // down 45.2 / 141.4 us at 16 / 64 tokens (reference 56.0 / 202.9, the staged kernels 72.2 /
 // 263.3), config 3's IQ3_S gate/up 30.8 / 96.2 / 299.5 us at 4 / 16 / 64 tokens (reference 40.0 /
