@@ -13,10 +13,13 @@
  * they write KT_DEV_TIMEOUT into the workspace's status word, which kt_workspace_status()
  * reads after the stream has finished.
  *
- * Types: ggml type ids KT_GGML_Q8_0 (8), KT_GGML_Q4_K (12), KT_GGML_Q6_K (14),
- * KT_GGML_IQ3_S (21) everywhere; the decode GEMV, the dense GEMV and the dequantizer also
- * take the 32-value blocks KT_GGML_Q4_0 (2), KT_GGML_Q4_1 (3), KT_GGML_Q5_0 (6),
- * KT_GGML_Q5_1 (7) and KT_GGML_IQ4_NL (20) (the prefill layer returns KT_ERR_TYPE for them).
+ * Types (ggml type ids, KT_GGML_* below): the prefill layer takes Q8_0 (8), Q4_K (12),
+ * Q6_K (14) and IQ3_S (21). The decode GEMV, the dense GEMV and the dequantizer take those and
+ * every other type of the reference kernel's switch (kt_gguf_moe_multi.cu:671-932): the
+ * 32-value blocks Q4_0 (2), Q4_1 (3), Q5_0 (6), Q5_1 (7), IQ4_NL (20); the K-quants Q2_K (10),
+ * Q3_K (11), Q5_K (13); the i-quants IQ2_XXS (16), IQ2_XS (17), IQ3_XXS (18), IQ1_S (19),
+ * IQ2_S (22), IQ4_XS (23), IQ1_M (29); and the reference's own 64-value 2-bit Q2_0 (42)
+ * (kt_gguf_moe_multi.cu:33-46). The prefill layer returns KT_ERR_TYPE for the GEMV-only types.
  * Activation dtypes: KT_DTYPE_F32 (0), KT_DTYPE_F16 (1), KT_DTYPE_BF16 (2).
  *
  * Weight layout (as the reference's KTGGUFHotExpertsMethod, hot/kt_gguf_hot.py:17-20):
@@ -53,10 +56,21 @@ extern "C" {
 #define KT_GGML_Q5_0 6
 #define KT_GGML_Q5_1 7
 #define KT_GGML_Q8_0 8
-#define KT_GGML_IQ4_NL 20
+#define KT_GGML_Q2_K 10
+#define KT_GGML_Q3_K 11
 #define KT_GGML_Q4_K 12
+#define KT_GGML_Q5_K 13
 #define KT_GGML_Q6_K 14
+#define KT_GGML_IQ2_XXS 16
+#define KT_GGML_IQ2_XS 17
+#define KT_GGML_IQ3_XXS 18
+#define KT_GGML_IQ1_S 19
+#define KT_GGML_IQ4_NL 20
 #define KT_GGML_IQ3_S 21
+#define KT_GGML_IQ2_S 22
+#define KT_GGML_IQ4_XS 23
+#define KT_GGML_IQ1_M 29
+#define KT_GGML_Q2_0 42
 
 #define KT_DTYPE_F32 0
 #define KT_DTYPE_F16 1
@@ -116,6 +130,12 @@ int kt_moe_a8_vec_routes(const void* x, int x_dtype, int64_t tokens, int64_t col
 int kt_moe_a8_vec_multi_static(const void* x, int x_dtype, int64_t tokens, int64_t cols, const void* w, int w_is_table,
                                int n_slots, const int32_t* topk_ids, int64_t top_k, int ggml_type, int64_t rows,
                                void* y, void* stream);
+
+/* The device status word of the most recent kt_moe_a8_vec_multi_static call on the current
+ * device (the counterpart of kt_workspace_status for the library's own scratch): synchronizes
+ * `stream`, then *status = KT_DEV_OK or KT_DEV_TIMEOUT (meaningful once a static call has run
+ * on the device). No counterpart in the reference. */
+int kt_static_scratch_status(void* stream, int* status);
 
 /* Workspace for kt_dense_a8_vec. */
 size_t kt_dense_a8_vec_workspace_size(int64_t tokens, int64_t cols);
@@ -212,6 +232,32 @@ int kt_moe_prefill_timed(const void* x, int64_t tokens, int64_t hidden, int64_t 
                          const float* topk_weights, int64_t top_k, const void* w13, int type13, const void* w2, int type2,
                          int w_is_table, int n_slots, void* out, void* workspace, size_t workspace_bytes, void* stream,
                          void* const* stage_events);
+
+/* Workspace for kt_moe_gemm_routes. */
+size_t kt_moe_gemm_routes_workspace_size(int64_t tokens, int64_t top_k, int64_t cols, int64_t rows, int n_slots);
+
+/* The per-route projection of kt_moe_a8_vec_routes on tensor cores:
+ *   y[p] = bf16(W[ids[p]] . x[p / top_k])   for p < tokens*top_k, zero rows for ids outside
+ *   [0, n_slots),
+ * with bf16 activations x [tokens, cols], the GGUF weights (w [n_slots, rows, row_bytes(cols)]
+ * or a slot table) dequantized in shared memory to bf16 exactly as kt_gguf_dequantize rounds
+ * them, fp32 accumulation, y [tokens*top_k, rows] bf16. The prefill layer's own GEMM kernels
+ * run it: reductions of at most 512 the down projection's, longer ones the gate/up
+ * projection's without the SwiGLU, so a one-hot x reads back the dequantized weights those
+ * kernels multiply with. Replaces, at prefill sizes, the reference's per-route GEMV build
+ * (hot/kt_gguf_moe_multi.py:85-87) for a single projection. Types as kt_moe_prefill;
+ * cols % 256 == 0, rows % 256 == 0; x and y 16-byte aligned. */
+int kt_moe_gemm_routes(const void* x, int64_t tokens, int64_t cols, const int32_t* topk_ids, int64_t top_k,
+                       const void* w, int ggml_type, int64_t rows, int w_is_table, int n_slots, void* y,
+                       void* workspace, size_t workspace_bytes, void* stream);
+
+/* Self-test of the failure path the prefill GEMMs rely on: one CTA pair sets up as they do
+ * (barriers, the pair's TMEM), waits on a barrier that nothing arrives on with the library's
+ * bounded wait (limit_ns, 1 ms to 2 s, instead of the GEMMs' 2 s), then drains, meets its peer
+ * and frees TMEM as the GEMMs do after a timeout. Clears the status word (the first int of
+ * `workspace`) first; after the stream has finished, kt_workspace_status reports
+ * KT_DEV_TIMEOUT and the context stays usable. No counterpart in the reference. */
+int kt_selftest_bounded_wait(void* workspace, size_t workspace_bytes, int64_t limit_ns, void* stream);
 
 /* ---- Expert-parallel plumbing (no counterpart in the reference, which runs the hot experts on
  * one GPU per tensor-parallel rank). Around an all-to-all of bf16 rows over n_ranks <= 8

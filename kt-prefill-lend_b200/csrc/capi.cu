@@ -123,6 +123,42 @@ PreWs pre_ws(void* ws, int64_t tokens, int64_t top_k, int64_t hidden, int64_t in
   return p;
 }
 
+// per-route expert GEMM workspace layout (kt_moe_gemm_routes)
+struct RouteWs {
+  int* status;
+  int32_t* counts;
+  int32_t* hist;
+  int32_t* tiles;
+  int32_t* n_tiles;
+  int32_t* chunks;
+  int32_t* sorted_token;
+  int32_t* route_pos;
+  uint16_t* xs;  // activation rows in slot order (reductions <= 512 only)
+  uint16_t* ys;  // outputs in slot order
+  size_t bytes;
+};
+
+constexpr int64_t kRouteShortReduction = 512;  // reductions up to this run the down kernels
+
+RouteWs route_ws(void* ws, int64_t tokens, int64_t top_k, int64_t cols, int64_t rows, int n_slots) {
+  Carve c(ws);
+  RouteWs r;
+  const int64_t R = tokens * top_k;
+  const int tn = kt_gemm_tile_tokens();
+  r.status = c.take<int>(4);
+  r.counts = c.take<int32_t>(n_slots);
+  r.hist = c.take<int32_t>((size_t)kt_permute_hist_ints(R, n_slots));
+  r.tiles = c.take<int32_t>(3 * (size_t)(R / tn + n_slots + 1));
+  r.n_tiles = c.take<int32_t>(4);
+  r.chunks = c.take<int32_t>(3 * (size_t)(R / tn + n_slots + 1));
+  r.sorted_token = c.take<int32_t>(R);
+  r.route_pos = c.take<int32_t>(R);
+  r.xs = c.take<uint16_t>(cols <= kRouteShortReduction ? (size_t)R * cols : 0, 1024);
+  r.ys = c.take<uint16_t>((size_t)R * rows, 1024);
+  r.bytes = align_up(c.off, 256);
+  return r;
+}
+
 }  // namespace
 
 KT_EXPORT int kt_version(void) { return 100; }
@@ -345,6 +381,55 @@ KT_EXPORT int kt_moe_prefill_ex(const void* x, int64_t tokens, int64_t hidden, i
                      n_slots, id_base, acc, acc_flags, out, workspace, workspace_bytes, stream, nullptr);
 }
 
+KT_EXPORT int kt_selftest_bounded_wait(void* workspace, size_t workspace_bytes, int64_t limit_ns, void* stream) {
+  if (!workspace || workspace_bytes < sizeof(int)) return KT_ERR_ARG;
+  if (limit_ns < 1000000 || limit_ns > 2000000000) return KT_ERR_ARG;  // 1 ms .. 2 s
+  if (cudaMemsetAsync(workspace, 0, sizeof(int), S(stream)) != cudaSuccess) return KT_ERR_CUDA;
+  return launch_rc(kt_launch_selftest_wait((int*)workspace, (uint64_t)limit_ns, S(stream)));
+}
+
+// ------------------------------------------------------------------ per-route expert GEMM
+
+KT_EXPORT size_t kt_moe_gemm_routes_workspace_size(int64_t tokens, int64_t top_k, int64_t cols, int64_t rows,
+                                                   int n_slots) {
+  return route_ws(nullptr, tokens, top_k, cols, rows, n_slots).bytes;
+}
+
+KT_EXPORT int kt_moe_gemm_routes(const void* x, int64_t tokens, int64_t cols, const int32_t* topk_ids, int64_t top_k,
+                                 const void* w, int ggml_type, int64_t rows, int w_is_table, int n_slots, void* y,
+                                 void* workspace, size_t workspace_bytes, void* stream) {
+  if (!kt_prefill_type(ggml_type)) return KT_ERR_TYPE;
+  if (tokens < 0 || top_k <= 0 || n_slots <= 0 || n_slots > kPermMaxSlots || cols <= 0 || rows <= 0) return KT_ERR_ARG;
+  if (cols % 256 || rows % 256 || cols > (1 << 20) || rows > (1 << 20)) return KT_ERR_ARG;
+  if (tokens * top_k > (int64_t)1 << 30) return KT_ERR_ARG;
+  if (tokens == 0) return KT_OK;
+  if (!x || !topk_ids || !w || !y || !workspace || (((uintptr_t)x | (uintptr_t)y) & 15)) return KT_ERR_ARG;
+  RouteWs r = route_ws(workspace, tokens, top_k, cols, rows, n_slots);
+  if (workspace_bytes < r.bytes) return KT_ERR_WORKSPACE;
+  cudaStream_t s = S(stream);
+  const int64_t R = tokens * top_k;
+  if (cudaMemsetAsync(r.status, 0, sizeof(int), s) != cudaSuccess) return KT_ERR_CUDA;
+  int rc = kt_launch_permute(topk_ids, R, (int)top_k, n_slots, kt_gemm_tile_tokens(), kt_gemm_chunk_tiles(), r.counts,
+                             r.hist, r.tiles, r.n_tiles, r.chunks, r.sorted_token, r.route_pos, s, 0);
+  if (rc) return launch_rc(rc);
+  const int grid = num_sms();
+  if (cols <= kRouteShortReduction) {
+    // short reductions: the activation rows in slot order, then the down projection's kernels
+    // (the resident-strip kernel; KT_B200_DOWN_STREAM selects the streaming one)
+    rc = kt_launch_gather_rows((const uint16_t*)x, cols, r.sorted_token, R, r.n_tiles + 1, r.xs, s);
+    if (rc) return launch_rc(rc);
+    rc = kt_launch_gemm_down(ggml_type, r.xs, R, (int)rows, (int)cols, w, w_is_table, n_slots, r.tiles, r.n_tiles,
+                             r.chunks, r.ys, r.status, grid, s);
+  } else {
+    // longer ones: the gate/up kernel (token rows gathered in the kernel) without the activation
+    rc = kt_launch_gemm_gate_up(ggml_type, x, tokens, (int)cols, (int)(rows / 2), w, w_is_table, n_slots, r.tiles,
+                                r.n_tiles, r.sorted_token, r.ys, r.status, grid, s, 1);
+  }
+  if (rc) return launch_rc(rc);
+  // back to route order, zero rows for routes without a resident slot
+  return launch_rc(kt_launch_gather_rows(r.ys, rows, r.route_pos, R, nullptr, (uint16_t*)y, s));
+}
+
 // ------------------------------------------------------------------ expert-parallel plumbing
 
 KT_EXPORT size_t kt_ep_plan_workspace_size(int64_t tokens, int n_ranks) {
@@ -421,4 +506,18 @@ KT_EXPORT int kt_moe_a8_vec_multi_static(const void* x, int x_dtype, int64_t tok
   // reads is written earlier in the same call
   return moe_vec(x, x_dtype, tokens, cols, w, w_is_table, n_slots, topk_ids, top_k, ggml_type, rows, y, scratch,
                  (size_t)KT_STATIC_SCRATCH_BYTES, stream);
+}
+
+// The device status word of the last kt_moe_a8_vec_multi_static call on the current device: the
+// first int of the static scratch (the GEMV's workspace layout starts with it). Reading it goes
+// through the symbol itself, so it needs no address lookup and allocates nothing. The word only
+// means something once a static call has run on the device.
+KT_EXPORT int kt_static_scratch_status(void* stream, int* status) {
+  if (!status) return KT_ERR_ARG;
+  if (cudaStreamSynchronize(S(stream)) != cudaSuccess) return KT_ERR_CUDA;
+  int v = 0;
+  if (cudaMemcpyFromSymbol(&v, kt_static_scratch, sizeof(int), 0, cudaMemcpyDeviceToHost) != cudaSuccess)
+    return KT_ERR_CUDA;
+  *status = v;
+  return KT_OK;
 }

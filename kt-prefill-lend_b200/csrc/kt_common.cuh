@@ -194,20 +194,25 @@ __device__ __forceinline__ uint64_t kt_globaltimer_ns() {
   return t;
 }
 
-// Bounded wait: gives up after KT_WAIT_NS of wall time (global timer), records
-// KT_DEV_TIMEOUT in *status (global) and sets *abort (shared) so the CTA's other roles leave
-// their loops too; returns false then. A wait also returns false once *abort is set.
-__device__ __forceinline__ bool kt_mbar_wait(uint64_t* bar, uint32_t parity, int* status, volatile int* abort) {
+// Bounded wait: gives up after limit_ns of wall time (global timer), records KT_DEV_TIMEOUT
+// in *status (global) and sets *abort (shared) so the CTA's other roles leave their loops
+// too; returns false then. A wait also returns false once *abort is set. The kernels use
+// kt_mbar_wait (limit KT_WAIT_NS); the library's self-test of this path passes a short limit.
+__device__ __forceinline__ bool kt_mbar_wait_for(uint64_t* bar, uint32_t parity, int* status, volatile int* abort,
+                                                 uint64_t limit_ns) {
   if (kt_mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = kt_globaltimer_ns();
   for (uint32_t i = 1;; ++i) {
     if (kt_mbar_try_wait(bar, parity)) return true;
     if (abort && *abort) return false;
-    if ((i & 255) == 0 && kt_globaltimer_ns() - t0 > KT_WAIT_NS) break;
+    if ((i & 255) == 0 && kt_globaltimer_ns() - t0 > limit_ns) break;
   }
   if (status) atomicExch(status, KT_DEV_TIMEOUT);
   if (abort) *abort = 1;
   return false;
+}
+__device__ __forceinline__ bool kt_mbar_wait(uint64_t* bar, uint32_t parity, int* status, volatile int* abort) {
+  return kt_mbar_wait_for(bar, parity, status, abort, KT_WAIT_NS);
 }
 
 // spin for `ns` nanoseconds of wall time (the global timer), bounded by construction
@@ -251,17 +256,21 @@ __device__ __forceinline__ bool kt_mbar_try_wait_cluster(uint64_t* bar, uint32_t
   return ok != 0;
 }
 // bounded wait on a barrier that also receives arrivals from the peer CTA
-__device__ __forceinline__ bool kt_mbar_wait_cluster(uint64_t* bar, uint32_t parity, int* status, volatile int* abort) {
+__device__ __forceinline__ bool kt_mbar_wait_cluster_for(uint64_t* bar, uint32_t parity, int* status,
+                                                         volatile int* abort, uint64_t limit_ns) {
   if (kt_mbar_try_wait_cluster(bar, parity)) return true;
   const uint64_t t0 = kt_globaltimer_ns();
   for (uint32_t i = 1;; ++i) {
     if (kt_mbar_try_wait_cluster(bar, parity)) return true;
     if (abort && *abort) return false;
-    if ((i & 255) == 0 && kt_globaltimer_ns() - t0 > KT_WAIT_NS) break;
+    if ((i & 255) == 0 && kt_globaltimer_ns() - t0 > limit_ns) break;
   }
   if (status) atomicExch(status, KT_DEV_TIMEOUT);
   if (abort) *abort = 1;
   return false;
+}
+__device__ __forceinline__ bool kt_mbar_wait_cluster(uint64_t* bar, uint32_t parity, int* status, volatile int* abort) {
+  return kt_mbar_wait_cluster_for(bar, parity, status, abort, KT_WAIT_NS);
 }
 __device__ __forceinline__ void kt_cluster_sync() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
@@ -281,21 +290,6 @@ __device__ __forceinline__ void kt_tma_2d(void* dst, const CUtensorMap* map, int
       "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
           kt_smem_addr(dst)),
       "l"(map), "r"(x), "r"(y), "r"(kt_smem_addr(bar))
-      : "memory");
-}
-
-// L2 prefetch of one box of a 2-D tensor map (coordinates past the tensor are ignored)
-__device__ __forceinline__ void kt_tma_prefetch_2d(const CUtensorMap* map, int x, int y) {
-  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(map), "r"(x), "r"(y) : "memory");
-}
-
-// four rows (y0..y3) of a 2-D tensor map whose box is one row high, columns x..x+box-1
-__device__ __forceinline__ void kt_tma_gather4(void* dst, const CUtensorMap* map, int x, int y0, int y1, int y2, int y3,
-                                               uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, "
-      "%5, %6}], [%7];" ::"r"(kt_smem_addr(dst)),
-      "l"(map), "r"(x), "r"(y0), "r"(y1), "r"(y2), "r"(y3), "r"(kt_smem_addr(bar))
       : "memory");
 }
 
@@ -339,30 +333,8 @@ __device__ __forceinline__ void kt_mma2_commit_mc(uint64_t* bar, uint16_t mask) 
                : "memory");
 }
 
-__device__ __forceinline__ void kt_tmem_alloc(uint32_t* dst_smem, uint32_t ncols) {
-  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(kt_smem_addr(dst_smem)), "r"(ncols));
-  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
-}
-__device__ __forceinline__ void kt_tmem_dealloc(uint32_t taddr, uint32_t ncols) {
-  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols));
-}
 __device__ __forceinline__ void kt_tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void kt_tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-
-// D[tmem] (+)= A[smem desc] * B[smem desc]^T, kind::f16 (bf16 inputs, fp32 accumulate)
-__device__ __forceinline__ void kt_mma_bf16_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
-                                               uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate));
-}
-// arrive on an mbarrier once every tcgen05.mma issued so far by this thread has completed
-__device__ __forceinline__ void kt_mma_commit(uint64_t* bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(kt_smem_addr(bar))
-               : "memory");
-}
 
 // 32 lanes x 32 consecutive 32-bit columns starting at taddr (lane field = warp's quadrant)
 __device__ __forceinline__ void kt_tmem_ld32(uint32_t taddr, uint32_t* r) {

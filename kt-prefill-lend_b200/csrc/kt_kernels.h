@@ -45,6 +45,10 @@ int kt_launch_combine(const void* out, int dtype, const float* w, int64_t T, int
 // acc instead of bf16 to res (tokens with no present route are then skipped)
 int kt_launch_combine_sorted(const uint16_t* y, const int32_t* route_pos, const float* w, int64_t T, int64_t top_k,
                              int64_t K, uint16_t* res, cudaStream_t s, float* acc = nullptr, int acc_flags = 0);
+// dst[i] = src[idx[i]] (rows of `cols` bf16, 16-byte aligned) for i < n, zero rows where
+// idx[i] < 0; with n_limit, rows i >= *n_limit (a device count) are left untouched
+int kt_launch_gather_rows(const uint16_t* src, int64_t cols, const int32_t* idx, int64_t n, const int32_t* n_limit,
+                          uint16_t* dst, cudaStream_t s);
 int kt_launch_route(const int32_t* ids, int64_t n, const int32_t* slot_tab, const int32_t* cpu_tab, float* counts,
                     int32_t* slot_out, int32_t* cpu_out, cudaStream_t s);
 int kt_launch_topk_softmax(const float* logits, int64_t T, int E, int k, int renorm, float* weights, int32_t* ids,
@@ -63,13 +67,17 @@ int kt_launch_permute(const int32_t* ids, int64_t routes, int top_k, int n_slots
                       int32_t* counts, int32_t* hist, int32_t* tiles, int32_t* n_tiles, int32_t* chunks,
                       int32_t* sorted_token, int32_t* route_pos, cudaStream_t s, int id_base = 0);
 
+// linear = 1: no activation, the raw projection [R, 2N] (rows of w13 in order) instead of H [R, N]
 int kt_launch_gemm_gate_up(int type, const void* x, int64_t T, int K, int N, const void* w13, int table, int n_slots,
                            const int32_t* tiles, const int32_t* n_tiles, const int32_t* sorted_token, void* h,
-                           int* status, int grid, cudaStream_t s);
+                           int* status, int grid, cudaStream_t s, int linear = 0);
 int kt_launch_gemm_down(int type, const void* h, int64_t R, int K, int N, const void* w2, int table, int n_slots,
                         const int32_t* tiles, const int32_t* n_tiles, const int32_t* chunks, void* y, int* status,
                         int grid, cudaStream_t s);
 int kt_gemm_tile_tokens();
+// the GEMM kernels' bounded-wait and exit path around a barrier nothing arrives on (one CTA
+// pair); writes KT_DEV_TIMEOUT to *status after limit_ns
+int kt_launch_selftest_wait(int* status, uint64_t limit_ns, cudaStream_t s);
 int kt_gemm_chunk_tiles();  // tiles per chunk of the down projection's work units
 
 // expert-parallel plumbing (ep.cu): dispatch plan, row packing, combine of partials (bf16 rows)

@@ -138,7 +138,9 @@ __device__ __forceinline__ int64_t a_row(int rh, int wt, uint32_t cr, int N) {
 
 }  // namespace
 
-template <int TYPE, int PHASE>
+// LINEAR (phase 1 only): the epilogue stores both halves of the projection as they are, with
+// no activation (kt_moe_gemm_routes), instead of silu(gate) * up
+template <int TYPE, int PHASE, bool LINEAR = false>
 __global__ void __launch_bounds__(Roles<PHASE>::kThreads, 1) kt_moe_gemm_kernel(const __grid_constant__ CUtensorMap bmap,
                                                                   const __grid_constant__ CUtensorMap wmap,
                                                                   const KtGemmArgs a) {
@@ -453,7 +455,23 @@ __global__ void __launch_bounds__(Roles<PHASE>::kThreads, 1) kt_moe_gemm_kernel(
         uint32_t v[32];
         kt_tmem_ld32(lane_base + c0, v);
         kt_tmem_wait_ld();
-        if constexpr (PHASE == 1) {
+        if constexpr (PHASE == 1 && LINEAR) {
+          // lanes 0-63 hold rows [wt*128 + 64cr, +64) of the weight, lanes 64-127 the rows N
+          // above them: staged [token][128 positions], then each half to its own output columns
+#pragma unroll
+          for (int j = 0; j < 32; ++j) sEpi[j * 128 + wr] = kt_f2bf(__uint_as_float(v[j]));
+          epi_bar();
+          const int t = l, c = t & 15;
+          const int64_t col = (c < 8 ? 0 : (int64_t)a.N) + (int64_t)wt * 128 + 64 * cr + 8 * (c & 7);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const int tok = (t >> 4) + 8 * i;
+            if (c0 + tok < ntok)
+              *reinterpret_cast<uint4*>(a.out + (int64_t)(pos0 + c0 + tok) * a.out_ld + col) =
+                  *reinterpret_cast<const uint4*>(sEpi + tok * 128 + 8 * c);
+          }
+          epi_bar();
+        } else if constexpr (PHASE == 1) {
           // lanes 0-63 hold gate rows, 64-127 the matching up rows: the up warps hand their
           // values to the gate warps through shared memory; h is staged [token][feature]
           float* xq = sX + (q & 1) * 32 * 32;
@@ -999,11 +1017,11 @@ static int make_raw_map(CUtensorMap* m, const void* w, int64_t row_bytes, int64_
   return r == CUDA_SUCCESS ? G : 0;
 }
 
-template <int TYPE, int PHASE>
+template <int TYPE, int PHASE, bool LINEAR = false>
 static int launch_t(const CUtensorMap& m, const CUtensorMap& wm, const KtGemmArgs& a, int grid, cudaStream_t s) {
   constexpr int smem = smem_bytes<TYPE>();
   static_assert(smem <= 227 * 1024, "shared memory budget");
-  auto k = kt_moe_gemm_kernel<TYPE, PHASE>;
+  auto k = kt_moe_gemm_kernel<TYPE, PHASE, LINEAR>;
   if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) return -3;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)(grid & ~1), 1, 1);  // whole CTA pairs
@@ -1043,22 +1061,23 @@ static int launch_res(const CUtensorMap& m, const CUtensorMap& wm, const KtGemmA
   return cudaGetLastError() == cudaSuccess ? 0 : -4;
 }
 
-template <int PHASE>
+template <int PHASE, bool LINEAR = false>
 static int launch_phase(int type, const CUtensorMap& m, const CUtensorMap& wm, const KtGemmArgs& a, int grid,
                         cudaStream_t s) {
   switch (type) {
-    case KT_Q8_0: return launch_t<KT_Q8_0, PHASE>(m, wm, a, grid, s);
-    case KT_Q4_K: return launch_t<KT_Q4_K, PHASE>(m, wm, a, grid, s);
-    case KT_Q6_K: return launch_t<KT_Q6_K, PHASE>(m, wm, a, grid, s);
-    case KT_IQ3_S: return launch_t<KT_IQ3_S, PHASE>(m, wm, a, grid, s);
+    case KT_Q8_0: return launch_t<KT_Q8_0, PHASE, LINEAR>(m, wm, a, grid, s);
+    case KT_Q4_K: return launch_t<KT_Q4_K, PHASE, LINEAR>(m, wm, a, grid, s);
+    case KT_Q6_K: return launch_t<KT_Q6_K, PHASE, LINEAR>(m, wm, a, grid, s);
+    case KT_IQ3_S: return launch_t<KT_IQ3_S, PHASE, LINEAR>(m, wm, a, grid, s);
   }
   return -1;
 }
 
-// phase 1: X [T, K] bf16 gathered by sorted_token; W13 slots [2N, K]; out H [R, N]
+// phase 1: X [T, K] bf16 gathered by sorted_token; W13 slots [2N, K]; out H [R, N], or with
+// linear the raw projection [R, 2N] (no activation)
 int kt_launch_gemm_gate_up(int type, const void* x, int64_t T, int K, int N, const void* w13, int table, int n_slots,
                            const int32_t* tiles, const int32_t* n_tiles, const int32_t* sorted_token, void* h,
-                           int* status, int grid, cudaStream_t s) {
+                           int* status, int grid, cudaStream_t s, int linear) {
   if (K % 256 || N % 128) return -1;
   if (((uintptr_t)x) & 15) return -1;
   CUtensorMap m, wm;
@@ -1078,9 +1097,9 @@ int kt_launch_gemm_gate_up(int type, const void* x, int64_t T, int K, int N, con
   a.n_wtiles = N / 128;
   a.sorted_token = sorted_token;
   a.out = (uint16_t*)h;
-  a.out_ld = N;
+  a.out_ld = linear ? 2 * (int64_t)N : N;
   a.status = status;
-  return launch_phase<1>(type, m, wm, a, grid, s);
+  return linear ? launch_phase<1, true>(type, m, wm, a, grid, s) : launch_phase<1>(type, m, wm, a, grid, s);
 }
 
 // phase 2: H [R, N] bf16 (sorted rows); W2 slots [K, N]; out Y [R, K]
@@ -1119,6 +1138,62 @@ int kt_launch_gemm_down(int type, const void* h, int64_t R, int K, int N, const 
     return -1;
   }
   return launch_phase<2>(type, m, wm, a, grid, s);
+}
+
+// ------------------------------------------------------------------ self-test of the failure path
+//
+// One CTA pair that takes the GEMM kernels' set-up and exit path around a wait that cannot end:
+// both CTAs allocate the pair's TMEM, one warp per CTA waits on a local barrier and one on the
+// same barrier through the cluster-variant wait, and nothing ever arrives on it. The waits give
+// up after limit_ns, record KT_DEV_TIMEOUT in *status and raise the CTA's abort flag; the CTA
+// then drains as the GEMMs do after a timeout, meets its peer at the cluster barrier and frees
+// TMEM. No copy or MMA is issued, so nothing is in flight when the kernel ends.
+__global__ void __launch_bounds__(96, 1) kt_selftest_wait_kernel(int* status, uint64_t limit_ns) {
+  __shared__ __align__(8) uint64_t bar;
+  __shared__ uint32_t tmem_slot;
+  __shared__ int abort_word;
+  volatile int* abort_flag = &abort_word;
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  if (threadIdx.x == 0) {
+    kt_mbar_init(&bar, 1);  // one arrival expected, none made
+    *abort_flag = 0;
+    kt_fence_mbar_init();
+  }
+  kt_cluster_sync();
+  if (warp == 0) kt_tmem_alloc2(&tmem_slot, 512);
+  kt_tc_fence_before();
+  __syncthreads();
+  kt_tc_fence_after();
+  const uint32_t tmem = tmem_slot;
+  if (lane == 0) {
+    if (warp == 1) kt_mbar_wait_for(&bar, 0, status, abort_flag, limit_ns);
+    if (warp == 2) kt_mbar_wait_cluster_for(&bar, 0, status, abort_flag, limit_ns);
+  }
+  __syncwarp();
+  kt_tc_fence_before();
+  __syncthreads();
+  if (*abort_flag) kt_drain_ns(200000);
+  kt_cluster_sync();
+  if (warp == 0) {
+    kt_tc_fence_after();
+    kt_tmem_dealloc2(tmem, 512);
+  }
+}
+
+int kt_launch_selftest_wait(int* status, uint64_t limit_ns, cudaStream_t s) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2, 1, 1);
+  cfg.blockDim = dim3(96, 1, 1);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, kt_selftest_wait_kernel, status, limit_ns) != cudaSuccess) return -4;
+  return cudaGetLastError() == cudaSuccess ? 0 : -4;
 }
 
 int kt_gemm_tile_tokens() { return kTN; }

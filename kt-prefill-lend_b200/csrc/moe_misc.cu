@@ -238,6 +238,37 @@ int kt_launch_combine_sorted(const uint16_t* y, const int32_t* route_pos, const 
   return 0;
 }
 
+// ------------------------------------------------------------------ row gathers
+
+// one warp per row, 16 bytes per lane per step
+__global__ void kt_gather_rows_kernel(const uint16_t* __restrict__ src, int64_t cols, const int32_t* __restrict__ idx,
+                                      int64_t n, const int32_t* __restrict__ n_limit, uint16_t* __restrict__ dst) {
+  const int64_t lim = n_limit ? (int64_t)*n_limit : n;
+  const int64_t end = lim < n ? lim : n;
+  const int lane = threadIdx.x & 31;
+  const int64_t vec = cols / 8;
+  for (int64_t i = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) / 32; i < end;
+       i += (int64_t)gridDim.x * blockDim.x / 32) {
+    const int32_t j = idx[i];
+    uint4* d = reinterpret_cast<uint4*>(dst + i * cols);
+    if (j < 0) {
+      for (int64_t c = lane; c < vec; c += 32) d[c] = make_uint4(0, 0, 0, 0);
+    } else {
+      const uint4* sr = reinterpret_cast<const uint4*>(src + (int64_t)j * cols);
+      for (int64_t c = lane; c < vec; c += 32) d[c] = sr[c];
+    }
+  }
+}
+
+int kt_launch_gather_rows(const uint16_t* src, int64_t cols, const int32_t* idx, int64_t n, const int32_t* n_limit,
+                          uint16_t* dst, cudaStream_t s) {
+  if (n == 0) return 0;
+  if (cols % 8 || (((uintptr_t)src | (uintptr_t)dst) & 15)) return -1;
+  const int64_t warps = n < 148 * 64 ? n : 148 * 64;
+  kt_gather_rows_kernel<<<(unsigned)((warps + 7) / 8), 256, 0, s>>>(src, cols, idx, n, n_limit, dst);
+  return 0;
+}
+
 // ------------------------------------------------------------------ route (HotCache.route)
 
 __global__ void kt_route_kernel(const int32_t* __restrict__ ids, int64_t n, const int32_t* __restrict__ slot_tab,

@@ -42,6 +42,10 @@ SIGNATURES = {
     "kt_moe_a8_vec_multi": (_I, [_P, _I, _I64, _I64, _P, _I, _I, _P, _I64, _I, _I64, _P, _P, _SZ, _P]),
     "kt_moe_a8_vec_routes": (_I, [_P, _I, _I64, _I64, _P, _I, _I, _P, _I64, _I, _I64, _P, _P, _SZ, _P]),
     "kt_moe_a8_vec_multi_static": (_I, [_P, _I, _I64, _I64, _P, _I, _I, _P, _I64, _I, _I64, _P, _P]),
+    "kt_static_scratch_status": (_I, [_P, ctypes.POINTER(_I)]),
+    "kt_selftest_bounded_wait": (_I, [_P, _SZ, _I64, _P]),
+    "kt_moe_gemm_routes_workspace_size": (_SZ, [_I64, _I64, _I64, _I64, _I]),
+    "kt_moe_gemm_routes": (_I, [_P, _I64, _I64, _P, _I64, _P, _I, _I64, _I, _I, _P, _P, _SZ, _P]),
     "kt_ep_plan_workspace_size": (_SZ, [_I64, _I]),
     "kt_ep_plan": (_I, [_P, _P, _I64, _I64, _P, _P, _I, _I, _P, _P, _P, _P, _P, _SZ, _P]),
     "kt_ep_pack": (_I, [_P, _I64, _P, _I64, _P, _P]),

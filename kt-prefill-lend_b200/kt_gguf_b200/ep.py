@@ -218,11 +218,14 @@ class ExpertParallelMoE:
         k = topk_ids.shape[1]
         if self.world == 1 and x.is_cuda and self.shared_fn is None:
             # one rank: no exchange; the local slots straight from the logical ids
+            # ids outside [0, n_experts) are dropped, as kt_ep_plan drops them on the multi-rank path
             local = self.local.to(x.device, torch.int32)
             owned = self.owner.to(x.device) == 0
+            n = owned.numel()
             ids = topk_ids.long()
-            valid = (ids >= 0) & owned[ids.clamp(min=0)]
-            lid = torch.where(valid, local[ids.clamp(min=0)], torch.full_like(topk_ids, -1, dtype=torch.int32))
+            safe = ids.clamp(0, n - 1)
+            valid = (ids >= 0) & (ids < n) & owned[safe]
+            lid = torch.where(valid, local[safe], torch.full_like(topk_ids, -1, dtype=torch.int32))
             return self.expert_fn(x.contiguous(), lid.to(torch.int32).contiguous(),
                                   topk_weights.to(torch.float32).contiguous())
         C = min(self.chunks, max(1, T))

@@ -38,16 +38,46 @@ DENSE_MMV_Y = int(os.environ.get("KT_GGUF_DENSE_MMV_Y", "4"))
 DENSE_RPW = int(os.environ.get("KT_GGUF_DENSE_RPW", "1"))
 DENSE_MIN_ROWS = 513
 ROUTES = os.environ.get("KT_GGUF_MOE_ROUTES", "1") == "1"
-# ggml types this build has kernels for (Q8_0, Q4_K, Q6_K, IQ3_S)
-DENSE_TYPES = set(N.SUPPORTED_TYPES)
+# types the dense path is offered for (dense_ok), as the reference lists them
+# (hot/kt_gguf_moe_multi.py:48): the K-quants and i-quants of dense GGUF shards. dense_a8_vec
+# itself runs any GEMV type (SUPPORTED_TYPES), IQ2_XS, IQ1_M and Q2_0 included.
+DENSE_TYPES = {2, 3, 6, 7, 8, 10, 11, 12, 13, 14, 16, 18, 19, 20, 21, 22, 23}
+# types with a decode GEMV here: every type of the reference kernel's switch
+# (kt_gguf_moe_multi.cu:671-932) and its Q2_0
 SUPPORTED_TYPES = set(N.SUPPORTED_TYPES)
+# types of the tcgen05 prefill layer (Q8_0, Q4_K, Q6_K, IQ3_S)
 PREFILL_TYPES = set(N.PREFILL_TYPES)
 
 
+class _Op:
+    """One build configuration of the reference's extension, as `_load` returns it
+    (hot/kt_gguf_moe_multi.py:55-74): an object whose kt_moe_a8_vec_multi has the torch op's
+    signature and allocation contract (kt_gguf_moe_multi.cu:653-668): X [tokens, K] fp32 /
+    fp16 / bf16, W uint8 [E, row, row_bytes] (or, for a table build, the int64 table of slot
+    addresses), topk_ids int32 [tokens*top_k], returning a new Y [tokens*top_k, row] in X's
+    dtype. The window sizes of the reference's builds (mmv_y, rpw, KT_MAXM) have no meaning
+    here: one kernel serves every configuration with the same sums per route."""
+
+    def __init__(self, per_route: bool, table: bool):
+        self.per_route, self.table = per_route, table
+        self.lib = N.load()  # the C ABI library behind the op
+
+    def kt_moe_a8_vec_multi(self, X, W, topk_ids, top_k, type, row, tokens):  # noqa: A002 (the op's argument name)
+        entry = "kt_moe_a8_vec_routes" if self.per_route else "kt_moe_a8_vec_multi"
+        return _vec(entry, X, W, topk_ids, int(top_k), int(type), int(row), int(tokens), self.table)
+
+
+_ops: dict = {}
+
+
 def _load(mmv_y=None, rpw=None, per_route=False, table=False):
-    """The native library (the reference JIT-builds one extension per configuration; here
-    one prebuilt library serves every configuration)."""
-    return N.load()
+    """The op of one build configuration (the reference JIT-builds one extension per
+    (MAX_TOKENS, mmv_y, rpw, per_route, table); here one prebuilt library serves them all)."""
+    key = (bool(per_route), bool(table))
+    op = _ops.get(key)
+    if op is None:
+        op = _ops[key] = _Op(*key)
+    return op
 
 
 def enabled() -> bool:
@@ -199,3 +229,42 @@ def moe_prefill_ex(x, w13, w2, topk_ids, topk_weights, type13, type2, inter, tab
                                   int(acc_flags), None if to_acc else N.ptr(out), N.ptr(workspace), workspace.numel(),
                                   N.stream_of(x)), "kt_moe_prefill_ex")
     return acc if to_acc else out
+
+
+def moe_gemm_routes(X, W, ids, top_k, qtype, rows, tokens, table=False, workspace=None):
+    """moe_a8_vec_routes' contract on tensor cores (C ABI kt_moe_gemm_routes): Y [tokens*top_k,
+    rows] bf16, route p = W[ids[p]] . X[p // top_k] with bf16 activations, the GGUF weights
+    dequantized in shared memory to bf16 and fp32 accumulation; zero rows for ids < 0. Runs the
+    prefill layer's GEMM kernels for a single projection (prefill types; cols and rows
+    multiples of 256)."""
+    N.require_device(X)
+    if X.dtype != torch.bfloat16:
+        raise TypeError("moe_gemm_routes takes bf16 activations")
+    if qtype not in PREFILL_TYPES:
+        raise ValueError(f"ggml type {qtype}: the tensor-core path takes {sorted(PREFILL_TYPES)}")
+    if ids.dtype != torch.int32:
+        raise TypeError(f"topk ids must be int32 (got {ids.dtype})")
+    X = X.contiguous()
+    ids = ids.contiguous()
+    cols = X.shape[1]
+    if tokens > X.shape[0] or ids.numel() < tokens * top_k:
+        raise ValueError("tokens / top_k exceed X or ids")
+    if table:
+        if W.dtype != torch.int64 or W.dim() != 1:
+            raise TypeError("with table=True, W must be a 1-D int64 table of slot addresses")
+        n_slots = W.numel()
+    else:
+        if W.dtype != torch.uint8 or W.dim() != 3 or W.shape[1] != rows or W.shape[2] != N.row_bytes(qtype, cols):
+            raise TypeError("W must be a uint8 [slots, rows, row_bytes(cols)] GGUF tensor")
+        n_slots = W.shape[0]
+    Y = torch.empty((tokens * top_k, rows), dtype=torch.bfloat16, device=X.device)
+    if tokens == 0:
+        return Y
+    lib = N.load()
+    need = lib.kt_moe_gemm_routes_workspace_size(tokens, top_k, cols, rows, n_slots)
+    if workspace is None or workspace.numel() < need:
+        workspace = N.workspace(need, X.device)
+    N.check(lib.kt_moe_gemm_routes(N.ptr(X), tokens, cols, N.ptr(ids), top_k, N.ptr(W.contiguous()), qtype, rows,
+                                   int(table), n_slots, N.ptr(Y), N.ptr(workspace), workspace.numel(), N.stream_of(X)),
+            "kt_moe_gemm_routes")
+    return Y

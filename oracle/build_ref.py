@@ -7,7 +7,7 @@ KT_MMV_Y=2, KT_RPW=4) and the per-route build (KT_PER_ROUTE=1). The resulting Py
 modules travel to the GPU box with the tree; load() imports them there without the
 reference sources. Nothing in the product imports them.
 
-Usage: python oracle/build_ref.py
+Usage: KT_REFERENCE_ROOT=<reference checkout> python oracle/build_ref.py
 """
 import importlib.util
 import os
@@ -16,7 +16,9 @@ from pathlib import Path
 
 HERE = Path(__file__).resolve().parent
 OUT = HERE / "_ref"
-REF_DIR = Path(os.environ.get("KT_REFERENCE_ROOT", "/root/reference")) / "hot" / "kt_gguf_moe_multi"
+# the reference checkout is named by KT_REFERENCE_ROOT; without it nothing is built
+_ROOT = os.environ.get("KT_REFERENCE_ROOT")
+REF_DIR = Path(_ROOT) / "hot" / "kt_gguf_moe_multi" if _ROOT else None
 VARIANTS = {
     "kt_ref_window": ["-DKT_MAXM=4", "-DKT_MMV_Y=2", "-DKT_RPW=4", "-DKT_PER_ROUTE=0", "-DKT_PTR_TABLE=0"],
     "kt_ref_routes": ["-DKT_MAXM=4", "-DKT_MMV_Y=2", "-DKT_RPW=4", "-DKT_PER_ROUTE=1", "-DKT_PTR_TABLE=0"],
@@ -28,7 +30,7 @@ def _so(name: str) -> Path:
 
 
 def build(variants=None) -> None:
-    if not REF_DIR.exists():
+    if REF_DIR is None or not REF_DIR.exists():
         return
     names = [n for n in (variants or VARIANTS) if not _so(n).exists()]
     if not names:

@@ -86,6 +86,34 @@ def test_argument_errors_before_any_launch():
     assert lib.kt_moe_prefill(P(16), 16, 2048, 512, P(16), P(16), 8, P(16), 12, P(16), 14, 0, 8193, P(16), P(16),
                               1 << 40, None) == N.KT_ERR_ARG
     assert lib.kt_topk_softmax(None, 0, 256, 8, 0, None, None, None) == N.KT_OK
+    # the per-route tensor-core projection: prefill types only, sizes in multiples of 256
+    assert lib.kt_moe_gemm_routes(P(16), 4, 2048, P(16), 2, P(16), 10, 512, 0, 4, P(16), P(16), 1 << 40,
+                                  None) == N.KT_ERR_TYPE
+    assert lib.kt_moe_gemm_routes(P(16), 4, 2000, P(16), 2, P(16), 12, 512, 0, 4, P(16), P(16), 1 << 40,
+                                  None) == N.KT_ERR_ARG
+    assert lib.kt_moe_gemm_routes(P(16), 4, 2048, P(16), 2, P(16), 12, 500, 0, 4, P(16), P(16), 1 << 40,
+                                  None) == N.KT_ERR_ARG
+    assert lib.kt_moe_gemm_routes(P(16), 4, 2048, P(16), 2, P(16), 12, 512, 0, 4, P(16), P(16), 64,
+                                  None) == N.KT_ERR_WORKSPACE
+    assert lib.kt_moe_gemm_routes(None, 0, 2048, None, 2, None, 12, 512, 0, 4, None, None, 0, None) == N.KT_OK
+    assert lib.kt_moe_gemm_routes_workspace_size(64, 2, 512, 512, 4) >= 128 * (512 + 512) * 2
+    # the bounded-wait self-test: limits from 1 ms to 2 s, a workspace for the status word
+    assert lib.kt_selftest_bounded_wait(None, 256, 5_000_000, None) == N.KT_ERR_ARG
+    assert lib.kt_selftest_bounded_wait(P(256), 256, 10, None) == N.KT_ERR_ARG
+    assert lib.kt_selftest_bounded_wait(P(256), 256, 3_000_000_000, None) == N.KT_ERR_ARG
+    # the static scratch's status word needs somewhere to go
+    assert lib.kt_static_scratch_status(None, None) == N.KT_ERR_ARG
+
+
+def test_load_and_dense_types_follow_the_reference_module():
+    from kt_gguf_b200 import kt_gguf_moe_multi as M
+
+    # hot/kt_gguf_moe_multi.py:48
+    assert M.DENSE_TYPES == {2, 3, 6, 7, 8, 10, 11, 12, 13, 14, 16, 18, 19, 20, 21, 22, 23}
+    assert M.DENSE_TYPES <= M.SUPPORTED_TYPES and M.PREFILL_TYPES <= M.SUPPORTED_TYPES
+    op = M._load()
+    assert op is M._load(2, 4) and op is not M._load(per_route=True) and M._load(table=True).table
+    assert callable(op.kt_moe_a8_vec_multi) and hasattr(op.lib, "kt_moe_a8_vec_multi")
 
 
 def test_python_front_rejects_cpu_tensors():
@@ -98,3 +126,5 @@ def test_python_front_rejects_cpu_tensors():
     ids = torch.zeros((2,), dtype=torch.int32)
     with pytest.raises(ValueError, match="CUDA"):
         M.moe_a8_vec_multi(x, W, ids, 1, 12, 8, 2)
+    with pytest.raises(ValueError, match="CUDA"):
+        M._load().kt_moe_a8_vec_multi(x, W, ids, 1, 12, 8, 2)

@@ -1,4 +1,11 @@
-"""GGUF formats and the CPU oracle's dequantizers against the golden vectors (no GPU)."""
+"""GGUF formats and the CPU oracle's dequantizers against the golden vectors (no GPU).
+
+The library's code books are pinned to the reference's tables (hot/kt_gguf_moe_multi/
+ggml-common.h) through committed SHA-256 digests (tests/golden/make_reference_digests.py);
+with KT_REFERENCE_ROOT set to a reference checkout the tables are also compared directly."""
+import hashlib
+import json
+import os
 import re
 from pathlib import Path
 
@@ -11,7 +18,15 @@ GOLDEN = np.load(Path(__file__).with_name("golden") / "gguf_dequant.npz")
 TYPES = (8, 12, 14, 21)
 # the GEMV's wider type switch: 32-value blocks and the K-quants Q2_K / Q3_K / Q5_K / IQ4_XS
 LEGACY = (2, 3, 6, 7, 20, 10, 11, 13, 23, 42, 16, 17, 18, 19, 22, 29)  # Q2_0 and the code-book i-quants too
-REF_COMMON = Path("/root/reference/hot/kt_gguf_moe_multi/ggml-common.h")
+DIGESTS = json.loads((Path(__file__).with_name("golden") / "reference_table_digests.json").read_text())
+_REF_ROOT = os.environ.get("KT_REFERENCE_ROOT")
+REF_COMMON = Path(_REF_ROOT) / "hot" / "kt_gguf_moe_multi" / "ggml-common.h" if _REF_ROOT else None
+needs_reference = pytest.mark.skipif(REF_COMMON is None or not REF_COMMON.exists(),
+                                     reason="KT_REFERENCE_ROOT does not name a reference checkout")
+
+
+def _digest(a: np.ndarray) -> str:
+    return hashlib.sha256(np.ascontiguousarray(a).astype(a.dtype.newbyteorder("<")).tobytes()).hexdigest()
 
 
 def test_block_sizes_known_answers():
@@ -45,7 +60,20 @@ def test_iq3s_grid_matches_golden_and_header():
     assert importlib.util.find_spec("gguf") is not None
 
 
-@pytest.mark.skipif(not REF_COMMON.exists(), reason="reference tree not mounted")
+def test_code_books_match_reference_digests():
+    # the device code books in the form the reference's tables hold them: iq3s / iq3xxs as uint32,
+    # iq2xxs / iq2xs / iq2s as uint64 (byte j = element j), iq1s_grid_gpu in its nibble form
+    words = {"iq3s_grid": GOLDEN["iq3s_grid"].astype(np.uint32), "iq3xxs_grid": _header_words("IQ3XXS")}
+    for name, key in (("iq2xxs_grid", "IQ2XXS"), ("iq2xs_grid", "IQ2XS"), ("iq2s_grid", "IQ2S")):
+        words[name] = _header_words(key).view(np.uint64)
+    words["iq1s_grid_gpu"] = _header_words("IQ1S").astype(np.uint64)
+    for name, arr in words.items():
+        want = DIGESTS[name]
+        assert arr.dtype.name == want["dtype"] and arr.size == want["count"], name
+        assert _digest(arr) == want["sha256"], name
+
+
+@needs_reference
 def test_iq3s_grid_matches_reference_table():
     # the reference's own codebook (ggml-common.h:598-665), read as text
     src = REF_COMMON.read_text()
@@ -80,7 +108,7 @@ def test_iquant_books_match_gguf_py():
     assert all(int(ks[i]) == i | ((bin(i).count("1") & 1) << 7) for i in range(128))
 
 
-@pytest.mark.skipif(not REF_COMMON.exists(), reason="reference tree not mounted")
+@needs_reference
 def test_iquant_books_match_reference_tables():
     # the reference's ggml-common.h tables (read as text): iq2xxs_grid, iq2xs_grid, iq2s_grid
     # (uint64, byte j = element j), iq3xxs_grid, and iq1s_grid_gpu (the nibble form)

@@ -137,16 +137,49 @@ def test_gemv_many_routes_per_slot(cuda_device):
     close_enough(bits(y), want)
 
 
-def test_dense_a8_vec(cuda_device):
-    qtype, cols, rows = 14, 512, 1536
-    rng = np.random.default_rng(5)
-    W = synth.quantize(rng.standard_normal((rows, cols), dtype=np.float32) * 0.02, qtype)
-    x = torch.randn((3, cols), generator=torch.Generator().manual_seed(5)).to(torch.bfloat16)
-    want = _oracle_gemv(qtype, W[None], x, torch.zeros(3, dtype=torch.int32), 1, rows, cols)
-    assert M.dense_ok(x, torch.from_numpy(W), qtype)
+# every type dense_ok offers (the reference's DENSE_TYPES) and the three the GEMV adds
+# (IQ2_XS, IQ1_M, Q2_0: dense_a8_vec runs them, dense_ok does not offer them)
+@pytest.mark.parametrize("qtype", sorted(M.DENSE_TYPES) + [17, 29, 42])
+@pytest.mark.parametrize("tokens", [2, 4])
+def test_dense_a8_vec(cuda_device, qtype, tokens):
+    cols, rows = (512 if qtype in (6, 11, 14) else 2048), 640
+    rng = np.random.default_rng(5 + qtype)
+    if qtype in TYPES:
+        W = synth.quantize(rng.standard_normal((rows, cols), dtype=np.float32) * 0.02, qtype)
+    else:
+        W = synth.random_blocks(rng, qtype, rows, cols)
+    x = torch.randn((tokens, cols), generator=torch.Generator().manual_seed(5)).to(torch.bfloat16)
+    want = _oracle_gemv(qtype, W[None], x, torch.zeros(tokens, dtype=torch.int32), 1, rows, cols)
+    assert M.dense_ok(x, torch.from_numpy(W), qtype) == (qtype in M.DENSE_TYPES)
     y = M.dense_a8_vec(x.to(cuda_device), torch.from_numpy(W).to(cuda_device), qtype)
-    assert y.shape == (3, rows)
+    assert y.shape == (tokens, rows)
     close_enough(bits(y), want)
+    # the reference's own route to it: the one-slot MoE op of the dense build
+    # (hot/kt_gguf_moe_multi.py:103-112)
+    zero_ids = torch.zeros(tokens, dtype=torch.int32, device=cuda_device)
+    Wd = torch.from_numpy(W).to(cuda_device)
+    y_op = M._load(M.DENSE_MMV_Y, M.DENSE_RPW).kt_moe_a8_vec_multi(x.to(cuda_device), Wd.view(1, rows, -1), zero_ids,
+                                                                    1, qtype, rows, tokens)
+    assert torch.equal(y_op.view(tokens, rows), y)
+
+
+@pytest.mark.parametrize("per_route,table", [(False, False), (True, False), (False, True)])
+def test_load_returns_the_reference_op(cuda_device, per_route, table):
+    # _load(...).kt_moe_a8_vec_multi(X, W, ids, top_k, type, row, tokens): the op signature of
+    # kt_gguf_moe_multi.cu:653-660, a new Y per call, the same sums as the module functions
+    qtype, cols, rows, slots, tokens, top_k = 12, 2048, 512, 6, 3, 8
+    W, x, ids = _gemv_case(qtype, cols, rows, slots, tokens, top_k, seed=21)
+    Wd = torch.from_numpy(W).to(cuda_device)
+    xd, idd = x.to(cuda_device), ids.reshape(-1).to(cuda_device)
+    want = M.moe_a8_vec_multi(xd, Wd, idd, top_k, qtype, rows, tokens)
+    Warg = torch.tensor([Wd[s].data_ptr() for s in range(slots)], dtype=torch.int64, device=cuda_device) if table \
+        else Wd
+    op = M._load(per_route=per_route, table=table)
+    y1 = op.kt_moe_a8_vec_multi(xd, Warg, idd, top_k, qtype, rows, tokens)
+    y2 = op.kt_moe_a8_vec_multi(xd, Warg, idd, top_k, qtype, rows, tokens)
+    assert y1.shape == (tokens * top_k, rows) and y1.dtype == xd.dtype
+    assert y1.data_ptr() != y2.data_ptr()  # a new output per call, as the op allocates one
+    assert torch.equal(y1, want) and torch.equal(y2, want)
 
 
 def test_silu_and_mul_and_combine(cuda_device):

@@ -61,8 +61,9 @@ def test_window_kernel_vs_reference(cuda_device, ref_mods, qtype, cols, rows, to
     mismatch = (gb != rb).mean()
     print(f"\nREFPIN type={qtype} cols={cols} rows={rows} tokens={tokens} top_k={top_k}: "
           f"oracle!=ref {(ob != rb).mean():.2e}  b200!=ref {mismatch:.2e}  b200!=oracle {(gb != ob).mean():.2e}")
-    assert mismatch < 2e-3, mismatch
-    assert O.rel_l2(O.bf16_to_f32(gb), O.bf16_to_f32(rb)) < 1e-3
+    # the B200 GEMV keeps the reference's per-chunk arithmetic, lane order and butterfly:
+    # every output bit-identical to the reference kernel's
+    assert torch.equal(y, y_ref), f"{mismatch:.2e} of the outputs differ"
 
 
 @pytest.mark.parametrize("qtype,cols,rows", [(2, 2048, 512), (3, 2048, 512), (6, 512, 1024), (7, 2048, 512),
@@ -90,8 +91,8 @@ def test_legacy_blocks_vs_reference(cuda_device, ref_mods, qtype, cols, rows, to
     ob, rb, gb = O.f32_to_bf16(want), bits(y_ref), bits(y)
     print(f"\nREFPIN type={qtype} cols={cols} rows={rows} tokens={tokens} top_k={top_k}: "
           f"oracle!=ref {(ob != rb).mean():.2e}  b200!=ref {(gb != rb).mean():.2e}")
-    assert (ob != rb).mean() < 2e-3 and (gb != rb).mean() < 2e-3
-    assert O.rel_l2(O.bf16_to_f32(gb), O.bf16_to_f32(rb)) < 1e-3
+    assert (ob != rb).mean() < 2e-3  # the oracle: multiply-add contraction in the last fp32 bit
+    assert torch.equal(y, y_ref), f"{(gb != rb).mean():.2e} of the outputs differ"
 
 
 @pytest.mark.parametrize("qtype,cols,rows", [(12, 2048, 1024), (21, 512, 2048)])
@@ -106,7 +107,7 @@ def test_per_route_build_at_prefill_size(cuda_device, ref_mods, qtype, cols, row
     xd, Wd, idd = x.to(cuda_device), torch.from_numpy(W).to(cuda_device), ids.reshape(-1).to(cuda_device)
     y_ref = routes.kt_moe_a8_vec_multi(xd, Wd, idd, top_k, qtype, rows, tokens)
     y = M.moe_a8_vec_routes(xd, Wd, idd, top_k, qtype, rows, tokens)
-    assert (bits(y) != bits(y_ref)).mean() < 2e-3
+    assert torch.equal(y, y_ref), f"{(bits(y) != bits(y_ref)).mean():.2e} of the outputs differ"
 
 
 # (name, ggml type of the projection, layer) for the decode timing: config 2's gate/up (Q4_K) and

@@ -5,8 +5,10 @@ a CUDA graph capture with a frozen memory pool, host frameworks that own all of 
 memory, C callers without an allocator — and runs on a fixed 2 MiB scratch array inside the
 library instead of a caller workspace. Checked through the C ABI against the workspace entry
 point on two calls in a row (the second with different inputs, so stale scratch from the
-first call would show), plus the size limit. Collected last so that a run stopping at the
-first failure has run every other test already.
+first call would show), at route counts on both sides of the one-warp route grouping (up to
+32 routes) and the block-wide grouping above it, plus the size limit and the status word
+(kt_static_scratch_status). Collected last so that a run stopping at the first failure has run
+every other test already.
 """
 import ctypes
 
@@ -33,14 +35,23 @@ def _call_workspace(lib, x, w, ids, top_k, qtype, rows, n_slots, y):
                                    rows, Nt.ptr(y), Nt.ptr(ws), ws.numel(), torch.cuda.current_stream().cuda_stream)
 
 
+def _static_status(lib):
+    st = ctypes.c_int(-1)
+    assert lib.kt_static_scratch_status(torch.cuda.current_stream().cuda_stream, ctypes.byref(st)) == Nt.KT_OK
+    return st.value
+
+
+# (4, 3) tokens x top_k 8 = 32 / 24 routes: one-warp grouping; (16, 12) x 8 = 128 / 96 routes:
+# the block-wide grouping with its shared-memory counters
+@pytest.mark.parametrize("token_counts", [(4, 3), (16, 12)])
 @pytest.mark.parametrize("qtype,cols,rows", [(12, 2048, 1024), (21, 512, 2048)])
-def test_static_scratch_matches_workspace_entry_point(cuda_device, qtype, cols, rows):
+def test_static_scratch_matches_workspace_entry_point(cuda_device, qtype, cols, rows, token_counts):
     lib = Nt.load()
     rng = np.random.default_rng(qtype)
     slots, top_k = 8, 8
     W = torch.from_numpy(np.stack([synth.quantize(rng.standard_normal((rows, cols), dtype=np.float32) * 0.02, qtype)
                                    for _ in range(slots)])).to(cuda_device)
-    for call, tokens in enumerate((4, 3)):  # two calls in a row, different inputs and sizes
+    for call, tokens in enumerate(token_counts):  # two calls in a row, different inputs and sizes
         x = torch.randn((tokens, cols), generator=torch.Generator().manual_seed(call)).to(torch.bfloat16).to(cuda_device)
         ids = torch.from_numpy(np.stack([rng.permutation(slots)[:top_k] for _ in range(tokens)]).astype(np.int32))
         ids[0, 0] = -1  # a route on the CPU: zero row
@@ -53,6 +64,7 @@ def test_static_scratch_matches_workspace_entry_point(cuda_device, qtype, cols, 
         # same kernels, same arithmetic: bit-identical (the GEMV tests bound it vs the oracle)
         assert torch.equal(y_static, y_ws), f"call {call}"
         assert torch.all(y_static[0] == 0)
+        assert _static_status(lib) == Nt.KT_DEV_OK
 
 
 def test_static_scratch_rejects_oversized_calls(cuda_device):
