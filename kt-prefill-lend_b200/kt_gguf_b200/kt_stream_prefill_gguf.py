@@ -24,7 +24,11 @@ KT_GPU_STREAM_GROUP (experts per group; default 32 here, 8 in the reference: on 
 config 2's 192 streamed experts, groups of 8 / 16 / 32 reached 0.89 / 0.96 / 0.99 of a plain
 pinned copy of the same bytes, the smaller groups losing to per-group copy and launch gaps;
 two slots of 32 such experts are 128 MB), KT_GPU_STREAM_TIMING,
-KT_GPU_STREAM_EARLY_INIT. The reference's per-group CUDA graphs (and the row padding,
+KT_GPU_STREAM_EARLY_INIT, and KT_GPU_STREAM_SELFTEST=2: the first streamed layer of the process
+is recomputed by an independent path (each used expert's bank bytes dequantized on the GPU
+by kt_gguf_dequantize, then plain fp32 matmuls, SwiGLU and the weighted sum in torch) and the
+rel-L2 and cosine of the streamed output against it are logged and kept in `last_check` (the
+reference's _reference_check, its in-serving numerical guard on this path). The reference's per-group CUDA graphs (and the row padding,
 KT_GPU_STREAM_ROW_STEP, that keeps their count small) are not needed: a group is four
 kernel launches through the C ABI.
 """
@@ -42,6 +46,7 @@ STREAM_THRESHOLD = int(os.environ.get("KT_GPU_STREAM_PREFILL", "0") or 0)
 GROUP_SIZE = int(os.environ.get("KT_GPU_STREAM_GROUP", "32") or 32)
 TIMING = os.environ.get("KT_GPU_STREAM_TIMING") == "1"
 EARLY_INIT = os.environ.get("KT_GPU_STREAM_EARLY_INIT", "0") == "1"
+SELFTEST = os.environ.get("KT_GPU_STREAM_SELFTEST", "0")
 
 
 def _log(msg: str):
@@ -86,6 +91,7 @@ class KTStreamPrefillGGUF:
         self._workspace = None
         self.calls = 0
         self.bytes_staged = 0
+        self.last_check: Optional[dict] = None  # the self-check's result (KT_GPU_STREAM_SELFTEST=2)
 
     # -- geometry -----------------------------------------------------------
 
@@ -240,11 +246,47 @@ class KTStreamPrefillGGUF:
             if gi + 1 < len(groups):
                 self._stage(layer_idx, gi + 1, groups[gi + 1][0], groups[gi + 1][1], stats)
         self.calls += 1
+        if SELFTEST == "2" and self.last_check is None:
+            self._self_check(layer_idx, first, g, out)
         if TIMING:
             cur.synchronize()
             _log(f"rank {self.rank} layer {layer_idx} tokens={T} groups={len(groups)} dma_enq={stats['dma_enq'] * 1e3:.1f}ms "
                  f"enq={stats['enq'] * 1e3:.1f}ms total={(time.perf_counter() - t0) * 1e3:.1f}ms")
         return out
+
+
+    # -- self-check ---------------------------------------------------------
+
+    def _self_check(self, layer_idx: int, first: int, g: dict, out: torch.Tensor) -> dict:
+        """The streamed experts' output of this call recomputed from the bank bytes by an
+        independent path: each used expert dequantized on the GPU to fp32 (kt_gguf_dequantize,
+        bit-exact to ggml), then fp32 matmuls, SwiGLU and the fp32 weighted sum in torch."""
+        from . import kernels as Kn
+
+        torch.cuda.current_stream(self.device).synchronize()
+        (type13, type2), _ = self._geometry(layer_idx)
+        banks = self._bank(layer_idx)
+        x, ids, w = g["x"].float(), g["ids"].long(), g["w"]
+        ref = torch.zeros((x.shape[0], self.K), dtype=torch.float32, device=x.device)
+        used = 0
+        for e in range(first, self.E):
+            tok, kk = torch.where(ids == e)
+            if tok.numel() == 0:
+                continue
+            used += 1
+            w13 = Kn.gguf_dequantize(banks[0][e].to(x.device).view(2 * self.N, -1), type13, self.K, torch.float32)
+            w2 = Kn.gguf_dequantize(banks[1][e].to(x.device).view(self.K, -1), type2, self.N, torch.float32)
+            xe = x[tok]
+            h = torch.nn.functional.silu(xe @ w13[:self.N].t()) * (xe @ w13[self.N:].t())
+            ref.index_add_(0, tok, (h @ w2.t()) * w[tok, kk].unsqueeze(1))
+        got = out.float()
+        rel = float((got - ref).norm() / ref.norm().clamp_min(1e-30))
+        cos = float(torch.nn.functional.cosine_similarity(got.flatten(), ref.flatten(), dim=0))
+        self.last_check = {"layer": layer_idx, "tokens": int(x.shape[0]), "experts_used": used, "rel_l2": rel,
+                           "cosine": cos}
+        _log(f"rank {self.rank}: self-check layer {layer_idx}, {x.shape[0]} tokens, {used} streamed experts: "
+             f"rel-L2 {rel:.2e}, cosine {cos:.6f} against fp32 dequant + matmul")
+        return self.last_check
 
 
 _instance: Optional[KTStreamPrefillGGUF] = None

@@ -142,3 +142,69 @@ def test_hot_cache_route_on_gpu(cuda_device):
         assert torch.equal(cpu.cpu(), c.log2cpu_cpu[0][ids.long()])
         hist = torch.bincount(ids.reshape(-1).long(), minlength=E).float()
         assert torch.equal((c.counts - before)[0].cpu(), hist)
+
+
+class _DecodeMode:
+    @staticmethod
+    def is_decode():
+        return True
+
+    @staticmethod
+    def is_target_verify():
+        return False
+
+
+def test_dynamic_swap_then_layer_matches_oracle(cuda_device, tmp_path, monkeypatch):
+    # The whole decode-adaptive path on a real GGUF file: the hot method loads experts 0 and 1
+    # into its two slots; decode routes make expert 4 hot; before_forward swaps it in (the counts
+    # of a policy round come back one round late); then the layer, routed through the cache's
+    # tables, must equal the oracle on the logical experts that are now resident.
+    from gguf_fixture import E, INTER, K, write_gguf
+
+    monkeypatch.setattr(C, "INTERVAL", 1)
+    monkeypatch.setattr(C, "KV_LEND", False)
+    path = tmp_path / "experts.gguf"
+    data = write_gguf(path, seed=7)
+    H._readers.pop(str(path), None)
+    kt = SimpleNamespace(num_gpu_experts=2, weight_path=str(path), layer_idx=0, num_layers=1)
+    layer = torch.nn.Module()
+    layer.moe_tp_rank, layer.moe_tp_size = 0, 1
+    m = H.KTGGUFHotExpertsMethod(kt, layer)
+    m.create_weights(layer, 2, K, INTER, torch.bfloat16)
+    m.process_weights_after_loading(layer)
+    dev = cuda_device
+    c = C.HotCache(1, E, 2, dev, 0)
+    c.layers[0] = (m, layer)
+    c.seed(None)
+    assert c.slot2log[0] == [0, 1]
+    g = torch.Generator().manual_seed(5)
+    hot = torch.tensor([[4, 0], [4, 2], [4, 5], [3, 4]], dtype=torch.int32).to(dev)
+    batch = SimpleNamespace(forward_mode=_DecodeMode())
+    for _ in range(3):
+        c.route(0, hot)  # expert 4: 4 routes a step; expert 0: 1; expert 1: none
+        c.before_forward(batch)
+    torch.cuda.synchronize()
+    assert c.swaps >= 1 and 4 in c.slot2log[0] and c.check_tables() == ""
+    s4 = c.slot2log[0].index(4)
+    assert s4 == 1  # the colder slot (expert 1) gave way
+    w13_all = np.concatenate([data[(0, "gate")], data[(0, "up")]], axis=1)
+    w2_all = data[(0, "down")]
+    assert torch.equal(layer.w13_qweight[s4].cpu(), torch.from_numpy(w13_all[4]))
+    assert torch.equal(layer.w2_qweight[s4].cpu(), torch.from_numpy(w2_all[4]))
+    for T in (4, 256):  # a decode window (GEMV path) and a prefill chunk (tcgen05 path)
+        logical = torch.stack([torch.randperm(E, generator=g)[:2] for _ in range(T)]).to(torch.int32)
+        slot_ids, cpu_ids = c.route(0, logical.to(dev))
+        x = torch.randn((T, K), generator=g).to(torch.bfloat16)
+        w = torch.rand((T, 2), generator=g)
+        d = SimpleNamespace(hidden_states=x.to(dev), topk_output=(w.to(dev), slot_ids, None))
+        out = m.apply(layer, d).hidden_states.float().cpu().numpy()
+        res = slot_ids.cpu() >= 0
+        assert torch.equal(res, cpu_ids.cpu() < 0)  # each route on exactly one side
+        masked = torch.where(res, logical, torch.full_like(logical, -1)).numpy()
+        xb = x.view(torch.int16).numpy().view(np.uint16)
+        if T == 4:
+            want = O.bf16_to_f32(O.moe_ref_bf16(xb, masked, w.numpy(), 12, w13_all, 14, w2_all, INTER))
+            assert O.rel_l2(out, want) <= TOL_REF_LAYER
+        else:
+            want = O.moe_fp32(xb, masked, w.numpy(), 12, w13_all, 14, w2_all, INTER)
+            assert O.rel_l2(out, want) <= TOL_FP32_ORACLE

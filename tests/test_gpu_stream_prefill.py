@@ -156,3 +156,19 @@ def test_nothing_to_stream(cuda_device, layer40):
     out = sp.run(m, None, dispatch(L, cuda_device), L.topk_ids.to(cuda_device))
     torch.cuda.synchronize()
     assert torch.count_nonzero(out) == 0 and sp.bytes_staged == 0
+
+
+def test_stream_self_check_reports_parity(cuda_device, layer40, monkeypatch):
+    # KT_GPU_STREAM_SELFTEST=2: the first streamed layer is recomputed by fp32 dequant + matmul
+    # (the reference's _reference_check) and the result kept; later calls do not check again
+    monkeypatch.setattr(SP, "SELFTEST", "2")
+    L = layer40
+    sp = SP.KTStreamPrefillGGUF(method_for(L, 8), group_size=16)
+    out = sp.run(method_for(L, 8), None, dispatch(L, cuda_device), L.topk_ids.to(cuda_device))
+    chk = sp.last_check
+    assert chk is not None and chk["experts_used"] == 32 and chk["tokens"] == L.x.shape[0]
+    assert chk["rel_l2"] <= TOL_FP32_ORACLE and chk["cosine"] > 0.9999
+    want = oracle_streamed(L, 8)
+    assert O.rel_l2(out.float().cpu().numpy(), want) <= TOL_FP32_ORACLE
+    sp.run(method_for(L, 8), None, dispatch(L, cuda_device), L.topk_ids.to(cuda_device))
+    assert sp.last_check is chk

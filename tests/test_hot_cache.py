@@ -196,3 +196,151 @@ def test_row_bytes_and_block_table():
         H._row_bytes(100, 12)
     assert H.MMVQ_TYPES == {2, 3, 6, 7, 8, 10, 11, 12, 13, 14, 16, 17, 18, 19, 20, 21, 22, 23, 29}
     assert all(H.BLOCK_INFO[t] == O.BLOCK[t] for t in H.MMVQ_TYPES | {42})
+
+
+class CountingReader(FakeReader):
+    def __init__(self):
+        super().__init__()
+        self.calls = 0
+
+    def slice(self, li, proj, N, rank, experts):
+        self.calls += 1
+        return super().slice(li, proj, N, rank, experts)
+
+
+def test_own_bank_is_built_once_per_layer(monkeypatch):
+    c = make_cache(monkeypatch=monkeypatch)
+    rd = CountingReader()
+    for li in range(L):
+        c.layers[li][0].reader = rd
+    c.seed(None)
+    for e in (9, 10, 11):
+        c._set(0, 1, e)
+        c.fill(0, 1, e)
+        assert slot_bytes(c, 0, 1) == expect_bytes(0, e)
+    assert rd.calls == 3  # gate, up, down of layer 0, once
+    assert c._bank(0).source == "own"
+
+
+def test_banks_shared_with_the_streamer(monkeypatch):
+    # with the GGUF streamer loaded, fills read its pinned banks (one copy of every expert for
+    # both); KT_HOT_BANKS=own keeps the cache's own
+    from kt_gguf_b200 import kt_stream_prefill_gguf as G
+
+    class FakeStreamer:
+        def _bank(self, li):
+            w13 = torch.full((E, 2 * N_INTER * ROWB13), 200 + li, dtype=torch.uint8)
+            w2 = torch.full((E, 2 * N_INTER * ROWB2), 210 + li, dtype=torch.uint8)
+            return [w13, w2]
+
+    monkeypatch.setattr(G, "_instance", FakeStreamer())
+    c = make_cache(monkeypatch=monkeypatch)
+    rd = CountingReader()
+    c.layers[1][0].reader = rd
+    c.seed(None)
+    c._set(1, 2, 12)
+    c.fill(1, 2, 12)
+    assert slot_bytes(c, 1, 2) == (201, 201, 211) and rd.calls == 0
+    assert c._bank(1).source == "streamer"
+    monkeypatch.setattr(C, "OWN_BANKS", "own")
+    c2 = make_cache(monkeypatch=monkeypatch)
+    c2.seed(None)
+    c2._set(1, 2, 12)
+    c2.fill(1, 2, 12)
+    assert slot_bytes(c2, 1, 2) == expect_bytes(1, 12)
+
+
+def test_fill_writes_the_lend_mirror(monkeypatch):
+    # a resident slot's new expert also goes to the host mirror the weight return restores from
+    # (hot/kt_hot_cache.py:207-226, 264-270); lent slots have no mirror
+    c = make_cache(kv_lend=True, monkeypatch=monkeypatch)
+    c.seed(None)
+    _m, layer = c.layers[0]
+    m13, m2 = torch.zeros_like(layer.w13_qweight), torch.zeros_like(layer.w2_qweight)
+    c.register_mirror(layer.w13_qweight, m13)
+    c.register_mirror(layer.w2_qweight, m2)
+    with pytest.raises(ValueError):
+        c.register_mirror(layer.w2_qweight, torch.zeros(3, dtype=torch.uint8))
+    c._set(0, 3, 14)
+    c.fill(0, 3, 14)
+    g, u, d = expect_bytes(0, 14)
+    assert bool((m13[3, :N_INTER] == g).all() and (m13[3, N_INTER:] == u).all() and (m2[3] == d).all())
+    assert bool((m13[:3] == 0).all())
+    v13 = torch.zeros((2 * N_INTER, ROWB13), dtype=torch.uint8)
+    v2 = torch.zeros((2 * N_INTER, ROWB2), dtype=torch.uint8)
+    c.lend_slot(0, NS, v13, v2)
+    before = m13.clone()
+    c._set(0, NS, 15)
+    c.fill(0, NS, 15)
+    assert torch.equal(m13, before) and slot_bytes(c, 0, NS) == expect_bytes(0, 15)
+
+
+def test_q2_0_down_bank_is_repacked_once(monkeypatch):
+    # a layer whose Q2_0 downs are kept as their Q8_0 repack: the whole down bank is repacked
+    # once (hot/kt_hot_cache.py:228-243), each fill copies from it
+    rng = np.random.default_rng(1)
+    n_blk = 4  # Q2_0 blocks per down row (256 values)
+    down_raw = rng.integers(0, 256, size=(E, 2 * N_INTER, n_blk * 18), dtype=np.uint8)
+    down_raw.reshape(-1, 18)[:, 1] &= 0x3B  # finite fp16 scales
+
+    class Q2Reader(FakeReader):
+        def slice(self, li, proj, N, rank, experts):
+            if proj != "down":
+                return super().slice(li, proj, N, rank, experts)
+            return torch.from_numpy(down_raw[experts.numpy()])
+
+    monkeypatch.setattr(C, "KV_LEND", False)
+    c = C.HotCache(1, E, NS, torch.device("cpu"), 0)
+    method = SimpleNamespace(reader=Q2Reader(), N=N_INTER, rank=0, types=(12, 12, 42), type2=8)
+    layer = SimpleNamespace(w13_qweight=torch.zeros((NS, 2 * N_INTER, ROWB13), dtype=torch.uint8),
+                            w2_qweight=torch.zeros((NS, 2 * N_INTER, n_blk * 68), dtype=torch.uint8))
+    c.layers[0] = (method, layer)
+    c.seed(None)
+    for s, e in ((0, 7), (1, 9)):
+        c._set(0, s, e)
+        c.fill(0, s, e)
+        want = H.q2_0_to_q8_0(torch.from_numpy(down_raw[e]))
+        assert torch.equal(layer.w2_qweight[s], want)
+    assert list(c._q8_down) == [0]
+
+
+class _Mode:
+    def __init__(self, decode):
+        self.decode = decode
+
+    def is_decode(self):
+        return self.decode
+
+    def is_target_verify(self):
+        return False
+
+
+def test_before_forward_uses_counts_one_round_late(monkeypatch):
+    monkeypatch.setattr(C, "INTERVAL", 2)
+    monkeypatch.setattr(C, "MAX_SWAPS", 2)
+    monkeypatch.setattr(C, "DECAY", 0.5)
+    c = make_cache(monkeypatch=monkeypatch)
+    c.seed(None)
+    batch = SimpleNamespace(forward_mode=_Mode(True))
+    prefill = SimpleNamespace(forward_mode=_Mode(False))
+    c.counts[0, 12] = 40.0  # hot non-resident expert of layer 0
+    c.counts[0, :NS] = torch.tensor([9.0, 1.0, 9.0, 9.0])
+    c.before_forward(prefill)  # prefill steps do not count
+    c.before_forward(batch)    # step 1: not a policy step
+    assert c.step == 1 and c.rounds == 0
+    c.before_forward(batch)    # step 2: the first round only starts the copy of the counts
+    assert c.rounds == 0 and float(c.counts[0, 12]) == 20.0  # decayed after the copy
+    assert c.slot2log[0][:NS] == [0, 1, 2, 3]
+    c.before_forward(batch)
+    c.before_forward(batch)    # step 4: the counts of round 1 (40 vs 1) swap 12 into slot 1
+    assert c.rounds == 1 and c.swaps == 1
+    assert c.slot2log[0][1] == 12 and int(c.log2slot[0, 12]) == 1 and int(c.log2cpu[0, 1]) == 1
+    assert c.check_tables() == "" and slot_bytes(c, 0, 1) == expect_bytes(0, 12)
+
+
+def test_plan_swaps_function_matches_the_method(monkeypatch):
+    c = make_cache(monkeypatch=monkeypatch)
+    c.seed(None)
+    rng = np.random.default_rng(4)
+    counts = rng.integers(0, 6, size=(L, E)).astype(np.float32)
+    assert C.plan_swaps(counts, c.slot2log, C.MAX_SWAPS, C.MARGIN) == c.plan_swaps(torch.from_numpy(counts))
