@@ -578,19 +578,26 @@ def run_ep(args, rank, world, local_rank, cfg_id=2):
     ref = st["ref_fn"](n_chk)
     err = float((out[:n_chk].float() - ref.float()).norm() / ref.float().norm())
     # phases of one call (events around dispatch, local experts, combine)
+    p2p = world > 1 and layer.p2p and args.ep_chunks == 1
     ph = []
     for _ in range(5):
         e = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
-        e[0].record(stream)
-        xr, ir, wr, plan = layer.dispatch(x, ids, wts)
-        e[1].record(stream)
-        yr = layer.expert_fn(xr, ir, wr)
-        e[2].record(stream)
-        layer.combine(yr, plan, T)
-        e[3].record(stream)
+        if p2p:
+            layer._call_p2p(x, ids, wts, events=e)
+        else:
+            e[0].record(stream)
+            xr, ir, wr, plan = layer.dispatch(x, ids, wts)
+            e[1].record(stream)
+            yr = layer.expert_fn(xr, ir, wr)
+            e[2].record(stream)
+            layer.combine(yr, plan, T)
+            e[3].record(stream)
         torch.cuda.synchronize()
         ph.append([e[j].elapsed_time(e[j + 1]) for j in range(3)])
     phases = [statistics.median(p[j] for p in ph) for j in range(3)]
+    if p2p:  # the received rows, from the exchange buffers (outside the timed region)
+        n_recv = int(layer.peers.recv_total.item())
+        xr, ir, wr = layer.peers.x[:n_recv], layer.peers.ids[:n_recv], layer.peers.w[:n_recv]
     n_recv = int(xr.shape[0])
     # local GEMM stages on the received rows (for the roofline)
     lib = Nt.load()
@@ -689,8 +696,11 @@ def run_ep(args, rank, world, local_rank, cfg_id=2):
                    "chunks": args.ep_chunks,
                    "rows_received_per_rank": [int(v[1]) for v in every],
                    "check_rel_l2_vs_single_gpu_layer": max(v[0] for v in every),
-                   "collective": "torch.distributed.all_to_all_single over NCCL (counts, rows, metadata; "
-                                 "partials back)",
+                   "collective": ("peer memory over NVLink: the dispatch kernel stores rows into the other ranks' "
+                                  "receive buffers, the combine kernel loads the partials from their output buffers "
+                                  "(CUDA IPC); NCCL only for an all-gather of the row counts and two one-word "
+                                  "all-reduce barriers") if p2p else
+                                 "torch.distributed.all_to_all_single over NCCL (counts, rows, metadata; partials back)",
                    "nccl": {"version": ".".join(map(str, torch.cuda.nccl.version())), "ranks": world,
                             "backend": dist.get_backend() if world > 1 else None}},
             "stage_ms_local": {"permute": stage_ms[0], "gate_up_gemm": stage_ms[1], "down_gemm": stage_ms[2],
@@ -708,6 +718,7 @@ def run_ep(args, rank, world, local_rank, cfg_id=2):
         }
         print(json.dumps(line), flush=True)
     if world > 1:
+        layer.close()
         dist.barrier()
         dist.destroy_process_group()
 

@@ -284,6 +284,49 @@ int kt_ep_pack(const void* x, int64_t hidden, const int32_t* send_token, int64_t
 int kt_ep_combine(const void* back, const int32_t* row_of, int n_ranks, const void* shared, int64_t tokens,
                   int64_t hidden, void* out, void* stream);
 
+/* ---- The exchange over peer memory (no counterpart in the reference). Instead of moving rows
+ * with NCCL all-to-alls, each rank writes its rows straight into the other ranks' receive
+ * buffers and reads its partial outputs straight from their output buffers, over NVLink, with
+ * plain loads and stores from these kernels (no TMA, no multicast). The buffers are mapped into
+ * every rank's process by CUDA IPC (kt_ipc_*); the caller orders the steps with barriers (any
+ * collective on the stream): every rank's dispatch before any rank's layer, every layer before
+ * any combine. counts_all [n_ranks][n_ranks] int32 on the device: row counts of every rank's
+ * kt_ep_plan (counts_all[s][d]: rows s sends to d). peer_* are device arrays of n_ranks buffer
+ * addresses (this rank's own at index rank). Rank s's rows for rank d land in d's receive
+ * buffers at rows base(s, d) + j, base(s, d) = sum over s' < s of counts_all[s'][d], j the
+ * row's index among s's rows for d. */
+
+/* 64-byte handle and offset of the allocation holding ptr, for kt_ipc_import in another
+ * process on this node. */
+int kt_ipc_export(const void* ptr, void* handle, size_t* offset);
+/* *ptr = the exported buffer mapped into this process (peer access enabled). */
+int kt_ipc_import(const void* handle, size_t offset, void** ptr);
+/* Unmaps a buffer mapped by kt_ipc_import (ptr and offset as returned / passed there). */
+int kt_ipc_close(void* ptr, size_t offset);
+
+/* Dispatch: send row i of kt_ep_plan (token send_token[i], meta[i] = its k slot ids then k
+ * weights) goes to its destination rank d's buffers: x rows peer_x[d] bf16 [rows_cap, hidden],
+ * slot ids peer_ids[d] int32 [rows_cap, top_k], weights peer_w[d] fp32 [rows_cap, top_k].
+ * *recv_total = the rows this rank receives (sum over s of counts_all[s][rank]). */
+int kt_ep_dispatch_p2p(const void* x, int64_t hidden, const int32_t* send_token, const int32_t* meta, int64_t top_k,
+                       const int32_t* counts_all, int rank, int n_ranks, const int64_t* peer_x, const int64_t* peer_ids,
+                       const int64_t* peer_w, int64_t rows_cap, int32_t* recv_total, void* stream);
+
+/* Combine: out[t] = bf16(shared[t] + sum over ranks d, in rank order, of d's output row for
+ * this rank's row row_of[t][d]) with fp32 sums; the rows are read from peer_y[d] (each rank's
+ * layer output over its receive rows). shared may be NULL. */
+int kt_ep_combine_p2p(const int32_t* row_of, const int32_t* counts_all, int rank, int n_ranks, const int64_t* peer_y,
+                      const void* shared, int64_t tokens, int64_t hidden, void* out, void* stream);
+
+/* kt_moe_prefill over a device-resident token count: x, topk_ids, topk_weights and out have
+ * room for tokens_cap tokens, the call processes the first *tokens_dev of them (read on the
+ * device, so the host needs no copy of it) and writes only their output rows. For the rows an
+ * expert-parallel rank receives. */
+int kt_moe_prefill_counted(const void* x, int64_t tokens_cap, const int32_t* tokens_dev, int64_t hidden, int64_t inter,
+                           const int32_t* topk_ids, const float* topk_weights, int64_t top_k, const void* w13,
+                           int type13, const void* w2, int type2, int w_is_table, int n_slots, void* out,
+                           void* workspace, size_t workspace_bytes, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -309,7 +309,8 @@ KT_EXPORT int kt_moe_prefill_workspace_layout(int64_t tokens, int64_t top_k, int
 static int prefill_run(const void* x, int64_t tokens, int64_t hidden, int64_t inter, const int32_t* topk_ids,
                        const float* topk_weights, int64_t top_k, const void* w13, int type13, const void* w2, int type2,
                        int w_is_table, int n_slots, int32_t id_base, float* acc, int acc_flags, void* out,
-                       void* workspace, size_t workspace_bytes, void* stream, void* const* stage_events) {
+                       void* workspace, size_t workspace_bytes, void* stream, void* const* stage_events,
+                       const int32_t* tokens_dev = nullptr) {
   if (!kt_prefill_type(type13) || !kt_prefill_type(type2)) return KT_ERR_TYPE;
   if (tokens < 0 || top_k <= 0 || top_k > 32 || n_slots <= 0 || n_slots > kPermMaxSlots || hidden <= 0 || inter <= 0)
     return KT_ERR_ARG;
@@ -330,7 +331,7 @@ static int prefill_run(const void* x, int64_t tokens, int64_t hidden, int64_t in
   const int64_t R = tokens * top_k;
   if (cudaMemsetAsync(p.status, 0, sizeof(int), s) != cudaSuccess) return KT_ERR_CUDA;
   int rc = kt_launch_permute(topk_ids, R, (int)top_k, n_slots, kt_gemm_tile_tokens(), kt_gemm_chunk_tiles(), p.counts,
-                             p.hist, p.tiles, p.n_tiles, p.chunks, p.sorted_token, p.route_pos, s, id_base);
+                             p.hist, p.tiles, p.n_tiles, p.chunks, p.sorted_token, p.route_pos, s, id_base, tokens_dev);
   if (rc) return launch_rc(rc);
   mark(0);
   // SMs left to concurrent kernels (e.g. NCCL's while an expert-parallel layer overlaps its
@@ -351,7 +352,7 @@ static int prefill_run(const void* x, int64_t tokens, int64_t hidden, int64_t in
   if (rc) return launch_rc(rc);
   mark(2);
   rc = kt_launch_combine_sorted(p.y, p.route_pos, topk_weights, tokens, top_k, hidden, (uint16_t*)out, s, acc,
-                                acc_flags);
+                                acc_flags, tokens_dev);
   if (rc) return launch_rc(rc);
   mark(3);
   return launch_rc(0);
@@ -430,6 +431,15 @@ KT_EXPORT int kt_moe_gemm_routes(const void* x, int64_t tokens, int64_t cols, co
   return launch_rc(kt_launch_gather_rows(r.ys, rows, r.route_pos, R, nullptr, (uint16_t*)y, s));
 }
 
+KT_EXPORT int kt_moe_prefill_counted(const void* x, int64_t tokens_cap, const int32_t* tokens_dev, int64_t hidden,
+                                     int64_t inter, const int32_t* topk_ids, const float* topk_weights, int64_t top_k,
+                                     const void* w13, int type13, const void* w2, int type2, int w_is_table,
+                                     int n_slots, void* out, void* workspace, size_t workspace_bytes, void* stream) {
+  if (!tokens_dev) return KT_ERR_ARG;
+  return prefill_run(x, tokens_cap, hidden, inter, topk_ids, topk_weights, top_k, w13, type13, w2, type2, w_is_table,
+                     n_slots, 0, nullptr, 0, out, workspace, workspace_bytes, stream, nullptr, tokens_dev);
+}
+
 // ------------------------------------------------------------------ expert-parallel plumbing
 
 KT_EXPORT size_t kt_ep_plan_workspace_size(int64_t tokens, int n_ranks) {
@@ -463,6 +473,73 @@ KT_EXPORT int kt_ep_combine(const void* back, const int32_t* row_of, int n_ranks
   if (tokens == 0) return KT_OK;
   if (!row_of || !out || (!back && !shared)) return KT_ERR_ARG;
   return launch_rc(kt_launch_ep_combine(back, row_of, n_ranks, shared, tokens, hidden, out, S(stream)));
+}
+
+KT_EXPORT int kt_ep_dispatch_p2p(const void* x, int64_t hidden, const int32_t* send_token, const int32_t* meta,
+                                 int64_t top_k, const int32_t* counts_all, int rank, int n_ranks, const int64_t* peer_x,
+                                 const int64_t* peer_ids, const int64_t* peer_w, int64_t rows_cap,
+                                 int32_t* recv_total, void* stream) {
+  if (hidden <= 0 || hidden % 8 || top_k < 1 || top_k > 32 || n_ranks < 1 || n_ranks > 8 || rank < 0 ||
+      rank >= n_ranks || rows_cap < 0)
+    return KT_ERR_ARG;
+  if (!x || !send_token || !meta || !counts_all || !peer_x || !peer_ids || !peer_w || !recv_total) return KT_ERR_ARG;
+  return launch_rc(kt_launch_ep_dispatch_p2p(x, hidden, send_token, meta, (int)top_k, counts_all, rank, n_ranks, peer_x,
+                                             peer_ids, peer_w, rows_cap, recv_total, S(stream)));
+}
+
+KT_EXPORT int kt_ep_combine_p2p(const int32_t* row_of, const int32_t* counts_all, int rank, int n_ranks,
+                                const int64_t* peer_y, const void* shared, int64_t tokens, int64_t hidden, void* out,
+                                void* stream) {
+  if (tokens < 0 || hidden <= 0 || hidden % 8 || n_ranks < 1 || n_ranks > 8 || rank < 0 || rank >= n_ranks)
+    return KT_ERR_ARG;
+  if (tokens == 0) return KT_OK;
+  if (!row_of || !counts_all || !peer_y || !out) return KT_ERR_ARG;
+  return launch_rc(
+      kt_launch_ep_combine_p2p(row_of, counts_all, rank, n_ranks, peer_y, shared, tokens, hidden, out, S(stream)));
+}
+
+// ------------------------------------------------------------------ CUDA IPC of exchange buffers
+
+typedef CUresult (*PFN_getAddressRange)(CUdeviceptr*, size_t*, CUdeviceptr);
+
+static PFN_getAddressRange get_address_range() {
+  static PFN_getAddressRange fn = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      return (PFN_getAddressRange)p;
+    return (PFN_getAddressRange) nullptr;
+  }();
+  return fn;
+}
+
+KT_EXPORT int kt_ipc_export(const void* ptr, void* handle, size_t* offset) {
+  if (!ptr || !handle || !offset) return KT_ERR_ARG;
+  PFN_getAddressRange range = get_address_range();
+  CUdeviceptr base = 0;
+  size_t size = 0;
+  if (!range || range(&base, &size, (CUdeviceptr)(uintptr_t)ptr) != CUDA_SUCCESS) return KT_ERR_CUDA;
+  cudaIpcMemHandle_t h;
+  if (cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(base)) != cudaSuccess) return KT_ERR_CUDA;
+  memcpy(handle, &h, sizeof h);
+  *offset = (size_t)((uintptr_t)ptr - (uintptr_t)base);
+  return KT_OK;
+}
+
+KT_EXPORT int kt_ipc_import(const void* handle, size_t offset, void** ptr) {
+  if (!handle || !ptr) return KT_ERR_ARG;
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof h);
+  void* base = nullptr;
+  if (cudaIpcOpenMemHandle(&base, h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) return KT_ERR_CUDA;
+  *ptr = static_cast<uint8_t*>(base) + offset;
+  return KT_OK;
+}
+
+KT_EXPORT int kt_ipc_close(void* ptr, size_t offset) {
+  if (!ptr) return KT_ERR_ARG;
+  return cudaIpcCloseMemHandle(static_cast<uint8_t*>(ptr) - offset) == cudaSuccess ? KT_OK : KT_ERR_CUDA;
 }
 
 // ------------------------------------------------------------------ allocation-free decode GEMV

@@ -173,7 +173,140 @@ __global__ void kt_ep_combine_kernel(const uint16_t* __restrict__ back, const in
   }
 }
 
+// ---- exchange over peer memory (rows written into, and partials read from, the other ranks'
+// buffers mapped into this process by CUDA IPC)
+//
+// counts_all [P][P]: counts_all[s][d] = rows rank s sends to rank d (every rank's plan counts,
+// gathered). Rank s's rows for rank d land in d's receive buffers at rows
+// base(s, d) + j, base(s, d) = sum over s' < s of counts_all[s'][d], j the row's index within
+// s's send segment for d; d's layer writes its output row for receive row i at row i of its y.
+
+struct KtEpOffsets {
+  int32_t seg[kEpMaxRanks + 1];  // this rank's send segment starts (rank-major send rows)
+  int32_t base[kEpMaxRanks];     // this rank's first row in each destination's receive buffers
+};
+
+__device__ __forceinline__ void kt_ep_offsets(const int32_t* counts_all, int me, int P, KtEpOffsets& o) {
+  int32_t run = 0;
+  for (int d = 0; d < P; ++d) {
+    o.seg[d] = run;
+    run += counts_all[me * P + d];
+    int32_t b = 0;
+    for (int s2 = 0; s2 < me; ++s2) b += counts_all[s2 * P + d];
+    o.base[d] = b;
+  }
+  o.seg[P] = run;
+}
+
+// one warp per send row: the token's K bf16 values, then the row's k slot ids and k weights,
+// stored into the destination rank's buffers (16-byte stores, over NVLink for other ranks)
+__global__ void __launch_bounds__(256) kt_ep_dispatch_p2p_kernel(
+    const uint16_t* __restrict__ x, int64_t K, const int32_t* __restrict__ send_token,
+    const int32_t* __restrict__ meta, int k, const int32_t* __restrict__ counts_all, int me, int P,
+    const int64_t* __restrict__ peer_x, const int64_t* __restrict__ peer_ids, const int64_t* __restrict__ peer_w,
+    int64_t rows_cap, int32_t* __restrict__ recv_total) {
+  __shared__ KtEpOffsets o;
+  if (threadIdx.x == 0) kt_ep_offsets(counts_all, me, P, o);
+  if (blockIdx.x == 0 && threadIdx.x == 1) {  // rows this rank receives (its layer's token count)
+    int32_t r = 0;
+    for (int s2 = 0; s2 < P; ++s2) r += counts_all[s2 * P + me];
+    *recv_total = r;
+  }
+  __syncthreads();
+  const int lane = threadIdx.x & 31;
+  const int64_t n = o.seg[P];
+  const int64_t warps = (int64_t)gridDim.x * (blockDim.x / 32);
+  const int64_t chunks = K / 8;
+  for (int64_t i = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32; i < n; i += warps) {
+    int d = 0;
+    while (d + 1 < P && i >= o.seg[d + 1]) ++d;
+    const int64_t row = (int64_t)o.base[d] + (i - o.seg[d]);
+    if (row >= rows_cap) continue;  // cannot happen with buffers of the planned capacity
+    const uint4* src = reinterpret_cast<const uint4*>(x + (int64_t)send_token[i] * K);
+    uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(peer_x[d]) + row * K);
+    for (int64_t c = lane; c < chunks; c += 32) dst[c] = __ldg(src + c);
+    if (lane < k) {
+      reinterpret_cast<int32_t*>(peer_ids[d])[row * k + lane] = meta[i * 2 * k + lane];
+      reinterpret_cast<int32_t*>(peer_w[d])[row * k + lane] = meta[i * 2 * k + k + lane];
+    }
+  }
+  __threadfence_system();  // the stores reach the other GPUs before the barrier that follows
+}
+
+// out[t] = bf16(shared[t] + sum over ranks d in rank order of d's y row for token t), fp32
+// sums; the rows are read from the other ranks' y buffers (one CTA per token, 8 columns a thread)
+__global__ void kt_ep_combine_p2p_kernel(const int32_t* __restrict__ row_of, const int32_t* __restrict__ counts_all,
+                                         int me, int P, const int64_t* __restrict__ peer_y,
+                                         const uint16_t* __restrict__ shared, int64_t K, uint16_t* __restrict__ out) {
+  __shared__ KtEpOffsets o;
+  if (threadIdx.x == 0) kt_ep_offsets(counts_all, me, P, o);
+  __syncthreads();
+  const int64_t t = blockIdx.x;
+  const uint16_t* src[kEpMaxRanks];
+#pragma unroll
+  for (int d = 0; d < kEpMaxRanks; ++d) {
+    const int32_t r = d < P ? row_of[t * P + d] : -1;
+    src[d] = r >= 0 ? reinterpret_cast<const uint16_t*>(peer_y[d]) + ((int64_t)o.base[d] + (r - o.seg[d])) * K
+                    : nullptr;
+  }
+  for (int64_t c = (int64_t)threadIdx.x * 8; c < K; c += (int64_t)blockDim.x * 8) {
+    uint4 v[kEpMaxRanks];
+#pragma unroll
+    for (int d = 0; d < kEpMaxRanks; ++d)  // every rank's load in flight before the sums
+      v[d] = src[d] ? __ldcg(reinterpret_cast<const uint4*>(src[d] + c)) : make_uint4(0, 0, 0, 0);
+    float acc[8];
+    if (shared) {
+      const uint4 sv = *reinterpret_cast<const uint4*>(shared + t * K + c);
+      const uint32_t u[4] = {sv.x, sv.y, sv.z, sv.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        acc[2 * j] = kt_bf2f((uint16_t)(u[j] & 0xffff));
+        acc[2 * j + 1] = kt_bf2f((uint16_t)(u[j] >> 16));
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc[j] = 0.0f;
+    }
+#pragma unroll
+    for (int d = 0; d < kEpMaxRanks; ++d) {
+      if (!src[d]) continue;
+      const uint32_t u[4] = {v[d].x, v[d].y, v[d].z, v[d].w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        acc[2 * j] += kt_bf2f((uint16_t)(u[j] & 0xffff));
+        acc[2 * j + 1] += kt_bf2f((uint16_t)(u[j] >> 16));
+      }
+    }
+    uint4 ov;
+    ov.x = kt_pack_bf2(acc[0], acc[1]);
+    ov.y = kt_pack_bf2(acc[2], acc[3]);
+    ov.z = kt_pack_bf2(acc[4], acc[5]);
+    ov.w = kt_pack_bf2(acc[6], acc[7]);
+    *reinterpret_cast<uint4*>(out + t * K + c) = ov;
+  }
+}
+
 }  // namespace
+
+int kt_launch_ep_dispatch_p2p(const void* x, int64_t K, const int32_t* send_token, const int32_t* meta, int k,
+                              const int32_t* counts_all, int me, int P, const int64_t* peer_x, const int64_t* peer_ids,
+                              const int64_t* peer_w, int64_t rows_cap, int32_t* recv_total, cudaStream_t s) {
+  if (K % 8 || P < 1 || P > kEpMaxRanks || me < 0 || me >= P || k < 1 || k > 32 || (((uintptr_t)x) & 15)) return -1;
+  kt_ep_dispatch_p2p_kernel<<<148 * 4, 256, 0, s>>>((const uint16_t*)x, K, send_token, meta, k, counts_all, me, P,
+                                                    peer_x, peer_ids, peer_w, rows_cap, recv_total);
+  return 0;
+}
+
+int kt_launch_ep_combine_p2p(const int32_t* row_of, const int32_t* counts_all, int me, int P, const int64_t* peer_y,
+                             const void* shared, int64_t T, int64_t K, void* out, cudaStream_t s) {
+  if (K % 8 || P < 1 || P > kEpMaxRanks || me < 0 || me >= P || T > 0x7fffffff) return -1;
+  if (T == 0) return 0;
+  const int64_t vec = K / 8;
+  const int threads = (int)(vec < 256 ? (vec + 31) / 32 * 32 : 256);
+  kt_ep_combine_p2p_kernel<<<(unsigned)T, threads, 0, s>>>(row_of, counts_all, me, P, peer_y, (const uint16_t*)shared,
+                                                          K, (uint16_t*)out);
+  return 0;
+}
 
 int64_t kt_ep_plan_ints(int64_t T, int P) { return ((T + kEpBlock - 1) / kEpBlock) * P; }
 

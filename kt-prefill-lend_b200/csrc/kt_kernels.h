@@ -43,8 +43,11 @@ int kt_launch_combine(const void* out, int dtype, const float* w, int64_t T, int
                       cudaStream_t s);
 // acc_flags bit 0: start each token's sum from acc (fp32 [T, K]); bit 1: write the fp32 sum to
 // acc instead of bf16 to res (tokens with no present route are then skipped)
+// tokens_dev (optional): the number of tokens, read on the device (T is then a capacity; tokens
+// at or past *tokens_dev are not written)
 int kt_launch_combine_sorted(const uint16_t* y, const int32_t* route_pos, const float* w, int64_t T, int64_t top_k,
-                             int64_t K, uint16_t* res, cudaStream_t s, float* acc = nullptr, int acc_flags = 0);
+                             int64_t K, uint16_t* res, cudaStream_t s, float* acc = nullptr, int acc_flags = 0,
+                             const int32_t* tokens_dev = nullptr);
 // dst[i] = src[idx[i]] (rows of `cols` bf16, 16-byte aligned) for i < n, zero rows where
 // idx[i] < 0; with n_limit, rows i >= *n_limit (a device count) are left untouched
 int kt_launch_gather_rows(const uint16_t* src, int64_t cols, const int32_t* idx, int64_t n, const int32_t* n_limit,
@@ -63,9 +66,11 @@ int kt_launch_topk_grouped(const float* logits, const float* bias, int64_t T, in
 constexpr int kPermMaxSlots = 8192;
 int64_t kt_permute_hist_ints(int64_t routes, int n_slots);
 // ids outside [id_base, id_base + n_slots) (and negative ids) are not present; slot = id - id_base
+// tokens_dev (optional): routes at or past *tokens_dev * top_k are not present
 int kt_launch_permute(const int32_t* ids, int64_t routes, int top_k, int n_slots, int tile_tokens, int chunk_tiles,
                       int32_t* counts, int32_t* hist, int32_t* tiles, int32_t* n_tiles, int32_t* chunks,
-                      int32_t* sorted_token, int32_t* route_pos, cudaStream_t s, int id_base = 0);
+                      int32_t* sorted_token, int32_t* route_pos, cudaStream_t s, int id_base = 0,
+                      const int32_t* tokens_dev = nullptr);
 
 // linear = 1: no activation, the raw projection [R, 2N] (rows of w13 in order) instead of H [R, N]
 int kt_launch_gemm_gate_up(int type, const void* x, int64_t T, int K, int N, const void* w13, int table, int n_slots,
@@ -88,3 +93,10 @@ int kt_launch_ep_plan(const int32_t* ids, const float* w, int64_t T, int k, cons
 int kt_launch_ep_pack(const void* x, int64_t K, const int32_t* send_token, int64_t n, void* rows, cudaStream_t s);
 int kt_launch_ep_combine(const void* back, const int32_t* row_of, int P, const void* shared, int64_t T, int64_t K,
                          void* out, cudaStream_t s);
+// the exchange over peer memory: peer_* are device arrays of P addresses (this rank's own
+// buffers at index me), counts_all [P][P] every rank's plan counts
+int kt_launch_ep_dispatch_p2p(const void* x, int64_t K, const int32_t* send_token, const int32_t* meta, int k,
+                              const int32_t* counts_all, int me, int P, const int64_t* peer_x, const int64_t* peer_ids,
+                              const int64_t* peer_w, int64_t rows_cap, int32_t* recv_total, cudaStream_t s);
+int kt_launch_ep_combine_p2p(const int32_t* row_of, const int32_t* counts_all, int me, int P, const int64_t* peer_y,
+                             const void* shared, int64_t T, int64_t K, void* out, cudaStream_t s);

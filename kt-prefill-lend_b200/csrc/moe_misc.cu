@@ -150,8 +150,10 @@ int kt_launch_combine(const void* out, int dtype, const float* w, int64_t T, int
 template <int KMAX, bool LOAD, bool STORE>
 __global__ void kt_combine_sorted_kernel(const uint16_t* __restrict__ y, const int32_t* __restrict__ route_pos,
                                          const float* __restrict__ w, int64_t T, int top_k, int64_t K,
-                                         uint16_t* __restrict__ res, float* __restrict__ acc_f32) {
+                                         uint16_t* __restrict__ res, float* __restrict__ acc_f32,
+                                         const int32_t* __restrict__ tokens_dev) {
   const int64_t t = blockIdx.x;
+  if (tokens_dev && t >= *tokens_dev) return;  // past the tokens present in this call
   // the token's routes: positions and weights (KMAX >= top_k), then all row loads in flight
   int32_t pos[KMAX];
   float wk[KMAX];
@@ -207,19 +209,21 @@ __global__ void kt_combine_sorted_kernel(const uint16_t* __restrict__ y, const i
 
 template <bool LOAD, bool STORE>
 static void launch_combine_sorted_mode(const uint16_t* y, const int32_t* route_pos, const float* w, int64_t T, int k,
-                                       int64_t K, uint16_t* res, float* acc, int threads, cudaStream_t s) {
+                                       int64_t K, uint16_t* res, float* acc, int threads, cudaStream_t s,
+                                       const int32_t* td) {
   if (k <= 4)
-    kt_combine_sorted_kernel<4, LOAD, STORE><<<(unsigned)T, threads, 0, s>>>(y, route_pos, w, T, k, K, res, acc);
+    kt_combine_sorted_kernel<4, LOAD, STORE><<<(unsigned)T, threads, 0, s>>>(y, route_pos, w, T, k, K, res, acc, td);
   else if (k <= 8)
-    kt_combine_sorted_kernel<8, LOAD, STORE><<<(unsigned)T, threads, 0, s>>>(y, route_pos, w, T, k, K, res, acc);
+    kt_combine_sorted_kernel<8, LOAD, STORE><<<(unsigned)T, threads, 0, s>>>(y, route_pos, w, T, k, K, res, acc, td);
   else if (k <= 16)
-    kt_combine_sorted_kernel<16, LOAD, STORE><<<(unsigned)T, threads, 0, s>>>(y, route_pos, w, T, k, K, res, acc);
+    kt_combine_sorted_kernel<16, LOAD, STORE><<<(unsigned)T, threads, 0, s>>>(y, route_pos, w, T, k, K, res, acc, td);
   else
-    kt_combine_sorted_kernel<32, LOAD, STORE><<<(unsigned)T, threads, 0, s>>>(y, route_pos, w, T, k, K, res, acc);
+    kt_combine_sorted_kernel<32, LOAD, STORE><<<(unsigned)T, threads, 0, s>>>(y, route_pos, w, T, k, K, res, acc, td);
 }
 
 int kt_launch_combine_sorted(const uint16_t* y, const int32_t* route_pos, const float* w, int64_t T, int64_t top_k,
-                             int64_t K, uint16_t* res, cudaStream_t s, float* acc, int acc_flags) {
+                             int64_t K, uint16_t* res, cudaStream_t s, float* acc, int acc_flags,
+                             const int32_t* tokens_dev) {
   if (T == 0) return 0;
   if (K % 8 || T > 0x7fffffff || top_k > 32) return -1;
   const bool load = acc_flags & 1, store = acc_flags & 2;
@@ -228,13 +232,13 @@ int kt_launch_combine_sorted(const uint16_t* y, const int32_t* route_pos, const 
   const int threads = (int)(vec < 256 ? (vec + 31) / 32 * 32 : 256);
   const int k = (int)top_k;
   if (load && store)
-    launch_combine_sorted_mode<true, true>(y, route_pos, w, T, k, K, res, acc, threads, s);
+    launch_combine_sorted_mode<true, true>(y, route_pos, w, T, k, K, res, acc, threads, s, tokens_dev);
   else if (load)
-    launch_combine_sorted_mode<true, false>(y, route_pos, w, T, k, K, res, acc, threads, s);
+    launch_combine_sorted_mode<true, false>(y, route_pos, w, T, k, K, res, acc, threads, s, tokens_dev);
   else if (store)
-    launch_combine_sorted_mode<false, true>(y, route_pos, w, T, k, K, res, acc, threads, s);
+    launch_combine_sorted_mode<false, true>(y, route_pos, w, T, k, K, res, acc, threads, s, tokens_dev);
   else
-    launch_combine_sorted_mode<false, false>(y, route_pos, w, T, k, K, res, acc, threads, s);
+    launch_combine_sorted_mode<false, false>(y, route_pos, w, T, k, K, res, acc, threads, s, tokens_dev);
   return 0;
 }
 
@@ -494,14 +498,24 @@ int kt_launch_topk_grouped(const float* logits, const float* bias, int64_t T, in
 //   scatter  position = hist[b][slot] + rank: sorted_token[pos], route_pos[route]
 constexpr int kPermBlock = 1024;
 
+// routes at or past `lim` (the present routes, when a device token count limits them) are absent
+__device__ __forceinline__ int64_t kt_perm_limit(int64_t routes, int top_k, const int32_t* tokens_dev) {
+  if (!tokens_dev) return routes;
+  const int64_t n = (int64_t)(*tokens_dev) * top_k;
+  return n < routes ? (n > 0 ? n : 0) : routes;
+}
+
 __global__ void __launch_bounds__(kPermBlock) kt_perm_hist_kernel(const int32_t* __restrict__ ids, int64_t routes,
-                                                                  int n_slots, int id_base, int32_t* __restrict__ hist,
+                                                                  int top_k, int n_slots, int id_base,
+                                                                  const int32_t* __restrict__ tokens_dev,
+                                                                  int32_t* __restrict__ hist,
                                                                   int32_t* __restrict__ rank) {
   extern __shared__ int32_t sh[];
   for (int e = threadIdx.x; e < n_slots; e += blockDim.x) sh[e] = 0;
   __syncthreads();
+  const int64_t lim = kt_perm_limit(routes, top_k, tokens_dev);
   const int64_t p = (int64_t)blockIdx.x * kPermBlock + threadIdx.x;
-  const int32_t e0 = p < routes ? ids[p] : -1;
+  const int32_t e0 = p < lim ? ids[p] : -1;
   const int32_t e = e0 >= id_base ? e0 - id_base : -1;  // slot of the id window [id_base, id_base + n_slots)
   const bool valid = e >= 0 && e < n_slots;
   const int lane = threadIdx.x & 31;
@@ -617,12 +631,14 @@ __global__ void __launch_bounds__(kPermBlock) kt_perm_scan_kernel(int32_t* __res
 
 __global__ void __launch_bounds__(kPermBlock) kt_perm_scatter_kernel(const int32_t* __restrict__ ids, int64_t routes,
                                                                      int top_k, int n_slots, int id_base,
+                                                                     const int32_t* __restrict__ tokens_dev,
                                                                      const int32_t* __restrict__ hist,
                                                                      int32_t* __restrict__ sorted_token,
                                                                      int32_t* __restrict__ route_pos) {
   const int64_t p = (int64_t)blockIdx.x * kPermBlock + threadIdx.x;
   if (p >= routes) return;
-  const int32_t e = ids[p] >= id_base ? ids[p] - id_base : -1;
+  const int64_t lim = kt_perm_limit(routes, top_k, tokens_dev);
+  const int32_t e = p < lim && ids[p] >= id_base ? ids[p] - id_base : -1;
   if (e >= 0 && e < n_slots) {
     const int32_t pos = hist[(int64_t)blockIdx.x * n_slots + e] + route_pos[p];
     sorted_token[pos] = (int32_t)(p / top_k);
@@ -636,16 +652,17 @@ int64_t kt_permute_hist_ints(int64_t routes, int n_slots) { return ((routes + kP
 
 int kt_launch_permute(const int32_t* ids, int64_t routes, int top_k, int n_slots, int tile_tokens, int chunk_tiles,
                       int32_t* counts, int32_t* hist, int32_t* tiles, int32_t* n_tiles, int32_t* chunks,
-                      int32_t* sorted_token, int32_t* route_pos, cudaStream_t s, int id_base) {
+                      int32_t* sorted_token, int32_t* route_pos, cudaStream_t s, int id_base,
+                      const int32_t* tokens_dev) {
   if (n_slots <= 0 || n_slots > kPermMaxSlots || chunk_tiles <= 0 || id_base < 0) return -1;
   const int nb = (int)((routes + kPermBlock - 1) / kPermBlock);
   if (nb > 0)
-    kt_perm_hist_kernel<<<nb, kPermBlock, n_slots * sizeof(int32_t), s>>>(ids, routes, n_slots, id_base, hist,
-                                                                          route_pos);
+    kt_perm_hist_kernel<<<nb, kPermBlock, n_slots * sizeof(int32_t), s>>>(ids, routes, top_k, n_slots, id_base,
+                                                                          tokens_dev, hist, route_pos);
   kt_perm_scan_kernel<<<1, kPermBlock, 0, s>>>(hist, nb, n_slots, tile_tokens, chunk_tiles, counts, tiles, n_tiles,
                                                chunks);
   if (nb > 0)
-    kt_perm_scatter_kernel<<<nb, kPermBlock, 0, s>>>(ids, routes, top_k, n_slots, id_base, hist, sorted_token,
-                                                     route_pos);
+    kt_perm_scatter_kernel<<<nb, kPermBlock, 0, s>>>(ids, routes, top_k, n_slots, id_base, tokens_dev, hist,
+                                                     sorted_token, route_pos);
   return 0;
 }

@@ -14,6 +14,8 @@
 // (the reference's window build does this for up to 4 routes, its per-route build not
 // at all). Each warp then walks rows with the reference's lane-to-chunk assignment and
 // butterfly, so every route's sum has the reference's order.
+#include <string.h>
+
 #include "gguf_dot.cuh"
 #include "kt_kernels.h"
 
@@ -292,6 +294,7 @@ struct KtVecArgs {
   void* y;                     // [routes, rows]
   int* status;                 // workspace status word (bounded waits)
   int tiles_per_group;         // pipelined kernel: row tiles of rows_per_cta rows per group
+  int stages;                  // bulk-staged member-stationary kernel: shared-memory stages
 };
 
 // LPR lanes per row: 32, or 16 when a row has at most 16 chunks (two rows per warp).
@@ -525,8 +528,10 @@ __global__ void __launch_bounds__(256) kt_moe_vec_pipe_kernel(const KtVecArgs a)
 // chunk's own fp32 expression (kt_dot_split). Per-lane sums run in chunk order and end in the
 // same xor butterfly, so every route's result is the reference's bit for bit; the saving is
 // the activation work per row and the weight work per member.
+// `tile` holds the raw rows from r0 on, row_bytes apart (the slot in global memory, or a
+// staged copy of the tile in shared memory)
 template <int TYPE, int DT, int R, int WM>
-__device__ __forceinline__ void kt_ms_item(const KtVecArgs& a, const uint8_t* wbase, int start, int r0,
+__device__ __forceinline__ void kt_ms_item(const KtVecArgs& a, const uint8_t* tile, int start, int r0,
                                            const uint32_t* grid) {
   using C = KtChunk<TYPE>;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -551,7 +556,7 @@ __device__ __forceinline__ void kt_ms_item(const KtVecArgs& a, const uint8_t* wb
       const int r = rbase + j;
       if (r < a.rows) {
         KtWgt<TYPE> w;
-        kt_wgt_load(w, wbase + (int64_t)r * a.row_bytes + (int64_t)i * C::BYTES, iqs, grid);
+        kt_wgt_load(w, tile + (int64_t)(r - r0) * a.row_bytes + (int64_t)i * C::BYTES, iqs, grid);
 #pragma unroll
         for (int m = 0; m < WM; ++m) acc[j][m] += kt_dot_split(w, act[m]);
       }
@@ -566,6 +571,32 @@ __device__ __forceinline__ void kt_ms_item(const KtVecArgs& a, const uint8_t* wb
       for (int mask = 16; mask > 0; mask >>= 1) t += __shfl_xor_sync(0xffffffffu, t, mask);
       if (lane == 0 && rbase + j < a.rows) kt_store_act<DT>(a.y, (int64_t)a.order[start + m] * a.rows + rbase + j, t);
     }
+}
+
+// one group of `count` routes (1, 2, 4 or 8, from the grouping in pieces of WMAX) on one tile
+template <int TYPE, int DT, int R, int WMAX>
+__device__ __forceinline__ void kt_ms_group(const KtVecArgs& a, const uint8_t* tile, int start, int count, int r0,
+                                            const uint32_t* grid) {
+  switch (count) {
+    case 8:
+      if constexpr (WMAX >= 8) {
+        kt_ms_item<TYPE, DT, R, 8>(a, tile, start, r0, grid);
+      } else {  // not produced with piece WMAX; in parts of WMAX if it were
+        for (int m = 0; m < 8; m += WMAX) kt_ms_item<TYPE, DT, R, WMAX>(a, tile, start + m, r0, grid);
+      }
+      break;
+    case 4:
+      if constexpr (WMAX >= 4) {
+        kt_ms_item<TYPE, DT, R, 4>(a, tile, start, r0, grid);
+      } else {
+        kt_ms_item<TYPE, DT, R, 2>(a, tile, start, r0, grid);
+        kt_ms_item<TYPE, DT, R, 2>(a, tile, start + 2, r0, grid);
+      }
+      break;
+    case 2: kt_ms_item<TYPE, DT, R, 2>(a, tile, start, r0, grid); break;
+    default:  // 1 (any other count only if the groups were not cut in powers of two)
+      for (int m = 0; m < count; ++m) kt_ms_item<TYPE, DT, R, 1>(a, tile, start + m, r0, grid);
+  }
 }
 
 // WMAX 8: two CTAs per SM (128 registers); WMAX 4: three (80), more warps to hide the loads
@@ -594,26 +625,79 @@ __global__ void __launch_bounds__(256, WMAX >= 8 ? 2 : 3) kt_moe_vec_ms_kernel(c
     }
     const uint8_t* wbase = a.table ? reinterpret_cast<const uint8_t*>(reinterpret_cast<const int64_t*>(a.w)[slot])
                                    : a.w + (int64_t)slot * a.rows * a.row_bytes;
-    switch (count) {
-      case 8:
-        if constexpr (WMAX >= 8) {
-          kt_ms_item<TYPE, DT, R, 8>(a, wbase, start, r0, grid_s);
-        } else {  // not produced with piece WMAX; in parts of WMAX if it were
-          for (int m = 0; m < 8; m += WMAX) kt_ms_item<TYPE, DT, R, WMAX>(a, wbase, start + m, r0, grid_s);
-        }
-        break;
-      case 4:
-        if constexpr (WMAX >= 4) {
-          kt_ms_item<TYPE, DT, R, 4>(a, wbase, start, r0, grid_s);
-        } else {
-          kt_ms_item<TYPE, DT, R, 2>(a, wbase, start, r0, grid_s);
-          kt_ms_item<TYPE, DT, R, 2>(a, wbase, start + 2, r0, grid_s);
-        }
-        break;
-      case 2: kt_ms_item<TYPE, DT, R, 2>(a, wbase, start, r0, grid_s); break;
-      default:  // 1 (any other count only if the groups were not cut in powers of two)
-        for (int m = 0; m < count; ++m) kt_ms_item<TYPE, DT, R, 1>(a, wbase, start + m, r0, grid_s);
+    kt_ms_group<TYPE, DT, R, WMAX>(a, wbase + (int64_t)r0 * a.row_bytes, start, count, r0, grid_s);
+  }
+}
+
+// Member-stationary kernel with the weight tiles staged in shared memory: the same work items
+// (a group of routes of one slot x a tile of 8R rows) and the same per-row arithmetic as
+// kt_moe_vec_ms_kernel, so every route's sum is unchanged bit for bit, but each tile's raw rows
+// (contiguous in HBM) arrive by one 1-D bulk copy into a ring of a.stages shared-memory stages,
+// issued a.stages items ahead by one thread. Many copies of whole tiles stay in flight per SM,
+// so HBM latency hides behind the previous tiles' arithmetic, and the warps read the weights
+// from shared memory instead of issuing small global loads.
+constexpr int kMsbMaxStages = 4;
+
+template <int TYPE, int DT, int R, int WMAX>
+__global__ void __launch_bounds__(256, 2) kt_moe_vec_msb_kernel(const KtVecArgs a) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  __shared__ uint32_t grid_s[KtGridSmem<TYPE>::WORDS];
+  __shared__ __align__(8) uint64_t full[kMsbMaxStages];
+  constexpr int kRows = 8 * R;
+  const int tid = threadIdx.x;
+  const int S = a.stages;
+  const int tiles = (a.rows + kRows - 1) / kRows;
+  const int n_items = a.groups[0] * tiles;
+  const int64_t tile_cap = ((int64_t)kRows * a.row_bytes + 127) & ~(int64_t)127;
+  if (tid == 0) {
+    for (int i = 0; i < S; ++i) kt_mbar_init(&full[i], 1);
+    kt_fence_mbar_init();
+  }
+  kt_stage_grid<TYPE>(grid_s, tid, blockDim.x);
+  __syncthreads();
+  auto issue = [&](int j) {  // the raw rows of this CTA's j-th item into stage j % S
+    const int item = blockIdx.x + j * gridDim.x;
+    if (item >= n_items) return;
+    uint64_t* bar = &full[j % S];
+    const int g = item / tiles, r0 = (item % tiles) * kRows;
+    const int slot = a.groups[1 + 3 * g + 0];
+    if (slot < 0) {
+      kt_mbar_arrive(bar);  // nothing to copy for routes that are not on this device
+      return;
     }
+    const uint8_t* wbase = a.table ? reinterpret_cast<const uint8_t*>(reinterpret_cast<const int64_t*>(a.w)[slot])
+                                   : a.w + (int64_t)slot * a.rows * a.row_bytes;
+    const uint32_t bytes = (uint32_t)((int64_t)min(kRows, a.rows - r0) * a.row_bytes);
+    kt_mbar_arrive_expect_tx(bar, bytes);
+    kt_bulk_g2s(smem + (j % S) * tile_cap, wbase + (int64_t)r0 * a.row_bytes, bytes, bar);
+  };
+  if (tid == 0)
+    for (int j = 0; j < S; ++j) issue(j);
+  for (int j = 0; blockIdx.x + j * gridDim.x < n_items; ++j) {
+    const int item = blockIdx.x + j * gridDim.x;
+    const int g = item / tiles, r0 = (item % tiles) * kRows;
+    const int slot = a.groups[1 + 3 * g + 0];
+    const int start = a.groups[1 + 3 * g + 1];
+    const int count = a.groups[1 + 3 * g + 2];
+    if (!kt_mbar_wait(&full[j % S], (j / S) & 1, a.status, nullptr)) {
+      // a copy that never landed (recorded in the status word): wait, bounded, for the other
+      // copies this CTA has in flight, then leave
+      if (tid == 0)
+        for (int jj = j + 1; jj < j + S && blockIdx.x + jj * gridDim.x < n_items; ++jj)
+          kt_mbar_wait(&full[jj % S], (jj / S) & 1, nullptr, nullptr);
+      break;
+    }
+    if (slot < 0) {  // routes not on this device: zero rows
+      const int nr = min(kRows, a.rows - r0);
+      for (int64_t i = tid; i < (int64_t)count * nr; i += blockDim.x) {
+        const int p = a.order[start + i / nr];
+        kt_store_act<DT>(a.y, (int64_t)p * a.rows + r0 + i % nr, 0.0f);
+      }
+    } else {
+      kt_ms_group<TYPE, DT, R, WMAX>(a, smem + (j % S) * tile_cap, start, count, r0, grid_s);
+    }
+    __syncthreads();  // every warp is done with the stage
+    if (tid == 0) issue(j + S);
   }
 }
 
@@ -671,17 +755,70 @@ int kt_vec_ms_piece() {
 // for tuning runs). Measured on config 2's Q4_K gate/up against the reference kernel (graph
 // replays): M=4 (31 routes) 22.6 us with 4 rows (24.7 reference), M=16 51.3 us and M=64 155.8 us
 // with 8 (53.7 and 188.6); 16 rows spill and lose (187 us at M=64).
+// Bulk-staged variant (kt_moe_vec_msb_kernel), for IQ3_S: tiles of 8R rows, R the largest of 4,
+// 2, 1 whose tile fits kMsbTileBytes, at least two stages within kMsbSmemBytes (two CTAs per SM),
+// tiles whose bytes are a 16-byte multiple covering the slot exactly, and a 16-byte aligned weight
+// base (or slot table). Returns R, or 0 when the global-load kernel runs. Measured (B200, graph
+// replays, config 3's IQ3_S gate/up): 82.2 / 244.2 us at 16 / 64 tokens against 96.2 / 299.5 for
+// the global-load kernel; on config 2's Q4_K gate/up and Q6_K down (about 11 routes per slot at 64
+// tokens) it was slower (168.8 vs 155.2, 147.7 vs 140.0 us), so those types keep the global-load
+// kernel. KT_B200_VEC_MSB=0 turns it off, =all takes it for every type (tuning runs).
+constexpr int64_t kMsbTileBytes = 36 * 1024;
+constexpr int64_t kMsbSmemBytes = 100 * 1024;
+static int pick_msb_rows(const KtVecArgs& a, int type, int* stages) {
+  static const int mode = [] {  // 0 off, 1 IQ3_S, 2 every type
+    const char* e = getenv("KT_B200_VEC_MSB");
+    return !e ? 1 : e[0] == '0' ? 0 : strcmp(e, "all") == 0 ? 2 : 1;
+  }();
+  if (mode == 0 || (mode == 1 && type != KT_IQ3_S)) return 0;
+  if (!a.table && (((uintptr_t)a.w) & 15)) return 0;
+  for (int R = 4; R >= 1; R /= 2) {
+    const int64_t rows = 8 * R, bytes = rows * a.row_bytes;
+    if (bytes > kMsbTileBytes || bytes % 16 || a.rows % rows) continue;
+    const int64_t cap = (bytes + 127) & ~(int64_t)127;
+    const int64_t st = kMsbSmemBytes / cap;
+    if (st < 2) continue;
+    *stages = (int)(st < kMsbMaxStages ? st : kMsbMaxStages);
+    return R;
+  }
+  return 0;
+}
+
+template <int TYPE, int DT, int R, int WM>
+static int launch_msb_t(KtVecArgs a, int stages, int max_groups, cudaStream_t s) {
+  a.stages = stages;
+  const int64_t cap = ((int64_t)8 * R * a.row_bytes + 127) & ~(int64_t)127;
+  const size_t smem = (size_t)(stages * cap);
+  auto k = kt_moe_vec_msb_kernel<TYPE, DT, R, WM>;
+  if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess) return -3;
+  const int64_t tiles = (a.rows + 8 * R - 1) / (8 * R);
+  const int64_t items = (int64_t)max_groups * tiles, cap_ctas = 2 * (int64_t)vec_num_sms();
+  k<<<(unsigned)(items < cap_ctas ? (items > 0 ? items : 1) : cap_ctas), 256, smem, s>>>(a);
+  return 0;
+}
+
 template <int TYPE, int DT>
 static int launch_ms(const KtVecArgs& a, int max_groups, cudaStream_t s) {
   static const int forced = [] {
     const char* e = getenv("KT_B200_VEC_MS_R");
     return e ? atoi(e) : 0;
   }();
+  int stages = 0;
+  const int wmax = kt_vec_ms_piece();
+  if (const int Rb = pick_msb_rows(a, TYPE, &stages)) {
+    if (wmax == 4) {
+      if (Rb == 4) return launch_msb_t<TYPE, DT, 4, 4>(a, stages, max_groups, s);
+      if (Rb == 2) return launch_msb_t<TYPE, DT, 2, 4>(a, stages, max_groups, s);
+      return launch_msb_t<TYPE, DT, 1, 4>(a, stages, max_groups, s);
+    }
+    if (Rb == 4) return launch_msb_t<TYPE, DT, 4, 8>(a, stages, max_groups, s);
+    if (Rb == 2) return launch_msb_t<TYPE, DT, 2, 8>(a, stages, max_groups, s);
+    return launch_msb_t<TYPE, DT, 1, 8>(a, stages, max_groups, s);
+  }
   const int R = forced == 1 || forced == 2 || forced == 4 || forced == 8 ? forced : max_groups >= 64 ? 8 : 4;
   const int64_t tiles = (a.rows + 8 * R - 1) / (8 * R);
   const int64_t items = (int64_t)max_groups * tiles, cap = 8 * (int64_t)vec_num_sms();
   const unsigned grid = (unsigned)(items < cap ? (items > 0 ? items : 1) : cap);
-  const int wmax = kt_vec_ms_piece();
 #define KT_MS_LAUNCH(RR, WW) kt_moe_vec_ms_kernel<TYPE, DT, RR, WW><<<grid, 256, 0, s>>>(a)
 #define KT_MS_ROWS(WW)            \
   if (R == 8) KT_MS_LAUNCH(8, WW);  \
@@ -772,7 +909,7 @@ int kt_launch_moe_vec(int type, const void* w, int table, const void* qx, int64_
                       int* status, cudaStream_t s) {
   const KtBlockInfo bi = kt_block_info(type);
   if (!bi.qk || cols % bi.qk) return -1;
-  KtVecArgs a;
+  KtVecArgs a{};
   a.w = (const uint8_t*)w;
   a.table = table;
   a.qx = (const uint8_t*)qx;

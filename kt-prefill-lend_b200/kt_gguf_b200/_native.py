@@ -50,6 +50,13 @@ SIGNATURES = {
     "kt_ep_plan": (_I, [_P, _P, _I64, _I64, _P, _P, _I, _I, _P, _P, _P, _P, _P, _SZ, _P]),
     "kt_ep_pack": (_I, [_P, _I64, _P, _I64, _P, _P]),
     "kt_ep_combine": (_I, [_P, _P, _I, _P, _I64, _I64, _P, _P]),
+    "kt_ep_dispatch_p2p": (_I, [_P, _I64, _P, _P, _I64, _P, _I, _I, _P, _P, _P, _I64, _P, _P]),
+    "kt_ep_combine_p2p": (_I, [_P, _P, _I, _I, _P, _P, _I64, _I64, _P, _P]),
+    "kt_ipc_export": (_I, [_P, _P, ctypes.POINTER(_SZ)]),
+    "kt_ipc_import": (_I, [_P, _SZ, ctypes.POINTER(_P)]),
+    "kt_ipc_close": (_I, [_P, _SZ]),
+    "kt_moe_prefill_counted": (_I, [_P, _I64, _P, _I64, _I64, _P, _P, _I64, _P, _I, _P, _I, _I, _I, _P, _P, _SZ,
+                                    _P]),
     "kt_dense_a8_vec_workspace_size": (_SZ, [_I64, _I64]),
     "kt_dense_a8_vec": (_I, [_P, _I, _I64, _I64, _P, _I, _I64, _P, _P, _SZ, _P]),
     "kt_gguf_dequantize": (_I, [_P, _I, _I64, _I64, _P, _I, _P]),

@@ -19,12 +19,25 @@ expert e. `contiguous_placement(E, P)` gives rank g the experts [g*E/P, (g+1)*E/
 deals experts listed hottest first to ranks 0..P-1, P-1..0, ... (config 2 of the benchmark:
 the 64 hot experts of a Zipf-skewed router, 8 per rank at 8 ranks).
 
-The exchange uses torch.distributed.all_to_all_single (NCCL on GPUs, gloo in the CPU tests).
-The split sizes need one device-to-host copy of the counts per call. On GPUs the plan, the row
-packing and the combine are the library's kernels (kt_ep_plan / kt_ep_pack / kt_ep_combine,
-csrc/ep.cu); `plan_dispatch` restates the same plan with PyTorch ops, which the CPU tests of the
-exchange run on gloo ranks.
+Two exchanges:
+- over peer memory (GPUs, the default with more than one rank): each rank's dispatch kernel
+  writes its rows straight into the other ranks' receive buffers, and its combine kernel reads
+  its partial outputs straight from their output buffers, over NVLink (kt_ep_dispatch_p2p /
+  kt_ep_combine_p2p; the buffers are mapped into every process by CUDA IPC once). The only
+  collectives are an all-gather of the per-destination row counts and two one-word
+  all-reduces used as barriers (every dispatch before any layer, every layer before any
+  combine); the layer reads its row count on the device (kt_moe_prefill_counted), so a call
+  makes no host synchronisation. Output buffers alternate between calls, so a rank's next
+  layer never overwrites rows another rank is still combining. Capacity: this rank receives
+  at most world x (max tokens of any rank) rows, fixed at the first call (max_tokens).
+- torch.distributed.all_to_all_single (NCCL, or gloo in the CPU tests; KT_B200_EP_P2P=0 on
+  GPUs): counts, rows and metadata by three all-to-alls, the partials back by a fourth; the
+  split sizes need one device-to-host copy of the counts per call.
+On GPUs the plan, the row packing and the combines are the library's kernels (kt_ep_plan /
+kt_ep_pack / kt_ep_combine, csrc/ep.cu); `plan_dispatch` restates the same plan with PyTorch
+ops, which the CPU tests of the exchange run on gloo ranks.
 """
+import os
 from dataclasses import dataclass
 from typing import Callable, List, Optional, Tuple
 
@@ -94,21 +107,88 @@ def plan_dispatch(topk_ids: torch.Tensor, topk_weights: torch.Tensor, owner: tor
     return token_of_row, dest_of_row, local_ids, local_w, send_counts
 
 
+class PeerBuffers:
+    """The receive and output buffers of one rank's expert-parallel layer, and every rank's
+    addresses of them: allocated here, exported with kt_ipc_export, exchanged by one all-gather,
+    mapped with kt_ipc_import. peer[b] is a device int64 [world] table of buffer b's address on
+    each rank (b: 0 rows, 1 slot ids, 2 weights, 3 and 4 the two alternating outputs)."""
+
+    N_BUF = 5
+
+    def __init__(self, group, world: int, rank: int, rows_cap: int, K: int, k: int, device):
+        import ctypes
+
+        from . import _native as N
+
+        self.world, self.rank, self.rows_cap = world, rank, rows_cap
+        self.x = torch.empty((rows_cap, K), dtype=torch.bfloat16, device=device)
+        self.ids = torch.empty((rows_cap, k), dtype=torch.int32, device=device)
+        self.w = torch.empty((rows_cap, k), dtype=torch.float32, device=device)
+        self.y = [torch.empty((rows_cap, K), dtype=torch.bfloat16, device=device) for _ in range(2)]
+        self.recv_total = torch.zeros(1, dtype=torch.int32, device=device)
+        self.counts_all = torch.zeros(world * world, dtype=torch.int32, device=device)
+        bufs = [self.x, self.ids, self.w, self.y[0], self.y[1]]
+        lib = N.load()
+        mine = torch.zeros((self.N_BUF, 9), dtype=torch.int64)  # 64-byte handle, then the offset
+        for i, b in enumerate(bufs):
+            h = (ctypes.c_uint8 * 64)()
+            off = ctypes.c_size_t(0)
+            N.check(lib.kt_ipc_export(N.ptr(b), ctypes.cast(h, ctypes.c_void_p), ctypes.byref(off)), "kt_ipc_export")
+            mine[i, :8] = torch.frombuffer(bytearray(h), dtype=torch.int64)
+            mine[i, 8] = off.value
+        every = [torch.empty_like(mine, device=device) for _ in range(world)]
+        dist.all_gather(every, mine.to(device), group=group)
+        every = [e.cpu() for e in every]
+        self._opened = []
+        addr = torch.zeros((self.N_BUF, world), dtype=torch.int64)
+        for r in range(world):
+            for i, b in enumerate(bufs):
+                if r == rank:
+                    addr[i, r] = b.data_ptr()
+                    continue
+                h = (ctypes.c_uint8 * 64).from_buffer_copy(every[r][i, :8].numpy().tobytes())
+                p = ctypes.c_void_p(0)
+                off = int(every[r][i, 8])
+                N.check(lib.kt_ipc_import(ctypes.cast(h, ctypes.c_void_p), off, ctypes.byref(p)), "kt_ipc_import")
+                self._opened.append((p.value, off))
+                addr[i, r] = p.value
+        self.peer = addr.to(device)
+
+    def close(self) -> None:
+        from . import _native as N
+
+        for p, off in self._opened:
+            N.load().kt_ipc_close(p, off)
+        self._opened = []
+
+
+def _p2p_default() -> bool:
+    return os.environ.get("KT_B200_EP_P2P", "1") != "0"
+
+
 class ExpertParallelMoE:
     """One MoE layer, experts sharded over the ranks of `group` (see the module docstring).
 
-    chunks > 1 pipelines the call: the tokens are split into chunks whose all-to-alls run
-    asynchronously (NCCL's stream) while other chunks compute, so the exchange hides behind
-    the expert GEMMs except for the first dispatch and the last combine."""
+    chunks > 1 pipelines the all-to-all exchange: the tokens are split into chunks whose
+    all-to-alls run asynchronously (NCCL's stream) while other chunks compute. p2p (default on
+    GPUs with more than one rank, KT_B200_EP_P2P=0 turns it off) exchanges over peer memory
+    instead; max_tokens bounds the tokens of a call on any rank (default: the largest first
+    call)."""
 
     def __init__(self, owner: torch.Tensor, local: torch.Tensor, expert_fn: Callable, group=None,
-                 shared_fn: Optional[Callable] = None, chunks: int = 1):
+                 shared_fn: Optional[Callable] = None, chunks: int = 1, p2p: Optional[bool] = None,
+                 max_tokens: Optional[int] = None):
         self.group = group
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
         self.owner, self.local = owner, local
         self.expert_fn, self.shared_fn = expert_fn, shared_fn
         self.chunks = max(1, int(chunks))
+        self.p2p = _p2p_default() if p2p is None else bool(p2p)
+        self.max_tokens = max_tokens
+        self.peers: Optional[PeerBuffers] = None
+        self.calls = 0
+        self._flag = None
         self._dev_tables = None
 
     # ---- exchange primitives
@@ -212,10 +292,77 @@ class ExpertParallelMoE:
         self._combine_rows(y_back, plan.plan, plan.send_counts, out, shared)
         return out
 
+    # ---- the exchange over peer memory
+    def _barrier(self, dev) -> None:
+        """every rank's work so far on its stream before any rank's next step (a one-word
+        all-reduce, ordered on the streams like the kernels around it)"""
+        if self._flag is None or self._flag.device != dev:
+            self._flag = torch.zeros(1, dtype=torch.int32, device=dev)
+        dist.all_reduce(self._flag, group=self.group)
+
+    def _peer_buffers(self, T: int, K: int, k: int, dev) -> PeerBuffers:
+        if self.peers is None:
+            cap = torch.tensor([max(T, self.max_tokens or 0)], dtype=torch.int64, device=dev)
+            dist.all_reduce(cap, op=dist.ReduceOp.MAX, group=self.group)
+            self.max_tokens = int(cap.item())
+            self.peers = PeerBuffers(self.group, self.world, self.rank, self.world * self.max_tokens, K, k, dev)
+        if T > self.max_tokens:
+            raise ValueError(f"{T} tokens exceed the exchange capacity of {self.max_tokens} tokens per rank "
+                             f"(max_tokens)")
+        return self.peers
+
+    def _call_p2p(self, x: torch.Tensor, topk_ids: torch.Tensor, topk_weights: torch.Tensor,
+                  events: Optional[list] = None) -> torch.Tensor:
+        """events (optional): four CUDA events recorded on the stream at the call's start, once
+        the rows are exchanged, after the local layer, and at the end (phase timing)."""
+        from . import _native as N
+
+        def mark(i):
+            if events is not None:
+                events[i].record()
+
+        T, K = x.shape
+        k = topk_ids.shape[1]
+        dev = x.device
+        pb = self._peer_buffers(T, K, k, dev)
+        lib = N.load()
+        st = N.stream_of(x)
+        x = x.contiguous()
+        mark(0)
+        plan = self._plan(x, topk_ids, topk_weights)
+        dist.all_gather_into_tensor(pb.counts_all, plan["counts"], group=self.group)
+        N.check(lib.kt_ep_dispatch_p2p(N.ptr(x), K, N.ptr(plan["send_token"]), N.ptr(plan["meta"]), k,
+                                       N.ptr(pb.counts_all), self.rank, self.world, N.ptr(pb.peer[0]),
+                                       N.ptr(pb.peer[1]), N.ptr(pb.peer[2]), pb.rows_cap, N.ptr(pb.recv_total), st),
+                "kt_ep_dispatch_p2p")
+        self._barrier(dev)  # every rank's rows are in place
+        mark(1)
+        b = self.calls % 2
+        self.expert_fn.counted(pb.x, pb.recv_total, pb.ids, pb.w, pb.y[b])
+        shared = self.shared_fn(x) if self.shared_fn is not None else None
+        mark(2)
+        self._barrier(dev)  # every rank's partial outputs are in place
+        out = torch.empty((T, K), dtype=x.dtype, device=dev)
+        sh = shared.to(x.dtype).contiguous() if shared is not None else None
+        N.check(lib.kt_ep_combine_p2p(N.ptr(plan["row_of"]), N.ptr(pb.counts_all), self.rank, self.world,
+                                      N.ptr(pb.peer[3 + b]), N.ptr(sh), T, K, N.ptr(out), st), "kt_ep_combine_p2p")
+        mark(3)
+        self.calls += 1
+        return out
+
+    def close(self) -> None:
+        """Unmaps the other ranks' buffers (after the last call, on every rank)."""
+        if self.peers is not None:
+            torch.cuda.synchronize()
+            self.peers.close()
+            self.peers = None
+
     # ---- ... or pipelined over chunks
     def __call__(self, x: torch.Tensor, topk_ids: torch.Tensor, topk_weights: torch.Tensor) -> torch.Tensor:
         T, K = x.shape
         k = topk_ids.shape[1]
+        if self.world > 1 and x.is_cuda and self.p2p and self.chunks == 1:
+            return self._call_p2p(x, topk_ids, topk_weights)
         if self.world == 1 and x.is_cuda and self.shared_fn is None:
             # one rank: no exchange; the local slots straight from the logical ids
             # ids outside [0, n_experts) are dropped, as kt_ep_plan drops them on the multi-rank path
@@ -281,12 +428,25 @@ def prefill_expert_fn(w13: torch.Tensor, w2: torch.Tensor, type13: int, type2: i
 
     cache = {}
 
-    def fn(x, ids, w):
-        T, k = ids.shape
-        need = N.load().kt_moe_prefill_workspace_size(T, k, x.shape[1], inter, w13.shape[0])
+    def workspace(T, k, dev):
+        need = N.load().kt_moe_prefill_workspace_size(T, k, w2.shape[1], inter, w13.shape[0])
         ws = cache.get("ws")
         if ws is None or ws.numel() < need:
-            ws = cache["ws"] = N.workspace(max(need, int(need * 1.25)), x.device)
-        return M.moe_prefill(x, w13, w2, ids, w, type13, type2, inter, workspace=ws)
+            ws = cache["ws"] = N.workspace(max(need, int(need * 1.25)), dev)
+        return ws
 
+    def fn(x, ids, w):
+        T, k = ids.shape
+        return M.moe_prefill(x, w13, w2, ids, w, type13, type2, inter, workspace=workspace(T, k, x.device))
+
+    def counted(x, n_dev, ids, w, out):
+        """the layer over the first n_dev[0] rows of x / ids / w (a device count), into out"""
+        cap, k = ids.shape
+        ws = workspace(cap, k, x.device)
+        N.check(N.load().kt_moe_prefill_counted(N.ptr(x), cap, N.ptr(n_dev), x.shape[1], inter, N.ptr(ids), N.ptr(w), k,
+                                                N.ptr(w13), type13, N.ptr(w2), type2, 0, w13.shape[0], N.ptr(out),
+                                                N.ptr(ws), ws.numel(), N.stream_of(x)), "kt_moe_prefill_counted")
+        return out
+
+    fn.counted = counted
     return fn
