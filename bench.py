@@ -28,7 +28,10 @@ the HBM roofline with L2 flushed before every call, and the prefill GEMMs at M =
 
 --impl reference times the reference's CPU implementation of the path as restated in
 oracle/ (the reference's own CPU expert library, kt-kernel + llama.cpp, ships only as
-patches on un-vendored sources and cannot be built here) on the host cores.
+patches on un-vendored sources and cannot be built here) on the host cores: the q8_1 x GGUF
+integer-dot arithmetic with AVX-512 VNNI dot products (oracle/kt_cpu_simd.c) where the host
+has them, else the scalar restatement. The same implementation is the cpu_baseline of the
+headline line.
 """
 import argparse
 import ctypes
@@ -158,26 +161,36 @@ def spread_tokens(T: int, n: int):
     return np.unique(np.linspace(0, T - 1, min(n, T)).round().astype(np.int64))
 
 
-def cpu_baseline(L, idx, threads):
-    """the restated reference arithmetic (q8_1 x GGUF integer dots, OpenMP) on the tokens idx
-    -> (tokens/s, bf16 bits of the output rows)"""
-    import numpy as np
-    import torch
-
+def cpu_layer_fn():
+    """the timed CPU implementation of the layer: the reference's arithmetic with AVX-512 VNNI
+    dot products (oracle/kt_cpu_simd.c) where the host has them, else the scalar restatement;
+    -> (function, kind label)"""
     from oracle import oracle as O
 
     O.build()
+    if O.simd_available():
+        return O.moe_cpu_simd, ("AVX-512 VNNI restatement of the reference's CPU arithmetic class (kt-kernel's "
+                                "q8_1 x GGUF integer dots), OpenMP over the host cores")
+    return O.moe_ref_bf16, "scalar restatement of the reference's q8_1 x GGUF integer-dot arithmetic, OpenMP"
+
+
+def cpu_baseline(L, idx, threads):
+    """the CPU implementation of the layer on the tokens idx -> (tokens/s, description)"""
+    import numpy as np
+    import torch
+
     os.environ["OMP_NUM_THREADS"] = str(threads)
+    fn, kind = cpu_layer_fn()
     xb = L.x[idx].view(torch.int16).numpy().view(np.uint16)
     ids = L.topk_ids[idx].numpy()
     w = L.topk_weights[idx].numpy()
-    O.moe_ref_bf16(xb[:8], ids[:8], w[:8], L.type13, L.w13, L.type2, L.w2, L.inter)  # warm-up
-    times, res = [], None
-    for _ in range(2):
+    fn(xb[:8], ids[:8], w[:8], L.type13, L.w13, L.type2, L.w2, L.inter)  # warm-up
+    times = []
+    for _ in range(3):
         t = time.perf_counter()
-        res = O.moe_ref_bf16(xb, ids, w, L.type13, L.w13, L.type2, L.w2, L.inter)
+        fn(xb, ids, w, L.type13, L.w13, L.type2, L.w2, L.inter)
         times.append(time.perf_counter() - t)
-    return len(idx) / min(times), res
+    return len(idx) / min(times), kind
 
 
 def headline_parity(L, idx, out_rows, ref_bits):
@@ -219,9 +232,7 @@ def run_reference(args, rank):
     import numpy as np
     import torch
 
-    from oracle import oracle as O
-
-    O.build()
+    fn, kind = cpu_layer_fn()
     L = synth.make_layer(args.seed, **synth.CONFIGS[2])
     n = min(args.cpu_sample, L.x.shape[0])
     xb = L.x.view(torch.int16).numpy().view(np.uint16)
@@ -231,7 +242,7 @@ def run_reference(args, rank):
 
     def step(i):
         s = (i * n) % (T - n + 1)
-        O.moe_ref_bf16(xb[s:s + n], ids[s:s + n], w[s:s + n], L.type13, L.w13, L.type2, L.w2, L.inter)
+        fn(xb[s:s + n], ids[s:s + n], w[s:s + n], L.type13, L.w13, L.type2, L.w2, L.inter)
 
     for i in range(args.warmup):
         step(i)
@@ -240,7 +251,7 @@ def run_reference(args, rank):
         step(args.warmup + i)
     dt = time.perf_counter() - t0
     value = n * args.steps / dt
-    sample = f"{n} consecutive tokens of the 16K chunk per step (all their routes), extrapolated per token"
+    sample = f"{n} consecutive tokens of the 16K chunk per step (all their routes), extrapolated per token; {kind}"
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3, "higher_is_better": True,
@@ -409,15 +420,16 @@ def run_b200(args, rank, world, local_rank):
         flops_down = 2.0 * K * N * r_hot
         gate_up_tflops = flops_gate_up / (stage_ms[1] * 1e-3) / 1e12
         traffic = profile_traffic("prefill_gate_up_config2.txt")
-        cpu, ref_bits = None, None
+        cpu = None
         idx = spread_tokens(T, args.cpu_sample)
         if world == 1 and not args.no_cpu_baseline:
             threads = host_threads()
-            v, ref_bits = cpu_baseline(L, idx, threads)
+            v, kind = cpu_baseline(L, idx, threads)
+            macs = 3.0 * K * N * float((L.topk_ids[idx] >= 0).sum())
             cpu = {"value": v, "unit": "tokens/s", "cores": threads, "kind": "port",
-                   "sample": f"{len(idx)} tokens spread evenly over the chunk (all their routes), restated "
-                             f"reference q8_1 x GGUF integer-dot arithmetic, OpenMP"}
-        parity = headline_parity(L, idx, out[torch.from_numpy(idx).to(dev)], ref_bits)
+                   "gmac_per_s": macs * v / len(idx) / 1e9,
+                   "sample": f"{len(idx)} tokens spread evenly over the chunk (all their routes); {kind}"}
+        parity = headline_parity(L, idx, out[torch.from_numpy(idx).to(dev)], None)
         value = world * T * args.steps / (ms * 1e-3)
         line = {
             "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
@@ -1046,19 +1058,19 @@ def run_config1(args):
     xb = L.x.view(torch.int16).numpy().view(np.uint16)
     want = O.moe_fp32(xb, L.topk_ids.numpy(), L.topk_weights.numpy(), 8, L.w13, 8, L.w2, N)
     err = O.rel_l2(out.float().cpu().numpy(), want)
-    O.build()
     threads = host_threads()
     os.environ["OMP_NUM_THREADS"] = str(threads)
-    O.moe_ref_bf16(xb[:8], L.topk_ids.numpy()[:8], L.topk_weights.numpy()[:8], 8, L.w13, 8, L.w2, N)
+    fn, kind = cpu_layer_fn()
+    fn(xb[:8], L.topk_ids.numpy()[:8], L.topk_weights.numpy()[:8], 8, L.w13, 8, L.w2, N)
     t = time.perf_counter()
-    O.moe_ref_bf16(xb, L.topk_ids.numpy(), L.topk_weights.numpy(), 8, L.w13, 8, L.w2, N)
+    fn(xb, L.topk_ids.numpy(), L.topk_weights.numpy(), 8, L.w13, 8, L.w2, N)
     cpu_s = time.perf_counter() - t
     line = {"metric": "config 1 layer", "value": T / (ms * 1e-3), "unit": "tokens/s", "ms_per_step": ms,
             "steps": args.steps, "config": {"workload": "Q8_0 MoE layer (BASELINE configs[0])", "tokens": T,
                                              "hidden": K, "inter": N, "experts": cfg["n_experts"], "top_k": k},
             "rel_l2_vs_fp32_oracle": err, "tolerance": 5e-3,
             "cpu_baseline": {"value": T / cpu_s, "unit": "tokens/s", "cores": threads, "kind": "port",
-                             "sample": "the whole 256-token chunk"},
+                             "sample": f"the whole 256-token chunk; {kind}"},
             "data": "synthetic (seeded)"}
     print(json.dumps(line), flush=True)
 

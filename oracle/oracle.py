@@ -27,7 +27,8 @@ _lib = None
 
 
 def build(force: bool = False) -> Path:
-    if force or not LIB_PATH.exists() or LIB_PATH.stat().st_mtime < (HERE / "kt_oracle.c").stat().st_mtime:
+    newest = max((HERE / f).stat().st_mtime for f in ("kt_oracle.c", "kt_cpu_simd.c"))
+    if force or not LIB_PATH.exists() or LIB_PATH.stat().st_mtime < newest:
         subprocess.run(["make", "-C", str(HERE), "-B" if force else "libkt_oracle.so"], check=True,
                        capture_output=True)
     return LIB_PATH
@@ -50,6 +51,8 @@ def lib():
         L.ko_combine_bf16.argtypes = [P, P, I64, I64, I64, P]
         L.ko_moe_ref_bf16.argtypes = [P, I64, I64, I64, P, P, I64, I, P, I, P, I64, P]
         L.ko_moe_fp32.argtypes = [P, I64, I64, I64, P, P, I64, I, P, I, P, I64, P]
+        L.kc_moe_layer.argtypes = [P, I64, I64, I64, P, P, I64, I, P, I, P, I64, P]
+        L.kc_simd_available.argtypes = []
         _lib = L
     return _lib
 
@@ -177,6 +180,30 @@ def moe_fp32(x_bf16: np.ndarray, ids: np.ndarray, w: np.ndarray, type13: int, w1
     if rc:
         raise ValueError("ko_moe_fp32 failed")
     return out
+
+
+def simd_available() -> bool:
+    """whether this host runs the SIMD CPU baseline (AVX-512 with VNNI)"""
+    return bool(lib().kc_simd_available())
+
+
+def moe_cpu_simd(x_bf16: np.ndarray, ids: np.ndarray, w: np.ndarray, type13: int, w13: np.ndarray, type2: int,
+                 w2: np.ndarray, inter: int) -> np.ndarray:
+    """The reference hot-expert layer with the SIMD dot products of kt_cpu_simd.c (the timed
+    CPU baseline; Q4_K / Q6_K / Q8_0): bf16 bits [T, K], as moe_ref_bf16 up to the fp32
+    summation order of the per-block terms."""
+    x = _c(x_bf16, np.uint16)
+    T, K = x.shape
+    ids = _c(ids, np.int32)
+    w = _c(w, np.float32)
+    w13, p13 = _slot_ptrs(w13)
+    w2, p2 = _slot_ptrs(w2)
+    res = np.empty((T, K), dtype=np.uint16)
+    rc = lib().kc_moe_layer(_p(x), T, K, inter, _p(ids), _p(w), ids.shape[1], type13, ctypes.cast(p13, ctypes.c_void_p),
+                            type2, ctypes.cast(p2, ctypes.c_void_p), w13.shape[0], _p(res))
+    if rc:
+        raise ValueError("kc_moe_layer failed (%s)" % ("no AVX-512 VNNI" if rc == -2 else "unsupported type"))
+    return res
 
 
 def rel_l2(a: np.ndarray, b: np.ndarray) -> float:

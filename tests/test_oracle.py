@@ -152,3 +152,20 @@ def test_masked_routes_contribute_nothing():
     f = O.moe_fp32(xb, ids, L.topk_weights.numpy(), 14, L.w13, 14, L.w2, 256)
     r = O.moe_ref_bf16(xb, ids, L.topk_weights.numpy(), 14, L.w13, 14, L.w2, 256)
     assert np.all(f == 0) and np.all(O.bf16_to_f32(r) == 0)
+
+
+@pytest.mark.skipif(not O.simd_available(), reason="host without AVX-512 VNNI")
+@pytest.mark.parametrize("type13,type2", [(12, 14), (8, 8), (14, 12)])
+def test_simd_cpu_baseline_matches_the_scalar_oracle(type13, type2):
+    # the timed CPU baseline (oracle/kt_cpu_simd.c) computes the reference layer's arithmetic;
+    # only the fp32 order of the per-block terms differs from the scalar restatement, so the
+    # outputs agree to within bf16 rounding flips
+    from kt_gguf_b200 import synth
+
+    L = synth.make_layer(3, 48, 2048, 512, 32, 8, type13, type2, n_hot=16, zipf=1.1)
+    xb = L.x.view(torch.int16).numpy().view(np.uint16)
+    args = (L.topk_ids.numpy(), L.topk_weights.numpy(), type13, L.w13, type2, L.w2, 512)
+    ref = O.moe_ref_bf16(xb, *args)
+    got = O.moe_cpu_simd(xb, *args)
+    assert O.rel_l2(O.bf16_to_f32(got), O.bf16_to_f32(ref)) < 1e-3
+    assert (got != ref).mean() < 0.02
