@@ -222,6 +222,15 @@ __device__ __forceinline__ void kt_drain_ns(uint64_t ns) {
   }
 }
 
+// ------------------------------------------------------------------ programmatic dependent launch
+// The prefill layer's kernels are launched with programmatic stream serialization: a kernel may
+// start (and run its prologue: barriers, TMEM, code books) while the previous kernel of the
+// stream is still finishing, and waits here before it reads anything that kernel wrote.
+// kt_pdl_trigger lets the next kernel of the stream launch early; both are no-ops for a kernel
+// launched without the attribute or with no dependent.
+__device__ __forceinline__ void kt_pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void kt_pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // ------------------------------------------------------------------ clusters (CTA pairs)
 
 __device__ __forceinline__ uint32_t kt_cluster_rank() {

@@ -23,6 +23,28 @@ struct KtGemmArgs {
   int* status;                  // device status word
 };
 
+// whether the prefill layer's kernels are launched with programmatic stream serialization
+// (KT_B200_PDL=0: plain stream order, for comparison runs)
+bool kt_pdl_enabled();
+
+// launch with programmatic stream serialization (the kernel calls kt_pdl_wait before it reads
+// what the previous kernel of the stream wrote); 0 on success
+template <typename... KArgs, typename... Args>
+inline int kt_launch_pdl(void (*kernel)(KArgs...), unsigned grid, unsigned block, size_t smem, cudaStream_t s,
+                         Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid, 1, 1);
+  cfg.blockDim = dim3(block, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = kt_pdl_enabled() ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...) == cudaSuccess ? 0 : -4;
+}
+
 int kt_launch_quantize_q8_1(const void* x, int dtype, int64_t rows, int64_t cols, void* qx, cudaStream_t s);
 // the GEMV runs its member-stationary kernel for this type, width and route count (routes grouped
 // in pieces of kt_vec_ms_piece(); kt_launch_moe_vec then takes max_groups = routes)

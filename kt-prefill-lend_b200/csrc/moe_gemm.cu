@@ -200,6 +200,8 @@ __global__ void __launch_bounds__(Roles<PHASE>::kThreads, 1) kt_moe_gemm_kernel(
   __syncthreads();
   kt_tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  kt_pdl_trigger();  // the next kernel may set itself up on SMs this grid leaves
+  kt_pdl_wait();     // the permutation (tiles, sorted tokens) and the inputs are complete
 
   const int n_tiles = *a.n_tiles;
   const int n_wt = a.n_wtiles;
@@ -641,6 +643,8 @@ __global__ void __launch_bounds__(ResRoles::kThreads, 1) kt_moe_down_res_kernel(
   __syncthreads();
   kt_tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  kt_pdl_trigger();
+  kt_pdl_wait();  // H (the gate/up kernel's output) and the chunk list are complete
 
   const int n_wt = a.n_wtiles;
   const int n_units = a.n_tiles[2] * n_wt;  // chunks x weight tiles
@@ -1028,13 +1032,15 @@ static int launch_t(const CUtensorMap& m, const CUtensorMap& wm, const KtGemmArg
   cfg.blockDim = dim3(Roles<PHASE>::kThreads, 1, 1);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = s;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 2;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = kt_pdl_enabled() ? 2 : 1;
   if (cudaLaunchKernelEx(&cfg, k, m, wm, a) != cudaSuccess) return -4;
   return cudaGetLastError() == cudaSuccess ? 0 : -4;
 }
@@ -1050,13 +1056,15 @@ static int launch_res(const CUtensorMap& m, const CUtensorMap& wm, const KtGemmA
   cfg.blockDim = dim3(ResRoles::kThreads, 1, 1);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = s;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 2;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = kt_pdl_enabled() ? 2 : 1;
   if (cudaLaunchKernelEx(&cfg, k, m, wm, a) != cudaSuccess) return -4;
   return cudaGetLastError() == cudaSuccess ? 0 : -4;
 }

@@ -8,6 +8,7 @@
 //                (hot/kt_hot_cache.py:62-75, 121-143)
 //   topk         router top-k: softmax, and DeepSeek-V3 grouped sigmoid routing
 //   permute      counting sort of routes by slot into 256-token tiles for the prefill GEMM
+#include <stdlib.h>
 #include "gguf_dot.cuh"
 #include "kt_kernels.h"
 
@@ -152,6 +153,7 @@ __global__ void kt_combine_sorted_kernel(const uint16_t* __restrict__ y, const i
                                          const float* __restrict__ w, int64_t T, int top_k, int64_t K,
                                          uint16_t* __restrict__ res, float* __restrict__ acc_f32,
                                          const int32_t* __restrict__ tokens_dev) {
+  kt_pdl_wait();  // Y (the down kernel's output) is complete
   const int64_t t = blockIdx.x;
   if (tokens_dev && t >= *tokens_dev) return;  // past the tokens present in this call
   // the token's routes: positions and weights (KMAX >= top_k), then all row loads in flight
@@ -211,14 +213,15 @@ template <bool LOAD, bool STORE>
 static void launch_combine_sorted_mode(const uint16_t* y, const int32_t* route_pos, const float* w, int64_t T, int k,
                                        int64_t K, uint16_t* res, float* acc, int threads, cudaStream_t s,
                                        const int32_t* td) {
+  const unsigned g = (unsigned)T;
   if (k <= 4)
-    kt_combine_sorted_kernel<4, LOAD, STORE><<<(unsigned)T, threads, 0, s>>>(y, route_pos, w, T, k, K, res, acc, td);
+    kt_launch_pdl(kt_combine_sorted_kernel<4, LOAD, STORE>, g, threads, 0, s, y, route_pos, w, T, k, K, res, acc, td);
   else if (k <= 8)
-    kt_combine_sorted_kernel<8, LOAD, STORE><<<(unsigned)T, threads, 0, s>>>(y, route_pos, w, T, k, K, res, acc, td);
+    kt_launch_pdl(kt_combine_sorted_kernel<8, LOAD, STORE>, g, threads, 0, s, y, route_pos, w, T, k, K, res, acc, td);
   else if (k <= 16)
-    kt_combine_sorted_kernel<16, LOAD, STORE><<<(unsigned)T, threads, 0, s>>>(y, route_pos, w, T, k, K, res, acc, td);
+    kt_launch_pdl(kt_combine_sorted_kernel<16, LOAD, STORE>, g, threads, 0, s, y, route_pos, w, T, k, K, res, acc, td);
   else
-    kt_combine_sorted_kernel<32, LOAD, STORE><<<(unsigned)T, threads, 0, s>>>(y, route_pos, w, T, k, K, res, acc, td);
+    kt_launch_pdl(kt_combine_sorted_kernel<32, LOAD, STORE>, g, threads, 0, s, y, route_pos, w, T, k, K, res, acc, td);
 }
 
 int kt_launch_combine_sorted(const uint16_t* y, const int32_t* route_pos, const float* w, int64_t T, int64_t top_k,
@@ -240,6 +243,14 @@ int kt_launch_combine_sorted(const uint16_t* y, const int32_t* route_pos, const 
   else
     launch_combine_sorted_mode<false, false>(y, route_pos, w, T, k, K, res, acc, threads, s, tokens_dev);
   return 0;
+}
+
+bool kt_pdl_enabled() {
+  static const bool on = [] {
+    const char* e = getenv("KT_B200_PDL");
+    return !(e && e[0] == '0');
+  }();
+  return on;
 }
 
 // ------------------------------------------------------------------ row gathers
@@ -511,6 +522,7 @@ __global__ void __launch_bounds__(kPermBlock) kt_perm_hist_kernel(const int32_t*
                                                                   int32_t* __restrict__ hist,
                                                                   int32_t* __restrict__ rank) {
   extern __shared__ int32_t sh[];
+  kt_pdl_trigger();  // the scan may launch; it waits for this grid before reading hist
   for (int e = threadIdx.x; e < n_slots; e += blockDim.x) sh[e] = 0;
   __syncthreads();
   const int64_t lim = kt_perm_limit(routes, top_k, tokens_dev);
@@ -565,6 +577,8 @@ __global__ void __launch_bounds__(kPermBlock) kt_perm_scan_kernel(int32_t* __res
                                                                   int32_t* __restrict__ chunks) {
   __shared__ int32_t warp_sums[32];
   __shared__ int32_t sbase[kPermMaxSlots];
+  kt_pdl_trigger();
+  kt_pdl_wait();  // the block histograms are complete
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
   // 1. per-slot totals
   for (int e = wid; e < n_slots; e += nw) {
@@ -635,6 +649,8 @@ __global__ void __launch_bounds__(kPermBlock) kt_perm_scatter_kernel(const int32
                                                                      const int32_t* __restrict__ hist,
                                                                      int32_t* __restrict__ sorted_token,
                                                                      int32_t* __restrict__ route_pos) {
+  kt_pdl_trigger();
+  kt_pdl_wait();  // the scan's bases are complete
   const int64_t p = (int64_t)blockIdx.x * kPermBlock + threadIdx.x;
   if (p >= routes) return;
   const int64_t lim = kt_perm_limit(routes, top_k, tokens_dev);
@@ -659,10 +675,11 @@ int kt_launch_permute(const int32_t* ids, int64_t routes, int top_k, int n_slots
   if (nb > 0)
     kt_perm_hist_kernel<<<nb, kPermBlock, n_slots * sizeof(int32_t), s>>>(ids, routes, top_k, n_slots, id_base,
                                                                           tokens_dev, hist, route_pos);
-  kt_perm_scan_kernel<<<1, kPermBlock, 0, s>>>(hist, nb, n_slots, tile_tokens, chunk_tiles, counts, tiles, n_tiles,
-                                               chunks);
-  if (nb > 0)
-    kt_perm_scatter_kernel<<<nb, kPermBlock, 0, s>>>(ids, routes, top_k, n_slots, id_base, tokens_dev, hist,
-                                                     sorted_token, route_pos);
+  if (kt_launch_pdl(kt_perm_scan_kernel, 1, kPermBlock, 0, s, (int32_t*)hist, nb, n_slots, tile_tokens, chunk_tiles,
+                    counts, tiles, n_tiles, chunks))
+    return -4;
+  if (nb > 0 && kt_launch_pdl(kt_perm_scatter_kernel, nb, kPermBlock, 0, s, ids, routes, top_k, n_slots, id_base,
+                              tokens_dev, (const int32_t*)hist, sorted_token, route_pos))
+    return -4;
   return 0;
 }
