@@ -55,6 +55,12 @@ int kt_vec_ms_piece();
 int kt_launch_quantize_group(const void* x, int dtype, int64_t rows, int64_t cols, void* qx, const int32_t* ids,
                              int64_t routes, int n_slots, int piece, int32_t* groups, int32_t* order, int* status,
                              cudaStream_t s);
+// the decode GEMV in one launch for at most 16 routes (quantization fused, one CTA per route and
+// 32-row tile); kt_vec_fused_ok says whether a call qualifies
+bool kt_vec_fused_ok(int type, const void* w, int table, const void* x, int64_t routes, int rows, int cols);
+int kt_launch_moe_vec_fused(int type, const void* w, int table, int n_slots, const void* x, int dtype,
+                            const int32_t* ids, int64_t routes, int top_k, int rows, int cols, void* y, int* status,
+                            cudaStream_t s);
 int kt_launch_moe_vec(int type, const void* w, int table, const void* qx, int64_t qrow, const int32_t* groups,
                       const int32_t* order, int max_groups, int top_k, int rows, int cols, int dtype, void* y,
                       int* status, cudaStream_t s);

@@ -391,6 +391,135 @@ __global__ void __launch_bounds__(256) kt_moe_vec_kernel(const KtVecArgs a) {
   }
 }
 
+// q8_1 of one activation row into shared memory (split layout), one thread per 8 consecutive
+// values, so a 32-value block is 4 adjacent lanes. The values equal the 32-lanes-per-block
+// quantizer's (kt_quantize_q8_1_kernel): amax is exact in any order, and the block sum follows
+// the same addition tree as that kernel's xor butterfly (partners 16, 8, 4, 2, 1: values 16
+// apart, then 8 apart -- the lanes two and one apart here -- then 4, 2 and 1 apart inside the
+// thread), so d, the codes and the half2 (d, sum) match bit for bit. One 16-byte load per
+// thread instead of one 2-byte load and ten shuffles per value. Needs cols % 32 == 0 (every GGUF
+// block size) and a 16-byte aligned row start; blockDim a multiple of 32.
+template <int DT>
+__device__ __forceinline__ void kt_quantize_row_split(const void* __restrict__ x, int64_t off, int cols, int64_t kpad,
+                                                      uint8_t* act, int tid, int nthreads) {
+  for (int64_t u = tid; u < kpad / 8; u += nthreads) {  // kpad / 8 is a multiple of 64: whole warps
+    const int64_t c0 = u * 8;
+    float v[8];
+    if (c0 < cols) {
+      if constexpr (DT == KT_DT_F32) {
+        const float4* s4 = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(x) + off + c0);
+        const float4 lo = __ldg(s4), hi = __ldg(s4 + 1);
+        v[0] = lo.x, v[1] = lo.y, v[2] = lo.z, v[3] = lo.w, v[4] = hi.x, v[5] = hi.y, v[6] = hi.z, v[7] = hi.w;
+      } else {
+        const uint4 r = __ldg(reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(x) + off + c0));
+        const uint32_t w[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          v[2 * j] = DT == KT_DT_F16 ? kt_h2f((uint16_t)(w[j] & 0xffff)) : kt_bf2f((uint16_t)(w[j] & 0xffff));
+          v[2 * j + 1] = DT == KT_DT_F16 ? kt_h2f((uint16_t)(w[j] >> 16)) : kt_bf2f((uint16_t)(w[j] >> 16));
+        }
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[j] = 0.0f;
+    }
+    float amax = fabsf(v[0]);
+#pragma unroll
+    for (int j = 1; j < 8; ++j) amax = fmaxf(amax, fabsf(v[j]));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+    float t[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) t[j] = v[j] + __shfl_xor_sync(0xffffffffu, v[j], 2);  // values 16 apart
+#pragma unroll
+    for (int j = 0; j < 8; ++j) t[j] = t[j] + __shfl_xor_sync(0xffffffffu, t[j], 1);  // 8 apart
+#pragma unroll
+    for (int j = 0; j < 4; ++j) t[j] = t[j] + t[j + 4];
+    t[0] = t[0] + t[2];
+    t[1] = t[1] + t[3];
+    const float sum = t[0] + t[1];
+    const float d = amax / 127;
+    uint32_t q[2] = {0u, 0u};
+    if (amax != 0.0f) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) q[j / 4] |= (uint32_t)(uint8_t)(int8_t)roundf(v[j] / d) << (8 * (j % 4));
+    }
+    *reinterpret_cast<uint2*>(act + c0) = make_uint2(q[0], q[1]);
+    if ((u & 3) == 0) *reinterpret_cast<half2*>(act + kpad + 4 * (u / 4)) = __halves2half2(__float2half(d), __float2half(sum));
+  }
+}
+
+// Fused path for a handful of routes (a decode step of one or two tokens): one launch, one CTA
+// per (route, tile of 8, 16 or 32 rows). One thread streams the tile's raw rows into shared memory with a
+// single bulk copy while the CTA quantizes the route's activation row into shared memory (the
+// reference's q8_1 rounding, in the split layout); then each row is the per-route arithmetic of
+// kt_moe_vec_kernel (the reference's lane-to-chunk order and butterfly), so the sums are the
+// same bit for bit. The separate quantize-and-group launch and its global round trip are gone,
+// which is most of a one-token projection's time. Routes not on this device write zero rows.
+constexpr int kFusedMaxRoutes = 16;
+constexpr int kFusedSmemBytes = 192 * 1024;  // dynamic: the tile and the q8_1 row (code books are static)
+
+template <int TYPE, int DT, int LPR>
+__global__ void __launch_bounds__(256) kt_moe_vec_fused_kernel(const KtVecArgs a, const void* __restrict__ x,
+                                                               const int32_t* __restrict__ ids, int n_slots) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  __shared__ uint32_t grid_s[KtGridSmem<TYPE>::WORDS];
+  __shared__ __align__(8) uint64_t full;
+  using C = KtChunk<TYPE>;
+  const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
+  const int R = a.rows_per_cta;
+  const int tiles = a.rows / R;
+  const int64_t p = blockIdx.x / tiles;
+  const int r0 = (blockIdx.x % tiles) * R;
+  // the call's status word: block 0 clears it when it starts, long before any bounded wait of
+  // this grid could run out
+  if (blockIdx.x == 0 && tid == 0 && a.status) *a.status = KT_DEV_OK;
+  const int32_t e = ids[p];
+  if (e < 0 || e >= n_slots) {
+    for (int i = tid; i < R; i += blockDim.x) kt_store_act<DT>(a.y, p * a.rows + r0 + i, 0.0f);
+    return;
+  }
+  const int64_t tile_bytes = (int64_t)R * a.row_bytes;  // a 16-byte multiple (host check)
+  uint8_t* wt = smem;
+  uint8_t* act = smem + ((tile_bytes + 127) & ~(int64_t)127);
+  const uint8_t* wbase = a.table ? reinterpret_cast<const uint8_t*>(reinterpret_cast<const int64_t*>(a.w)[e])
+                                 : a.w + (int64_t)e * a.rows * a.row_bytes;
+  const uint8_t* src = wbase + (int64_t)r0 * a.row_bytes;
+  // a slot table may hold any address: bulk copies only from 16-byte aligned tiles
+  const bool bulk = (((uintptr_t)src) & 15) == 0;
+  if (bulk && tid == 0) {
+    kt_mbar_init(&full, 1);
+    kt_fence_mbar_init();
+    kt_mbar_arrive_expect_tx(&full, (uint32_t)tile_bytes);
+    kt_bulk_g2s(wt, src, (uint32_t)tile_bytes, &full);
+  }
+  if (!bulk) {  // GGUF blocks are always 2-byte aligned
+    const uint16_t* s2 = reinterpret_cast<const uint16_t*>(src);
+    uint16_t* d2 = reinterpret_cast<uint16_t*>(wt);
+    for (int64_t i = tid; i < tile_bytes / 2; i += blockDim.x) d2[i] = __ldg(s2 + i);
+  }
+  kt_stage_grid<TYPE>(grid_s, tid, blockDim.x);
+  kt_quantize_row_split<DT>(x, (p / a.top_k) * a.cols, a.cols, a.kpad, act, tid, blockDim.x);
+  __syncthreads();
+  if (bulk && !kt_mbar_wait(&full, 0, a.status, nullptr)) return;  // the one copy in flight never landed
+  const int nchunks = (a.cols / C::QK) * C::CPB;
+  constexpr int RPW = 32 / LPR;
+  const int sub = lane / LPR, sl = lane % LPR;
+  for (int rr = warp * RPW; rr < R; rr += (blockDim.x / 32) * RPW) {
+    const int r = rr + sub;
+    const uint8_t* wrow = wt + (int64_t)r * a.row_bytes;
+    float acc = 0.0f;
+    for (int c = sl; c < nchunks; c += LPR) {
+      const int i = c / C::CPB, iqs = C::VDR * (c % C::CPB);
+      const int64_t qb = (int64_t)i * (C::QK / 32);
+      acc += kt_vec_dot<TYPE>(wrow + (int64_t)i * C::BYTES, act + 32 * qb, act + a.kpad + 4 * qb, iqs, grid_s);
+    }
+#pragma unroll
+    for (int mask = LPR / 2; mask > 0; mask >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, mask);
+    if (sl == 0) kt_store_act<DT>(a.y, p * a.rows + r0 + r, acc);
+  }
+}
+
 // One row (this lane's share) against W consecutive members of a group: per-lane sums in the
 // reference's chunk order, xor butterfly over the LPR lanes of the row, one store per member.
 // W is a compile-time width so that no work is issued for absent members.
@@ -668,8 +797,16 @@ __global__ void __launch_bounds__(256, 2) kt_moe_vec_msb_kernel(const KtVecArgs 
     const uint8_t* wbase = a.table ? reinterpret_cast<const uint8_t*>(reinterpret_cast<const int64_t*>(a.w)[slot])
                                    : a.w + (int64_t)slot * a.rows * a.row_bytes;
     const uint32_t bytes = (uint32_t)((int64_t)min(kRows, a.rows - r0) * a.row_bytes);
+    const uint8_t* src = wbase + (int64_t)r0 * a.row_bytes;
+    if (((uintptr_t)src) & 15) {  // a slot table may hold any address: copy such a tile with plain loads
+      const uint16_t* s2 = reinterpret_cast<const uint16_t*>(src);
+      uint16_t* d2 = reinterpret_cast<uint16_t*>(smem + (j % S) * tile_cap);
+      for (uint32_t i = 0; i < bytes / 2; ++i) d2[i] = __ldg(s2 + i);
+      kt_mbar_arrive(bar);
+      return;
+    }
     kt_mbar_arrive_expect_tx(bar, bytes);
-    kt_bulk_g2s(smem + (j % S) * tile_cap, wbase + (int64_t)r0 * a.row_bytes, bytes, bar);
+    kt_bulk_g2s(smem + (j % S) * tile_cap, src, bytes, bar);
   };
   if (tid == 0)
     for (int j = 0; j < S; ++j) issue(j);
@@ -904,6 +1041,132 @@ static int pick_pipe_rows(int64_t row_bytes, int rows, const void* w, int table)
   return 0;
 }
 
+template <int TYPE, int DT>
+static int launch_fused_t(const KtVecArgs& a, const void* x, const int32_t* ids, int64_t routes, int n_slots, int lpr,
+                          size_t smem, cudaStream_t s) {
+  const unsigned grid = (unsigned)(routes * (a.rows / a.rows_per_cta));
+  // the shared-memory limit is raised once per instantiation to the most any call asks for
+  static const bool ok16 = cudaFuncSetAttribute(kt_moe_vec_fused_kernel<TYPE, DT, 16>,
+                                                cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                kFusedSmemBytes) == cudaSuccess;
+  static const bool ok32 = cudaFuncSetAttribute(kt_moe_vec_fused_kernel<TYPE, DT, 32>,
+                                                cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                kFusedSmemBytes) == cudaSuccess;
+  if (smem > (size_t)kFusedSmemBytes || !(lpr == 16 ? ok16 : ok32)) return -3;
+  if (lpr == 16)
+    kt_moe_vec_fused_kernel<TYPE, DT, 16><<<grid, 256, smem, s>>>(a, x, ids, n_slots);
+  else
+    kt_moe_vec_fused_kernel<TYPE, DT, 32><<<grid, 256, smem, s>>>(a, x, ids, n_slots);
+  return 0;
+}
+
+template <int TYPE>
+static int launch_fused_dt(const KtVecArgs& a, int dtype, const void* x, const int32_t* ids, int64_t routes,
+                           int n_slots, int lpr, size_t smem, cudaStream_t s) {
+  switch (dtype) {
+    case KT_DT_F32: return launch_fused_t<TYPE, KT_DT_F32>(a, x, ids, routes, n_slots, lpr, smem, s);
+    case KT_DT_F16: return launch_fused_t<TYPE, KT_DT_F16>(a, x, ids, routes, n_slots, lpr, smem, s);
+    case KT_DT_BF16: return launch_fused_t<TYPE, KT_DT_BF16>(a, x, ids, routes, n_slots, lpr, smem, s);
+  }
+  return -1;
+}
+
+static int vec_chunks_per_block(int type) {
+  return type == KT_Q8_0     ? KtChunk<KT_Q8_0>::CPB
+         : type == KT_Q4_K   ? KtChunk<KT_Q4_K>::CPB
+         : type == KT_Q6_K   ? KtChunk<KT_Q6_K>::CPB
+         : type == KT_IQ3_S  ? KtChunk<KT_IQ3_S>::CPB
+         : type == KT_Q2_K   ? KtChunk<KT_Q2_K>::CPB
+         : type == KT_Q3_K   ? KtChunk<KT_Q3_K>::CPB
+         : type == KT_Q5_K   ? KtChunk<KT_Q5_K>::CPB
+         : type == KT_IQ4_XS ? KtChunk<KT_IQ4_XS>::CPB
+         : type == KT_Q2_0   ? KtChunk<KT_Q2_0>::CPB
+         : kt_grid_words(type) > 0 ? 8  // the i-quants: one sub-block a chunk
+                                   : KtChunk<KT_Q4_0>::CPB;  // the 32-value legacy blocks
+}
+
+// Rows per CTA of the fused single-launch path, or 0 when it does not take the call. It takes at
+// most kFusedMaxRoutes routes with a 16-byte aligned weight base (or a slot table) and rows in
+// whole tiles of 8, 16 or 32 whose bytes are a 16-byte multiple (one bulk copy per tile), the
+// tile plus the activation row fitting in shared memory. Of those it picks the largest tile that
+// still gives about four CTAs per SM: one or two tokens are bound by latency, so more CTAs in
+// flight (more bulk copies outstanding, fewer rows per warp) finish sooner. The activations'
+// base must be 16-byte aligned (each thread of the quantizer loads 8 values at once).
+// KT_B200_VEC_FUSED=0 turns the path off, KT_B200_VEC_FUSED_ROWS=8/16/32 fixes the tile (tuning).
+static int fused_rows(int type, const void* w, int table, const void* x, int64_t routes, int rows, int cols) {
+  static const int mode = [] {
+    const char* e = getenv("KT_B200_VEC_FUSED");
+    const char* r = getenv("KT_B200_VEC_FUSED_ROWS");
+    if (e && e[0] == '0') return 0;
+    const int n = r ? atoi(r) : 0;
+    return n == 8 || n == 16 || n == 32 ? n : 1;
+  }();
+  const KtBlockInfo bi = kt_block_info(type);
+  if (!mode || !bi.qk || routes < 1 || routes > kFusedMaxRoutes || rows <= 0 || cols <= 0 || cols % bi.qk) return 0;
+  if ((!table && (((uintptr_t)w) & 15)) || (((uintptr_t)x) & 15)) return 0;
+  const int64_t row_bytes = (int64_t)cols / bi.qk * bi.bytes;
+  int pick = 0;
+  for (int R = 32; R >= 8; R /= 2) {
+    const int64_t tile = (int64_t)R * row_bytes;
+    const int64_t smem = ((tile + 127) & ~(int64_t)127) + kt_q8_1_row_bytes(cols);
+    if (rows % R || tile % 16 || smem > kFusedSmemBytes || routes * (rows / R) >= 0x7fffffff) continue;
+    pick = R;
+    if (mode == R || (mode == 1 && routes * (rows / R) >= 4 * (int64_t)vec_num_sms())) break;
+  }
+  return pick;
+}
+
+bool kt_vec_fused_ok(int type, const void* w, int table, const void* x, int64_t routes, int rows, int cols) {
+  return fused_rows(type, w, table, x, routes, rows, cols) != 0;
+}
+
+int kt_launch_moe_vec_fused(int type, const void* w, int table, int n_slots, const void* x, int dtype,
+                            const int32_t* ids, int64_t routes, int top_k, int rows, int cols, void* y, int* status,
+                            cudaStream_t s) {
+  const int R = fused_rows(type, w, table, x, routes, rows, cols);
+  if (!R) return -1;
+  const KtBlockInfo bi = kt_block_info(type);
+  KtVecArgs a{};
+  a.w = (const uint8_t*)w;
+  a.table = table;
+  a.kpad = ((int64_t)cols + 511) / 512 * 512;
+  a.qrow = kt_q8_1_row_bytes(cols);
+  a.top_k = top_k;
+  a.rows = rows;
+  a.cols = cols;
+  a.row_bytes = (int64_t)cols / bi.qk * bi.bytes;
+  a.status = status;
+  a.y = y;
+  a.rows_per_cta = R;
+  const size_t smem = (size_t)((((int64_t)R * a.row_bytes + 127) & ~(int64_t)127) + a.qrow);
+  const int lpr = cols / bi.qk * vec_chunks_per_block(type) <= 16 ? 16 : 32;
+  switch (type) {
+#define KT_FUSED_CASE(T)   case T: return launch_fused_dt<T>(a, dtype, x, ids, routes, n_slots, lpr, smem, s);
+    KT_FUSED_CASE(KT_Q8_0)
+    KT_FUSED_CASE(KT_Q4_0)
+    KT_FUSED_CASE(KT_Q4_1)
+    KT_FUSED_CASE(KT_Q5_0)
+    KT_FUSED_CASE(KT_Q5_1)
+    KT_FUSED_CASE(KT_IQ4_NL)
+    KT_FUSED_CASE(KT_Q2_K)
+    KT_FUSED_CASE(KT_Q3_K)
+    KT_FUSED_CASE(KT_Q5_K)
+    KT_FUSED_CASE(KT_IQ4_XS)
+    KT_FUSED_CASE(KT_Q2_0)
+    KT_FUSED_CASE(KT_IQ2_XXS)
+    KT_FUSED_CASE(KT_IQ2_XS)
+    KT_FUSED_CASE(KT_IQ2_S)
+    KT_FUSED_CASE(KT_IQ3_XXS)
+    KT_FUSED_CASE(KT_IQ1_S)
+    KT_FUSED_CASE(KT_IQ1_M)
+    KT_FUSED_CASE(KT_Q4_K)
+    KT_FUSED_CASE(KT_Q6_K)
+    KT_FUSED_CASE(KT_IQ3_S)
+#undef KT_FUSED_CASE
+  }
+  return -1;
+}
+
 int kt_launch_moe_vec(int type, const void* w, int table, const void* qx, int64_t qrow, const int32_t* groups,
                       const int32_t* order, int max_groups, int top_k, int rows, int cols, int dtype, void* y,
                       int* status, cudaStream_t s) {
@@ -940,18 +1203,7 @@ int kt_launch_moe_vec(int type, const void* w, int table, const void* qx, int64_
   a.members_per_pass = mpp;
   const size_t smem = (size_t)(wt_bytes + mpp * qrow);
   if (smem + 4 * (size_t)kt_grid_words(type) > 222 * 1024) return -2;  // + the static code book
-  const int chunks_per_block = type == KT_Q8_0     ? KtChunk<KT_Q8_0>::CPB
-                               : type == KT_Q4_K   ? KtChunk<KT_Q4_K>::CPB
-                               : type == KT_Q6_K   ? KtChunk<KT_Q6_K>::CPB
-                               : type == KT_IQ3_S  ? KtChunk<KT_IQ3_S>::CPB
-                               : type == KT_Q2_K   ? KtChunk<KT_Q2_K>::CPB
-                               : type == KT_Q3_K   ? KtChunk<KT_Q3_K>::CPB
-                               : type == KT_Q5_K   ? KtChunk<KT_Q5_K>::CPB
-                               : type == KT_IQ4_XS ? KtChunk<KT_IQ4_XS>::CPB
-                               : type == KT_Q2_0   ? KtChunk<KT_Q2_0>::CPB
-                               : kt_grid_words(type) > 0 ? 8  // the i-quants: one sub-block a chunk
-                                                   : KtChunk<KT_Q4_0>::CPB;  // the 32-value legacy blocks
-  const int nchunks = cols / bi.qk * chunks_per_block;
+  const int nchunks = cols / bi.qk * vec_chunks_per_block(type);
   const int lpr = nchunks <= 16 ? 16 : 32;
   switch (type) {
     case KT_Q8_0: return launch_vec_dt<KT_Q8_0>(a, dtype, max_groups, lpr, smem, s);

@@ -211,3 +211,39 @@ def test_prefill_headline_config2_16k(cuda_device):
     assert err_fp32 < TOL_FP32_ORACLE, err_fp32
     # the reference's own arithmetic sits ~1.2% from fp32; the layer is closer to fp32 than it is
     assert err_fp32 < ref_fp32 and err_ref < 3e-2
+
+
+def test_prefill_maximum_top_k_and_slot_count(cuda_device):
+    # the layer's limits: top_k 32 and 8192 slots (the permutation's shared-memory histogram);
+    # the slots are a pointer table whose 8192 entries alias 12 distinct experts, and every
+    # token routes to 32 distinct slots
+    dev = cuda_device
+    T, k, S, E = 96, 32, 8192, 12
+    L = synth.make_layer(seed=31, tokens=T, hidden=512, inter=256, n_experts=E, top_k=4, type13=12, type2=14)
+    w13, w2 = torch.from_numpy(L.w13).to(dev), torch.from_numpy(L.w2).to(dev)
+    g = torch.Generator().manual_seed(31)
+    slot_expert = torch.randint(0, E, (S,), generator=g)
+    t13 = torch.tensor([w13[e].data_ptr() for e in slot_expert.tolist()], dtype=torch.int64, device=dev)
+    t2 = torch.tensor([w2[e].data_ptr() for e in slot_expert.tolist()], dtype=torch.int64, device=dev)
+    ids = torch.stack([torch.randperm(S, generator=g)[:k] for _ in range(T)]).to(torch.int32)
+    ids[::9, 5] = -1
+    w = torch.rand((T, k), generator=g) / k
+    out = M.moe_prefill(L.x.to(dev), t13, t2, ids.to(dev), w.to(dev), 12, 14, L.inter, table=True)
+    torch.cuda.synchronize()
+    logical = torch.where(ids >= 0, slot_expert[ids.clamp(min=0).long()].to(torch.int32), ids)
+    xb = L.x.view(torch.int16).numpy().view(np.uint16)
+    want = O.moe_fp32(xb, logical.numpy(), w.numpy(), 12, L.w13, 14, L.w2, L.inter)
+    assert O.rel_l2(out.float().cpu().numpy(), want) < TOL_FP32_ORACLE
+    with pytest.raises(Nt.KtError):  # one slot more than the permutation holds
+        M.moe_prefill(L.x.to(dev), torch.cat([t13, t13[:1]]), torch.cat([t2, t2[:1]]), ids.to(dev), w.to(dev), 12, 14,
+                      L.inter, table=True)
+
+
+def test_prefill_empty_chunk(cuda_device):
+    L = synth.make_layer(seed=2, tokens=4, hidden=512, inter=256, n_experts=4, top_k=2, type13=12, type2=14)
+    dev = cuda_device
+    x = torch.empty((0, 512), dtype=torch.bfloat16, device=dev)
+    out = M.moe_prefill(x, torch.from_numpy(L.w13).to(dev), torch.from_numpy(L.w2).to(dev),
+                        torch.empty((0, 2), dtype=torch.int32, device=dev),
+                        torch.empty((0, 2), dtype=torch.float32, device=dev), 12, 14, 256)
+    assert out.shape == (0, 512)
