@@ -304,6 +304,13 @@ def run_b200(args, rank, world, local_rank):
                                           Nt.ptr(w2), L.type2, 0, S, Nt.ptr(out), Nt.ptr(ws), ws.numel(), stream.cuda_stream,
                                           timed[1] if timed is not None else None), "kt_moe_prefill")
 
+    # the clock sampler starts before the warm-up, so the GPU does not idle between the warm-up
+    # and the timed steps
+    uuid = torch.cuda.get_device_properties(dev).uuid
+    sampler = ClockSampler(f"GPU-{uuid}") if rank == 0 else None
+    if sampler:
+        sampler.start()
+        time.sleep(0.3)
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize()
@@ -321,11 +328,6 @@ def run_b200(args, rank, world, local_rank):
     stage = [[evs[i][j].elapsed_time(evs[i][j + 1]) for i in range(1, n_stage)] for j in range(4)]
     stage_ms = [statistics.median(s) for s in stage]
 
-    uuid = torch.cuda.get_device_properties(dev).uuid
-    sampler = ClockSampler(f"GPU-{uuid}") if rank == 0 else None
-    if sampler:
-        sampler.start()
-        time.sleep(0.3)
     if dist:
         dist.barrier()
     torch.cuda.synchronize()
@@ -583,6 +585,11 @@ def run_ep(args, rank, world, local_rank, cfg_id=2):
     T = x.shape[0]
     stream = torch.cuda.current_stream(dev)
 
+    uuid = torch.cuda.get_device_properties(dev).uuid
+    sampler = ClockSampler(f"GPU-{uuid}") if rank == 0 else None
+    if sampler:
+        sampler.start()
+        time.sleep(0.3)
     for _ in range(args.warmup):
         out = layer(x, ids, wts)
     torch.cuda.synchronize()
@@ -627,12 +634,9 @@ def run_ep(args, rank, world, local_rank, cfg_id=2):
     torch.cuda.synchronize()
     stage_ms = [statistics.median(evs[i][j].elapsed_time(evs[i][j + 1]) for i in range(1, 6)) for j in range(4)]
     r_local = int((ir >= 0).sum())
+    for _ in range(2):  # back to the exchange after the stage pass (untimed)
+        out = layer(x, ids, wts)
 
-    uuid = torch.cuda.get_device_properties(dev).uuid
-    sampler = ClockSampler(f"GPU-{uuid}") if rank == 0 else None
-    if sampler:
-        sampler.start()
-        time.sleep(0.3)
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()

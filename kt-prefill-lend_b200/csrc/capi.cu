@@ -79,7 +79,7 @@ int moe_vec(const void* x, int x_dtype, int64_t tokens, int64_t cols, const void
   VecWs v = vec_ws(ws, tokens, cols, routes, n_slots);
   if (ws_bytes < v.bytes) return KT_ERR_WORKSPACE;
   cudaStream_t s = S(stream);
-  if (cols <= (1 << 24) && kt_vec_fused_ok(type, w, table, x, routes, (int)rows, (int)cols))  // one or two tokens
+  if (cols <= (1 << 24) && kt_vec_fused_ok(type, w, table, x, routes, (int)rows, (int)cols))  // a few tokens
     return launch_rc(kt_launch_moe_vec_fused(type, w, table, n_slots, x, x_dtype, ids, routes, (int)top_k, (int)rows,
                                              (int)cols, y, v.status, s));
   const int piece = kt_vec_ms_ok(type, (int)cols, routes) ? kt_vec_ms_piece() : 0;

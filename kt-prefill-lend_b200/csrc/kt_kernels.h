@@ -55,8 +55,8 @@ int kt_vec_ms_piece();
 int kt_launch_quantize_group(const void* x, int dtype, int64_t rows, int64_t cols, void* qx, const int32_t* ids,
                              int64_t routes, int n_slots, int piece, int32_t* groups, int32_t* order, int* status,
                              cudaStream_t s);
-// the decode GEMV in one launch for at most 16 routes (quantization fused, one CTA per route and
-// 32-row tile); kt_vec_fused_ok says whether a call qualifies
+// the decode GEMV in one launch for at most 40 routes (quantization fused, one CTA per route and
+// tile of 8, 16 or 32 rows); kt_vec_fused_ok says whether a call qualifies
 bool kt_vec_fused_ok(int type, const void* w, int table, const void* x, int64_t routes, int rows, int cols);
 int kt_launch_moe_vec_fused(int type, const void* w, int table, int n_slots, const void* x, int dtype,
                             const int32_t* ids, int64_t routes, int top_k, int rows, int cols, void* y, int* status,

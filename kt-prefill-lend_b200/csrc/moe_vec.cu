@@ -449,14 +449,17 @@ __device__ __forceinline__ void kt_quantize_row_split(const void* __restrict__ x
   }
 }
 
-// Fused path for a handful of routes (a decode step of one or two tokens): one launch, one CTA
+// Fused path for a handful of routes (a decode step of up to a few tokens): one launch, one CTA
 // per (route, tile of 8, 16 or 32 rows). One thread streams the tile's raw rows into shared memory with a
 // single bulk copy while the CTA quantizes the route's activation row into shared memory (the
 // reference's q8_1 rounding, in the split layout); then each row is the per-route arithmetic of
 // kt_moe_vec_kernel (the reference's lane-to-chunk order and butterfly), so the sums are the
 // same bit for bit. The separate quantize-and-group launch and its global round trip are gone,
 // which is most of a one-token projection's time. Routes not on this device write zero rows.
-constexpr int kFusedMaxRoutes = 16;
+// Route counts up to 40 take the one-launch path. Measured at four tokens (20-call graph replays,
+// one-launch / grouped): config 2 Q4_K gate/up (31 routes) 18.5 / 17.9 us, Q6_K down (32 routes)
+// 15.7 / 17.0 us, config 3 IQ3_S gate/up (40 routes) 23.9 / 25.5 us.
+constexpr int kFusedMaxRoutes = 40;
 constexpr int kFusedSmemBytes = 192 * 1024;  // dynamic: the tile and the q8_1 row (code books are static)
 
 template <int TYPE, int DT, int LPR>
@@ -1089,10 +1092,13 @@ static int vec_chunks_per_block(int type) {
 // most kFusedMaxRoutes routes with a 16-byte aligned weight base (or a slot table) and rows in
 // whole tiles of 8, 16 or 32 whose bytes are a 16-byte multiple (one bulk copy per tile), the
 // tile plus the activation row fitting in shared memory. Of those it picks the largest tile that
-// still gives about four CTAs per SM: one or two tokens are bound by latency, so more CTAs in
-// flight (more bulk copies outstanding, fewer rows per warp) finish sooner. The activations'
+// still gives three CTAs per SM: a larger tile quantizes the activation row fewer times, a
+// smaller one puts more bulk copies in flight. Measured (B200, 20-call graph replays, one token):
+// config 2 Q4_K gate/up 8.5 / 7.8 / 7.8 us at 8 / 16 / 32 rows, Q6_K down 8.8 / 6.7 / 5.8 us,
+// config 3 IQ3_S gate/up 10.8 / 9.3 / 10.0 us; the rule takes 16, 32 and 16. The activations'
 // base must be 16-byte aligned (each thread of the quantizer loads 8 values at once).
-// KT_B200_VEC_FUSED=0 turns the path off, KT_B200_VEC_FUSED_ROWS=8/16/32 fixes the tile (tuning).
+// KT_B200_VEC_FUSED=0 turns the path off, KT_B200_VEC_FUSED_ROWS=8/16/32 fixes the tile and
+// KT_B200_VEC_FUSED_MAX the largest route count it takes (tuning runs).
 static int fused_rows(int type, const void* w, int table, const void* x, int64_t routes, int rows, int cols) {
   static const int mode = [] {
     const char* e = getenv("KT_B200_VEC_FUSED");
@@ -1102,7 +1108,12 @@ static int fused_rows(int type, const void* w, int table, const void* x, int64_t
     return n == 8 || n == 16 || n == 32 ? n : 1;
   }();
   const KtBlockInfo bi = kt_block_info(type);
-  if (!mode || !bi.qk || routes < 1 || routes > kFusedMaxRoutes || rows <= 0 || cols <= 0 || cols % bi.qk) return 0;
+  static const int64_t max_routes = [] {
+    const char* e = getenv("KT_B200_VEC_FUSED_MAX");
+    const int n = e ? atoi(e) : 0;
+    return (int64_t)(n > 0 && n <= 64 ? n : kFusedMaxRoutes);
+  }();
+  if (!mode || !bi.qk || routes < 1 || routes > max_routes || rows <= 0 || cols <= 0 || cols % bi.qk) return 0;
   if ((!table && (((uintptr_t)w) & 15)) || (((uintptr_t)x) & 15)) return 0;
   const int64_t row_bytes = (int64_t)cols / bi.qk * bi.bytes;
   int pick = 0;
@@ -1111,7 +1122,7 @@ static int fused_rows(int type, const void* w, int table, const void* x, int64_t
     const int64_t smem = ((tile + 127) & ~(int64_t)127) + kt_q8_1_row_bytes(cols);
     if (rows % R || tile % 16 || smem > kFusedSmemBytes || routes * (rows / R) >= 0x7fffffff) continue;
     pick = R;
-    if (mode == R || (mode == 1 && routes * (rows / R) >= 4 * (int64_t)vec_num_sms())) break;
+    if (mode == R || (mode == 1 && routes * (rows / R) >= 3 * (int64_t)vec_num_sms())) break;
   }
   return pick;
 }

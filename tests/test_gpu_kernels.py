@@ -126,7 +126,7 @@ def test_gemv_f32_output_and_table_mode(cuda_device, qtype):
 @pytest.mark.parametrize("qtype,tokens,top_k", [(12, 1, 8), (14, 2, 8), (21, 1, 8), (21, 6, 8), (8, 2, 4)])
 def test_gemv_table_slots_at_odd_addresses(cuda_device, qtype, tokens, top_k):
     # slot addresses 2 bytes past a 16-byte boundary: the kernels that stage weight tiles with bulk
-    # copies (the one-launch decode path at 16 routes or fewer, the staged IQ3_S kernel) take plain
+    # copies (the one-launch decode path at 40 routes or fewer, the staged IQ3_S kernel) take plain
     # loads for such tiles; the sums stay those of the plain layout bit for bit
     cols, rows, slots = (2048 if qtype != 14 else 512), 256, 9
     W, x, ids = _gemv_case(qtype, cols, rows, slots, tokens, top_k, seed=5 + qtype + tokens)
@@ -147,21 +147,21 @@ def test_gemv_table_slots_at_odd_addresses(cuda_device, qtype, tokens, top_k):
 @pytest.mark.parametrize("dtype", [torch.float32, torch.float16, torch.bfloat16], ids=["f32", "f16", "bf16"])
 @pytest.mark.parametrize("qtype", (8, 12, 14, 21, 2, 16, 42))
 def test_gemv_one_launch_path_matches_grouped_path(cuda_device, qtype, dtype):
-    # up to 16 routes take the one-launch path (the activation row quantized inside each CTA,
+    # up to 40 routes take the one-launch path (the activation row quantized inside each CTA,
     # 8 values per thread); more routes take the quantize-and-group launch and the grouped GEMV
     # (32 values per warp). The same routes give the same bits either way; zero and negative-zero
     # blocks and large values included.
     cols, rows, slots, top_k = (2048 if qtype != 14 else 512), 256, 6, 8
-    W, x, ids = _gemv_case(qtype, cols, rows, slots, 3, top_k, seed=19 + qtype, dtype=dtype)
+    W, x, ids = _gemv_case(qtype, cols, rows, slots, 6, top_k, seed=19 + qtype, dtype=dtype)
     x[0, :32] = 0.0
     x[1, 32:64] = -0.0
     x[1, 64:96] *= 300.0
     Wd = torch.from_numpy(W).to(cuda_device)
-    y3 = M.moe_a8_vec_multi(x.to(cuda_device), Wd, ids.reshape(-1).to(cuda_device), top_k, qtype, rows, 3)
+    y6 = M.moe_a8_vec_multi(x.to(cuda_device), Wd, ids.reshape(-1).to(cuda_device), top_k, qtype, rows, 6)
     y2 = M.moe_a8_vec_multi(x[:2].contiguous().to(cuda_device), Wd, ids[:2].reshape(-1).contiguous().to(cuda_device),
                             top_k, qtype, rows, 2)
     assert y2.shape[0] == 2 * top_k
-    assert torch.equal(y2.view(torch.uint8), y3[:2 * top_k].view(torch.uint8))
+    assert torch.equal(y2.view(torch.uint8), y6[:2 * top_k].view(torch.uint8))
 
 
 def test_gemv_many_routes_per_slot(cuda_device):
