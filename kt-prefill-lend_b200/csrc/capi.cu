@@ -104,8 +104,25 @@ struct PreWs {
   int32_t* route_pos;
   uint16_t* h;
   uint16_t* y;
+  uint16_t* w13b;  // gate/up weights dequantized to bf16 [n_slots * 2 inter, hidden] (when pre_dequant)
   size_t bytes;
+  size_t bytes_min;  // without w13b
 };
+
+// Whether a prefill call of this shape dequantizes the gate/up weights to bf16 once, before the
+// GEMM, instead of in the GEMM's producers for every token tile. Worth it when the slots average
+// four token tiles or more (each weight tile is decoded once instead of once per tile; the pass
+// costs about (raw + bf16 bytes) / HBM bandwidth, 53 us at config 2) and the bf16 copy stays
+// under 4 GiB. KT_B200_PREDQ=0 turns it off, =1 on for every shape.
+bool pre_dequant(int64_t tokens, int64_t top_k, int64_t hidden, int64_t inter, int n_slots) {
+  static const int mode = [] {
+    const char* e = getenv("KT_B200_PREDQ");
+    return !e ? 2 : e[0] == '0' ? 0 : 1;
+  }();
+  const int64_t bytes = (int64_t)n_slots * 2 * inter * hidden * 2;
+  if (mode == 0 || bytes > ((int64_t)4 << 30)) return false;
+  return mode == 1 || tokens * top_k >= 4 * (int64_t)kt_gemm_tile_tokens() * n_slots;
+}
 
 PreWs pre_ws(void* ws, int64_t tokens, int64_t top_k, int64_t hidden, int64_t inter, int n_slots) {
   Carve c(ws);
@@ -122,6 +139,10 @@ PreWs pre_ws(void* ws, int64_t tokens, int64_t top_k, int64_t hidden, int64_t in
   p.route_pos = c.take<int32_t>(R);
   p.h = c.take<uint16_t>((size_t)R * inter, 1024);
   p.y = c.take<uint16_t>((size_t)R * hidden, 1024);
+  p.bytes_min = align_up(c.off, 256);
+  p.w13b = pre_dequant(tokens, top_k, hidden, inter, n_slots)
+               ? c.take<uint16_t>((size_t)n_slots * 2 * inter * hidden, 1024)
+               : nullptr;
   p.bytes = align_up(c.off, 256);
   return p;
 }
@@ -300,6 +321,10 @@ KT_EXPORT size_t kt_moe_prefill_workspace_size(int64_t tokens, int64_t top_k, in
   return pre_ws(nullptr, tokens, top_k, hidden, inter, n_slots).bytes;
 }
 
+KT_EXPORT int kt_moe_prefill_predequant(int64_t tokens, int64_t top_k, int64_t hidden, int64_t inter, int n_slots) {
+  return pre_dequant(tokens, top_k, hidden, inter, n_slots) ? 1 : 0;
+}
+
 KT_EXPORT int kt_moe_prefill_workspace_layout(int64_t tokens, int64_t top_k, int64_t hidden, int64_t inter,
                                               int n_slots, size_t offsets[8]) {
   if (!offsets) return KT_ERR_ARG;
@@ -326,7 +351,13 @@ static int prefill_run(const void* x, int64_t tokens, int64_t hidden, int64_t in
   if (acc_flags && (!acc || ((uintptr_t)acc & 15))) return KT_ERR_ARG;
   if (((uintptr_t)x | (uintptr_t)(to_acc ? nullptr : out)) & 15) return KT_ERR_ARG;
   PreWs p = pre_ws(workspace, tokens, top_k, hidden, inter, n_slots);
-  if (workspace_bytes < p.bytes) return KT_ERR_WORKSPACE;
+  if (workspace_bytes < p.bytes_min) return KT_ERR_WORKSPACE;
+  // the one-pass bf16 dequantization of the gate/up weights: plain calls (not an expert group of
+  // a streamed layer, which has few tokens per expert) with contiguous slots and the room for it
+  const void* w13b = p.w13b && workspace_bytes >= p.bytes && !w_is_table && id_base == 0 && !acc_flags &&
+                             !(((uintptr_t)w13) & 15)
+                         ? p.w13b
+                         : nullptr;
   cudaStream_t s = S(stream);
   auto mark = [&](int i) {
     if (stage_events && stage_events[i]) cudaEventRecord(reinterpret_cast<cudaEvent_t>(stage_events[i]), s);
@@ -336,6 +367,10 @@ static int prefill_run(const void* x, int64_t tokens, int64_t hidden, int64_t in
   int rc = kt_launch_permute(topk_ids, R, (int)top_k, n_slots, kt_gemm_tile_tokens(), kt_gemm_chunk_tiles(), p.counts,
                              p.hist, p.tiles, p.n_tiles, p.chunks, p.sorted_token, p.route_pos, s, id_base, tokens_dev);
   if (rc) return launch_rc(rc);
+  if (w13b) {  // timed with the permutation (stage 0), so the gate/up stage is the GEMM alone
+    rc = kt_launch_dequant(type13, w13, (int64_t)n_slots * 2 * inter, hidden, (void*)w13b, KT_DT_BF16, s);
+    if (rc) return launch_rc(rc);
+  }
   mark(0);
   // SMs left to concurrent kernels (e.g. NCCL's while an expert-parallel layer overlaps its
   // all-to-alls with these GEMMs): KT_B200_RESERVE_SMS, read once; the GEMMs are persistent
@@ -347,7 +382,7 @@ static int prefill_run(const void* x, int64_t tokens, int64_t hidden, int64_t in
   }();
   const int grid = num_sms() - reserve >= 2 ? num_sms() - reserve : 2;
   rc = kt_launch_gemm_gate_up(type13, x, tokens, (int)hidden, (int)inter, w13, w_is_table, n_slots, p.tiles, p.n_tiles,
-                              p.sorted_token, p.h, p.status, grid, s);
+                              p.sorted_token, p.h, p.status, grid, s, 0, w13b);
   if (rc) return launch_rc(rc);
   mark(1);
   rc = kt_launch_gemm_down(type2, p.h, R, (int)hidden, (int)inter, w2, w_is_table, n_slots, p.tiles, p.n_tiles,

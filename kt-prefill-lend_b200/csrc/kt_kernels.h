@@ -100,10 +100,12 @@ int kt_launch_permute(const int32_t* ids, int64_t routes, int top_k, int n_slots
                       int32_t* sorted_token, int32_t* route_pos, cudaStream_t s, int id_base = 0,
                       const int32_t* tokens_dev = nullptr);
 
-// linear = 1: no activation, the raw projection [R, 2N] (rows of w13 in order) instead of H [R, N]
+// linear = 1: no activation, the raw projection [R, 2N] (rows of w13 in order) instead of H [R, N];
+// w13_bf16: the slots' weights already dequantized to bf16 [n_slots * 2N, K] (A tiles by TMA, no
+// in-kernel dequantization), or null
 int kt_launch_gemm_gate_up(int type, const void* x, int64_t T, int K, int N, const void* w13, int table, int n_slots,
                            const int32_t* tiles, const int32_t* n_tiles, const int32_t* sorted_token, void* h,
-                           int* status, int grid, cudaStream_t s, int linear = 0);
+                           int* status, int grid, cudaStream_t s, int linear = 0, const void* w13_bf16 = nullptr);
 int kt_launch_gemm_down(int type, const void* h, int64_t R, int K, int N, const void* w2, int table, int n_slots,
                         const int32_t* tiles, const int32_t* n_tiles, const int32_t* chunks, void* y, int* status,
                         int grid, cudaStream_t s);

@@ -80,6 +80,13 @@ constexpr int kXchgBytes = 2 * 32 * 32 * 4;  // phase-1 epilogue: up values for 
 constexpr int kEpiBytes = 4 * 32 * 32 * 2;   // per-warp transpose buffers
 constexpr int kFixedSmem = kStages * (kAStageBytes + kBStageBytes) + kXchgBytes + kEpiBytes + 2048 /* grid */ +
                            1024 /* barriers */ + 1024 /* alignment slack */;
+// A/B stages: 4 with the raw ring of the in-kernel dequant; 6 when A arrives as bf16 by TMA
+// (PRE: no raw ring)
+template <bool PRE>
+struct Stages {
+  static constexpr int N = PRE ? 6 : kStages;
+  static constexpr int SMEM = N * (kAStageBytes + kBStageBytes) + kXchgBytes + kEpiBytes + 2048 + 1024 + 1024;
+};
 
 // Raw staging: a "unit" is UV consecutive values of one weight row (a 256-value super-block,
 // or four 32-value Q8_0 blocks); a raw stage holds one unit for the CTA's 128 rows. Each
@@ -140,7 +147,7 @@ __device__ __forceinline__ int64_t a_row(int rh, int wt, uint32_t cr, int N) {
 
 // LINEAR (phase 1 only): the epilogue stores both halves of the projection as they are, with
 // no activation (kt_moe_gemm_routes), instead of silu(gate) * up
-template <int TYPE, int PHASE, bool LINEAR = false>
+template <int TYPE, int PHASE, bool LINEAR = false, bool PRE = false>
 __global__ void __launch_bounds__(Roles<PHASE>::kThreads, 1) kt_moe_gemm_kernel(const __grid_constant__ CUtensorMap bmap,
                                                                   const __grid_constant__ CUtensorMap wmap,
                                                                   const KtGemmArgs a) {
@@ -150,17 +157,18 @@ __global__ void __launch_bounds__(Roles<PHASE>::kThreads, 1) kt_moe_gemm_kernel(
                 kGatherWarps = RL::kGather;
   uint8_t* smem = reinterpret_cast<uint8_t*>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   using R = Raw<TYPE>;
+  constexpr int NS = Stages<PRE>::N;
   uint8_t* sA = smem;
-  uint8_t* sB = sA + kStages * kAStageBytes;
-  uint8_t* sRaw = sB + kStages * kBStageBytes;
-  float* sX = reinterpret_cast<float*>(sRaw + R::NRAW * R::STAGE_BYTES);
+  uint8_t* sB = sA + NS * kAStageBytes;
+  uint8_t* sRaw = sB + NS * kBStageBytes;
+  float* sX = reinterpret_cast<float*>(sRaw + (PRE ? 0 : R::NRAW * R::STAGE_BYTES));
   uint16_t* sEpi = reinterpret_cast<uint16_t*>(reinterpret_cast<uint8_t*>(sX) + kXchgBytes);
   uint32_t* sGrid = reinterpret_cast<uint32_t*>(reinterpret_cast<uint8_t*>(sEpi) + kEpiBytes);
   uint64_t* bars = reinterpret_cast<uint64_t*>(sGrid + 512);
-  uint64_t* full = bars;                 // [kStages] even CTA: A and B of both CTAs landed
-  uint64_t* empty = full + kStages;      // [kStages] both CTAs: MMAs of the stage done
-  uint64_t* bfull = empty + kStages;     // [kStages] odd CTA: its A and B of the stage landed
-  uint64_t* raw_full = bfull + kStages;  // [NRAW]
+  uint64_t* full = bars;                 // [NS] even CTA: A and B of both CTAs landed
+  uint64_t* empty = full + NS;      // [NS] both CTAs: MMAs of the stage done
+  uint64_t* bfull = empty + NS;     // [NS] odd CTA: its A and B of the stage landed
+  uint64_t* raw_full = bfull + NS;  // [NRAW]
   uint64_t* raw_empty = raw_full + R::NRAW;
   uint64_t* acc_full = raw_empty + R::NRAW;  // [2]
   uint64_t* acc_empty = acc_full + 2;        // [2] even CTA
@@ -172,12 +180,13 @@ __global__ void __launch_bounds__(Roles<PHASE>::kThreads, 1) kt_moe_gemm_kernel(
   const uint32_t cr = kt_cluster_rank();
   const bool leader = cr == 0;
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kStages; ++s) {
-      // even CTA: its producer warps, its B copies, and one forwarded arrival for the odd CTA's
-      // producers and B copies (which arrive on the odd CTA's bfull)
-      kt_mbar_init(&full[s], kProdWarps + (PHASE == 1 ? 32 * kGatherWarps : 1) + 1);
+    for (int s = 0; s < NS; ++s) {
+      // even CTA: its producer warps (PRE: the one thread that loads A), its B copies, and one
+      // forwarded arrival for the odd CTA's producers and B copies (which arrive on its bfull)
+      constexpr int kProdArrive = PRE ? 1 : kProdWarps;
+      kt_mbar_init(&full[s], kProdArrive + (PHASE == 1 ? 32 * kGatherWarps : 1) + 1);
       kt_mbar_init(&empty[s], 1);
-      kt_mbar_init(&bfull[s], kProdWarps + (PHASE == 1 ? 32 * kGatherWarps : 1));
+      kt_mbar_init(&bfull[s], kProdArrive + (PHASE == 1 ? 32 * kGatherWarps : 1));
     }
     for (int s = 0; s < R::NRAW; ++s) {
       kt_mbar_init(&raw_full[s], 1);
@@ -191,7 +200,7 @@ __global__ void __launch_bounds__(Roles<PHASE>::kThreads, 1) kt_moe_gemm_kernel(
     *abort_flag = 0;
     kt_fence_mbar_init();
   }
-  if constexpr (TYPE == KT_IQ3_S) {
+  if constexpr (TYPE == KT_IQ3_S && !PRE) {
     for (int i = threadIdx.x; i < 512; i += blockDim.x) sGrid[i] = kt_iq3s_grid_dev[i];
   }
   kt_cluster_sync();  // the peer's barriers are initialised before any remote arrival
@@ -211,7 +220,31 @@ __global__ void __launch_bounds__(Roles<PHASE>::kThreads, 1) kt_moe_gemm_kernel(
   const int first_item = blockIdx.x >> 1, item_stride = gridDim.x >> 1;
   const int64_t rows_total = PHASE == 1 ? 2 * (int64_t)a.N : (int64_t)a.K_out;
 
-  if (warp < kProdWarps) {
+  if (PRE && warp < kProdWarps) {
+    // ---------------------------------------------------------------- A loader (PRE)
+    // the weights were dequantized to bf16 [slots * rows, K] before this kernel: per k-step one
+    // thread loads this CTA's 64 gate (or first) rows and 64 up (or next) rows with two 2-D TMA
+    // loads in the 128-byte swizzle, the layout the dequant producers write
+    if (warp == 0 && lane == 0) {
+      uint64_t* stage_bar = leader ? full : bfull;
+      uint32_t kit = 0;
+      for (int item = first_item; item < n_items && !*abort_flag; item += item_stride) {
+        const int tile = item / n_wt, wt = item % n_wt;
+        const int64_t r0 = (int64_t)a.tiles[3 * tile + 0] * rows_total;
+        for (int ks = 0; ks < ksteps; ++ks, ++kit) {
+          const int s = kit % NS;
+          if (!kt_mbar_wait(&empty[s], ((kit / NS) & 1) ^ 1, a.status, abort_flag)) break;
+          uint8_t* dst = sA + s * kAStageBytes;
+          kt_mbar_arrive_expect_tx(&stage_bar[s], (uint32_t)kAStageBytes);
+#pragma unroll
+          for (int sg = 0; sg < 2; ++sg)
+            kt_tma_2d(dst + sg * (kAStageBytes / 2), &wmap, ks * 64, (int)(r0 + a_row<PHASE>(64 * sg, wt, cr, a.N)),
+                      &stage_bar[s]);
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp < kProdWarps) {
     // ---------------------------------------------------------------- dequant producers
     // thread -> A row rh (= TMEM lane) -> raw slot in load order: the G sub-tiles of a
     // segment hold weight rows j, j+G, ...; lane rh holds weight row seg*64 + wrow(rh)
@@ -245,8 +278,8 @@ __global__ void __launch_bounds__(Roles<PHASE>::kThreads, 1) kt_moe_gemm_kernel(
           bool ok = true;
 #pragma unroll
           for (int kk = 0; kk < R::KPU; ++kk) {
-            const int s = (kit + kk) % kStages;
-            if (ok && !kt_mbar_wait(&empty[s], (((kit + kk) / kStages) & 1) ^ 1, a.status, abort_flag)) ok = false;
+            const int s = (kit + kk) % NS;
+            if (ok && !kt_mbar_wait(&empty[s], (((kit + kk) / NS) & 1) ^ 1, a.status, abort_flag)) ok = false;
             if (ok) {
               uint8_t* arow = sA + s * kAStageBytes;
               // quarters beat one wider half per thread here: more independent loads in flight
@@ -281,7 +314,7 @@ __global__ void __launch_bounds__(Roles<PHASE>::kThreads, 1) kt_moe_gemm_kernel(
   } else if (warp == kWarpRaw) {
     // ---------------------------------------------------------------- raw loader
     uint32_t uit = 0;
-    for (int item = first_item; item < n_items && !*abort_flag; item += item_stride) {
+    for (int item = first_item; !PRE && item < n_items && !*abort_flag; item += item_stride) {  // idle with PRE
       const int tile = item / n_wt, wt = item % n_wt;
       const int slot = a.tiles[3 * tile + 0];
       const uint8_t* wbase = a.table ? reinterpret_cast<const uint8_t*>(reinterpret_cast<const int64_t*>(a.w)[slot])
@@ -348,8 +381,8 @@ __global__ void __launch_bounds__(Roles<PHASE>::kThreads, 1) kt_moe_gemm_kernel(
         }
       }
       for (int ks = 0; ks < ksteps && !*abort_flag; ++ks, ++kit) {
-        const int s = kit % kStages;
-        if (!kt_mbar_wait(&empty[s], ((kit / kStages) & 1) ^ 1, a.status, abort_flag)) break;
+        const int s = kit % NS;
+        if (!kt_mbar_wait(&empty[s], ((kit / NS) & 1) ^ 1, a.status, abort_flag)) break;
         uint8_t* dst = sB + s * kBStageBytes;
         uint64_t* bar = leader ? &full[s] : &bfull[s];
         if constexpr (PHASE == 1) {
@@ -404,7 +437,7 @@ __global__ void __launch_bounds__(Roles<PHASE>::kThreads, 1) kt_moe_gemm_kernel(
 #pragma unroll
             for (int kk = 0; kk < 4; ++kk) kt_mma2_bf16_ss(d, da + 2 * kk, db + 2 * kk, idesc, (ks | kk) != 0);
             kt_mma2_commit_mc(&empty[s], 3);
-            if (++s == kStages) {
+            if (++s == NS) {
               s = 0;
               ph ^= 1;
             }
@@ -428,7 +461,7 @@ __global__ void __launch_bounds__(Roles<PHASE>::kThreads, 1) kt_moe_gemm_kernel(
               break;
             }
             kt_mbar_arrive_cluster(full0 + 8 * s);
-            if (++s == kStages) {
+            if (++s == NS) {
               s = 0;
               ph ^= 1;
             }
@@ -1021,11 +1054,11 @@ static int make_raw_map(CUtensorMap* m, const void* w, int64_t row_bytes, int64_
   return r == CUDA_SUCCESS ? G : 0;
 }
 
-template <int TYPE, int PHASE, bool LINEAR = false>
+template <int TYPE, int PHASE, bool LINEAR = false, bool PRE = false>
 static int launch_t(const CUtensorMap& m, const CUtensorMap& wm, const KtGemmArgs& a, int grid, cudaStream_t s) {
-  constexpr int smem = smem_bytes<TYPE>();
+  constexpr int smem = PRE ? Stages<true>::SMEM : smem_bytes<TYPE>();
   static_assert(smem <= 227 * 1024, "shared memory budget");
-  auto k = kt_moe_gemm_kernel<TYPE, PHASE, LINEAR>;
+  auto k = kt_moe_gemm_kernel<TYPE, PHASE, LINEAR, PRE>;
   if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) return -3;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)(grid & ~1), 1, 1);  // whole CTA pairs
@@ -1085,7 +1118,7 @@ static int launch_phase(int type, const CUtensorMap& m, const CUtensorMap& wm, c
 // linear the raw projection [R, 2N] (no activation)
 int kt_launch_gemm_gate_up(int type, const void* x, int64_t T, int K, int N, const void* w13, int table, int n_slots,
                            const int32_t* tiles, const int32_t* n_tiles, const int32_t* sorted_token, void* h,
-                           int* status, int grid, cudaStream_t s, int linear) {
+                           int* status, int grid, cudaStream_t s, int linear, const void* w13_bf16) {
   if (K % 256 || N % 128) return -1;
   if (((uintptr_t)x) & 15) return -1;
   CUtensorMap m, wm;
@@ -1095,7 +1128,12 @@ int kt_launch_gemm_gate_up(int type, const void* x, int64_t T, int K, int N, con
   a.w = (const uint8_t*)w13;
   a.table = table;
   a.row_bytes = (int64_t)K / kt_block_info(type).qk * kt_block_info(type).bytes;
-  a.raw_group = table ? 0 : make_raw_map(&wm, w13, a.row_bytes, 2 * (int64_t)N, n_slots, type);
+  if (w13_bf16) {  // the weights already dequantized to bf16 [n_slots * 2N, K]
+    if (((uintptr_t)w13_bf16) & 15 || make_map(&wm, w13_bf16, (int64_t)n_slots * 2 * N, K, 64)) return -2;
+    a.raw_group = 1;  // A rows in natural order (the epilogue's row map)
+  } else {
+    a.raw_group = table ? 0 : make_raw_map(&wm, w13, a.row_bytes, 2 * (int64_t)N, n_slots, type);
+  }
   a.x = (const uint16_t*)x;
   a.K = K;
   a.N = N;
@@ -1107,6 +1145,8 @@ int kt_launch_gemm_gate_up(int type, const void* x, int64_t T, int K, int N, con
   a.out = (uint16_t*)h;
   a.out_ld = linear ? 2 * (int64_t)N : N;
   a.status = status;
+  if (w13_bf16)  // the GGUF type no longer matters: one instance serves every type
+    return linear ? launch_t<KT_Q8_0, 1, true, true>(m, wm, a, grid, s) : launch_t<KT_Q8_0, 1, false, true>(m, wm, a, grid, s);
   return linear ? launch_phase<1, true>(type, m, wm, a, grid, s) : launch_phase<1>(type, m, wm, a, grid, s);
 }
 

@@ -32,6 +32,51 @@ __global__ void kt_dequant_kernel(const uint8_t* __restrict__ w, int64_t rows, i
   for (int j = 0; j < 32; ++j) kt_store_act<DT>(out, r * cols + sub * 32 + j, y[j]);
 }
 
+// 2-byte outputs, written through shared memory: thread t decodes 32-value sub-block i0 + t as
+// above, and since sub-block i lands at output values [32 i, 32 i + 32), the block's 256
+// sub-blocks are one contiguous 16 KB run, which the block then stores with coalesced 16-byte
+// stores (512 contiguous bytes per warp instruction). Needs a 16-byte aligned output.
+template <int TYPE, int DT>
+__global__ void __launch_bounds__(256) kt_dequant16_kernel(const uint8_t* __restrict__ w, int64_t rows, int64_t cols,
+                                                           int64_t row_bytes, void* __restrict__ out) {
+  __shared__ uint32_t grid_s[KtGridSmem<TYPE>::WORDS];
+  __shared__ __align__(16) uint4 stage[256 * 4];
+  if constexpr (kt_grid_words(TYPE) > 0) {
+    kt_stage_grid<TYPE>(grid_s, threadIdx.x, blockDim.x);
+    __syncthreads();
+  }
+  const int64_t subs = cols / 32, n = rows * subs;
+  const int64_t i0 = (int64_t)blockIdx.x * 256;
+  const int t = threadIdx.x;
+  if (i0 + t < n) {
+    const int64_t r = (i0 + t) / subs, sub = (i0 + t) % subs;
+    float y[32];
+    kt_dq32<TYPE>(w + r * row_bytes, (int)sub, y, grid_s);
+    uint32_t pk[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      if constexpr (DT == KT_DT_BF16) {
+        pk[j] = kt_pack_bf2(y[2 * j], y[2 * j + 1]);
+      } else {
+        const half2 hv = __floats2half2_rn(y[2 * j], y[2 * j + 1]);
+        pk[j] = *reinterpret_cast<const uint32_t*>(&hv);
+      }
+    }
+    // chunk j of thread t at 4t + (j ^ ((t >> 1) & 3)): eight neighbouring threads' stores of
+    // one j cover all eight 16-byte bank groups
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      stage[4 * t + (j ^ ((t >> 1) & 3))] = make_uint4(pk[4 * j], pk[4 * j + 1], pk[4 * j + 2], pk[4 * j + 3]);
+  }
+  __syncthreads();
+  const int64_t nsub = n - i0 < 256 ? n - i0 : 256;
+  uint4* o = reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(out) + i0 * 32);
+  for (int c = t; c < 4 * nsub; c += 256) {
+    const int owner = c >> 2;
+    o[c] = stage[4 * owner + ((c & 3) ^ ((owner >> 1) & 3))];
+  }
+}
+
 template <int TYPE>
 static int dequant_t(const void* w, int64_t rows, int64_t cols, void* out, int dt, cudaStream_t s) {
   const KtBlockInfo bi = kt_block_info(TYPE);
@@ -39,6 +84,13 @@ static int dequant_t(const void* w, int64_t rows, int64_t cols, void* out, int d
   const int64_t n = rows * (cols / 32);
   const unsigned blocks = (unsigned)((n + 255) / 256);
   if (n == 0) return 0;
+  if ((dt == KT_DT_BF16 || dt == KT_DT_F16) && (((uintptr_t)out) & 15) == 0) {
+    if (dt == KT_DT_BF16)
+      kt_dequant16_kernel<TYPE, KT_DT_BF16><<<blocks, 256, 0, s>>>((const uint8_t*)w, rows, cols, rb, out);
+    else
+      kt_dequant16_kernel<TYPE, KT_DT_F16><<<blocks, 256, 0, s>>>((const uint8_t*)w, rows, cols, rb, out);
+    return 0;
+  }
   switch (dt) {
     case KT_DT_F32: kt_dequant_kernel<TYPE, KT_DT_F32><<<blocks, 256, 0, s>>>((const uint8_t*)w, rows, cols, rb, out); break;
     case KT_DT_F16: kt_dequant_kernel<TYPE, KT_DT_F16><<<blocks, 256, 0, s>>>((const uint8_t*)w, rows, cols, rb, out); break;

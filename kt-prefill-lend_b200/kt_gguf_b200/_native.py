@@ -66,6 +66,7 @@ SIGNATURES = {
     "kt_topk_softmax": (_I, [_P, _I64, _I, _I, _I, _P, _P, _P]),
     "kt_topk_grouped": (_I, [_P, _P, _I64, _I, _I, _I, _I, _I, _F, _P, _P, _P]),
     "kt_moe_prefill_workspace_size": (_SZ, [_I64, _I64, _I64, _I64, _I]),
+    "kt_moe_prefill_predequant": (_I, [_I64, _I64, _I64, _I64, _I]),
     "kt_moe_prefill_workspace_layout": (_I, [_I64, _I64, _I64, _I64, _I, ctypes.POINTER(_SZ)]),
     "kt_moe_prefill": (_I, [_P, _I64, _I64, _I64, _P, _P, _I64, _P, _I, _P, _I, _I, _I, _P, _P, _SZ, _P]),
     "kt_moe_prefill_timed": (_I, [_P, _I64, _I64, _I64, _P, _P, _I64, _P, _I, _P, _I, _I, _I, _P, _P, _SZ, _P,

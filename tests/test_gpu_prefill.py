@@ -247,3 +247,39 @@ def test_prefill_empty_chunk(cuda_device):
                         torch.empty((0, 2), dtype=torch.int32, device=dev),
                         torch.empty((0, 2), dtype=torch.float32, device=dev), 12, 14, 256)
     assert out.shape == (0, 512)
+
+
+_PREDQ_SCRIPT = r"""
+import sys, torch
+sys.path.insert(0, sys.argv[1])
+from kt_gguf_b200 import kt_gguf_moe_multi as M
+from kt_gguf_b200 import synth
+out = {}
+for t13, t2 in ((12, 14), (8, 21), (21, 8)):
+    L = synth.make_layer(seed=t13, tokens=2048, hidden=1024, inter=512, n_experts=16, top_k=8, type13=t13, type2=t2)
+    dev = torch.device("cuda", 0)
+    y = M.moe_prefill(L.x.to(dev), torch.from_numpy(L.w13).to(dev), torch.from_numpy(L.w2).to(dev),
+                      L.topk_ids.to(dev), L.topk_weights.to(dev), t13, t2, L.inter)
+    out[(t13, t2)] = y.cpu()
+torch.save(out, sys.argv[2])
+"""
+
+
+def test_prefill_predequant_matches_in_kernel_decode(tmp_path):
+    # the gate/up weights dequantized to bf16 in one pass (A tiles by TMA) against the in-kernel
+    # decode of the raw GGUF bytes: the same bf16 operands in the same layout and the same MMAs,
+    # so the layer's output is the same bit for bit. Two processes, one per setting of
+    # KT_B200_PREDQ (read once per process).
+    import os
+    import pathlib
+    import subprocess
+    import sys
+    pkg = str(pathlib.Path(M.__file__).resolve().parents[1])
+    res = {}
+    for mode in ("0", "1"):
+        f = tmp_path / f"out{mode}.pt"
+        env = dict(os.environ, KT_B200_PREDQ=mode)
+        subprocess.run([sys.executable, "-c", _PREDQ_SCRIPT, pkg, str(f)], env=env, check=True, timeout=600)
+        res[mode] = torch.load(f)
+    for key in res["0"]:
+        assert torch.equal(res["0"][key].view(torch.int16), res["1"][key].view(torch.int16)), key
