@@ -32,26 +32,37 @@ __global__ void kt_dequant_kernel(const uint8_t* __restrict__ w, int64_t rows, i
   for (int j = 0; j < 32; ++j) kt_store_act<DT>(out, r * cols + sub * 32 + j, y[j]);
 }
 
-// 2-byte outputs, written through shared memory: thread t decodes 32-value sub-block i0 + t as
-// above, and since sub-block i lands at output values [32 i, 32 i + 32), the block's 256
-// sub-blocks are one contiguous 16 KB run, which the block then stores with coalesced 16-byte
-// stores (512 contiguous bytes per warp instruction). Needs a 16-byte aligned output.
+// 2-byte outputs through shared memory on both sides. Sub-block i (32 values) of the matrix
+// lands at output values [32 i, 32 i + 32), and its GGUF bytes lie in block i / SPB (SPB
+// sub-blocks per GGUF block, rows being whole blocks), so a CTA's 256 sub-blocks read one
+// contiguous run of raw bytes and write one contiguous 16 KB run. The CTA copies the raw run
+// into shared memory with 16-byte loads, each thread decodes its sub-block there with the same
+// decoder as above (kt_dq32, the same values bit for bit), and the CTA stores the bf16 / f16
+// run with coalesced 16-byte stores (512 contiguous bytes per warp instruction). Needs 16-byte
+// aligned weights and output (every CTA's raw run then starts on a 16-byte boundary: 256 / SPB
+// blocks of an even size).
 template <int TYPE, int DT>
 __global__ void __launch_bounds__(256) kt_dequant16_kernel(const uint8_t* __restrict__ w, int64_t rows, int64_t cols,
-                                                           int64_t row_bytes, void* __restrict__ out) {
+                                                           void* __restrict__ out) {
+  constexpr int SPB = kt_block_info(TYPE).qk / 32, BS = kt_block_info(TYPE).bytes;
+  constexpr int RAW = (256 / SPB) * BS;
   __shared__ uint32_t grid_s[KtGridSmem<TYPE>::WORDS];
   __shared__ __align__(16) uint4 stage[256 * 4];
-  if constexpr (kt_grid_words(TYPE) > 0) {
-    kt_stage_grid<TYPE>(grid_s, threadIdx.x, blockDim.x);
-    __syncthreads();
-  }
-  const int64_t subs = cols / 32, n = rows * subs;
-  const int64_t i0 = (int64_t)blockIdx.x * 256;
+  __shared__ __align__(16) uint8_t raw[RAW];
   const int t = threadIdx.x;
-  if (i0 + t < n) {
-    const int64_t r = (i0 + t) / subs, sub = (i0 + t) % subs;
+  if constexpr (kt_grid_words(TYPE) > 0) kt_stage_grid<TYPE>(grid_s, t, blockDim.x);
+  const int64_t n = rows * (cols / 32);
+  const int64_t i0 = (int64_t)blockIdx.x * 256;
+  const int nsub = (int)(n - i0 < 256 ? n - i0 : 256);  // a multiple of SPB
+  const int raw_len = nsub / SPB * BS;
+  const uint8_t* g = w + i0 / SPB * BS;
+  for (int c = t; c < raw_len / 16; c += 256) reinterpret_cast<uint4*>(raw)[c] = __ldg(reinterpret_cast<const uint4*>(g) + c);
+  for (int c = raw_len / 16 * 16 + 2 * t; c < raw_len; c += 512)  // the last CTA's ragged end (even sizes)
+    *reinterpret_cast<uint16_t*>(raw + c) = __ldg(reinterpret_cast<const uint16_t*>(g + c));
+  __syncthreads();
+  if (t < nsub) {
     float y[32];
-    kt_dq32<TYPE>(w + r * row_bytes, (int)sub, y, grid_s);
+    kt_dq32<TYPE>(raw, t, y, grid_s);  // the run as one row: sub-block t of the CTA
     uint32_t pk[16];
 #pragma unroll
     for (int j = 0; j < 16; ++j) {
@@ -69,7 +80,6 @@ __global__ void __launch_bounds__(256) kt_dequant16_kernel(const uint8_t* __rest
       stage[4 * t + (j ^ ((t >> 1) & 3))] = make_uint4(pk[4 * j], pk[4 * j + 1], pk[4 * j + 2], pk[4 * j + 3]);
   }
   __syncthreads();
-  const int64_t nsub = n - i0 < 256 ? n - i0 : 256;
   uint4* o = reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(out) + i0 * 32);
   for (int c = t; c < 4 * nsub; c += 256) {
     const int owner = c >> 2;
@@ -84,11 +94,11 @@ static int dequant_t(const void* w, int64_t rows, int64_t cols, void* out, int d
   const int64_t n = rows * (cols / 32);
   const unsigned blocks = (unsigned)((n + 255) / 256);
   if (n == 0) return 0;
-  if ((dt == KT_DT_BF16 || dt == KT_DT_F16) && (((uintptr_t)out) & 15) == 0) {
+  if ((dt == KT_DT_BF16 || dt == KT_DT_F16) && ((((uintptr_t)out) | ((uintptr_t)w)) & 15) == 0) {
     if (dt == KT_DT_BF16)
-      kt_dequant16_kernel<TYPE, KT_DT_BF16><<<blocks, 256, 0, s>>>((const uint8_t*)w, rows, cols, rb, out);
+      kt_dequant16_kernel<TYPE, KT_DT_BF16><<<blocks, 256, 0, s>>>((const uint8_t*)w, rows, cols, out);
     else
-      kt_dequant16_kernel<TYPE, KT_DT_F16><<<blocks, 256, 0, s>>>((const uint8_t*)w, rows, cols, rb, out);
+      kt_dequant16_kernel<TYPE, KT_DT_F16><<<blocks, 256, 0, s>>>((const uint8_t*)w, rows, cols, out);
     return 0;
   }
   switch (dt) {
