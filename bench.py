@@ -50,6 +50,9 @@ sys.path.insert(0, str(ROOT))
 sys.path.insert(0, str(ROOT / "kt-prefill-lend_b200"))
 
 METRIC = "MoE-layer prefill tok/s @16K chunk"
+# name of the first stage by kt_moe_prefill_predequant's bits: the permutation, then the weight
+# passes
+PASS_STAGE = {1: "permute_and_w13_bf16_pass", 3: "permute_and_bf16_weight_passes"}
 CONFIG_NAME = "qwen3.5-35b-a3b-like MoE layer (BASELINE configs[1])"
 
 
@@ -422,7 +425,7 @@ def run_b200(args, rank, world, local_rank):
         flops_down = 2.0 * K * N * r_hot
         gate_up_tflops = flops_gate_up / (stage_ms[1] * 1e-3) / 1e12
         traffic = profile_traffic("prefill_gate_up_config2.txt")
-        predq = bool(lib.kt_moe_prefill_predequant(T, k, K, N, S))
+        predq = int(lib.kt_moe_prefill_predequant(T, k, K, N, S))  # bit 0: gate/up weights, bit 1: down
         cpu = None
         idx = spread_tokens(T, args.cpu_sample)
         if world == 1 and not args.no_cpu_baseline:
@@ -438,7 +441,9 @@ def run_b200(args, rank, world, local_rank):
             "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None,
-            "dtype": ("bf16 (GGUF Q4_K gate/up weights dequantized to bf16 once per call, Q6_K down weights "
+            "dtype": ("bf16 (GGUF Q4_K gate/up and Q6_K down weights dequantized to bf16 once per call, "
+                      "fp32 accumulate)" if predq == 3 else
+                      "bf16 (GGUF Q4_K gate/up weights dequantized to bf16 once per call, Q6_K down weights "
                       "dequantized in-kernel, fp32 accumulate)" if predq else
                       "bf16 (GGUF Q4_K/Q6_K weights dequantized in-kernel, fp32 accumulate)"),
             "data": "synthetic (seeded)",
@@ -446,12 +451,12 @@ def run_b200(args, rank, world, local_rank):
                        "top_k": k, "resident_experts": S, "routed_to_resident": r_hot,
                        "types": "Q4_K gate/up, Q6_K down", "parallelism": f"token-parallel x{world} (replicated slots)",
                        "l2": "no flush: one step's working set (130 MB weights + 67 MB x + 0.66 GB H/Y) exceeds the 126 MB L2"},
-            "stage_ms": {("permute_and_w13_bf16_pass" if predq else "permute"): stage_ms[0],
+            "stage_ms": {PASS_STAGE.get(predq, "permute"): stage_ms[0],
                          "gate_up_gemm": stage_ms[1], "down_gemm": stage_ms[2], "combine": stage_ms[3]},
             # the kernel runs for well under a second at the maximum SM clock (clocks below): the
             # burst cuBLAS figure is its ceiling; the sustained one applies under the power cap
             "roofline": {"bound": "tensor",
-                         "kernel": ("kt_moe_gemm_kernel<gate/up, bf16 A by TMA> (the one-pass W13 dequant is "
+                         "kernel": ("kt_moe_gemm_kernel<gate/up, bf16 A by TMA> (the one-pass weight dequant is "
                                     "timed in stage_ms' first stage)" if predq else
                                     "kt_moe_gemm_kernel<Q4_K, gate/up>"),
                          "achieved": gate_up_tflops, "peak": tf_burst, "unit": "TFLOP/s",
@@ -463,7 +468,7 @@ def run_b200(args, rank, world, local_rank):
             "parity": parity,
             "cpu_baseline": cpu,
             "e2e": e2e,
-            "gpu_launches": (7 if predq else 6) * args.steps,
+            "gpu_launches": (6 + bin(predq).count("1")) * args.steps,
             "clocks": clocks,
         }
         print(json.dumps(line), flush=True)
@@ -641,7 +646,7 @@ def run_ep(args, rank, world, local_rank, cfg_id=2):
     torch.cuda.synchronize()
     stage_ms = [statistics.median(evs[i][j].elapsed_time(evs[i][j + 1]) for i in range(1, 6)) for j in range(4)]
     r_local = int((ir >= 0).sum())
-    predq_ep = int(lib.kt_moe_prefill_predequant(n_recv, ir.shape[1], K, N, w13.shape[0]))  # the one-pass W13 dequant
+    predq_ep = int(lib.kt_moe_prefill_predequant(n_recv, ir.shape[1], K, N, w13.shape[0]))  # the one-pass dequant bits
     for _ in range(2):  # back to the exchange after the stage pass (untimed)
         out = layer(x, ids, wts)
 
@@ -727,7 +732,7 @@ def run_ep(args, rank, world, local_rank, cfg_id=2):
                                  "torch.distributed.all_to_all_single over NCCL (counts, rows, metadata; partials back)",
                    "nccl": {"version": ".".join(map(str, torch.cuda.nccl.version())), "ranks": world,
                             "backend": dist.get_backend() if world > 1 else None}},
-            "stage_ms_local": {("permute_and_w13_bf16_pass" if predq_ep else "permute"): stage_ms[0],
+            "stage_ms_local": {PASS_STAGE.get(predq_ep, "permute"): stage_ms[0],
                                "gate_up_gemm": stage_ms[1], "down_gemm": stage_ms[2], "combine": stage_ms[3]},
             "roofline": {"bound": "tensor", "kernel": "kt_moe_gemm_kernel<Q4_K, gate/up> (rank 0's received rows)",
                          "achieved": tf13, "peak": tf_burst, "unit": "TFLOP/s", "frac": tf13 / tf_burst,
@@ -737,7 +742,7 @@ def run_ep(args, rank, world, local_rank, cfg_id=2):
             "e2e": e2e,
             # per call: the plan (3 kernels), the row packing, the layer (6), the combine of the
             # partials; one rank skips the exchange and runs the layer alone
-            "gpu_launches": ((11 if world > 1 else 6) + predq_ep) * args.steps * args.ep_chunks,
+            "gpu_launches": ((11 if world > 1 else 6) + bin(predq_ep).count("1")) * args.steps * args.ep_chunks,
             "clocks": clocks,
         }
         print(json.dumps(line), flush=True)

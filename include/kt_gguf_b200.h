@@ -177,16 +177,18 @@ int kt_topk_grouped(const float* logits, const float* bias, int64_t tokens, int 
                     int k, int renormalize, float scale, float* weights, int32_t* ids, void* stream);
 
 /* Prefill MoE layer workspace (permutation, H and Y staging, status word; and, for the shapes
- * kt_moe_prefill_predequant accepts, room for the gate/up weights in bf16). */
+ * kt_moe_prefill_predequant accepts, room for the expert weights in bf16). */
 size_t kt_moe_prefill_workspace_size(int64_t tokens, int64_t top_k, int64_t hidden, int64_t inter, int n_slots);
 
-/* 1 if a kt_moe_prefill / kt_moe_prefill_counted call of this shape dequantizes the gate/up
- * weights of all n_slots slots to bf16 in one pass before the GEMM (A tiles then arrive by
- * TMA, with no decoding in the GEMM), 0 if the GEMM decodes the GGUF bytes itself. The pass
- * is taken when the slots average four 256-token tiles or more and the bf16 copy is at most
- * 4 GiB, for contiguous slots (not a table), when the workspace holds it (the size above);
- * KT_B200_PREDQ=0 turns it off, =1 on for every shape. Either way the outputs are the same bit
- * for bit. No counterpart in the reference (its streamed prefill dequantizes every group). */
+/* Which expert weights a kt_moe_prefill / kt_moe_prefill_counted call of this shape
+ * dequantizes to bf16 in one pass before the GEMMs (A tiles then arrive by TMA, with no
+ * decoding in the GEMMs): bit 0 the gate/up weights, bit 1 the down weights; 0 if the GEMMs
+ * decode the GGUF bytes themselves. The passes are taken when the slots average four 256-token
+ * tiles or more and the bf16 copies are at most 4 GiB together, for contiguous 16-byte aligned
+ * slots (not a table), when the workspace holds them (the size above); KT_B200_PREDQ=0 turns
+ * them off, =1 on for every shape, KT_B200_PREDQ_DOWN=0 keeps the down weights in the GEMM's
+ * decoding. Either way the outputs are the same bit for bit. No counterpart in the reference
+ * (its streamed prefill dequantizes every group). */
 int kt_moe_prefill_predequant(int64_t tokens, int64_t top_k, int64_t hidden, int64_t inter, int n_slots);
 
 /* Byte offsets inside a kt_moe_prefill workspace, for inspection after a call:
@@ -205,7 +207,7 @@ int kt_moe_prefill_workspace_layout(int64_t tokens, int64_t top_k, int64_t hidde
  *   out[t] = sum_k w[t,k] * W2[s] (silu(W13g[s] x_t) * W13u[s] x_t),  s = topk_ids[t, k]
  * with bf16 activations x/out [tokens, hidden], fp32 topk_weights, slot ids as above.
  * The expert GEMMs run on tcgen05 with the GGUF weights dequantized to bf16 (in shared memory,
- * or for the gate/up weights in one pass first: kt_moe_prefill_predequant; fp32 accumulation);
+ * or in one pass first: kt_moe_prefill_predequant; fp32 accumulation);
  * H and the per-route outputs are rounded to bf16, and the
  * weighted sum over k is accumulated in fp32 with the fp32 router weights and rounded once
  * (the finalize of the fused MoE the reference's streamed prefill uses). Replaces the hot

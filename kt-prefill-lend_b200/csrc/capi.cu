@@ -105,23 +105,32 @@ struct PreWs {
   uint16_t* h;
   uint16_t* y;
   uint16_t* w13b;  // gate/up weights dequantized to bf16 [n_slots * 2 inter, hidden] (when pre_dequant)
+  uint16_t* w2b;   // down weights dequantized to bf16 [n_slots * hidden, inter] (when pre_dequant has kPreDown)
   size_t bytes;
-  size_t bytes_min;  // without w13b
+  size_t bytes_min;  // without w13b and w2b
 };
 
-// Whether a prefill call of this shape dequantizes the gate/up weights to bf16 once, before the
-// GEMM, instead of in the GEMM's producers for every token tile. Worth it when the slots average
-// four token tiles or more (each weight tile is decoded once instead of once per tile; the pass
-// costs about (raw + bf16 bytes) / HBM bandwidth, 53 us at config 2) and the bf16 copy stays
-// under 4 GiB. KT_B200_PREDQ=0 turns it off, =1 on for every shape.
-bool pre_dequant(int64_t tokens, int64_t top_k, int64_t hidden, int64_t inter, int n_slots) {
+// Whether a prefill call of this shape dequantizes the expert weights to bf16 once, before the
+// GEMMs, instead of in the GEMMs' producers for every token tile (gate/up) or chunk of four
+// tiles (down). Worth it when the slots average four token tiles or more: each weight tile is
+// then decoded once instead of ~8 (gate/up) or ~2-3 (down) times, for a pass that costs about
+// (raw + bf16 bytes) / HBM bandwidth. Both copies together stay under 4 GiB. KT_B200_PREDQ=0
+// turns it off, =1 on for every shape; KT_B200_PREDQ_DOWN=0 keeps the down weights in the
+// GEMM's own decoding. Returns kPreGateUp | kPreDown bits.
+constexpr int kPreGateUp = 1, kPreDown = 2;
+int pre_dequant(int64_t tokens, int64_t top_k, int64_t hidden, int64_t inter, int n_slots) {
   static const int mode = [] {
     const char* e = getenv("KT_B200_PREDQ");
     return !e ? 2 : e[0] == '0' ? 0 : 1;
   }();
-  const int64_t bytes = (int64_t)n_slots * 2 * inter * hidden * 2;
-  if (mode == 0 || bytes > ((int64_t)4 << 30)) return false;
-  return mode == 1 || tokens * top_k >= 4 * (int64_t)kt_gemm_tile_tokens() * n_slots;
+  static const bool down = [] {
+    const char* e = getenv("KT_B200_PREDQ_DOWN");
+    return !(e && e[0] == '0');
+  }();
+  const int64_t bytes = (int64_t)n_slots * 3 * inter * hidden * 2;
+  if (mode == 0 || bytes > ((int64_t)4 << 30)) return 0;
+  if (mode == 2 && tokens * top_k < 4 * (int64_t)kt_gemm_tile_tokens() * n_slots) return 0;
+  return kPreGateUp | (down ? kPreDown : 0);
 }
 
 PreWs pre_ws(void* ws, int64_t tokens, int64_t top_k, int64_t hidden, int64_t inter, int n_slots) {
@@ -140,9 +149,9 @@ PreWs pre_ws(void* ws, int64_t tokens, int64_t top_k, int64_t hidden, int64_t in
   p.h = c.take<uint16_t>((size_t)R * inter, 1024);
   p.y = c.take<uint16_t>((size_t)R * hidden, 1024);
   p.bytes_min = align_up(c.off, 256);
-  p.w13b = pre_dequant(tokens, top_k, hidden, inter, n_slots)
-               ? c.take<uint16_t>((size_t)n_slots * 2 * inter * hidden, 1024)
-               : nullptr;
+  const int pre = pre_dequant(tokens, top_k, hidden, inter, n_slots);
+  p.w13b = pre & kPreGateUp ? c.take<uint16_t>((size_t)n_slots * 2 * inter * hidden, 1024) : nullptr;
+  p.w2b = pre & kPreDown ? c.take<uint16_t>((size_t)n_slots * hidden * inter, 1024) : nullptr;
   p.bytes = align_up(c.off, 256);
   return p;
 }
@@ -322,7 +331,7 @@ KT_EXPORT size_t kt_moe_prefill_workspace_size(int64_t tokens, int64_t top_k, in
 }
 
 KT_EXPORT int kt_moe_prefill_predequant(int64_t tokens, int64_t top_k, int64_t hidden, int64_t inter, int n_slots) {
-  return pre_dequant(tokens, top_k, hidden, inter, n_slots) ? 1 : 0;
+  return pre_dequant(tokens, top_k, hidden, inter, n_slots);
 }
 
 KT_EXPORT int kt_moe_prefill_workspace_layout(int64_t tokens, int64_t top_k, int64_t hidden, int64_t inter,
@@ -352,12 +361,12 @@ static int prefill_run(const void* x, int64_t tokens, int64_t hidden, int64_t in
   if (((uintptr_t)x | (uintptr_t)(to_acc ? nullptr : out)) & 15) return KT_ERR_ARG;
   PreWs p = pre_ws(workspace, tokens, top_k, hidden, inter, n_slots);
   if (workspace_bytes < p.bytes_min) return KT_ERR_WORKSPACE;
-  // the one-pass bf16 dequantization of the gate/up weights: plain calls (not an expert group of
+  // the one-pass bf16 dequantization of the expert weights: plain calls (not an expert group of
   // a streamed layer, which has few tokens per expert) with contiguous slots and the room for it
-  const void* w13b = p.w13b && workspace_bytes >= p.bytes && !w_is_table && id_base == 0 && !acc_flags &&
-                             !(((uintptr_t)w13) & 15)
-                         ? p.w13b
-                         : nullptr;
+  const bool pre_ok = workspace_bytes >= p.bytes && !w_is_table && id_base == 0 && !acc_flags &&
+                      !(((uintptr_t)w13) & 15) && !(((uintptr_t)w2) & 15);
+  const void* w13b = pre_ok ? p.w13b : nullptr;
+  const void* w2b = pre_ok ? p.w2b : nullptr;
   cudaStream_t s = S(stream);
   auto mark = [&](int i) {
     if (stage_events && stage_events[i]) cudaEventRecord(reinterpret_cast<cudaEvent_t>(stage_events[i]), s);
@@ -367,8 +376,13 @@ static int prefill_run(const void* x, int64_t tokens, int64_t hidden, int64_t in
   int rc = kt_launch_permute(topk_ids, R, (int)top_k, n_slots, kt_gemm_tile_tokens(), kt_gemm_chunk_tiles(), p.counts,
                              p.hist, p.tiles, p.n_tiles, p.chunks, p.sorted_token, p.route_pos, s, id_base, tokens_dev);
   if (rc) return launch_rc(rc);
-  if (w13b) {  // timed with the permutation (stage 0), so the gate/up stage is the GEMM alone
-    rc = kt_launch_dequant(type13, w13, (int64_t)n_slots * 2 * inter, hidden, (void*)w13b, KT_DT_BF16, s);
+  // the weight passes, timed with the permutation (stage 0) so the GEMM stages are the GEMMs alone
+  if (w13b) {
+    rc = kt_launch_dequant(type13, w13, (int64_t)n_slots * 2 * inter, hidden, (void*)w13b, KT_DT_BF16, s, p.status);
+    if (rc) return launch_rc(rc);
+  }
+  if (w2b) {
+    rc = kt_launch_dequant(type2, w2, (int64_t)n_slots * hidden, inter, (void*)w2b, KT_DT_BF16, s, p.status);
     if (rc) return launch_rc(rc);
   }
   mark(0);
@@ -386,7 +400,7 @@ static int prefill_run(const void* x, int64_t tokens, int64_t hidden, int64_t in
   if (rc) return launch_rc(rc);
   mark(1);
   rc = kt_launch_gemm_down(type2, p.h, R, (int)hidden, (int)inter, w2, w_is_table, n_slots, p.tiles, p.n_tiles,
-                           p.chunks, p.y, p.status, grid, s);
+                           p.chunks, p.y, p.status, grid, s, w2b);
   if (rc) return launch_rc(rc);
   mark(2);
   rc = kt_launch_combine_sorted(p.y, p.route_pos, topk_weights, tokens, top_k, hidden, (uint16_t*)out, s, acc,

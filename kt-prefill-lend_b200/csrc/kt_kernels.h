@@ -65,7 +65,9 @@ int kt_launch_moe_vec(int type, const void* w, int table, const void* qx, int64_
                       const int32_t* order, int max_groups, int top_k, int rows, int cols, int dtype, void* y,
                       int* status, cudaStream_t s);
 
-int kt_launch_dequant(int type, const void* w, int64_t rows, int64_t cols, void* out, int out_dtype, cudaStream_t s);
+// status (optional): the workspace status word for the bounded waits of the pipelined pass
+int kt_launch_dequant(int type, const void* w, int64_t rows, int64_t cols, void* out, int out_dtype, cudaStream_t s,
+                      int* status = nullptr);
 int kt_launch_silu_and_mul(const void* h13, int dtype, int64_t rows, int64_t n, void* h, cudaStream_t s);
 int kt_launch_combine(const void* out, int dtype, const float* w, int64_t T, int64_t top_k, int64_t K, void* res,
                       cudaStream_t s);
@@ -106,9 +108,11 @@ int kt_launch_permute(const int32_t* ids, int64_t routes, int top_k, int n_slots
 int kt_launch_gemm_gate_up(int type, const void* x, int64_t T, int K, int N, const void* w13, int table, int n_slots,
                            const int32_t* tiles, const int32_t* n_tiles, const int32_t* sorted_token, void* h,
                            int* status, int grid, cudaStream_t s, int linear = 0, const void* w13_bf16 = nullptr);
+// w2_bf16: the slots' down weights already dequantized to bf16 [n_slots * K, N] (A tiles by TMA, the
+// streaming kernel's instance without producers), or null
 int kt_launch_gemm_down(int type, const void* h, int64_t R, int K, int N, const void* w2, int table, int n_slots,
                         const int32_t* tiles, const int32_t* n_tiles, const int32_t* chunks, void* y, int* status,
-                        int grid, cudaStream_t s);
+                        int grid, cudaStream_t s, const void* w2_bf16 = nullptr);
 int kt_gemm_tile_tokens();
 // the GEMM kernels' bounded-wait and exit path around a barrier nothing arrives on (one CTA
 // pair); writes KT_DEV_TIMEOUT to *status after limit_ns

@@ -1153,11 +1153,30 @@ int kt_launch_gemm_gate_up(int type, const void* x, int64_t T, int K, int N, con
 // phase 2: H [R, N] bf16 (sorted rows); W2 slots [K, N]; out Y [R, K]
 int kt_launch_gemm_down(int type, const void* h, int64_t R, int K, int N, const void* w2, int table, int n_slots,
                         const int32_t* tiles, const int32_t* n_tiles, const int32_t* chunks, void* y, int* status,
-                        int grid, cudaStream_t s) {
+                        int grid, cudaStream_t s, const void* w2_bf16) {
   if (N % 256 || K % 256) return -1;
   CUtensorMap m, wm;
   memset(&wm, 0, sizeof wm);
   if (make_map(&m, h, R, N, kHalfN)) return -2;
+  if (w2_bf16) {
+    // the down weights already dequantized to bf16 [n_slots * K, N]: A rows by two 2-D TMA loads
+    // per k-step, no producers; one instance for every GGUF type
+    if (((uintptr_t)w2_bf16) & 15 || make_map(&wm, w2_bf16, (int64_t)n_slots * K, N, 64)) return -2;
+    KtGemmArgs a{};
+    a.w = (const uint8_t*)w2_bf16;
+    a.raw_group = 1;  // A rows in natural order (the epilogue's row map)
+    a.K = N;          // reduction length
+    a.N = N;
+    a.K_out = K;      // rows of W2
+    a.tiles = tiles;
+    a.n_tiles = n_tiles;
+    a.chunks = chunks;
+    a.n_wtiles = K / 256;
+    a.out = (uint16_t*)y;
+    a.out_ld = K;
+    a.status = status;
+    return launch_t<KT_Q8_0, 2, false, true>(m, wm, a, grid, s);
+  }
   // reductions of up to kResSlices k-steps keep the dequantized weight strip resident
   const bool res = N / 64 <= kResSlices && getenv("KT_B200_DOWN_STREAM") == nullptr;
   KtGemmArgs a{};

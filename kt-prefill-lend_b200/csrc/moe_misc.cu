@@ -87,6 +87,152 @@ __global__ void __launch_bounds__(256) kt_dequant16_kernel(const uint8_t* __rest
   }
 }
 
+// Persistent, pipelined form of the 2-byte pass for large matrices (the prefill layer's weight
+// passes): the same work items (256 sub-blocks: one contiguous raw run in, one contiguous 16 KB
+// run out) and the same decoder, so the values are the same bit for bit. Each CTA walks items
+// blockIdx.x, +gridDim.x, ...; one thread keeps kDqStages raw runs in flight by 1-D bulk copies
+// into a ring of shared-memory stages, and the decoded run leaves by one bulk store from one of
+// two staging buffers. Several runs per SM stay in flight on both sides, where the one-shot
+// kernel above held one load phase per CTA. The thread writes of a staging buffer are made
+// conflict-free without a permuted layout: thread t writes its four 16-byte chunks in the order
+// c ^ ((t >> 1) & 3), chosen by two conditional swaps in registers. Waits are bounded: a raw
+// copy that never lands records KT_DEV_TIMEOUT in *status (when given) and the CTA stops after
+// letting its other copies land. Needs 16-byte aligned weights and output.
+constexpr int kDqStages = 3;
+template <int TYPE>
+struct DqRun {
+  static constexpr int SPB = kt_block_info(TYPE).qk / 32, BS = kt_block_info(TYPE).bytes;
+  static constexpr int RAW = (256 / SPB) * BS;           // a full item's raw run (a multiple of 16)
+  static constexpr int RAWA = (RAW + 127) / 128 * 128;    // its stage, 128-byte aligned
+  static constexpr int SMEM = kDqStages * RAWA + 2 * 256 * 64;
+};
+__device__ __forceinline__ void kt_swap4(uint32_t* a, uint32_t* b, bool c) {
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const uint32_t x = a[i], y = b[i];
+    a[i] = c ? y : x;
+    b[i] = c ? x : y;
+  }
+}
+__device__ __forceinline__ void kt_bulk_s2g(void* dst, const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst), "r"(kt_smem_addr(src)),
+               "r"(bytes)
+               : "memory");
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+template <int TYPE, int DT>
+__global__ void __launch_bounds__(256, 3) kt_dequant16p_kernel(const uint8_t* __restrict__ w, int64_t n_sub,
+                                                               void* __restrict__ out, int* status) {
+  using D = DqRun<TYPE>;
+  extern __shared__ __align__(128) uint8_t dq_smem[];
+  __shared__ uint32_t grid_s[KtGridSmem<TYPE>::WORDS];
+  __shared__ __align__(8) uint64_t full[kDqStages];
+  __shared__ int abort_word;
+  volatile int* abort_flag = &abort_word;
+  const int t = threadIdx.x;
+  const int64_t items = (n_sub + 255) / 256;
+  if (t == 0) {
+    for (int i = 0; i < kDqStages; ++i) kt_mbar_init(&full[i], 1);
+    *abort_flag = 0;
+    kt_fence_mbar_init();
+  }
+  kt_stage_grid<TYPE>(grid_s, t, blockDim.x);
+  __syncthreads();
+  auto run_len = [&](int64_t item) -> int {  // raw bytes of an item (the last one may be short)
+    const int64_t nsub = n_sub - item * 256 < 256 ? n_sub - item * 256 : 256;
+    return (int)(nsub / D::SPB * D::BS);
+  };
+  auto issue = [&](int j) {  // thread 0: the raw run of this CTA's j-th item into stage j % kDqStages
+    const int64_t item = blockIdx.x + (int64_t)j * gridDim.x;
+    if (item >= items) return;
+    uint64_t* bar = &full[j % kDqStages];
+    const int len = run_len(item);
+    if (len % 16) {  // a short last run that is not a 16-byte multiple: the CTA loads it itself
+      kt_mbar_arrive(bar);
+      return;
+    }
+    kt_mbar_arrive_expect_tx(bar, (uint32_t)len);
+    kt_bulk_g2s(dq_smem + (j % kDqStages) * D::RAWA, w + item * D::RAW, (uint32_t)len, bar);
+  };
+  if (t == 0)
+    for (int j = 0; j < kDqStages; ++j) issue(j);
+  int j = 0;
+  for (;; ++j) {
+    const int64_t item = blockIdx.x + (int64_t)j * gridDim.x;
+    if (item >= items) break;
+    uint8_t* raw = dq_smem + (j % kDqStages) * D::RAWA;
+    uint64_t* bar = &full[j % kDqStages];
+    const uint32_t parity = (j / kDqStages) & 1;
+    // thread 0 alone runs the bounded wait, so the whole CTA takes one decision after the
+    // barrier below; it also waits until staging buffer j & 1 is no longer read by the bulk
+    // store of item j - 2
+    if (t == 0 && kt_mbar_wait(bar, parity, status, abort_flag))
+      asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+    __syncthreads();
+    if (*abort_flag) break;
+    kt_mbar_try_wait(bar, parity);  // the phase has completed: every thread acquires the copy
+    const int nsub = (int)(n_sub - item * 256 < 256 ? n_sub - item * 256 : 256);
+    const int len = run_len(item);
+    if (len % 16) {
+      const uint16_t* g = reinterpret_cast<const uint16_t*>(w + item * D::RAW);
+      for (int c = t; c < len / 2; c += 256) reinterpret_cast<uint16_t*>(raw)[c] = __ldg(g + c);
+      __syncthreads();
+    }
+    uint4* stage = reinterpret_cast<uint4*>(dq_smem + kDqStages * D::RAWA + (j & 1) * 256 * 64);
+    if (t < nsub) {
+      float y[32];
+      kt_dq32<TYPE>(raw, t, y, grid_s);
+      uint32_t pk[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        if constexpr (DT == KT_DT_BF16) {
+          pk[i] = kt_pack_bf2(y[2 * i], y[2 * i + 1]);
+        } else {
+          const half2 hv = __floats2half2_rn(y[2 * i], y[2 * i + 1]);
+          pk[i] = *reinterpret_cast<const uint32_t*>(&hv);
+        }
+      }
+      // chunk c moves to register position c ^ sw: step i then writes chunk i ^ sw
+      const int sw = (t >> 1) & 3;
+      kt_swap4(pk + 0, pk + 4, sw & 1);
+      kt_swap4(pk + 8, pk + 12, sw & 1);
+      kt_swap4(pk + 0, pk + 8, sw & 2);
+      kt_swap4(pk + 4, pk + 12, sw & 2);
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+        stage[4 * t + (i ^ sw)] = make_uint4(pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]);
+      kt_fence_proxy_async_smem();
+    }
+    __syncthreads();  // the run is staged; every thread is done with the raw stage
+    if (t == 0) {
+      kt_bulk_s2g(reinterpret_cast<uint16_t*>(out) + item * 256 * 32, stage, (uint32_t)nsub * 64);
+      issue(j + kDqStages);
+    }
+  }
+  if (*abort_flag) kt_drain_ns(200000);  // raw copies issued but never consumed land first
+  if (t == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+}
+
+template <int TYPE, int DT>
+static int dequant16p_t(const void* w, int64_t rows, int64_t cols, void* out, int* status, cudaStream_t s) {
+  static int grid_cap = 0;
+  auto k = kt_dequant16p_kernel<TYPE, DT>;
+  if (!grid_cap) {
+    if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, DqRun<TYPE>::SMEM) != cudaSuccess) return -3;
+    int dev = 0, sms = 148, per_sm = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k, 256, DqRun<TYPE>::SMEM) != cudaSuccess || per_sm < 1)
+      per_sm = 1;
+    grid_cap = sms * per_sm;
+  }
+  const int64_t n = rows * (cols / 32);
+  const int64_t items = (n + 255) / 256;
+  const unsigned grid = (unsigned)(items < grid_cap ? items : grid_cap);
+  k<<<grid, 256, DqRun<TYPE>::SMEM, s>>>((const uint8_t*)w, n, out, status);
+  return cudaGetLastError() == cudaSuccess ? 0 : -4;
+}
+
 template <int TYPE>
 static int dequant_t(const void* w, int64_t rows, int64_t cols, void* out, int dt, cudaStream_t s) {
   const KtBlockInfo bi = kt_block_info(TYPE);
@@ -110,9 +256,25 @@ static int dequant_t(const void* w, int64_t rows, int64_t cols, void* out, int d
   return 0;
 }
 
-int kt_launch_dequant(int type, const void* w, int64_t rows, int64_t cols, void* out, int out_dtype, cudaStream_t s) {
+int kt_launch_dequant(int type, const void* w, int64_t rows, int64_t cols, void* out, int out_dtype, cudaStream_t s,
+                      int* status) {
   const KtBlockInfo bi = kt_block_info(type);
   if (!bi.qk || cols % bi.qk) return -1;
+  // large bf16 passes of the prefill types (the prefill layer's weight passes): the pipelined
+  // kernel, from four items per SM on; KT_B200_DQ_PIPE=0 keeps the one-shot kernel
+  static const bool pipe = [] {
+    const char* e = getenv("KT_B200_DQ_PIPE");
+    return !(e && e[0] == '0');
+  }();
+  if (pipe && out_dtype == KT_DT_BF16 && ((((uintptr_t)out) | ((uintptr_t)w)) & 15) == 0 &&
+      rows * (cols / 32) >= (int64_t)4 * 148 * 256) {
+    switch (type) {
+      case KT_Q8_0: return dequant16p_t<KT_Q8_0, KT_DT_BF16>(w, rows, cols, out, status, s);
+      case KT_Q4_K: return dequant16p_t<KT_Q4_K, KT_DT_BF16>(w, rows, cols, out, status, s);
+      case KT_Q6_K: return dequant16p_t<KT_Q6_K, KT_DT_BF16>(w, rows, cols, out, status, s);
+      case KT_IQ3_S: return dequant16p_t<KT_IQ3_S, KT_DT_BF16>(w, rows, cols, out, status, s);
+    }
+  }
   switch (type) {
     case KT_Q8_0: return dequant_t<KT_Q8_0>(w, rows, cols, out, out_dtype, s);
     case KT_Q4_0: return dequant_t<KT_Q4_0>(w, rows, cols, out, out_dtype, s);

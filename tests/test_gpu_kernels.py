@@ -41,6 +41,19 @@ def test_dequant_bit_exact_vs_golden(cuda_device, qtype):
     assert np.array_equal(gh, want.astype(np.float16))
 
 
+# sizes that take the pipelined bf16 pass (four 256-sub-block items per SM or more): whole items,
+# and a short last item whose raw run is not a 16-byte multiple (loaded by the CTA itself)
+@pytest.mark.parametrize("qtype,rows,cols", [(12, 640, 8192), (14, 607, 8448), (8, 2401, 2080), (21, 600, 8192),
+                                             (14, 1200, 4096)])
+def test_dequant_bf16_pass_matches_fp32(cuda_device, qtype, rows, cols):
+    rng = np.random.default_rng(qtype * 7 + rows)
+    blocks = torch.from_numpy(synth.random_blocks(rng, qtype, rows, cols)).to(cuda_device)
+    want = Kn.gguf_dequantize(blocks, qtype, cols, torch.float32).cpu().numpy()
+    got = Kn.gguf_dequantize(blocks, qtype, cols, torch.bfloat16)
+    torch.cuda.synchronize()
+    assert np.array_equal(bits(got), O.f32_to_bf16(want).reshape(rows, cols))
+
+
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32, torch.float16])
 @pytest.mark.parametrize("cols", [2048, 512, 768, 100])
 def test_quantize_q8_1_bit_exact(cuda_device, dtype, cols):

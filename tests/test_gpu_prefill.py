@@ -266,20 +266,26 @@ torch.save(out, sys.argv[2])
 
 
 def test_prefill_predequant_matches_in_kernel_decode(tmp_path):
-    # the gate/up weights dequantized to bf16 in one pass (A tiles by TMA) against the in-kernel
+    # the expert weights dequantized to bf16 in one pass (A tiles by TMA) against the in-kernel
     # decode of the raw GGUF bytes: the same bf16 operands in the same layout and the same MMAs,
-    # so the layer's output is the same bit for bit. Two processes, one per setting of
-    # KT_B200_PREDQ (read once per process).
+    # so the layer's output is the same bit for bit. One process per setting (the variables are
+    # read once per process).
     import os
     import pathlib
     import subprocess
     import sys
     pkg = str(pathlib.Path(M.__file__).resolve().parents[1])
+    # modes: in-kernel decode; both passes (the default for these shapes); the one-shot pass
+    # kernel instead of the pipelined one; the gate/up pass only, down decoded in its GEMM
+    modes = {"decode": {"KT_B200_PREDQ": "0"}, "passes": {"KT_B200_PREDQ": "1"},
+             "one_shot_pass": {"KT_B200_PREDQ": "1", "KT_B200_DQ_PIPE": "0"},
+             "gate_up_only": {"KT_B200_PREDQ": "1", "KT_B200_PREDQ_DOWN": "0"}}
     res = {}
-    for mode in ("0", "1"):
-        f = tmp_path / f"out{mode}.pt"
-        env = dict(os.environ, KT_B200_PREDQ=mode)
+    for mode, extra in modes.items():
+        f = tmp_path / f"out_{mode}.pt"
+        env = dict(os.environ, **extra)
         subprocess.run([sys.executable, "-c", _PREDQ_SCRIPT, pkg, str(f)], env=env, check=True, timeout=600)
         res[mode] = torch.load(f)
-    for key in res["0"]:
-        assert torch.equal(res["0"][key].view(torch.int16), res["1"][key].view(torch.int16)), key
+    for mode in modes:
+        for key in res["decode"]:
+            assert torch.equal(res["decode"][key].view(torch.int16), res[mode][key].view(torch.int16)), (mode, key)
