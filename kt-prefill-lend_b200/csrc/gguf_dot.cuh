@@ -789,6 +789,63 @@ __device__ __forceinline__ float kt_dot_split(const KtWgt<KT_IQ3_S>& w, const Kt
   return d * sumi;
 }
 
+// IQ3_S weight side that reads a 32 KB signed code book in shared memory instead of the 512-word
+// grid plus sign masks built per lookup. It produces each chunk's signed codes, whose dp4a chain
+// is the same integer as the reference's ((g ^ s) - s) chain, so the chunk's fp32 expression and
+// every route's result are unchanged bit for bit. (Grid bytes are odd, 1..15, so the bytewise
+// negation (g ^ m) + (m & 0x01010101) never carries.)
+//
+// KtWgtS3, the signed book: entry (q | nib << 8 | h << 12) = the grid word of the 9-bit index
+// (q | h << 8) with byte j negated where bit j of the sign nibble nib is set. The eight 13-bit
+// entry indices come from the chunk's bytes with byte permutes: the sign nibbles and the ninth
+// index bits are merged into one byte per lookup, then paired with the code bytes into 16-bit
+// halves. One lookup per 4 values and no sign work. (A 512-word grid replicated for 16 lane
+// columns, with conflict-free lookups and the signs applied in registers, measured no faster than
+// the plain grid on config 3.)
+constexpr int kIq3sBookWords = 8192;
+__device__ __forceinline__ void kt_stage_iq3s_signed(uint32_t* tab, int tid, int nthreads) {
+  for (int e = tid; e < kIq3sBookWords; e += nthreads) {
+    const uint32_t g = kt_iq3s_grid_dev[(e & 255) | ((e >> 12) << 8)];
+    const uint32_t m = kt_nibble_mask((e >> 8) & 15);
+    tab[e] = (g ^ m) + (m & 0x01010101u);
+  }
+}
+struct KtWgtS3 {
+  int g[8];   // signed codes of the chunk's eight 4-value groups
+  float dsc;  // d * (1 + 2 * scale)
+};
+__device__ __forceinline__ void kt_wgt_load(KtWgtS3& w, const uint8_t* bx, int ib32, const uint32_t* tab) {
+  const uint32_t qs0 = (uint32_t)kt_ld_b2(bx + 2 + 8 * ib32), qs1 = (uint32_t)kt_ld_b2(bx + 6 + 8 * ib32);
+  const uint32_t qh = bx[66 + ib32];
+  const uint32_t sg = (uint32_t)kt_ld_b2(bx + 74 + 4 * ib32);
+  // byte l of ce / co: the sign nibble and the ninth index bit of lookup 2l / 2l+1 (bit 4 of the
+  // byte = bit 2l / 2l+1 of qh, spread by one multiply; its stray carries land on odd bits that
+  // the mask drops)
+  const uint32_t he = ((qh & 0x55u) * 0x00410410u) & 0x10101010u;
+  const uint32_t ho = (((qh >> 1) & 0x55u) * 0x00410410u) & 0x10101010u;
+  const uint32_t ce = (sg & 0x0f0f0f0fu) | he;
+  const uint32_t co = ((sg >> 4) & 0x0f0f0f0fu) | ho;
+  const uint32_t x = __byte_perm(ce, co, 0x5140), y = __byte_perm(ce, co, 0x7362);  // [ce_l, co_l] pairs
+  const uint32_t e[4] = {__byte_perm(qs0, x, 0x5140), __byte_perm(qs0, x, 0x7362), __byte_perm(qs1, y, 0x5140),
+                         __byte_perm(qs1, y, 0x7362)};
+#pragma unroll
+  for (int l = 0; l < 4; ++l) {  // e[l]: the entries of lookups 2l (low half) and 2l+1 (high half)
+    w.g[2 * l] = (int)tab[e[l] & 0xffffu];
+    w.g[2 * l + 1] = (int)tab[e[l] >> 16];
+  }
+  w.dsc = kt_h2f(*reinterpret_cast<const uint16_t*>(bx)) * (1 + 2 * ((bx[106 + ib32 / 2] >> 4 * (ib32 % 2)) & 0xf));
+}
+
+template <typename W>
+__device__ __forceinline__ float kt_dot_signed(const W& w, const KtAct<KT_IQ3_S>& a) {
+  int sumi = 0;
+#pragma unroll
+  for (int l = 0; l < 8; ++l) sumi = __dp4a(w.g[l], a.q[l], sumi);
+  const float d = w.dsc * a.d8;
+  return d * sumi;
+}
+__device__ __forceinline__ float kt_dot_split(const KtWgtS3& w, const KtAct<KT_IQ3_S>& a) { return kt_dot_signed(w, a); }
+
 // ------------------------------------------------------------------ dequantization
 // Each function writes the fp32 values of 32 consecutive elements [32*sub, 32*sub + 32)
 // of one block, with ggml's operation order (products that are exact in fp32 first, one

@@ -662,7 +662,7 @@ __global__ void __launch_bounds__(256) kt_moe_vec_pipe_kernel(const KtVecArgs a)
 // the activation work per row and the weight work per member.
 // `tile` holds the raw rows from r0 on, row_bytes apart (the slot in global memory, or a
 // staged copy of the tile in shared memory)
-template <int TYPE, int DT, int R, int WM>
+template <int TYPE, int DT, int R, int WM, typename WT = KtWgt<TYPE>>
 __device__ __forceinline__ void kt_ms_item(const KtVecArgs& a, const uint8_t* tile, int start, int r0,
                                            const uint32_t* grid) {
   using C = KtChunk<TYPE>;
@@ -687,7 +687,7 @@ __device__ __forceinline__ void kt_ms_item(const KtVecArgs& a, const uint8_t* ti
     for (int j = 0; j < R; ++j) {
       const int r = rbase + j;
       if (r < a.rows) {
-        KtWgt<TYPE> w;
+        WT w;
         kt_wgt_load(w, tile + (int64_t)(r - r0) * a.row_bytes + (int64_t)i * C::BYTES, iqs, grid);
 #pragma unroll
         for (int m = 0; m < WM; ++m) acc[j][m] += kt_dot_split(w, act[m]);
@@ -706,28 +706,28 @@ __device__ __forceinline__ void kt_ms_item(const KtVecArgs& a, const uint8_t* ti
 }
 
 // one group of `count` routes (1, 2, 4 or 8, from the grouping in pieces of WMAX) on one tile
-template <int TYPE, int DT, int R, int WMAX>
+template <int TYPE, int DT, int R, int WMAX, typename WT = KtWgt<TYPE>>
 __device__ __forceinline__ void kt_ms_group(const KtVecArgs& a, const uint8_t* tile, int start, int count, int r0,
                                             const uint32_t* grid) {
   switch (count) {
     case 8:
       if constexpr (WMAX >= 8) {
-        kt_ms_item<TYPE, DT, R, 8>(a, tile, start, r0, grid);
+        kt_ms_item<TYPE, DT, R, 8, WT>(a, tile, start, r0, grid);
       } else {  // not produced with piece WMAX; in parts of WMAX if it were
-        for (int m = 0; m < 8; m += WMAX) kt_ms_item<TYPE, DT, R, WMAX>(a, tile, start + m, r0, grid);
+        for (int m = 0; m < 8; m += WMAX) kt_ms_item<TYPE, DT, R, WMAX, WT>(a, tile, start + m, r0, grid);
       }
       break;
     case 4:
       if constexpr (WMAX >= 4) {
-        kt_ms_item<TYPE, DT, R, 4>(a, tile, start, r0, grid);
+        kt_ms_item<TYPE, DT, R, 4, WT>(a, tile, start, r0, grid);
       } else {
-        kt_ms_item<TYPE, DT, R, 2>(a, tile, start, r0, grid);
-        kt_ms_item<TYPE, DT, R, 2>(a, tile, start + 2, r0, grid);
+        kt_ms_item<TYPE, DT, R, 2, WT>(a, tile, start, r0, grid);
+        kt_ms_item<TYPE, DT, R, 2, WT>(a, tile, start + 2, r0, grid);
       }
       break;
-    case 2: kt_ms_item<TYPE, DT, R, 2>(a, tile, start, r0, grid); break;
+    case 2: kt_ms_item<TYPE, DT, R, 2, WT>(a, tile, start, r0, grid); break;
     default:  // 1 (any other count only if the groups were not cut in powers of two)
-      for (int m = 0; m < count; ++m) kt_ms_item<TYPE, DT, R, 1>(a, tile, start + m, r0, grid);
+      for (int m = 0; m < count; ++m) kt_ms_item<TYPE, DT, R, 1, WT>(a, tile, start + m, r0, grid);
   }
 }
 
@@ -768,12 +768,15 @@ __global__ void __launch_bounds__(256, WMAX >= 8 ? 2 : 3) kt_moe_vec_ms_kernel(c
 // issued a.stages items ahead by one thread. Many copies of whole tiles stay in flight per SM,
 // so HBM latency hides behind the previous tiles' arithmetic, and the warps read the weights
 // from shared memory instead of issuing small global loads.
+// BOOK (IQ3_S): 0 the 512-word grid and sign masks (KtWgt), 1 the signed code book (KtWgtS3,
+// 32 KB of shared memory after the stages; the same integers with fewer instructions and shared
+// loads per chunk).
 constexpr int kMsbMaxStages = 4;
 
-template <int TYPE, int DT, int R, int WMAX>
+template <int TYPE, int DT, int R, int WMAX, int BOOK = 0>
 __global__ void __launch_bounds__(256, 2) kt_moe_vec_msb_kernel(const KtVecArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
-  __shared__ uint32_t grid_s[KtGridSmem<TYPE>::WORDS];
+  __shared__ uint32_t grid_s[BOOK ? 1 : KtGridSmem<TYPE>::WORDS];
   __shared__ __align__(8) uint64_t full[kMsbMaxStages];
   constexpr int kRows = 8 * R;
   const int tid = threadIdx.x;
@@ -781,11 +784,17 @@ __global__ void __launch_bounds__(256, 2) kt_moe_vec_msb_kernel(const KtVecArgs 
   const int tiles = (a.rows + kRows - 1) / kRows;
   const int n_items = a.groups[0] * tiles;
   const int64_t tile_cap = ((int64_t)kRows * a.row_bytes + 127) & ~(int64_t)127;
+  uint32_t* book = grid_s;
   if (tid == 0) {
     for (int i = 0; i < S; ++i) kt_mbar_init(&full[i], 1);
     kt_fence_mbar_init();
   }
-  kt_stage_grid<TYPE>(grid_s, tid, blockDim.x);
+  if constexpr (BOOK == 1) {
+    book = reinterpret_cast<uint32_t*>(smem + S * tile_cap);
+    kt_stage_iq3s_signed(book, tid, blockDim.x);
+  } else {
+    kt_stage_grid<TYPE>(grid_s, tid, blockDim.x);
+  }
   __syncthreads();
   auto issue = [&](int j) {  // the raw rows of this CTA's j-th item into stage j % S
     const int item = blockIdx.x + j * gridDim.x;
@@ -833,8 +842,10 @@ __global__ void __launch_bounds__(256, 2) kt_moe_vec_msb_kernel(const KtVecArgs 
         const int p = a.order[start + i / nr];
         kt_store_act<DT>(a.y, (int64_t)p * a.rows + r0 + i % nr, 0.0f);
       }
+    } else if constexpr (BOOK == 1) {
+      kt_ms_group<TYPE, DT, R, WMAX, KtWgtS3>(a, smem + (j % S) * tile_cap, start, count, r0, book);
     } else {
-      kt_ms_group<TYPE, DT, R, WMAX>(a, smem + (j % S) * tile_cap, start, count, r0, grid_s);
+      kt_ms_group<TYPE, DT, R, WMAX>(a, smem + (j % S) * tile_cap, start, count, r0, book);
     }
     __syncthreads();  // every warp is done with the stage
     if (tid == 0) issue(j + S);
@@ -905,6 +916,16 @@ int kt_vec_ms_piece() {
 // kernel. KT_B200_VEC_MSB=0 turns it off, =all takes it for every type (tuning runs).
 constexpr int64_t kMsbTileBytes = 36 * 1024;
 constexpr int64_t kMsbSmemBytes = 100 * 1024;
+// IQ3_S's code book in the bulk-staged kernel (see kt_moe_vec_msb_kernel): the signed book (32 KB
+// of the shared-memory budget) unless KT_B200_VEC_IQ3S_BOOK=0. Config 3's gate/up (B200, L2
+// flushed): 236 / 87 us at 64 / 16 tokens against 251 / 91 with the plain grid.
+static int msb_book(int type) {
+  static const int book = [] {
+    const char* e = getenv("KT_B200_VEC_IQ3S_BOOK");
+    return e && e[0] == '0' ? 0 : 1;
+  }();
+  return type == KT_IQ3_S ? book : 0;
+}
 static int pick_msb_rows(const KtVecArgs& a, int type, int* stages) {
   static const int mode = [] {  // 0 off, 1 IQ3_S, 2 every type
     const char* e = getenv("KT_B200_VEC_MSB");
@@ -912,11 +933,12 @@ static int pick_msb_rows(const KtVecArgs& a, int type, int* stages) {
   }();
   if (mode == 0 || (mode == 1 && type != KT_IQ3_S)) return 0;
   if (!a.table && (((uintptr_t)a.w) & 15)) return 0;
+  const int64_t budget = kMsbSmemBytes - (msb_book(type) ? 4 * kIq3sBookWords : 0);
   for (int R = 4; R >= 1; R /= 2) {
     const int64_t rows = 8 * R, bytes = rows * a.row_bytes;
     if (bytes > kMsbTileBytes || bytes % 16 || a.rows % rows) continue;
     const int64_t cap = (bytes + 127) & ~(int64_t)127;
-    const int64_t st = kMsbSmemBytes / cap;
+    const int64_t st = budget / cap;
     if (st < 2) continue;
     *stages = (int)(st < kMsbMaxStages ? st : kMsbMaxStages);
     return R;
@@ -928,8 +950,10 @@ template <int TYPE, int DT, int R, int WM>
 static int launch_msb_t(KtVecArgs a, int stages, int max_groups, cudaStream_t s) {
   a.stages = stages;
   const int64_t cap = ((int64_t)8 * R * a.row_bytes + 127) & ~(int64_t)127;
-  const size_t smem = (size_t)(stages * cap);
-  auto k = kt_moe_vec_msb_kernel<TYPE, DT, R, WM>;
+  constexpr bool kBooks = TYPE == KT_IQ3_S;
+  const int book = kBooks ? msb_book(TYPE) : 0;
+  const size_t smem = (size_t)(stages * cap) + (book ? 4 * kIq3sBookWords : 0);
+  auto k = book ? kt_moe_vec_msb_kernel<TYPE, DT, R, WM, kBooks ? 1 : 0> : kt_moe_vec_msb_kernel<TYPE, DT, R, WM, 0>;
   if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess) return -3;
   const int64_t tiles = (a.rows + 8 * R - 1) / (8 * R);
   const int64_t items = (int64_t)max_groups * tiles, cap_ctas = 2 * (int64_t)vec_num_sms();
