@@ -610,11 +610,15 @@ def run_ep(args, rank, world, local_rank, cfg_id=2):
     err = float((out[:n_chk].float() - ref.float()).norm() / ref.float().norm())
     # phases of one call (events around dispatch, local experts, combine)
     p2p = world > 1 and layer.p2p and args.ep_chunks == 1
-    ph = []
+    ph, fine = [], []
     for _ in range(5):
         e = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
         if p2p:
-            layer._call_p2p(x, ids, wts, events=e)
+            e8 = [torch.cuda.Event(enable_timing=True) for _ in range(8)]
+            layer._call_p2p(x, ids, wts, events=e8)
+            torch.cuda.synchronize()
+            fine.append([e8[j].elapsed_time(e8[j + 1]) for j in range(7)])
+            e = [e8[0], e8[4], e8[5], e8[7]]
         else:
             e[0].record(stream)
             xr, ir, wr, plan = layer.dispatch(x, ids, wts)
@@ -626,6 +630,11 @@ def run_ep(args, rank, world, local_rank, cfg_id=2):
         torch.cuda.synchronize()
         ph.append([e[j].elapsed_time(e[j + 1]) for j in range(3)])
     phases = [statistics.median(p[j] for p in ph) for j in range(3)]
+    fine_ms = None
+    if fine:
+        names = ("plan", "count_all_gather", "dispatch_kernel", "barrier_rows_in_place", "local_experts",
+                 "barrier_partials_in_place", "combine_kernel")
+        fine_ms = {n: statistics.median(f[j] for f in fine) for j, n in enumerate(names)}
     if p2p:  # the received rows, from the exchange buffers (outside the timed region)
         n_recv = int(layer.peers.recv_total.item())
         xr, ir, wr = layer.peers.x[:n_recv], layer.peers.ids[:n_recv], layer.peers.w[:n_recv]
@@ -712,12 +721,16 @@ def run_ep(args, rank, world, local_rank, cfg_id=2):
             "metric": st["metric"], "value": world * T * args.steps / (ms * 1e-3), "unit": "tokens/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None,
-            "dtype": "bf16 (GGUF weights dequantized in-kernel, fp32 accumulate)", "data": "synthetic (seeded)",
+            "dtype": ("bf16 (GGUF weights dequantized to bf16 once per call, fp32 accumulate)" if predq_ep == 3 else
+                      "bf16 (GGUF gate/up weights dequantized to bf16 once per call, down in-kernel, fp32 accumulate)"
+                      if predq_ep else "bf16 (GGUF weights dequantized in-kernel, fp32 accumulate)"),
+            "data": "synthetic (seeded)",
             "config": dict({"workload": st["workload"], "tokens_per_gpu": T, "hidden": K, "inter": N,
                             "parallelism": f"ep{world}",
                             "l2": "no flush: one step's working set exceeds the 126 MB L2"}, **st["config"]),
             "layer_tflops": world * st["flops"] * args.steps / (ms * 1e-3) / 1e12,
             "ep": {"phase_ms_unpipelined": {"dispatch": phases[0], "local_experts": phases[1], "combine": phases[2]},
+                   "exchange_ms_rank0": fine_ms,
                    "local_experts_ms_per_rank": [v[3] for v in every],
                    "local_experts_imbalance_ms": max(v[3] for v in every) - min(v[3] for v in every),
                    "dispatch_ms_per_rank": [v[2] for v in every],

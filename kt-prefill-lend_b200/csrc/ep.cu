@@ -224,7 +224,17 @@ __global__ void __launch_bounds__(256) kt_ep_dispatch_p2p_kernel(
     if (row >= rows_cap) continue;  // cannot happen with buffers of the planned capacity
     const uint4* src = reinterpret_cast<const uint4*>(x + (int64_t)send_token[i] * K);
     uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(peer_x[d]) + row * K);
-    for (int64_t c = lane; c < chunks; c += 32) dst[c] = __ldg(src + c);
+    // a lane's loads of up to 8 chunks are all in flight before its (remote) stores
+    constexpr int U = 8;
+    for (int64_t c0 = lane; c0 < chunks; c0 += 32 * U) {
+      uint4 v[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u)
+        if (c0 + 32 * u < chunks) v[u] = __ldg(src + c0 + 32 * u);
+#pragma unroll
+      for (int u = 0; u < U; ++u)
+        if (c0 + 32 * u < chunks) dst[c0 + 32 * u] = v[u];
+    }
     if (lane < k) {
       reinterpret_cast<int32_t*>(peer_ids[d])[row * k + lane] = meta[i * 2 * k + lane];
       reinterpret_cast<int32_t*>(peer_w[d])[row * k + lane] = meta[i * 2 * k + k + lane];

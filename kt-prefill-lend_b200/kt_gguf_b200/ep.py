@@ -313,12 +313,21 @@ class ExpertParallelMoE:
 
     def _call_p2p(self, x: torch.Tensor, topk_ids: torch.Tensor, topk_weights: torch.Tensor,
                   events: Optional[list] = None) -> torch.Tensor:
-        """events (optional): four CUDA events recorded on the stream at the call's start, once
-        the rows are exchanged, after the local layer, and at the end (phase timing)."""
+        """events (optional): CUDA events recorded on the stream for phase timing: four (the
+        call's start, once the rows are exchanged, after the local layer, the end) or eight (the
+        start, after the plan, after the count all-gather, after the dispatch kernel, once the rows
+        are exchanged, after the local layer, after the second barrier, the end)."""
         from . import _native as N
+
+        fine = events is not None and len(events) >= 8
+        where = {0: 0, 1: 4, 2: 5, 3: 7} if fine else {0: 0, 1: 1, 2: 2, 3: 3}
 
         def mark(i):
             if events is not None:
+                events[where[i]].record()
+
+        def mark_fine(i):
+            if fine:
                 events[i].record()
 
         T, K = x.shape
@@ -330,11 +339,14 @@ class ExpertParallelMoE:
         x = x.contiguous()
         mark(0)
         plan = self._plan(x, topk_ids, topk_weights)
+        mark_fine(1)
         dist.all_gather_into_tensor(pb.counts_all, plan["counts"], group=self.group)
+        mark_fine(2)
         N.check(lib.kt_ep_dispatch_p2p(N.ptr(x), K, N.ptr(plan["send_token"]), N.ptr(plan["meta"]), k,
                                        N.ptr(pb.counts_all), self.rank, self.world, N.ptr(pb.peer[0]),
                                        N.ptr(pb.peer[1]), N.ptr(pb.peer[2]), pb.rows_cap, N.ptr(pb.recv_total), st),
                 "kt_ep_dispatch_p2p")
+        mark_fine(3)
         self._barrier(dev)  # every rank's rows are in place
         mark(1)
         b = self.calls % 2
@@ -342,6 +354,7 @@ class ExpertParallelMoE:
         shared = self.shared_fn(x) if self.shared_fn is not None else None
         mark(2)
         self._barrier(dev)  # every rank's partial outputs are in place
+        mark_fine(6)
         out = torch.empty((T, K), dtype=x.dtype, device=dev)
         sh = shared.to(x.dtype).contiguous() if shared is not None else None
         N.check(lib.kt_ep_combine_p2p(N.ptr(plan["row_of"]), N.ptr(pb.counts_all), self.rank, self.world,
