@@ -792,7 +792,18 @@ __device__ __forceinline__ int32_t kt_block_exclusive_scan(int32_t v, int32_t* w
   return excl;
 }
 
-// warp w handles slots w, w + 32, ...; lanes walk the blocks (independent loads in flight)
+// Up to 1024 slots: G threads per slot (G the largest power of two <= 32 with G * n_slots <=
+// 1024), thread (slot e, run j) owning the blocks [j * ceil(nb / G), ...): its loads of one block
+// row are coalesced with the other slots' threads, eight independent loads in flight, and the
+// per-slot prefix over the G runs is taken in shared memory. More slots: warp w handles slots
+// w, w + 32, ...; lanes walk the blocks. Both give hist[b][e] = base(e) + the routes of slot e
+// in the blocks before b.
+__device__ __forceinline__ int kt_scan_threads_per_slot(int n_slots) {
+  if (n_slots > kPermBlock) return 0;
+  int g = 32;
+  while (g > 1 && g * n_slots > kPermBlock) g >>= 1;
+  return g;
+}
 __global__ void __launch_bounds__(kPermBlock) kt_perm_scan_kernel(int32_t* __restrict__ hist, int n_blocks, int n_slots,
                                                                   int tile_tokens, int chunk_tiles,
                                                                   int32_t* __restrict__ counts,
@@ -801,16 +812,45 @@ __global__ void __launch_bounds__(kPermBlock) kt_perm_scan_kernel(int32_t* __res
                                                                   int32_t* __restrict__ chunks) {
   __shared__ int32_t warp_sums[32];
   __shared__ int32_t sbase[kPermMaxSlots];
+  __shared__ int32_t part[kPermBlock];  // [run j][slot e]: routes of the run, then its exclusive prefix
   kt_pdl_trigger();
   kt_pdl_wait();  // the block histograms are complete
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  const int G = kt_scan_threads_per_slot(n_slots);
+  const int nbp = G ? (n_blocks + G - 1) / G : 0;  // blocks per run
+  const int my_e = G ? (int)threadIdx.x % n_slots : 0, my_j = G ? (int)threadIdx.x / n_slots : 0;
+  const bool runs = G && (int)threadIdx.x < G * n_slots;
+  const int rb0 = my_j * nbp, rb1 = min(n_blocks, rb0 + nbp);
+  constexpr int U = 8;
   // 1. per-slot totals
-  for (int e = wid; e < n_slots; e += nw) {
-    int32_t v = 0;
-    for (int b = lane; b < n_blocks; b += 32) v += hist[(int64_t)b * n_slots + e];
+  if (G) {
+    if (runs) {
+      int32_t v = 0;
+      for (int b = rb0; b < rb1; b += U) {
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-    if (lane == 0) counts[e] = v;
+        for (int u = 0; u < U; ++u)
+          if (b + u < rb1) v += hist[(int64_t)(b + u) * n_slots + my_e];
+      }
+      part[my_j * n_slots + my_e] = v;
+    }
+    __syncthreads();
+    if ((int)threadIdx.x < n_slots) {
+      int32_t acc = 0;
+      for (int j = 0; j < G; ++j) {
+        const int32_t v = part[j * n_slots + threadIdx.x];
+        part[j * n_slots + threadIdx.x] = acc;
+        acc += v;
+      }
+      counts[threadIdx.x] = acc;
+    }
+  } else {
+    for (int e = wid; e < n_slots; e += nw) {
+      int32_t v = 0;
+      for (int b = lane; b < n_blocks; b += 32) v += hist[(int64_t)b * n_slots + e];
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+      if (lane == 0) counts[e] = v;
+    }
   }
   __syncthreads();
   // 2. slot bases and tile offsets: exclusive scans over the slots (thread t owns [e0, e1))
@@ -845,7 +885,21 @@ __global__ void __launch_bounds__(kPermBlock) kt_perm_scan_kernel(int32_t* __res
   }
   __syncthreads();
   // 3. hist[b][e] <- base(e) + routes of slot e in the blocks before b
-  for (int e = wid; e < n_slots; e += nw) {
+  if (runs) {
+    int32_t carry = sbase[my_e] + part[my_j * n_slots + my_e];
+    for (int b = rb0; b < rb1; b += U) {
+      int32_t v[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u) v[u] = b + u < rb1 ? hist[(int64_t)(b + u) * n_slots + my_e] : 0;
+#pragma unroll
+      for (int u = 0; u < U; ++u)
+        if (b + u < rb1) {
+          hist[(int64_t)(b + u) * n_slots + my_e] = carry;
+          carry += v[u];
+        }
+    }
+  }
+  for (int e = wid; !G && e < n_slots; e += nw) {
     int32_t carry = sbase[e];
     for (int b0 = 0; b0 < n_blocks; b0 += 32) {
       const int b = b0 + lane;

@@ -213,6 +213,47 @@ def test_prefill_headline_config2_16k(cuda_device):
     assert err_fp32 < ref_fp32 and err_ref < 3e-2
 
 
+@pytest.mark.parametrize("S", [3, 64, 513, 1024, 1500])
+def test_permutation_exact_across_slot_counts(cuda_device, S):
+    # the routing permutation's scan takes 32..1 threads per slot up to 1024 slots (3, 64, 513,
+    # 1024 here) and one warp per slot above (1500): counts, the sorted position of every route
+    # and the token of every sorted row, exact, over 47 blocks of routes; the slots are a pointer
+    # table aliasing 4 experts
+    dev = cuda_device
+    T, k, E = 6000, 8, 4
+    L = synth.make_layer(seed=S, tokens=8, hidden=512, inter=256, n_experts=E, top_k=2, type13=12, type2=14)
+    w13, w2 = torch.from_numpy(L.w13).to(dev), torch.from_numpy(L.w2).to(dev)
+    g = torch.Generator().manual_seed(S)
+    slot_expert = torch.randint(0, E, (S,), generator=g)
+    t13 = torch.tensor([w13[e].data_ptr() for e in slot_expert.tolist()], dtype=torch.int64, device=dev)
+    t2 = torch.tensor([w2[e].data_ptr() for e in slot_expert.tolist()], dtype=torch.int64, device=dev)
+    ids = torch.randint(0, S, (T, k), generator=g, dtype=torch.int32)
+    ids[::7, 3] = -1
+    ids[::11, 1] = S + 5  # not a resident slot
+    w = torch.rand((T, k), generator=g) / k
+    x = (torch.randn((T, 512), generator=g)).to(torch.bfloat16)
+    lib = Nt.load()
+    ws = Nt.workspace(lib.kt_moe_prefill_workspace_size(T, k, 512, 256, S), dev)
+    M.moe_prefill(x.to(dev), t13, t2, ids.to(dev), w.to(dev), 12, 14, 256, table=True, workspace=ws)
+    torch.cuda.synchronize()
+    offs = (ctypes.c_size_t * 8)()
+    lib.kt_moe_prefill_workspace_layout(T, k, 512, 256, S, offs)
+    R = T * k
+    view = lambda i, n: ws[offs[i]:offs[i] + 4 * n].view(torch.int32).cpu()  # noqa: E731
+    flat = ids.reshape(-1)
+    resident = (flat >= 0) & (flat < S)
+    assert torch.equal(view(1, S), torch.bincount(flat[resident].long(), minlength=S).int())
+    pos = view(5, R)
+    assert torch.all(pos[~resident] == -1)
+    rp = pos[resident].long()
+    assert torch.equal(torch.sort(rp).values, torch.arange(int(resident.sum())))
+    assert torch.equal(view(4, R)[rp], (torch.arange(R) // k)[resident].int())
+    # sorted rows are grouped by slot in slot order
+    slot_of_row = torch.empty(int(resident.sum()), dtype=torch.int64)
+    slot_of_row[rp] = flat[resident].long()
+    assert torch.all(slot_of_row[1:] >= slot_of_row[:-1])
+
+
 def test_prefill_maximum_top_k_and_slot_count(cuda_device):
     # the layer's limits: top_k 32 and 8192 slots (the permutation's shared-memory histogram);
     # the slots are a pointer table whose 8192 entries alias 12 distinct experts, and every
