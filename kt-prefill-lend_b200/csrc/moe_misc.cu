@@ -9,7 +9,10 @@
 //   topk         router top-k: softmax, and DeepSeek-V3 grouped sigmoid routing
 //   permute      counting sort of routes by slot into 256-token tiles for the prefill GEMM
 #include <stdlib.h>
+
+#include <type_traits>
 #include "gguf_dot.cuh"
+#include "gguf_tile.cuh"
 #include "kt_kernels.h"
 
 // ------------------------------------------------------------------ dequant
@@ -179,7 +182,37 @@ __global__ void __launch_bounds__(256, 3) kt_dequant16p_kernel(const uint8_t* __
       __syncthreads();
     }
     uint4* stage = reinterpret_cast<uint4*>(dq_smem + kDqStages * D::RAWA + (j & 1) * 256 * 64);
-    if (t < nsub) {
+    if constexpr (TYPE == KT_Q4_K || TYPE == KT_Q6_K || TYPE == KT_IQ3_S) {
+      static_assert(DT == KT_DT_BF16, "the tile decoders produce bf16");
+      // the prefill GEMM producers' decoders (gguf_tile.cuh: the same bf16 values, with aligned
+      // 16-byte reads and packed f32x2 arithmetic): task = (block u, quarter qt), the quarter's
+      // 16 values of each of the block's four 64-value k-steps
+      for (int task = t; task < (nsub / D::SPB) * 4; task += 256) {
+        const int u = task >> 2, qt = task & 3;
+        const int ub = u * D::BS;
+        const uint8_t* slot = raw + (ub & ~15);
+        const int off = ub & 15;
+        KtTileDq<TYPE> dq;
+        auto run = [&](auto a16) {
+          constexpr bool A16 = decltype(a16)::value;
+          dq.template unit<A16>(slot, off, qt);
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) {
+            uint32_t pk[8];
+            dq.template kstep_quarter<A16>(slot, off, kk, qt, pk, grid_s);
+            uint4* d = stage + (u * 256 + kk * 64 + qt * 16) / 8;
+            d[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+            d[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+          }
+        };
+        if constexpr (KtTileDq<TYPE>::kAlignable) {  // Q4_K: 144-byte blocks, always on a boundary
+          run(std::integral_constant<bool, true>());
+        } else {
+          run(std::integral_constant<bool, false>());
+        }
+      }
+      kt_fence_proxy_async_smem();
+    } else if (t < nsub) {
       float y[32];
       kt_dq32<TYPE>(raw, t, y, grid_s);
       uint32_t pk[16];
